@@ -1,0 +1,302 @@
+/*
+ * tvarant.h — C ABI of the B200 runtime and kernels behind the `tvarant`
+ * PyTorch device.
+ *
+ * This header replaces the reference's internal runtime boundary: the
+ * `tvarant::TvarantRuntime` virtual interface and the `LaunchParams`
+ * grab-bag that every ATen kernel fills before `runtime().launch(p)`
+ * (csrc/runtime/TvarantRuntime.h:17-61 in samthakur587/Tvarant).  Where the
+ * reference dispatches on a kernel-name string (csrc/runtime/CpuSimRuntime.cpp:109-218),
+ * each kernel here is its own typed entry point.
+ *
+ * Conventions (all entry points):
+ *   - return 0 (TVR_OK) on success, a TVR_ERR_* code otherwise; the message
+ *     for the calling thread is available from tvr_last_error();
+ *   - buffers are borrowed raw device pointers; no entry point keeps a
+ *     pointer after it returns (the caching allocator owns what it hands out);
+ *   - sizes, strides and element counts are int64_t, in elements;
+ *   - `stream` is a cudaStream_t passed as void* (NULL = legacy default
+ *     stream); work is enqueued asynchronously on it;
+ *   - all floating-point kernels compute in fp32.
+ * Kernels that wait on a barrier inside the device give up after a bounded
+ * number of polls and record TVR_DEV_* in a per-device status word, read with
+ * tvr_get_status(); they never trap.
+ */
+#ifndef TVARANT_H_
+#define TVARANT_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#pragma GCC visibility push(default)
+#endif
+
+/* ---- status codes ------------------------------------------------------ */
+#define TVR_OK 0
+#define TVR_ERR_INVALID 1     /* bad argument (shape, null pointer, op id)      */
+#define TVR_ERR_CUDA 2        /* a CUDA runtime/driver call failed              */
+#define TVR_ERR_UNSUPPORTED 3 /* valid request this build does not implement   */
+#define TVR_ERR_OOM 4         /* device or pinned allocation failed             */
+#define TVR_ERR_TIMEOUT 5     /* a bounded wait expired (host or device side)   */
+#define TVR_ERR_NCCL 6        /* NCCL missing or an NCCL call failed            */
+#define TVR_ERR_JIT 7         /* NVRTC compilation or module load failed        */
+
+/* device-side status word values (tvr_get_status) */
+#define TVR_DEV_OK 0
+#define TVR_DEV_TIMEOUT_PRODUCER 1 /* TMA producer gave up waiting for a free stage */
+#define TVR_DEV_TIMEOUT_MMA 2      /* MMA issuer gave up waiting for data / TMEM    */
+#define TVR_DEV_TIMEOUT_EPILOGUE 3 /* epilogue gave up waiting for an accumulator   */
+#define TVR_DEV_TIMEOUT_DRAIN 4    /* exit-time drain of async copies gave up       */
+
+/* GEMM precision modes */
+#define TVR_GEMM_AUTO 0    /* TVARANT_GEMM_MODE env, else 3xTF32               */
+#define TVR_GEMM_TF32 1    /* tcgen05 kind::tf32, one pass                      */
+#define TVR_GEMM_3XTF32 2  /* hi*hi + hi*lo + lo*hi split, fp32-faithful        */
+#define TVR_GEMM_FP32 3    /* CUDA-core fp32 FMA (exact fp32 products)          */
+
+/* activations; same numbering as the reference `jit::apply_act`
+ * (csrc/jit/Jit.h:48-56): 0 none, 1 relu, 2 silu */
+#define TVR_ACT_NONE 0
+#define TVR_ACT_RELU 1
+#define TVR_ACT_SILU 2
+
+/* unary op ids for tvr_unary; each replaces one OpenCL kernel / host loop
+ * (csrc/kernels/host/HostKernels.cpp:39-98, csrc/runtime/OpenCLRuntime.cpp:49-88) */
+#define TVR_UNARY_RELU 0
+#define TVR_UNARY_SILU 1
+#define TVR_UNARY_NEG 2
+#define TVR_UNARY_ABS 3
+#define TVR_UNARY_EXP 4
+#define TVR_UNARY_EXP2 5
+#define TVR_UNARY_SQRT 6
+#define TVR_UNARY_RSQRT 7      /* 1/sqrt(x), as HostKernels.cpp:94-98      */
+#define TVR_UNARY_SCALE 8      /* x * scalar   (scale_kernel)              */
+#define TVR_UNARY_ADD_SCALAR 9 /* x + scalar   (add_scalar_kernel)         */
+#define TVR_UNARY_SIGMOID 10
+#define TVR_UNARY_COPY 11
+
+/* binary op ids for tvr_binary */
+#define TVR_BINARY_ADD 0 /* a + alpha*b (add_kernel, HostKernels.cpp:27-31) */
+#define TVR_BINARY_MUL 1 /* a * b       (mul_kernel, HostKernels.cpp:33-37) */
+
+#define TVR_MAX_DIMS 8
+
+/* ---- errors / init ----------------------------------------------------- */
+
+/* Thread-local message of the last failing call on this thread ("" if none). */
+const char* tvr_last_error(void);
+
+/* Idempotent process-wide initialisation (device enumeration, driver entry
+ * points).  Replaces tvarant::initialize_runtime (csrc/runtime/Runtime.cpp:39-47). */
+int tvr_init(void);
+
+/* Backend name, "cuda".  Replaces TvarantRuntime::name (TvarantRuntime.h:42). */
+const char* tvr_backend_name(void);
+
+/* ---- devices ----------------------------------------------------------- */
+
+/* Number of visible GPUs.  Replaces kDeviceCount (TvarantRuntime.h:12). */
+int tvr_device_count(int* count);
+/* Current device of the calling thread.  Replaces current_device /
+ * set_device (csrc/runtime/Runtime.cpp:55-71). */
+int tvr_get_device(int* device);
+int tvr_set_device(int device);
+/* Number of SMs, for grid sizing in callers and tests. */
+int tvr_device_sm_count(int device, int* sms);
+/* Wait for all work on `device`.  Replaces TvarantRuntime::synchronize
+ * (TvarantRuntime.h:60). */
+int tvr_device_synchronize(int device);
+/* Device-side status word (TVR_DEV_*), set by kernels whose bounded waits
+ * expired.  tvr_clear_status resets it to TVR_DEV_OK. */
+int tvr_get_status(int device, int* code);
+int tvr_clear_status(int device);
+
+/* ---- memory ------------------------------------------------------------ */
+
+/* Stream-ordered caching allocation on `device` (a pool that keeps freed
+ * blocks).  Replaces TvarantRuntime::alloc/free (TvarantRuntime.h:45-46) and
+ * the posix_memalign sim allocator (csrc/runtime/CpuSimRuntime.cpp:63-81).
+ * nbytes == 0 returns NULL.  Allocations are 256-byte aligned. */
+int tvr_malloc(void** ptr, size_t nbytes, int device, void* stream);
+int tvr_free(void* ptr);
+/* Make the free of `ptr` wait for the work queued so far on `stream`
+ * (a cross-stream use; c10 recordDataPtrOnStream). */
+int tvr_record_stream(void* ptr, void* stream);
+/* Device index of an allocation made by tvr_malloc, or -1.  Replaces
+ * TvarantRuntime::owns (TvarantRuntime.h:47) used by getDeviceFromPtr. */
+int tvr_pointer_device(const void* ptr, int* device);
+/* Bytes held by the pool (reserved) and handed out (in use) on `device`. */
+int tvr_memory_stats(int device, size_t* reserved, size_t* in_use);
+/* Return cached, unused blocks of `device` to the driver. */
+int tvr_empty_cache(int device);
+/* Page-locked host memory for asynchronous copies. */
+int tvr_host_alloc(void** ptr, size_t nbytes);
+int tvr_host_free(void* ptr);
+int tvr_is_pinned(const void* ptr, int* pinned);
+
+/* Asynchronous copies on `stream`.  Replace TvarantRuntime::copy_h2d /
+ * copy_d2h / copy_d2d (TvarantRuntime.h:49-51).  With pageable host memory
+ * the copy is staged by the driver and returns after the host side is read. */
+int tvr_memcpy_h2d(void* dst, const void* src, size_t nbytes, void* stream);
+int tvr_memcpy_d2h(void* dst, const void* src, size_t nbytes, void* stream);
+int tvr_memcpy_d2d(void* dst, const void* src, size_t nbytes, void* stream);
+
+/* ---- streams and events (the reference has only the DEFAULT stream,
+ * csrc/runtime/Guard.cpp:43-62) ------------------------------------------ */
+int tvr_stream_create(void** stream, int device, int priority);
+int tvr_stream_destroy(void* stream);
+int tvr_stream_synchronize(void* stream);
+int tvr_stream_query(void* stream, int* done);
+int tvr_stream_wait_event(void* stream, void* event);
+int tvr_event_create(void** event, int enable_timing);
+int tvr_event_destroy(void* event);
+int tvr_event_record(void* event, void* stream);
+int tvr_event_synchronize(void* event);
+int tvr_event_query(void* event, int* done);
+int tvr_event_elapsed_ms(void* start, void* end, float* ms);
+
+/* ---- dense contractions (tensor cores) --------------------------------- */
+
+/* C[m,n] = act(alpha * sum_k A[m,k]*B(k,n) + beta * P[m,n]) where
+ * P[m,n] = bias[n] if bias != NULL, else C[m,n] if beta != 0, else 0.
+ * A is row-major [m,k] with row stride lda.  B is [n,k] (row stride ldb) when
+ * trans_b != 0 (nn.Linear weight), else [k,n] (row stride ldb).  C is
+ * row-major [m,n] with row stride ldc.  `mode` is a TVR_GEMM_* value.
+ * Replaces ops::gemm_bias_act (csrc/aten/AtenCommon.h:33-86) ->
+ * LaunchParams{"gemm_bias_act_kernel"} -> host::gemm_bias_act_f32
+ * (csrc/kernels/host/HostKernels.cpp:100-144) / gemm.cl:27-64. */
+int tvr_gemm_bias_act(const float* a, const float* b, const float* bias, float* c,
+                      int64_t m, int64_t n, int64_t k,
+                      int64_t lda, int64_t ldb, int64_t ldc,
+                      float alpha, float beta, int act, int trans_b, int mode,
+                      void* stream);
+
+/* Batched C[i] = A[i] * op(B[i]) for i < batch, each as tvr_gemm_bias_act
+ * with alpha 1, beta 0, no activation; matrices are dense row-major with the
+ * given element strides between batch entries (stride_b may be 0 to
+ * broadcast one B).  Replaces LaunchParams{"bmm_kernel"} -> host::bmm_f32
+ * (csrc/kernels/host/HostKernels.cpp:146-172) / gemm.cl:66-95. */
+int tvr_bmm(const float* a, const float* b, float* c,
+            int64_t batch, int64_t m, int64_t n, int64_t k,
+            int64_t stride_a, int64_t stride_b, int64_t stride_c,
+            int trans_b, int mode, void* stream);
+
+/* ---- reductions and gathers (memory-bound) ----------------------------- */
+
+/* Softmax over `dim` of a contiguous (outer, dim, inner) view:
+ * y = exp(x - max) * (1 / sum exp(x - max)).  Replaces
+ * LaunchParams{"softmax_kernel"} -> host::softmax_f32
+ * (csrc/kernels/host/HostKernels.cpp:174-198) / reduce.cl:2-30. */
+int tvr_softmax(const float* x, float* y, int64_t outer, int64_t dim, int64_t inner,
+                void* stream);
+
+/* Row layer norm of x[rows, n]: mean, biased variance (two-pass),
+ * rstd = 1/sqrt(var + eps), y = (x - mean) * rstd [* gamma] [+ beta].
+ * gamma, beta, mean, rstd may be NULL.  Replaces
+ * LaunchParams{"layernorm_kernel"} -> host::layer_norm_f32
+ * (csrc/kernels/host/HostKernels.cpp:200-242) / reduce.cl:32-74. */
+int tvr_layer_norm(const float* x, const float* gamma, const float* beta, float* y,
+                   float* mean, float* rstd, int64_t rows, int64_t n, float eps,
+                   void* stream);
+
+/* out[i, :] = weight[idx[i], :] for i < n_idx; an index outside [0, vocab)
+ * gives a zero row.  `indices` are int64 (index_bits 64) or int32
+ * (index_bits 32) read directly on the device.  Replaces
+ * LaunchParams{"embedding_kernel"} -> host::embedding_f32
+ * (csrc/kernels/host/HostKernels.cpp:244-260) / reduce.cl:76-95, and the
+ * host round trip of the indices in ops::embedding (csrc/aten/LlmOps.cpp:238-246). */
+int tvr_embedding(const float* weight, const void* indices, int index_bits, float* out,
+                  int64_t n_idx, int64_t dim, int64_t vocab, void* stream);
+
+/* ---- elementwise ------------------------------------------------------- */
+
+/* y[i] = op(x[i]) (TVR_UNARY_*), scalar used by SCALE / ADD_SCALAR.  x and y
+ * may alias.  Replaces relu/silu/neg/abs/exp/exp2/sqrt/rsqrt/scale/
+ * add_scalar/copy kernels (HostKernels.cpp:23-98). */
+int tvr_unary(int op, const float* x, float* y, int64_t n, float scalar, void* stream);
+
+/* Fill n elements of `elem_size` bytes (1, 2, 4 or 8) with the bit pattern
+ * at `value` (host pointer).  Replaces fill_kernel (HostKernels.cpp:17-21). */
+int tvr_fill(void* dst, const void* value, int elem_size, int64_t n, void* stream);
+
+/* out = a (op) b over an `ndim`-dimensional output of `sizes`, with
+ * per-operand element strides (0 for a broadcast dimension); `out` is
+ * contiguous.  ADD computes a + alpha*b, MUL a*b.  Replaces add_kernel /
+ * mul_kernel and the expand().contiguous() materialisation in front of them
+ * (csrc/aten/Ops.cpp:283-327). */
+int tvr_binary(int op, const float* a, const float* b, float* out, int ndim,
+               const int64_t* sizes, const int64_t* a_strides, const int64_t* b_strides,
+               float alpha, void* stream);
+
+/* Strided -> strided copy of elements of `elem_size` bytes (1, 2, 4, 8 or
+ * 16) over an `ndim`-dimensional index space.  Replaces the CPU-view
+ * strided copy of _copy_from / clone / contiguous (csrc/aten/Ops.cpp:185-212,
+ * csrc/aten/ExtendedOps.cpp:100-143). */
+int tvr_strided_copy(void* dst, const void* src, int64_t elem_size, int ndim,
+                     const int64_t* sizes, const int64_t* dst_strides,
+                     const int64_t* src_strides, void* stream);
+
+/* Element type conversion between float32 (0), float64 (1), int32 (2),
+ * int64 (3), bool/uint8 (4) on contiguous buffers of n elements. */
+int tvr_convert(void* dst, int dst_type, const void* src, int src_type, int64_t n,
+                void* stream);
+
+/* ---- pointwise JIT ----------------------------------------------------- */
+
+/* One SSA node.  Opcodes 0-8 keep the reference numbering
+ * (csrc/jit/Jit.h:11-21): Load, Const, Add (a + alpha*b), Mul, Relu, Silu,
+ * Neg, Scale (alpha*a), Sigmoid; this build appends Sub (a - alpha*b) = 9,
+ * Exp = 10, Abs = 11. */
+typedef struct tvr_pw_node {
+  int32_t op;
+  int32_t a;
+  int32_t b;
+  int32_t input_id;
+  float alpha;
+  float c;
+} tvr_pw_node;
+
+#define TVR_PW_MAX_INPUTS 16
+
+/* out[i] = value of the last node at element i, for i < n.  The program is
+ * emitted as CUDA C, compiled by NVRTC for sm_100a and cached by its
+ * structure.  Replaces TvarantRuntime::launch_pointwise
+ * (TvarantRuntime.h:53-58) -> jit::run_pointwise_host (csrc/jit/Jit.cpp:34-87)
+ * / codegen_opencl (csrc/jit/Jit.cpp:89-138). */
+int tvr_pointwise(const tvr_pw_node* nodes, int n_nodes, int n_inputs,
+                  const float* const* inputs, float* out, int64_t n, void* stream);
+
+/* Writes the CUDA C source generated for a program into buf (NUL
+ * terminated, truncated to cap) and its length into *len.  Host only. */
+int tvr_pointwise_source(const tvr_pw_node* nodes, int n_nodes, int n_inputs, char* buf,
+                         size_t cap, size_t* len);
+
+/* ---- NCCL (no counterpart in the reference, which has one device) ------ */
+
+/* NCCL is loaded at run time; these return TVR_ERR_NCCL when it is absent.
+ * The unique id is NCCL's 128-byte ncclUniqueId. */
+int tvr_nccl_available(int* available);
+int tvr_nccl_get_unique_id(void* id128);
+int tvr_nccl_comm_init(void** comm, int nranks, const void* id128, int rank, int device);
+/* dtype: 0 float32; op: 0 sum.  In place when send == recv. */
+int tvr_nccl_all_reduce(const void* send, void* recv, int64_t count, int dtype, int op,
+                        void* comm, void* stream);
+int tvr_nccl_all_gather(const void* send, void* recv, int64_t send_count, int dtype,
+                        void* comm, void* stream);
+int tvr_nccl_comm_destroy(void* comm);
+int tvr_nccl_comm_abort(void* comm);
+
+#if defined(__GNUC__)
+#pragma GCC visibility pop
+#endif
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TVARANT_H_ */

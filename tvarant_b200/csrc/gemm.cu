@@ -1,0 +1,90 @@
+// C-ABI entry points of the dense contractions: precision-mode resolution
+// and the choice between the tcgen05 tensor-core kernel and the exact
+// CUDA-core kernel.
+//
+// Replaces ops::gemm_bias_act (csrc/aten/AtenCommon.h:33-86) and the
+// gemm_bias_act_kernel / bmm_kernel launches (csrc/runtime/CpuSimRuntime.cpp:166-188).
+#include "internal.h"
+
+#include <cstdlib>
+#include <cstring>
+
+#include "gemm_common.cuh"
+
+namespace tvr {
+namespace {
+
+// TVR_GEMM_AUTO resolves from TVARANT_GEMM_MODE (tf32 | 3xtf32 | fp32),
+// defaulting to the fp32-faithful 3xTF32 split.
+int resolve_mode(int mode) {
+  if (mode != TVR_GEMM_AUTO) return mode;
+  const char* env = std::getenv("TVARANT_GEMM_MODE");
+  if (env != nullptr) {
+    if (std::strcmp(env, "tf32") == 0) return TVR_GEMM_TF32;
+    if (std::strcmp(env, "3xtf32") == 0) return TVR_GEMM_3XTF32;
+    if (std::strcmp(env, "fp32") == 0 || std::strcmp(env, "ieee") == 0) return TVR_GEMM_FP32;
+  }
+  return TVR_GEMM_3XTF32;
+}
+
+// Below this many multiply-adds a launch of the persistent tensor-core
+// kernel costs more than it saves.
+constexpr int64_t kSmallMacs = int64_t(1) << 21;
+
+int run(const float* a, const float* b, const float* bias, float* c, int64_t m, int64_t n,
+        int64_t k, int64_t lda, int64_t ldb, int64_t ldc, int64_t batch, int64_t sa,
+        int64_t sb, int64_t sc, float alpha, float beta, int act, bool trans_b, int mode,
+        cudaStream_t stream) {
+  mode = resolve_mode(mode);
+  if (mode != TVR_GEMM_TF32 && mode != TVR_GEMM_3XTF32 && mode != TVR_GEMM_FP32) {
+    return fail(TVR_ERR_INVALID, "gemm: unknown precision mode %d", mode);
+  }
+  const int64_t macs = batch * m * n * k;
+  bool tensor = mode != TVR_GEMM_FP32 && macs > kSmallMacs;
+  // Skinny 3xTF32 problems are weight-bandwidth bound: the exact CUDA-core
+  // kernel reads each operand once and is as accurate.
+  if (mode == TVR_GEMM_3XTF32 && m <= 16) tensor = false;
+  if (tensor) {
+    const int rc = gemm_tcgen05(a, b, bias, c, m, n, k, lda, ldb, ldc, batch, sa, sb, sc, alpha,
+                                beta, act, trans_b, mode == TVR_GEMM_3XTF32, stream);
+    if (rc != TVR_ERR_UNSUPPORTED) return rc;
+  }
+  return gemm_simt(a, b, bias, c, m, n, k, lda, ldb, ldc, batch, sa, sb, sc, alpha, beta, act,
+                   trans_b, stream);
+}
+
+}  // namespace
+}  // namespace tvr
+
+using namespace tvr;
+
+extern "C" {
+
+int tvr_gemm_bias_act(const float* a, const float* b, const float* bias, float* c, int64_t m,
+                      int64_t n, int64_t k, int64_t lda, int64_t ldb, int64_t ldc, float alpha,
+                      float beta, int act, int trans_b, int mode, void* stream) {
+  TVR_CHECK(m >= 0 && n >= 0 && k >= 0, "gemm: negative size (%lld, %lld, %lld)",
+            (long long)m, (long long)n, (long long)k);
+  TVR_CHECK(act >= 0 && act <= 2, "gemm: unknown activation %d", act);
+  if (m == 0 || n == 0) return TVR_OK;
+  TVR_CHECK(c != nullptr, "gemm: null output");
+  TVR_CHECK(k == 0 || (a != nullptr && b != nullptr), "gemm: null operand");
+  TVR_CHECK(lda >= k && ldc >= n, "gemm: leading dimension too small");
+  TVR_CHECK(trans_b ? ldb >= k : ldb >= n, "gemm: leading dimension of B too small");
+  return run(a, b, bias, c, m, n, k, lda, ldb, ldc, 1, 0, 0, 0, alpha, beta, act, trans_b != 0,
+             mode, as_stream(stream));
+}
+
+int tvr_bmm(const float* a, const float* b, float* c, int64_t batch, int64_t m, int64_t n,
+            int64_t k, int64_t stride_a, int64_t stride_b, int64_t stride_c, int trans_b,
+            int mode, void* stream) {
+  TVR_CHECK(batch >= 0 && m >= 0 && n >= 0 && k >= 0, "bmm: negative size");
+  if (batch == 0 || m == 0 || n == 0) return TVR_OK;
+  TVR_CHECK(c != nullptr, "bmm: null output");
+  TVR_CHECK(k == 0 || (a != nullptr && b != nullptr), "bmm: null operand");
+  const int64_t lda = k, ldb = trans_b ? k : n, ldc = n;
+  return run(a, b, nullptr, c, m, n, k, lda, ldb, ldc, batch, stride_a, stride_b, stride_c, 1.f,
+             0.f, 0, trans_b != 0, mode, as_stream(stream));
+}
+
+}  // extern "C"

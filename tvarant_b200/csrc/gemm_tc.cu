@@ -1,0 +1,856 @@
+// Tensor-core fp32 GEMM for sm_100a: tcgen05.mma kind::tf32, accumulators in
+// tensor memory, operands staged by TMA into 128-byte-swizzled shared memory.
+//
+// Computes C = act(alpha * A * op(B) + beta * P) for the linear / addmm / mm
+// / bmm family — the reference's host::gemm_bias_act_f32 and host::bmm_f32
+// (csrc/kernels/host/HostKernels.cpp:100-172), there a scalar 32^3-tiled loop.
+//
+// Structure (one CTA per SM, persistent over output tiles):
+//   warp 0      TMA producer: A tile [128 x 32] and B tile [BN x 32] per
+//               k-block into a STAGES-deep ring (mbarrier full/empty pairs)
+//   warp 1      allocates TMEM; one lane issues the MMAs (4 x K=8 per
+//               k-block, 12 in 3xTF32 mode) and commits each stage back
+//   warps 2-5   epilogue: tcgen05.ld of the 128 x BN accumulator, bias /
+//               alpha / beta / activation, staged through swizzled shared
+//               memory and written with TMA stores
+// The accumulator is double-buffered in TMEM (2 x BN columns) so the
+// epilogue of tile i overlaps the main loop of tile i+1.
+//
+// Two precisions (TVR_GEMM_TF32 / TVR_GEMM_3XTF32).  kind::tf32 reads the
+// top 19 bits of each fp32 operand.  3xTF32 splits each operand into
+// hi = x with the low 13 mantissa bits cleared and lo = x - hi (exact in
+// fp32) and accumulates lo*hi + hi*lo + hi*hi, which restores fp32-level
+// accuracy at three times the tensor work.
+//
+// Every wait on an mbarrier is bounded.  A wait that expires records a
+// TVR_DEV_* code in the device status word and sets a CTA-wide abort flag;
+// all roles then leave their loops, in-flight TMA loads and MMAs are
+// drained (again with bounded waits), TMEM is freed and the kernel returns.
+//
+// No TMA load uses cluster multicast.
+#include "internal.h"
+
+#include <mutex>
+
+#include "gemm_common.cuh"
+
+namespace tvr {
+namespace tc {
+
+constexpr int BM = 128;
+constexpr int BK = 32;  // fp32 elements per k-block = 128 bytes = one swizzle row
+constexpr int NUM_THREADS = 192;
+constexpr int EPI_WARPS = 4;
+constexpr int STAGE_SMEM = 192 * 1024;
+constexpr int EPI_BUF_BYTES = 32 * 32 * 4;                 // one 32 x 32 fp32 sub-tile
+constexpr int EPI_SMEM = EPI_WARPS * 2 * EPI_BUF_BYTES;    // double-buffered per warp
+constexpr int GROUP_M = 8;                                 // tile raster group height
+constexpr unsigned long long WAIT_TIMEOUT_NS = 2000000000ull;  // 2 s per barrier phase
+constexpr unsigned WAIT_MAX_POLLS = 1u << 30;
+
+template <int BN, bool SPLIT3>
+struct Cfg {
+  static constexpr int A_BYTES = BM * BK * 4;
+  static constexpr int B_BYTES = BN * BK * 4;
+  static constexpr int OPERANDS = SPLIT3 ? 2 : 1;
+  static constexpr int STAGE_BYTES = OPERANDS * (A_BYTES + B_BYTES);
+  static constexpr int STAGES = STAGE_SMEM / STAGE_BYTES;
+  static constexpr int TMEM_COLS = 2 * BN;  // 128, 256 or 512: powers of two
+  static constexpr int BAR_BYTES = 8 * (2 * STAGES + 5) + 8;
+  static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + EPI_SMEM + BAR_BYTES;
+  static_assert(SMEM_BYTES <= 232448 - 64, "shared memory budget");
+  static_assert(BN == 64 || BN == 128 || BN == 256, "BN");
+};
+
+struct Params {
+  CUtensorMap tma_a;     // A or A_hi: dims {K, M, batch}
+  CUtensorMap tma_b;     // B or B_hi: {K, N, batch} (K-major) or {N, K, batch} (N-major)
+  CUtensorMap tma_a_lo;  // 3xTF32 low parts, same geometry
+  CUtensorMap tma_b_lo;
+  CUtensorMap tma_c;     // output (or split-K workspace): {N, M, batch | splits}
+  const float* bias;
+  float* c;
+  int64_t ldc;
+  int64_t stride_c;
+  float alpha;
+  float beta;
+  int act;
+  int use_prev;
+  int c_tma;        // 1: TMA stores through tma_c; 0: bounds-checked direct stores
+  int m, n, k;
+  int batch;
+  int b_broadcast;  // every batch entry uses B[0]
+  int tiles_m, tiles_n;
+  int splits;       // > 1: split-K, raw partial sums to the workspace in tma_c
+  int kb_per_split;
+  int num_kb;
+  int total_units;
+  int* status;
+};
+
+// ---- PTX wrappers ------------------------------------------------------------
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Waits for the phase of `bar` with parity `parity` to complete.  Gives up
+// (returns false) when the CTA abort flag is raised (if `abort` is given) or
+// after WAIT_TIMEOUT_NS / WAIT_MAX_POLLS.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity,
+                                          const volatile int* abort) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const unsigned long long t0 = global_ns();
+  for (unsigned polls = 1; polls < WAIT_MAX_POLLS; ++polls) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((polls & 31u) == 0) {
+      if (abort != nullptr && *abort) return false;
+      if (global_ns() - t0 > WAIT_TIMEOUT_NS) return false;
+    }
+  }
+  return false;
+}
+
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, uint32_t bar,
+                                            int c0, int c1, int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, uint32_t src, int c0, int c1,
+                                             int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(src), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read_1() {
+  asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+}
+__device__ __forceinline__ void bulk_wait_all() {
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// Shared-memory matrix descriptors (tcgen05 "matrix descriptor" format):
+// start address >> 4 in bits [0,14), leading byte offset >> 4 in [16,30),
+// stride byte offset >> 4 in [32,46), version 1 in [46,48), layout type in
+// [61,64): 2 = 128-byte swizzle of 16-byte chunks, 1 = 128-byte swizzle of
+// 32-byte chunks (the only N-major layout kind::tf32 accepts).
+__device__ __forceinline__ uint64_t make_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo,
+                                              uint32_t layout) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
+  d |= static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16;
+  d |= static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32;
+  d |= static_cast<uint64_t>(1) << 46;
+  d |= static_cast<uint64_t>(layout) << 61;
+  return d;
+}
+
+// K-major tile: rows of 128 bytes (32 fp32 along K) with 16-byte chunks
+// swizzled over 8 rows; 8-row groups 1024 B apart.  The leading offset is
+// unused for swizzled K-major layouts.
+__device__ __forceinline__ uint64_t desc_kmajor(uint32_t saddr) {
+  return make_desc(saddr, 16, 1024, 2);
+}
+
+// N-major tile: 32-wide N atoms of [BK rows x 128 B] placed BK*128 B apart
+// (leading offset); 32-byte chunks swizzled over 4 rows, so K groups are
+// 4 rows = 512 B apart (stride offset).
+__device__ __forceinline__ uint64_t desc_nmajor(uint32_t saddr) {
+  return make_desc(saddr, BK * 128, 512, 1);
+}
+
+// Instruction descriptor for kind::tf32: D f32 (bits 4-5 = 1), A and B tf32
+// (bits 7-9 and 10-12 = 2), B major-ness in bit 16, N >> 3 in bits 17-22,
+// M >> 4 in bits 24-28.
+__host__ __device__ constexpr uint32_t make_idesc(int n, bool b_nmajor) {
+  return (1u << 4) | (2u << 7) | (2u << 10) | ((b_nmajor ? 1u : 0u) << 16) |
+         (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(BM >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma_tf32(uint32_t d_tmem, uint64_t da, uint64_t db,
+                                         uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(da), "l"(db), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void mma_commit(uint32_t bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+      : "memory");
+}
+
+// 32 lanes x 32 columns of 32-bit accumulator -> 32 registers per thread
+// (thread t holds TMEM lane base+t, columns col..col+31).
+__device__ __forceinline__ void tmem_load_32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
+        "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]),
+        "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]),
+        "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ void record_status(int* status, int code) {
+  if (status != nullptr) atomicCAS(status, TVR_DEV_OK, code);
+}
+
+// Work unit -> (operand batch index, k split, tile row, tile column).
+// Tiles are rastered in groups of GROUP_M tile rows so CTAs running at the
+// same time share A and B panels in L2.
+__device__ __forceinline__ void decode_unit(const Params& p, int u, int& b, int& s, int& tm,
+                                            int& tn) {
+  const int per = p.tiles_m * p.tiles_n;
+  const int outer = u / per;
+  const int r = u - outer * per;
+  b = outer / p.splits;
+  s = outer - b * p.splits;
+  const int span = GROUP_M * p.tiles_n;
+  const int g = r / span;
+  const int first_m = g * GROUP_M;
+  const int gm = min(p.tiles_m - first_m, GROUP_M);
+  const int rr = r - g * span;
+  tm = first_m + rr % gm;
+  tn = rr / gm;
+}
+
+template <int BN, bool SPLIT3, bool B_NMAJOR>
+__global__ void __launch_bounds__(NUM_THREADS, 1) gemm_tc_kernel(const __grid_constant__ Params p) {
+  using Cf = Cfg<BN, SPLIT3>;
+  constexpr int STAGES = Cf::STAGES;
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ int s_abort;
+
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  const uint32_t stage0 = base;
+  const uint32_t epi0 = base + STAGES * Cf::STAGE_BYTES;
+  const uint32_t bar0 = epi0 + EPI_SMEM;
+  const uint32_t full_bar = bar0;                       // [STAGES]
+  const uint32_t empty_bar = bar0 + 8 * STAGES;         // [STAGES]
+  const uint32_t tfull_bar = bar0 + 16 * STAGES;        // [2]
+  const uint32_t tempty_bar = tfull_bar + 16;           // [2]
+  const uint32_t drain_bar = tempty_bar + 16;           // [1]
+  const uint32_t holder = drain_bar + 8;                // TMEM base address
+  uint32_t* holder_ptr = reinterpret_cast<uint32_t*>(smem_raw + (holder - raw));
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const volatile int* abort_flag = &s_abort;
+
+  if (threadIdx.x == 0) {
+    s_abort = 0;
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(full_bar + 8 * s, 1);
+      mbar_init(empty_bar + 8 * s, 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(tfull_bar + 8 * b, 1);
+      mbar_init(tempty_bar + 8 * b, EPI_WARPS);
+    }
+    mbar_init(drain_bar, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(holder),
+                 "r"(Cf::TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *reinterpret_cast<volatile uint32_t*>(holder_ptr);
+
+  if (warp == 0) {
+    // ------------------------------ TMA producer ------------------------------
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t issued_mask = 0;  // stages with a load issued
+      uint32_t issued_parity = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; ok && u < p.total_units; u += gridDim.x) {
+        int b, s, tm, tn;
+        decode_unit(p, u, b, s, tm, tn);
+        const int kb0 = s * p.kb_per_split;
+        const int kb1 = min(p.num_kb, kb0 + p.kb_per_split);
+        const int zb = p.b_broadcast ? 0 : b;
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(empty_bar + 8 * stage, phase ^ 1u, abort_flag)) {
+            ok = false;
+            break;
+          }
+          const uint32_t fb = full_bar + 8 * stage;
+          mbar_expect_tx(fb, Cf::STAGE_BYTES);
+          const uint32_t sa = stage0 + stage * Cf::STAGE_BYTES;
+          const uint32_t sb = sa + Cf::A_BYTES;
+          const int kx = kb * BK;
+          tma_load_3d(sa, &p.tma_a, fb, kx, tm * BM, b);
+          if (B_NMAJOR) {
+#pragma unroll
+            for (int j = 0; j < BN / 32; ++j)
+              tma_load_3d(sb + j * (BK * 128), &p.tma_b, fb, tn * BN + 32 * j, kx, zb);
+          } else {
+            tma_load_3d(sb, &p.tma_b, fb, kx, tn * BN, zb);
+          }
+          if (SPLIT3) {
+            const uint32_t sa_lo = sb + Cf::B_BYTES;
+            const uint32_t sb_lo = sa_lo + Cf::A_BYTES;
+            tma_load_3d(sa_lo, &p.tma_a_lo, fb, kx, tm * BM, b);
+            if (B_NMAJOR) {
+#pragma unroll
+              for (int j = 0; j < BN / 32; ++j)
+                tma_load_3d(sb_lo + j * (BK * 128), &p.tma_b_lo, fb, tn * BN + 32 * j, kx, zb);
+            } else {
+              tma_load_3d(sb_lo, &p.tma_b_lo, fb, kx, tn * BN, zb);
+            }
+          }
+          issued_mask |= 1u << stage;
+          issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok) {
+        record_status(p.status, TVR_DEV_TIMEOUT_PRODUCER);
+        *const_cast<volatile int*>(abort_flag) = 1;
+      }
+      // Every issued load must land before the CTA may exit.
+      for (int st = 0; st < STAGES; ++st) {
+        if (issued_mask & (1u << st)) {
+          if (!mbar_wait(full_bar + 8 * st, (issued_parity >> st) & 1u, nullptr)) {
+            record_status(p.status, TVR_DEV_TIMEOUT_DRAIN);
+          }
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------ MMA issuer ------------------------------
+    if (lane == 0) {
+      constexpr uint32_t idesc = make_idesc(BN, B_NMAJOR);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      bool issued = false;
+      for (int u = blockIdx.x; ok && u < p.total_units; u += gridDim.x) {
+        int b, s, tm, tn;
+        decode_unit(p, u, b, s, tm, tn);
+        const int kb0 = s * p.kb_per_split;
+        const int kb1 = min(p.num_kb, kb0 + p.kb_per_split);
+        if (!mbar_wait(tempty_bar + 8 * acc, acc_phase ^ 1u, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d = tmem_base + static_cast<uint32_t>(acc * BN);
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(full_bar + 8 * stage, phase, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = stage0 + stage * Cf::STAGE_BYTES;
+          const uint32_t sb = sa + Cf::A_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < BK / 8; ++kk) {
+            const uint64_t da = desc_kmajor(sa + kk * 32);
+            const uint64_t db = B_NMAJOR ? desc_nmajor(sb + kk * 1024) : desc_kmajor(sb + kk * 32);
+            const uint32_t first = (kb > kb0 || kk > 0) ? 1u : 0u;
+            if (SPLIT3) {
+              const uint32_t sa_lo = sb + Cf::B_BYTES;
+              const uint32_t sb_lo = sa_lo + Cf::A_BYTES;
+              const uint64_t da_lo = desc_kmajor(sa_lo + kk * 32);
+              const uint64_t db_lo =
+                  B_NMAJOR ? desc_nmajor(sb_lo + kk * 1024) : desc_kmajor(sb_lo + kk * 32);
+              mma_tf32(d, da_lo, db, idesc, first);
+              mma_tf32(d, da, db_lo, idesc, 1u);
+              mma_tf32(d, da, db, idesc, 1u);
+            } else {
+              mma_tf32(d, da, db, idesc, first);
+            }
+          }
+          issued = true;
+          mma_commit(empty_bar + 8 * stage);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        mma_commit(tfull_bar + 8 * acc);
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1u;
+      }
+      if (!ok) {
+        record_status(p.status, TVR_DEV_TIMEOUT_MMA);
+        *const_cast<volatile int*>(abort_flag) = 1;
+      }
+      // All issued MMAs must retire before TMEM is released.
+      if (issued) {
+        mma_commit(drain_bar);
+        if (!mbar_wait(drain_bar, 0, nullptr)) record_status(p.status, TVR_DEV_TIMEOUT_DRAIN);
+      }
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------ epilogue ------------------------------
+    const int q = warp & 3;          // TMEM lane quarter this warp may access
+    const int ew = warp - 2;         // epilogue warp index -> staging buffers
+    const uint32_t ebuf0 = epi0 + ew * 2 * EPI_BUF_BYTES;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    int buf = 0;
+    bool ok = true;
+    for (int u = blockIdx.x; u < p.total_units; u += gridDim.x) {
+      int b, s, tm, tn;
+      decode_unit(p, u, b, s, tm, tn);
+      const bool got = mbar_wait(tfull_bar + 8 * acc, acc_phase, abort_flag);
+      if (!__all_sync(0xffffffffu, got)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const int row_in_tile = 32 * q + lane;
+      const int64_t row = static_cast<int64_t>(tm) * BM + row_in_tile;
+      const int zc = p.splits > 1 ? s : b;
+      float* crow = p.c + static_cast<int64_t>(zc) * p.stride_c + row * p.ldc;
+#pragma unroll 1
+      for (int ch = 0; ch < BN / 32; ++ch) {
+        float v[32];
+        tmem_load_32(tmem_base + (static_cast<uint32_t>(32 * q) << 16) +
+                         static_cast<uint32_t>(acc * BN + 32 * ch),
+                     v);
+        if (ch == BN / 32 - 1) {
+          // accumulator fully read: hand the TMEM buffer back to the MMA warp
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(tempty_bar + 8 * acc);
+          __syncwarp();
+        }
+        const int col0 = tn * BN + 32 * ch;
+        if (p.splits == 1) {
+          const bool row_ok = row < p.m;
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            float prev = 0.f;
+            const int col = col0 + j;
+            if (p.bias != nullptr) {
+              prev = col < p.n ? __ldg(p.bias + col) : 0.f;
+            } else if (p.use_prev) {
+              prev = (row_ok && col < p.n) ? crow[col] : 0.f;
+            }
+            v[j] = epilogue_value(v[j], prev, p.alpha, p.beta, p.act);
+          }
+        }
+        if (p.c_tma) {
+          const uint32_t eb = ebuf0 + buf * EPI_BUF_BYTES;
+          if (lane == 0) bulk_wait_read_1();  // the store issued from this buffer 2 chunks ago
+          __syncwarp();
+          // 128-byte swizzle: 16-byte chunk j of row r lives at chunk j ^ (r & 7)
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const uint32_t addr = eb + lane * 128 + ((j ^ (lane & 7)) << 4);
+            asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(v[4 * j]),
+                         "f"(v[4 * j + 1]), "f"(v[4 * j + 2]), "f"(v[4 * j + 3])
+                         : "memory");
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_3d(&p.tma_c, eb, col0, tm * BM + 32 * q, zc);
+            bulk_commit();
+          }
+          __syncwarp();
+          buf ^= 1;
+        } else if (row < p.m) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            if (col0 + j < p.n) crow[col0 + j] = v[j];
+          }
+        }
+      }
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1u;
+    }
+    if (!ok) {
+      record_status(p.status, TVR_DEV_TIMEOUT_EPILOGUE);
+      *const_cast<volatile int*>(abort_flag) = 1;
+    }
+    if (lane == 0) bulk_wait_all();
+    __syncwarp();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                 "r"(Cf::TMEM_COLS)
+                 : "memory");
+  }
+}
+
+// hi = x with the low 13 mantissa bits cleared, lo = x - hi (exact).
+__global__ void __launch_bounds__(256) split_tf32_kernel(const float* __restrict__ src,
+                                                         float* __restrict__ hi,
+                                                         float* __restrict__ lo, int64_t rows,
+                                                         int64_t cols, int64_t ld,
+                                                         int64_t batch_stride, int64_t ld_out,
+                                                         int64_t batch) {
+  const int64_t per = rows * cols;
+  const int64_t total = per * batch;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += stride) {
+    const int64_t bb = i / per;
+    const int64_t rem = i - bb * per;
+    const int64_t r = rem / cols, c = rem - (rem / cols) * cols;
+    const float x = src[bb * batch_stride + r * ld + c];
+    const float h = __uint_as_float(__float_as_uint(x) & 0xFFFFE000u);
+    const int64_t o = (bb * rows + r) * ld_out + c;
+    hi[o] = h;
+    lo[o] = x - h;
+  }
+}
+
+__global__ void __launch_bounds__(256) split_tf32_vec4_kernel(const float4* __restrict__ src,
+                                                              float4* __restrict__ hi,
+                                                              float4* __restrict__ lo,
+                                                              int64_t n4) {
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n4;
+       i += stride) {
+    const float4 x = src[i];
+    float4 h, l;
+    h.x = __uint_as_float(__float_as_uint(x.x) & 0xFFFFE000u);
+    h.y = __uint_as_float(__float_as_uint(x.y) & 0xFFFFE000u);
+    h.z = __uint_as_float(__float_as_uint(x.z) & 0xFFFFE000u);
+    h.w = __uint_as_float(__float_as_uint(x.w) & 0xFFFFE000u);
+    l.x = x.x - h.x;
+    l.y = x.y - h.y;
+    l.z = x.z - h.z;
+    l.w = x.w - h.w;
+    hi[i] = h;
+    lo[i] = l;
+  }
+}
+
+// Split-K finalisation: C = act(alpha * sum_s W[s] + beta * P), summed in
+// split order so the result does not depend on scheduling.
+__global__ void __launch_bounds__(256) splitk_reduce_kernel(
+    const float* __restrict__ ws, int splits, const float* __restrict__ bias,
+    float* __restrict__ c, int64_t m, int64_t n, int64_t ldc, float alpha, float beta, int act,
+    int use_prev) {
+  const int64_t total = m * n;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += stride) {
+    const int64_t r = i / n, col = i - (i / n) * n;
+    float acc = ws[i];
+    for (int s = 1; s < splits; ++s) acc += ws[static_cast<int64_t>(s) * total + i];
+    float prev = 0.f;
+    if (bias != nullptr) prev = bias[col];
+    else if (use_prev) prev = c[r * ldc + col];
+    c[r * ldc + col] = epilogue_value(acc, prev, alpha, beta, act);
+  }
+}
+
+// ---- host side -----------------------------------------------------------------
+
+int encode_3d(CUtensorMap* map, const void* ptr, uint64_t d0, uint64_t d1, uint64_t d2,
+              uint64_t stride1_bytes, uint64_t stride2_bytes, uint32_t box0, uint32_t box1,
+              CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {
+  const DriverApi* drv = driver();
+  if (drv == nullptr) return TVR_ERR_CUDA;
+  const cuuint64_t dims[3] = {d0, d1, d2};
+  const cuuint64_t strides[2] = {stride1_bytes, stride2_bytes};
+  const cuuint32_t box[3] = {box0, box1, 1};
+  const cuuint32_t elem_strides[3] = {1, 1, 1};
+  CUresult r = drv->tensorMapEncodeTiled(
+      map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<void*>(ptr), dims, strides, box,
+      elem_strides, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
+      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    const char* msg = "?";
+    if (drv->getErrorString) drv->getErrorString(r, &msg);
+    return fail(TVR_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d: %s) dims {%llu, %llu, %llu}",
+                static_cast<int>(r), msg, (unsigned long long)d0, (unsigned long long)d1,
+                (unsigned long long)d2);
+  }
+  return TVR_OK;
+}
+
+inline bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+template <int BN, bool SPLIT3, bool B_NMAJOR>
+int launch_kernel(const Params& p, int grid, cudaStream_t stream, int dev) {
+  using Cf = Cfg<BN, SPLIT3>;
+  static std::once_flag once[64];
+  static cudaError_t attr_err[64];
+  std::call_once(once[dev & 63], [&]() {
+    attr_err[dev & 63] = cudaFuncSetAttribute(gemm_tc_kernel<BN, SPLIT3, B_NMAJOR>,
+                                              cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                              Cf::SMEM_BYTES);
+  });
+  TVR_CUDA_TRY(attr_err[dev & 63]);
+  gemm_tc_kernel<BN, SPLIT3, B_NMAJOR><<<grid, NUM_THREADS, Cf::SMEM_BYTES, stream>>>(p);
+  TVR_LAUNCH_CHECK();
+  return TVR_OK;
+}
+
+template <int BN>
+int launch_bn(const Params& p, bool split3, bool b_nmajor, int grid, cudaStream_t s, int dev) {
+  if (split3) {
+    return b_nmajor ? launch_kernel<BN, true, true>(p, grid, s, dev)
+                    : launch_kernel<BN, true, false>(p, grid, s, dev);
+  }
+  return b_nmajor ? launch_kernel<BN, false, true>(p, grid, s, dev)
+                  : launch_kernel<BN, false, false>(p, grid, s, dev);
+}
+
+// Writes hi / lo parts of a [batch][rows][cols] operand (row stride ld,
+// batch stride bs) densely packed with row stride ld_out.
+int split_operand(const float* src, float* hi, float* lo, int64_t rows, int64_t cols,
+                  int64_t ld, int64_t bs, int64_t ld_out, int64_t batch, cudaStream_t s,
+                  int dev) {
+  const int64_t total = rows * cols * batch;
+  if (total == 0) return TVR_OK;
+  const bool dense = ld == cols && ld_out == cols && (batch == 1 || bs == rows * cols);
+  if (dense && total % 4 == 0 && al16(src) && al16(hi) && al16(lo)) {
+    split_tf32_vec4_kernel<<<elementwise_grid(total / 4, 256, dev), 256, 0, s>>>(
+        reinterpret_cast<const float4*>(src), reinterpret_cast<float4*>(hi),
+        reinterpret_cast<float4*>(lo), total / 4);
+  } else {
+    split_tf32_kernel<<<elementwise_grid(total, 256, dev), 256, 0, s>>>(src, hi, lo, rows, cols,
+                                                                         ld, bs, ld_out, batch);
+  }
+  TVR_LAUNCH_CHECK();
+  return TVR_OK;
+}
+
+}  // namespace tc
+
+int gemm_tcgen05(const float* a, const float* b, const float* bias, float* c, int64_t m,
+                 int64_t n, int64_t k, int64_t lda, int64_t ldb, int64_t ldc, int64_t batch,
+                 int64_t sa, int64_t sb, int64_t sc, float alpha, float beta, int act,
+                 bool trans_b, bool split3, cudaStream_t stream) {
+  using namespace tc;
+  // TMA addressability: 16-byte aligned bases, row and batch strides in
+  // multiples of 16 bytes, extents that fit the 32-bit coordinates.
+  const bool b_bcast = batch > 1 && sb == 0;
+  if (!al16(a) || !al16(b) || lda % 4 != 0 || ldb % 4 != 0 || k < 1 ||
+      (batch > 1 && (sa == 0 || sa % 4 != 0)) || (batch > 1 && !b_bcast && sb % 4 != 0) ||
+      m > 0x7fffff00 || n > 0x7fffff00 || k > 0x7fffff00 || batch > 65535) {
+    return TVR_ERR_UNSUPPORTED;
+  }
+  const int dev = current_device();
+  const int sms = sm_count(dev);
+  const int num_kb = static_cast<int>(ceil_div(k, BK));
+
+  // Tile width: the widest BN (not wider than N rounded up) that still gives
+  // ~a full wave of tiles; otherwise split K across CTAs.
+  int bn = 64;
+  int64_t tiles = 0;
+  const int bn_cap = n > 128 ? 256 : (n > 64 ? 128 : 64);
+  for (int cand : {256, 128, 64}) {
+    if (cand > bn_cap) continue;
+    const int64_t t = batch * ceil_div(m, BM) * ceil_div(n, cand);
+    bn = cand;
+    tiles = t;
+    if (t >= (sms * 4) / 5) break;
+  }
+  const bool c_tma = al16(c) && ldc % 4 == 0 && (batch == 1 || (sc != 0 && sc % 4 == 0));
+  int splits = 1;
+  if (batch == 1 && tiles < (sms * 4) / 5 && n % 4 == 0) {
+    int s = static_cast<int>(sms / tiles);
+    s = std::min(s, std::max(1, num_kb / 4));
+    s = std::min(s, 16);
+    if (s > 1) splits = s;
+  }
+  int kb_per_split = static_cast<int>(ceil_div(num_kb, splits));
+  splits = static_cast<int>(ceil_div(num_kb, kb_per_split));
+
+  Params p;
+  memset(&p, 0, sizeof(p));
+  Scratch split_a, split_b, workspace;
+  const float* a_hi = a;
+  const float* b_hi = b;
+  const float* a_lo = nullptr;
+  const float* b_lo = nullptr;
+  int64_t lda_u = lda, ldb_u = ldb, sa_u = sa, sb_u = sb;
+  const int64_t b_rows = trans_b ? n : k;  // B stored as [b_rows][b_cols]
+  const int64_t b_cols = trans_b ? k : n;
+  const int64_t b_batches = b_bcast ? 1 : batch;
+  int rc;
+  if (split3) {
+    const int64_t lda_p = (k + 3) / 4 * 4;
+    const int64_t ldb_p = (b_cols + 3) / 4 * 4;
+    const size_t a_elems = static_cast<size_t>(batch * m * lda_p);
+    const size_t b_elems = static_cast<size_t>(b_batches * b_rows * ldb_p);
+    if ((rc = split_a.alloc(2 * a_elems * sizeof(float), dev, stream)) != TVR_OK) return rc;
+    if ((rc = split_b.alloc(2 * b_elems * sizeof(float), dev, stream)) != TVR_OK) return rc;
+    float* ah = static_cast<float*>(split_a.ptr);
+    float* al = ah + a_elems;
+    float* bh = static_cast<float*>(split_b.ptr);
+    float* bl = bh + b_elems;
+    if ((rc = split_operand(a, ah, al, m, k, lda, sa, lda_p, batch, stream, dev)) != TVR_OK) return rc;
+    if ((rc = split_operand(b, bh, bl, b_rows, b_cols, ldb, sb, ldb_p, b_batches, stream, dev)) != TVR_OK)
+      return rc;
+    a_hi = ah;
+    a_lo = al;
+    b_hi = bh;
+    b_lo = bl;
+    lda_u = lda_p;
+    ldb_u = ldb_p;
+    sa_u = m * lda_p;
+    sb_u = b_rows * ldb_p;
+  }
+  // A: dims {K, M, batch}
+  const uint64_t a_bs = static_cast<uint64_t>(batch > 1 ? sa_u : m * lda_u) * 4;
+  if ((rc = encode_3d(&p.tma_a, a_hi, k, m, batch, lda_u * 4, a_bs ? a_bs : 16, BK, BM)) != TVR_OK)
+    return rc;
+  if (split3 &&
+      (rc = encode_3d(&p.tma_a_lo, a_lo, k, m, batch, lda_u * 4, a_bs ? a_bs : 16, BK, BM)) != TVR_OK)
+    return rc;
+  const uint64_t b_bs =
+      static_cast<uint64_t>((b_batches > 1) ? sb_u : b_rows * ldb_u) * 4;
+  if (trans_b) {
+    if ((rc = encode_3d(&p.tma_b, b_hi, k, n, b_batches, ldb_u * 4, b_bs ? b_bs : 16, BK, bn)) != TVR_OK)
+      return rc;
+    if (split3 &&
+        (rc = encode_3d(&p.tma_b_lo, b_lo, k, n, b_batches, ldb_u * 4, b_bs ? b_bs : 16, BK, bn)) != TVR_OK)
+      return rc;
+  } else {
+    // N-major tiles use the 32-byte-chunk swizzle the N-major tf32 MMA reads
+    constexpr CUtensorMapSwizzle kSw = CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B;
+    if ((rc = encode_3d(&p.tma_b, b_hi, n, k, b_batches, ldb_u * 4, b_bs ? b_bs : 16, 32, BK,
+                        kSw)) != TVR_OK)
+      return rc;
+    if (split3 && (rc = encode_3d(&p.tma_b_lo, b_lo, n, k, b_batches, ldb_u * 4,
+                                  b_bs ? b_bs : 16, 32, BK, kSw)) != TVR_OK)
+      return rc;
+  }
+  float* out = c;
+  int64_t out_ld = ldc, out_bs = sc;
+  int out_tma = c_tma ? 1 : 0;
+  if (splits > 1) {
+    const size_t ws_elems = static_cast<size_t>(splits) * m * n;
+    if ((rc = workspace.alloc(ws_elems * sizeof(float), dev, stream)) != TVR_OK) return rc;
+    out = static_cast<float*>(workspace.ptr);
+    out_ld = n;
+    out_bs = m * n;
+    out_tma = 1;
+    if ((rc = encode_3d(&p.tma_c, out, n, m, splits, n * 4, static_cast<uint64_t>(m * n) * 4, 32, 32)) != TVR_OK)
+      return rc;
+  } else if (c_tma) {
+    const uint64_t c_bs = static_cast<uint64_t>(batch > 1 ? sc : m * ldc) * 4;
+    if ((rc = encode_3d(&p.tma_c, c, n, m, batch, ldc * 4, c_bs ? c_bs : 16, 32, 32)) != TVR_OK)
+      return rc;
+  }
+  p.bias = bias;
+  p.c = out;
+  p.ldc = out_ld;
+  p.stride_c = out_bs;
+  p.alpha = alpha;
+  p.beta = beta;
+  p.act = act;
+  p.use_prev = (bias == nullptr && beta != 0.f) ? 1 : 0;
+  p.c_tma = out_tma;
+  p.m = static_cast<int>(m);
+  p.n = static_cast<int>(n);
+  p.k = static_cast<int>(k);
+  p.batch = static_cast<int>(batch);
+  p.b_broadcast = b_bcast ? 1 : 0;
+  p.tiles_m = static_cast<int>(ceil_div(m, BM));
+  p.tiles_n = static_cast<int>(ceil_div(n, bn));
+  p.splits = splits;
+  p.kb_per_split = kb_per_split;
+  p.num_kb = num_kb;
+  const int64_t units = static_cast<int64_t>(batch) * splits * p.tiles_m * p.tiles_n;
+  if (units > 0x7fffffff) return TVR_ERR_UNSUPPORTED;
+  p.total_units = static_cast<int>(units);
+  p.status = device_status_ptr(dev);
+  const int grid = static_cast<int>(std::min<int64_t>(units, sms));
+  const bool b_nmajor = !trans_b;
+  switch (bn) {
+    case 256: rc = launch_bn<256>(p, split3, b_nmajor, grid, stream, dev); break;
+    case 128: rc = launch_bn<128>(p, split3, b_nmajor, grid, stream, dev); break;
+    default: rc = launch_bn<64>(p, split3, b_nmajor, grid, stream, dev); break;
+  }
+  if (rc != TVR_OK) return rc;
+  if (splits > 1) {
+    splitk_reduce_kernel<<<elementwise_grid(m * n, 256, dev), 256, 0, stream>>>(
+        out, splits, bias, c, m, n, ldc, alpha, beta, act, p.use_prev);
+    TVR_LAUNCH_CHECK();
+  }
+  return TVR_OK;
+}
+
+}  // namespace tvr
