@@ -1,0 +1,403 @@
+"""The reference's user-level test suite, run against this backend.
+
+Each test restates one of samthakur587/Tvarant's tests/ cases (file cited
+per test) through ``import torch_tvarant`` and device ``"tvarant"``, with the
+reference's tolerances; device-count and backend-name checks are adapted to
+the CUDA runtime (one device per GPU, backend "cuda").
+"""
+
+from __future__ import annotations
+
+import pytest
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module", autouse=True)
+def tvarant():
+    import torch_tvarant
+
+    assert torch.tvarant.is_available()
+    return torch_tvarant
+
+
+# ---- tests/test_copy.py -----------------------------------------------------
+
+def test_roundtrip_cpu_tvarant_cpu():
+    src = torch.tensor([[1.0, 2.0], [3.0, 4.0]])
+    dev = src.to("tvarant")
+    assert dev.device.type == "tvarant"
+    back = dev.cpu()
+    assert back.device.type == "cpu"
+    assert torch.equal(back, src)
+
+
+def test_empty_and_copy_():
+    src = torch.arange(6, dtype=torch.float32).reshape(2, 3)
+    dst = torch.empty(2, 3, device="tvarant")
+    dst.copy_(src)
+    assert torch.allclose(dst.cpu(), src)
+
+
+def test_zeros_ones():
+    assert torch.equal(torch.zeros(3, 4, device="tvarant").cpu(), torch.zeros(3, 4))
+    assert torch.equal(torch.ones(3, 4, device="tvarant").cpu(), torch.ones(3, 4))
+
+
+def test_to_tvarant_helper():
+    x = torch.randn(5)
+    y = x.tvarant()
+    assert y.is_tvarant
+    assert torch.allclose(y.cpu(), x)
+
+
+# ---- tests/test_device.py ---------------------------------------------------
+
+def test_backend_name():
+    assert torch.utils.backend_registration._privateuse1_backend_name == "tvarant"
+
+
+def test_is_available():
+    assert torch.tvarant.is_available()
+    assert torch.tvarant.device_count() >= 1
+    assert torch.tvarant.current_device() == 0
+
+
+def test_device_object():
+    assert torch.device("tvarant").type == "tvarant"
+    assert torch.device("tvarant:0").index == 0
+
+
+def test_tensor_helpers():
+    x = torch.empty(2, 3, device="tvarant")
+    assert x.is_tvarant and x.device.type == "tvarant"
+    y = torch.empty(2, 3)
+    assert not y.is_tvarant
+    assert y.tvarant().is_tvarant
+
+
+def test_backend_is_cuda(tvarant):
+    assert tvarant._C.backend() == "cuda"
+
+
+# ---- tests/test_llm_ops.py --------------------------------------------------
+
+def test_silu_matches_cpu():
+    x = torch.randn(4, 8)
+    y = F.silu(x.to("tvarant"))
+    assert y.device.type == "tvarant"
+    assert torch.allclose(y.cpu(), F.silu(x), atol=1e-5)
+
+
+def test_softmax_matches_cpu():
+    x = torch.randn(2, 4, 8)
+    y = F.softmax(x.to("tvarant"), dim=-1)
+    assert torch.allclose(y.cpu(), F.softmax(x, dim=-1), atol=1e-5)
+
+
+def test_layer_norm_matches_cpu():
+    torch.manual_seed(0)
+    x = torch.randn(2, 4, 8)
+    ln = nn.LayerNorm(8)
+    y_cpu = ln(x)
+    y = ln.to("tvarant")(x.to("tvarant"))
+    assert y.device.type == "tvarant"
+    assert torch.allclose(y.cpu(), y_cpu, atol=1e-5)
+
+
+def test_bmm_matches_cpu():
+    a = torch.randn(3, 4, 5)
+    b = torch.randn(3, 5, 6)
+    y = torch.bmm(a.to("tvarant"), b.to("tvarant"))
+    assert torch.allclose(y.cpu(), torch.bmm(a, b), atol=1e-4)
+
+
+def test_matmul_batched():
+    q = torch.randn(2, 3, 4, 8)
+    k = torch.randn(2, 3, 8, 5)
+    y = q.to("tvarant") @ k.to("tvarant")
+    assert y.shape == (2, 3, 4, 5)
+    assert torch.allclose(y.cpu(), q @ k, atol=1e-4)
+
+
+def test_mul_scalar():
+    x = torch.randn(4, 8, device="tvarant")
+    assert torch.allclose((x * 0.125).cpu(), x.cpu() * 0.125, atol=1e-6)
+
+
+def test_embedding_matches_cpu():
+    torch.manual_seed(0)
+    emb = nn.Embedding(16, 8)
+    idx = torch.tensor([[1, 3, 0], [2, 2, 7]])
+    y_cpu = emb(idx)
+    y = emb.to("tvarant")(idx)
+    assert y.device.type == "tvarant"
+    assert torch.allclose(y.cpu(), y_cpu, atol=1e-6)
+
+
+def test_tiny_attention_block():
+    torch.manual_seed(0)
+    b, t, d = 2, 4, 8
+    x = torch.randn(b, t, d)
+    wq, wk, wv = torch.randn(d, d), torch.randn(d, d), torch.randn(d, d)
+    scale = d**-0.5
+
+    def attn(x_, wq_, wk_, wv_):
+        q, k, v = x_ @ wq_, x_ @ wk_, x_ @ wv_
+        scores = (q @ k.transpose(-2, -1)) * scale
+        return F.softmax(scores, dim=-1) @ v
+
+    y_cpu = attn(x, wq, wk, wv)
+    y = attn(x.to("tvarant"), wq.to("tvarant"), wk.to("tvarant"), wv.to("tvarant"))
+    assert y.device.type == "tvarant"
+    assert torch.allclose(y.cpu(), y_cpu, atol=1e-4)
+
+
+# ---- tests/test_mlp.py ------------------------------------------------------
+
+def test_linear_relu_matches_cpu():
+    torch.manual_seed(0)
+    cpu_net = nn.Sequential(nn.Linear(8, 8), nn.ReLU())
+    x_cpu = torch.randn(4, 8)
+    y_cpu = cpu_net(x_cpu)
+    y = cpu_net.to("tvarant")(x_cpu.to("tvarant"))
+    assert y.device.type == "tvarant"
+    assert torch.allclose(y.cpu(), y_cpu, atol=1e-5)
+
+
+def test_manual_linear_relu():
+    torch.manual_seed(1)
+    x = torch.randn(4, 8, device="tvarant")
+    w = torch.randn(8, 8, device="tvarant")
+    y = F.relu(x @ w)
+    assert torch.allclose(y.cpu(), torch.relu(x.cpu() @ w.cpu()), atol=1e-4)
+
+
+def test_two_layer_mlp():
+    torch.manual_seed(2)
+    model = nn.Sequential(nn.Linear(16, 32), nn.ReLU(), nn.Linear(32, 4))
+    x = torch.randn(2, 16)
+    y_cpu = model(x)
+    y = model.to("tvarant")(x.to("tvarant"))
+    assert torch.allclose(y.cpu(), y_cpu, atol=1e-4)
+
+
+# ---- tests/test_ops.py and tests/test_op_*.py -------------------------------
+
+def test_fill():
+    x = torch.empty(4, device="tvarant")
+    x.fill_(2.5)
+    assert torch.allclose(x.cpu(), torch.full((4,), 2.5))
+
+
+def test_add():
+    a = torch.tensor([1.0, 2.0, 3.0], device="tvarant")
+    b = torch.tensor([4.0, 5.0, 6.0], device="tvarant")
+    c = a + b
+    assert c.device.type == "tvarant"
+    assert torch.allclose(c.cpu(), torch.tensor([5.0, 7.0, 9.0]))
+
+
+def test_add_broadcast():
+    a = torch.ones(2, 3, device="tvarant")
+    b = torch.tensor([1.0, 2.0, 3.0], device="tvarant")
+    assert torch.allclose((a + b).cpu(), torch.tensor([[2.0, 3.0, 4.0], [2.0, 3.0, 4.0]]))
+
+
+def test_mul():
+    a = torch.tensor([2.0, 3.0], device="tvarant")
+    b = torch.tensor([4.0, 5.0], device="tvarant")
+    assert torch.allclose((a * b).cpu(), torch.tensor([8.0, 15.0]))
+
+
+def test_relu():
+    y = F.relu(torch.tensor([-1.0, 0.0, 2.5], device="tvarant"))
+    assert y.device.type == "tvarant"
+    assert torch.allclose(y.cpu(), torch.tensor([0.0, 0.0, 2.5]))
+
+
+def test_mm():
+    a = torch.tensor([[1.0, 2.0], [3.0, 4.0]], device="tvarant")
+    b = torch.tensor([[5.0, 6.0], [7.0, 8.0]], device="tvarant")
+    c = a @ b
+    assert c.device.type == "tvarant"
+    assert torch.allclose(c.cpu(), torch.tensor([[19.0, 22.0], [43.0, 50.0]]))
+
+
+def test_addmm_like_linear():
+    x = torch.tensor([[1.0, 2.0]], device="tvarant")
+    w = torch.tensor([[0.5, 0.0], [0.0, 0.25]], device="tvarant")
+    b = torch.tensor([1.0, -1.0], device="tvarant")
+    y = torch.addmm(b, x, w.t())
+    assert torch.allclose(y.cpu(), torch.addmm(b.cpu(), x.cpu(), w.cpu().t()))
+
+
+def test_item():
+    assert torch.tensor(3.0, device="tvarant").item() == 3.0
+
+
+def test_abs_neg():
+    x = torch.tensor([-4.0, -1.0, 0.25, 4.0], device="tvarant")
+    assert torch.allclose(torch.abs(x).cpu(), torch.abs(x.cpu()))
+    assert torch.allclose((-x).cpu(), -x.cpu())
+
+
+def test_clone_contiguous():
+    x = torch.randn(3, 4, device="tvarant")
+    y = x.clone()
+    assert y.device.type == "tvarant" and y.data_ptr() != x.data_ptr()
+    assert torch.allclose(y.cpu(), x.cpu())
+    c = x.t().contiguous()
+    assert c.is_contiguous()
+    assert torch.allclose(c.cpu(), x.cpu().t())
+
+
+def test_exp_exp2_sqrt_rsqrt():
+    x = torch.tensor([-1.0, 0.0, 0.5, 1.0], device="tvarant")
+    assert torch.allclose(torch.exp(x).cpu(), torch.exp(x.cpu()), atol=1e-5)
+    assert torch.allclose(torch.exp2(x).cpu(), torch.exp2(x.cpu()), atol=1e-5)
+    pos = torch.tensor([0.25, 1.0, 4.0], device="tvarant")
+    assert torch.allclose(torch.sqrt(pos).cpu(), torch.sqrt(pos.cpu()), atol=1e-5)
+    assert torch.allclose(torch.rsqrt(pos).cpu(), torch.rsqrt(pos.cpu()), atol=1e-5)
+
+
+def test_full_ones_zeros_like():
+    f = torch.full((2, 3), 2.5, device="tvarant")
+    assert f.device.type == "tvarant"
+    assert torch.allclose(f.cpu(), torch.full((2, 3), 2.5))
+    z = torch.zeros(2, 3, device="tvarant")
+    assert torch.allclose(torch.full_like(z, 7.0).cpu(), torch.full((2, 3), 7.0))
+    assert torch.allclose(torch.ones_like(z).cpu(), torch.ones(2, 3))
+    o = torch.ones(2, 3).to("tvarant")
+    assert torch.allclose(torch.zeros_like(o).cpu(), torch.zeros(2, 3))
+
+
+def test_sub():
+    a = torch.tensor([5.0, 7.0, 9.0], device="tvarant")
+    b = torch.tensor([1.0, 2.0, 3.0], device="tvarant")
+    assert torch.allclose((a - b).cpu(), torch.tensor([4.0, 5.0, 6.0]))
+    assert torch.allclose((a - 1.5).cpu(), a.cpu() - 1.5, atol=1e-5)
+
+
+# ---- tests/test_compiler.py -------------------------------------------------
+
+def test_linear_act_relu_matches_eager():
+    torch.manual_seed(0)
+    x = torch.randn(4, 8, device="tvarant")
+    w = torch.randn(16, 8, device="tvarant")
+    b = torch.randn(16, device="tvarant")
+    y = torch.ops.tvarant.linear_act(x, w, b, "relu", True)
+    assert y.device.type == "tvarant"
+    assert torch.allclose(y.cpu(), F.relu(F.linear(x.cpu(), w.cpu(), b.cpu())), atol=1e-4)
+
+
+def test_pointwise_relu_mul_add():
+    a = torch.tensor([1.0, -2.0, 3.0], device="tvarant")
+    b = torch.tensor([0.5, 0.5, 0.5], device="tvarant")
+    LOAD, CONST, ADD, MUL, RELU = 0, 1, 2, 3, 4
+    y = torch.ops.tvarant.pointwise(
+        [a, b],
+        [LOAD, RELU, LOAD, MUL, CONST, ADD],
+        [-1, 0, -1, 1, -1, 3],
+        [-1, -1, -1, 2, -1, 4],
+        [0, -1, 1, -1, -1, -1],
+        [1.0] * 6,
+        [0.0, 0.0, 0.0, 0.0, 1.0, 0.0],
+    )
+    assert torch.allclose(y.cpu(), F.relu(a.cpu()) * b.cpu() + 1, atol=1e-5)
+
+
+def test_compile_linear_relu_sequential(tvarant):
+    torch.manual_seed(1)
+    model = nn.Sequential(nn.Linear(8, 8), nn.ReLU())
+    x = torch.randn(4, 8)
+    y_cpu = model(x)
+    compiled = tvarant.compiler.compile(model.to("tvarant"))
+    y = compiled(x.to("tvarant"))
+    assert y.device.type == "tvarant"
+    assert torch.allclose(y.cpu(), y_cpu, atol=1e-4)
+    assert tvarant.compiler.last_log.get("gemm_epilogue", 0) >= 1
+
+
+def test_compile_fx_swiglu_like(tvarant):
+    class SwiGLU(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.w1 = nn.Linear(8, 16, bias=False)
+            self.w2 = nn.Linear(8, 16, bias=False)
+
+        def forward(self, x):
+            return F.silu(self.w1(x)) * self.w2(x)
+
+    torch.manual_seed(2)
+    m = SwiGLU()
+    x = torch.randn(2, 8)
+    y_cpu = m(x)
+    compiled = tvarant.compiler.compile_fx(tvarant.compiler.trace_module(m.to("tvarant")))
+    y = compiled(x.to("tvarant"))
+    assert torch.allclose(y.cpu(), y_cpu, atol=1e-4)
+
+
+def test_torch_compile_backend():
+    torch.manual_seed(3)
+    model = nn.Sequential(nn.Linear(16, 16), nn.SiLU()).to("tvarant")
+    x = torch.randn(4, 16)
+    ref = nn.Sequential(nn.Linear(16, 16), nn.SiLU())
+    ref.load_state_dict({k: v.cpu() for k, v in model.state_dict().items()})
+    compiled = torch.compile(model, backend="tvarant")
+    y = compiled(x.to("tvarant"))
+    assert torch.allclose(y.cpu(), ref(x), atol=1e-4)
+
+
+# ---- beyond the reference: streams, events, random, status ------------------
+
+def test_randn_matches_cpu_stream():
+    torch.manual_seed(0)
+    d = torch.randn(5, device="tvarant")
+    torch.manual_seed(0)
+    c = torch.randn(5)
+    assert torch.equal(d.cpu(), c)
+
+
+def test_streams_and_events():
+    s = torch.Stream(device="tvarant")
+    x = torch.randn(1000, device="tvarant")
+    with torch.tvarant.stream(s) if hasattr(torch.tvarant, "stream") else _nullctx():
+        y = x * 2.0
+    e = torch.Event(device="tvarant")
+    e.record()
+    e.synchronize()
+    assert torch.allclose(y.cpu(), x.cpu() * 2.0)
+
+
+class _nullctx:
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        return False
+
+
+def test_noncontiguous_binary_and_permute_copy():
+    x = torch.randn(8, 64, 3, 12, 16)
+    d = x.to("tvarant")
+    p = d.permute(2, 0, 3, 1, 4).contiguous()
+    assert torch.equal(p.cpu(), x.permute(2, 0, 3, 1, 4).contiguous())
+    t = torch.randn(32, 48)
+    s = (t.to("tvarant").t() + 1.0).cpu()
+    assert torch.allclose(s, t.t() + 1.0)
+
+
+def test_dtype_copies():
+    i = torch.arange(10, dtype=torch.int64)
+    d = i.to("tvarant")
+    assert torch.equal(d.cpu(), i)
+    f = d.to(torch.float32)
+    assert torch.equal(f.cpu(), i.float())
+
+
+def test_status_clean():
+    assert torch.tvarant.get_status() == 0

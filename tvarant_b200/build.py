@@ -162,7 +162,10 @@ def build_extension(jobs: int | None = None, force: bool = False) -> Path:
     obj_dir = BUILD / "ext"
     obj_dir.mkdir(parents=True, exist_ok=True)
     headers = sorted(EXT_SRC.glob("*.h")) + [ROOT / "include" / "tvarant.h"]
-    cxx = os.environ.get("CXX", "g++")
+    # The system compiler links the shared libstdc++ that PyTorch and
+    # libtvarant_cuda.so use; a toolchain that links a private static copy
+    # would export a second libstdc++ from _C.so.
+    cxx = os.environ.get("TVARANT_CXX") or ("/usr/bin/g++" if Path("/usr/bin/g++").exists() else "g++")
     flags = [
         "-O2",
         "-std=c++17",
@@ -192,7 +195,7 @@ def build_extension(jobs: int | None = None, force: bool = False) -> Path:
     with ThreadPoolExecutor(max_workers=jobs or os.cpu_count() or 4) as ex:
         objs = list(ex.map(compile_one, EXT_SOURCES))
     if force or _stale(EXT_LIB, [*objs, CUDA_LIB]):
-        link = [cxx, "-shared", "-o", str(EXT_LIB), *map(str, objs)]
+        link = [cxx, "-shared", "-Wl,--exclude-libs,ALL", "-o", str(EXT_LIB), *map(str, objs)]
         for d in libdirs:
             link += ["-L", d, f"-Wl,-rpath,{d}"]
         link += [

@@ -1,0 +1,117 @@
+// The tvarant operator library: tvarant::linear_act and tvarant::pointwise.
+//
+// Schemas are the reference's, verbatim (csrc/aten/CustomOps.cpp:101-106),
+// so graphs produced by torch_tvarant.compiler run unchanged.  linear_act
+// is one tcgen05 GEMM with bias and activation fused in the epilogue;
+// pointwise compiles its SSA program with NVRTC (tvr_pointwise).  Opcodes
+// 0-8 are the reference's (csrc/jit/Jit.h:11-21); 9 Sub, 10 Exp, 11 Abs are
+// appended.
+#include <ATen/ATen.h>
+#include <c10/core/DeviceGuard.h>
+#include <torch/library.h>
+
+#include <string>
+#include <vector>
+
+#include "TvarantExt.h"
+
+namespace tvarant::ops {
+namespace {
+
+// "none" / "identity" / "" -> 0, "relu" -> 1, "silu" / "swish" -> 2
+// (reference csrc/jit/Jit.cpp:140-152).
+int parse_act(const std::string& name) {
+  if (name.empty() || name == "none" || name == "identity") return TVR_ACT_NONE;
+  if (name == "relu") return TVR_ACT_RELU;
+  if (name == "silu" || name == "swish") return TVR_ACT_SILU;
+  TORCH_CHECK(false, "unknown activation '", name, "' (expected none|relu|silu)");
+}
+
+at::Tensor linear_act(const at::Tensor& x, const at::Tensor& weight,
+                      const std::optional<at::Tensor>& bias, std::string act, bool trans_b) {
+  check_fp32(x, "linear_act");
+  check_fp32(weight, "linear_act");
+  const int act_id = parse_act(act);
+  TORCH_CHECK(x.dim() >= 1, "linear_act: expected at least 1D input");
+  at::Tensor xc = x.is_contiguous() ? x : contiguous_copy(x);
+  const int64_t k = xc.size(-1);
+  const int64_t m = k > 0 ? xc.numel() / k : 0;
+  at::Tensor x2 = xc.reshape({m, k});
+  const at::Tensor* bptr = nullptr;
+  at::Tensor bstore;
+  if (bias.has_value() && bias->defined()) {
+    check_fp32(*bias, "linear_act");
+    bstore = *bias;
+    bptr = &bstore;
+  }
+  at::Tensor y2 = gemm_bias_act(x2, weight, bptr, 1.f, 1.f, act_id, trans_b);
+  auto out_sizes = xc.sizes().vec();
+  out_sizes.back() = y2.size(1);
+  return y2.reshape(out_sizes);
+}
+
+at::Tensor pointwise(at::TensorList inputs, at::IntArrayRef ops, at::IntArrayRef a,
+                     at::IntArrayRef b, at::IntArrayRef input_ids, at::ArrayRef<double> alphas,
+                     at::ArrayRef<double> consts) {
+  TORCH_CHECK(!inputs.empty(), "pointwise: need at least one input");
+  const size_t n_nodes = ops.size();
+  TORCH_CHECK(a.size() == n_nodes && b.size() == n_nodes && input_ids.size() == n_nodes &&
+                  alphas.size() == n_nodes && consts.size() == n_nodes,
+              "pointwise: SSA arrays must all have the same length");
+  TORCH_CHECK(n_nodes > 0, "pointwise: empty program");
+  TORCH_CHECK(inputs.size() <= TVR_PW_MAX_INPUTS, "pointwise: at most ", TVR_PW_MAX_INPUTS,
+              " inputs");
+  std::vector<tvr_pw_node> prog(n_nodes);
+  for (size_t i = 0; i < n_nodes; ++i) {
+    prog[i].op = static_cast<int32_t>(ops[i]);
+    prog[i].a = static_cast<int32_t>(a[i]);
+    prog[i].b = static_cast<int32_t>(b[i]);
+    prog[i].input_id = static_cast<int32_t>(input_ids[i]);
+    prog[i].alpha = static_cast<float>(alphas[i]);
+    prog[i].c = static_cast<float>(consts[i]);
+  }
+  // Inputs of equal numel are taken element by element (the reference's
+  // contract); otherwise they are broadcast to a common shape first, which
+  // the reference's fuser can produce but its kernel rejects.
+  bool same_numel = true;
+  std::vector<int64_t> shape = inputs[0].sizes().vec();
+  for (const auto& t : inputs) {
+    check_fp32(t, "pointwise");
+    TORCH_CHECK(t.device().is_privateuseone(), "pointwise: expected tvarant tensors");
+    same_numel = same_numel && t.numel() == inputs[0].numel();
+    shape = at::infer_size(shape, t.sizes());
+  }
+  if (same_numel) shape = inputs[0].sizes().vec();
+  c10::DeviceGuard guard(inputs[0].device());
+  std::vector<at::Tensor> held;
+  std::vector<const float*> ptrs;
+  for (const auto& t : inputs) {
+    at::Tensor c = t;
+    if (!same_numel && !t.sizes().equals(shape)) c = contiguous_copy(t.expand(shape));
+    else if (!c.is_contiguous()) c = contiguous_copy(c);
+    ptrs.push_back(static_cast<const float*>(c.data_ptr()));
+    held.push_back(std::move(c));
+  }
+  const int64_t numel = held[0].numel();
+  at::Tensor out = empty_device(shape, inputs[0].options());
+  TVR_TRY(tvr_pointwise(prog.data(), static_cast<int>(n_nodes), static_cast<int>(inputs.size()),
+                        ptrs.data(), static_cast<float*>(out.data_ptr()), numel,
+                        current_stream_handle()));
+  return out;
+}
+
+}  // namespace
+}  // namespace tvarant::ops
+
+TORCH_LIBRARY(tvarant, m) {
+  m.def("linear_act(Tensor x, Tensor weight, Tensor? bias, str act, bool trans_b=False) -> Tensor");
+  m.def(
+      "pointwise(Tensor[] inputs, int[] ops, int[] a, int[] b, int[] input_ids, float[] alphas, "
+      "float[] consts) -> Tensor");
+  m.def("all_reduce_(Tensor(a!) self, int comm) -> Tensor(a!)");
+}
+
+TORCH_LIBRARY_IMPL(tvarant, PrivateUse1, m) {
+  m.impl("linear_act", TORCH_FN(tvarant::ops::linear_act));
+  m.impl("pointwise", TORCH_FN(tvarant::ops::pointwise));
+}

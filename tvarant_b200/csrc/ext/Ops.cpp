@@ -234,7 +234,7 @@ at::Tensor gemm_bias_act(const at::Tensor& a_in, const at::Tensor& b_in, const a
   return out;
 }
 
-at::Tensor _copy_from(const at::Tensor& self, const at::Tensor& dst, bool non_blocking) {
+at::Tensor copy_from(const at::Tensor& self, const at::Tensor& dst, bool non_blocking) {
   TORCH_CHECK(self.defined() && dst.defined(), "copy: undefined tensor");
   if (self.numel() == 0 || dst.numel() == 0) return dst;
   const bool sd = is_device(self), dd = is_device(dst);
@@ -403,7 +403,7 @@ at::Tensor view(const at::Tensor& self, c10::SymIntArrayRef size_sym) {
 
 at::Tensor copy_from_and_resize(const at::Tensor& self, const at::Tensor& dst) {
   resize_(dst, self.sym_sizes(), std::nullopt);
-  return _copy_from(self, dst, false);
+  return copy_from(self, dst, false);
 }
 
 at::Scalar local_scalar_dense(const at::Tensor& self) {
@@ -424,8 +424,9 @@ at::Tensor& set_source_tensor(at::Tensor& self, const at::Tensor& source) {
 
 at::Tensor& set_source_storage(at::Tensor& self, at::Storage source) {
   const int64_t n = static_cast<int64_t>(source.nbytes() / self.dtype().itemsize());
+  const int64_t one = 1;
   self.unsafeGetTensorImpl()->set_storage_keep_dtype(std::move(source));
-  at::native::setStrided(self, {n}, {1}, 0);
+  at::native::setStrided(self, at::IntArrayRef(&n, 1), at::IntArrayRef(&one, 1), int64_t(0));
   return self;
 }
 
@@ -441,7 +442,7 @@ bool compatible_shallow_copy(const at::Tensor&, const at::Tensor&) { return true
 
 at::Tensor& write_into(const at::Tensor& value, at::Tensor& out) {
   if (!out.sizes().equals(value.sizes())) at::native::resize_output(out, value.sizes());
-  _copy_from(value, out, false);
+  copy_from(value, out, false);
   return out;
 }
 
@@ -454,18 +455,20 @@ at::Tensor& mul_out(const at::Tensor& self, const at::Tensor& other, at::Tensor&
   return write_into(mul_tensor(self, other), out);
 }
 
-at::Tensor relu(const at::Tensor& self) {
+at::Tensor relu_op(const at::Tensor& self) {
   check_fp32(self, "relu");
   return unary(self, TVR_UNARY_RELU, 0.f, "relu");
 }
 
-at::Tensor& relu_(at::Tensor& self) {
-  at::Tensor r = relu(self);
-  _copy_from(r, self, false);
+at::Tensor& relu_inplace(at::Tensor& self) {
+  at::Tensor r = relu_op(self);
+  tvarant::ops::copy_from(r, self, false);
   return self;
 }
 
-at::Tensor& relu_out(const at::Tensor& self, at::Tensor& out) { return write_into(relu(self), out); }
+at::Tensor& relu_out(const at::Tensor& self, at::Tensor& out) {
+  return write_into(relu_op(self), out);
+}
 
 at::Tensor mm(const at::Tensor& self, const at::Tensor& mat2) {
   check_fp32(self, "mm");
@@ -511,7 +514,7 @@ void host_random(at::Tensor& self, std::optional<at::Generator> gen, Fn&& draw) 
   } else {
     draw(host, gen);
   }
-  _copy_from(host, self, false);
+  copy_from(host, self, false);
 }
 
 at::Tensor& normal_(at::Tensor& self, double mean, double std, std::optional<at::Generator> gen) {
@@ -528,30 +531,29 @@ at::Tensor& uniform_(at::Tensor& self, double from, double to, std::optional<at:
 }  // namespace tvarant::ops
 
 TORCH_LIBRARY_IMPL(aten, PrivateUse1, m) {
-  using namespace tvarant::ops;
-  m.impl("empty.memory_format", TORCH_FN(empty_memory_format));
-  m.impl("empty_strided", TORCH_FN(empty_strided));
-  m.impl("as_strided", TORCH_FN(as_strided));
-  m.impl("resize_", TORCH_FN(resize_));
-  m.impl("_reshape_alias", TORCH_FN(reshape_alias));
-  m.impl("view", TORCH_FN(view));
-  m.impl("_copy_from", TORCH_FN(_copy_from));
-  m.impl("_copy_from_and_resize", TORCH_FN(copy_from_and_resize));
-  m.impl("_local_scalar_dense", TORCH_FN(local_scalar_dense));
-  m.impl("set_.source_Tensor", TORCH_FN(set_source_tensor));
-  m.impl("set_.source_Storage", TORCH_FN(set_source_storage));
-  m.impl("set_.source_Storage_storage_offset", TORCH_FN(set_source_storage_offset));
-  m.impl("_has_compatible_shallow_copy_type", TORCH_FN(compatible_shallow_copy));
-  m.impl("fill_.Scalar", TORCH_FN(fill_scalar));
-  m.impl("add.Tensor", TORCH_FN(add_tensor));
-  m.impl("add.out", TORCH_FN(add_out));
-  m.impl("mul.Tensor", TORCH_FN(mul_tensor));
-  m.impl("mul.out", TORCH_FN(mul_out));
-  m.impl("relu", TORCH_FN(relu));
-  m.impl("relu_", TORCH_FN(relu_));
-  m.impl("relu.out", TORCH_FN(relu_out));
-  m.impl("mm", TORCH_FN(mm));
-  m.impl("addmm", TORCH_FN(addmm));
-  m.impl("normal_", TORCH_FN(normal_));
-  m.impl("uniform_", TORCH_FN(uniform_));
+  m.impl("empty.memory_format", TORCH_FN(tvarant::ops::empty_memory_format));
+  m.impl("empty_strided", TORCH_FN(tvarant::ops::empty_strided));
+  m.impl("as_strided", TORCH_FN(tvarant::ops::as_strided));
+  m.impl("resize_", TORCH_FN(tvarant::ops::resize_));
+  m.impl("_reshape_alias", TORCH_FN(tvarant::ops::reshape_alias));
+  m.impl("view", TORCH_FN(tvarant::ops::view));
+  m.impl("_copy_from", TORCH_FN(tvarant::ops::copy_from));
+  m.impl("_copy_from_and_resize", TORCH_FN(tvarant::ops::copy_from_and_resize));
+  m.impl("_local_scalar_dense", TORCH_FN(tvarant::ops::local_scalar_dense));
+  m.impl("set_.source_Tensor", TORCH_FN(tvarant::ops::set_source_tensor));
+  m.impl("set_.source_Storage", TORCH_FN(tvarant::ops::set_source_storage));
+  m.impl("set_.source_Storage_storage_offset", TORCH_FN(tvarant::ops::set_source_storage_offset));
+  m.impl("_has_compatible_shallow_copy_type", TORCH_FN(tvarant::ops::compatible_shallow_copy));
+  m.impl("fill_.Scalar", TORCH_FN(tvarant::ops::fill_scalar));
+  m.impl("add.Tensor", TORCH_FN(tvarant::ops::add_tensor));
+  m.impl("add.out", TORCH_FN(tvarant::ops::add_out));
+  m.impl("mul.Tensor", TORCH_FN(tvarant::ops::mul_tensor));
+  m.impl("mul.out", TORCH_FN(tvarant::ops::mul_out));
+  m.impl("relu", TORCH_FN(tvarant::ops::relu_op));
+  m.impl("relu_", TORCH_FN(tvarant::ops::relu_inplace));
+  m.impl("relu.out", TORCH_FN(tvarant::ops::relu_out));
+  m.impl("mm", TORCH_FN(tvarant::ops::mm));
+  m.impl("addmm", TORCH_FN(tvarant::ops::addmm));
+  m.impl("normal_", TORCH_FN(tvarant::ops::normal_));
+  m.impl("uniform_", TORCH_FN(tvarant::ops::uniform_));
 }

@@ -70,7 +70,7 @@ at::Tensor gemm_bias_act(const at::Tensor& a, const at::Tensor& b, const at::Ten
 
 at::Tensor empty_like_contig(const at::Tensor& like, at::IntArrayRef sizes);
 at::Tensor empty_device(at::IntArrayRef sizes, const at::TensorOptions& opts);
-at::Tensor _copy_from(const at::Tensor& self, const at::Tensor& dst, bool non_blocking);
+at::Tensor copy_from(const at::Tensor& self, const at::Tensor& dst, bool non_blocking);
 at::Tensor& fill_scalar(at::Tensor& self, const at::Scalar& value);
 at::Tensor add_tensor(const at::Tensor& self, const at::Tensor& other, const at::Scalar& alpha);
 at::Tensor add_scalar(const at::Tensor& self, const at::Scalar& other, const at::Scalar& alpha);
