@@ -1,0 +1,519 @@
+#!/usr/bin/env python
+"""Benchmark of the tvarant B200 backend (one JSON line on rank 0).
+
+Default workload — the fused-GEMM sweep's largest point: ``nn.Linear(4096,
+4096)`` + SiLU on X [16384, 4096] (TF32 tensor cores), then the JIT-fused
+chain ``abs(neg(exp(Y - Z)))`` on the output, compiled by
+``torch_tvarant.compiler.compile`` into one ``tvarant.linear_act`` and one
+``tvarant.pointwise``.  A step is one pass of that graph over one batch.
+
+* ``value``: TFLOP/s of the GEMM (2*M*N*K per step) over the whole step with
+  inputs resident in HBM, summed over ranks (weak scaling: every rank runs
+  its own replica; this path has no exchange step).
+* ``e2e``: the same metric through the same API with host buffers: X and Z
+  copied from pinned host memory and the result copied back every step.
+* ``roofline``: the tcgen05 GEMM kernel, timed with events on the stream it
+  runs on, against the TF32 dense peak measured with cuBLAS in this run.
+* ``cpu_baseline``: the reference's own simulator kernels
+  (HostKernels.cpp, built into oracle/_ref) on a row sample, all host cores.
+
+Other workloads (``--workload llm-ops | mlp``) report the memory-bound LLM
+ops and the tensor-parallel Llama MLP stack.
+
+``--impl reference`` times the reference's CPU implementation of the same
+workload (rank 0 only) and prints the line with ``"impl": "reference"``.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+M_DEFAULT, K_DEFAULT, N_DEFAULT = 16384, 4096, 4096
+
+
+def _env_rank():
+    return (int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1")),
+            int(os.environ.get("LOCAL_RANK", "0")))
+
+
+def _peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        return json.loads(p.read_text())
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+
+
+def _traffic(key: str):
+    p = ROOT / "profiles" / "ncu_traffic.json"
+    if p.exists():
+        return json.loads(p.read_text()).get(key)
+    return None
+
+
+class ClockSampler:
+    """Polls SM clock and throttle reasons through NVML (every ~5 ms) while
+    the timed region runs; summary() keeps the samples taken inside it."""
+
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown",
+               0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown"}
+
+    def __init__(self, local_rank: int):
+        self.local_rank = local_rank
+        self.samples: list[tuple[float, float, float, int]] = []
+        self.window = None
+        self._stop = threading.Event()
+        self._thread = None
+        self._nvml = None
+        self._handle = None
+
+    def _open(self):
+        import pynvml
+
+        pynvml.nvmlInit()
+        vis = os.environ.get("CUDA_VISIBLE_DEVICES", "")
+        entries = [v.strip() for v in vis.split(",") if v.strip()]
+        if entries and self.local_rank < len(entries):
+            e = entries[self.local_rank]
+            if e.isdigit():
+                handle = pynvml.nvmlDeviceGetHandleByIndex(int(e))
+            else:
+                handle = pynvml.nvmlDeviceGetHandleByUUID(e)
+        else:
+            handle = pynvml.nvmlDeviceGetHandleByIndex(self.local_rank)
+        self._nvml, self._handle = pynvml, handle
+
+    def _poll(self):
+        nv, h = self._nvml, self._handle
+        max_mhz = float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM))
+        while not self._stop.is_set():
+            try:
+                mhz = float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM))
+                try:
+                    bits = int(nv.nvmlDeviceGetCurrentClocksEventReasons(h))
+                except AttributeError:
+                    bits = int(nv.nvmlDeviceGetCurrentClocksThrottleReasons(h))
+                self.samples.append((time.perf_counter(), mhz, max_mhz, bits))
+            except Exception:
+                pass
+            time.sleep(0.005)
+
+    def __enter__(self):
+        try:
+            self._open()
+            self._thread = threading.Thread(target=self._poll, daemon=True)
+            self._thread.start()
+            t0 = time.perf_counter()
+            while not self.samples and time.perf_counter() - t0 < 2.0:
+                time.sleep(0.005)
+        except Exception:
+            self._nvml = None
+        return self
+
+    def mark(self, start: float, end: float):
+        self.window = (start, end)
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._thread is not None:
+            self._thread.join(timeout=2)
+        return False
+
+    def summary(self) -> dict:
+        pts = self.samples
+        if self.window is not None:
+            inside = [p for p in pts if self.window[0] <= p[0] <= self.window[1]]
+            pts = inside or pts[-3:]
+        if not pts:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0,
+                    "source": "unavailable"}
+        reasons = set()
+        for _, _, _, bits in pts:
+            for bit, name in self.REASONS.items():
+                if bits & bit:
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(p[1] for p in pts), "sm_max_mhz": max(p[2] for p in pts),
+                "reasons": sorted(reasons), "samples": len(pts), "source": "NVML, 5 ms polling"}
+
+
+# ------------------------------------------------------------------ CPU side
+
+def _cpu_cores() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
+
+
+def reference_gemm_chain_rows(rows: int, threads: int, seed: int = 0) -> tuple[float, float]:
+    """Times the reference simulator path (HostKernels gemm_bias_act + the
+    eager sub/exp/neg/abs) on `rows` rows of the workload split over
+    `threads` host threads.  Returns (seconds, flops)."""
+    import ctypes
+    from concurrent.futures import ThreadPoolExecutor
+
+    import numpy as np
+
+    import oracle
+
+    impl = "ref" if oracle.available("ref") else "port"
+    lib = oracle._lib(impl)
+    pre = "ref_" if impl == "ref" else "tvo_"
+    gemm = getattr(lib, pre + "gemm_bias_act")
+    unary = getattr(lib, pre + "unary")
+    binary = getattr(lib, pre + "binary")
+    rng = np.random.default_rng(seed)
+    K, N = K_DEFAULT, N_DEFAULT
+    x = rng.standard_normal((rows, K), dtype=np.float32)
+    w = rng.uniform(-1 / 64, 1 / 64, (N, K)).astype(np.float32)
+    b = rng.uniform(-1 / 64, 1 / 64, N).astype(np.float32)
+    z = rng.standard_normal((rows, N), dtype=np.float32)
+    y = np.empty((rows, N), np.float32)
+    t1 = np.empty_like(y)
+    t2 = np.empty_like(y)
+    chunks = np.array_split(np.arange(rows), max(1, min(threads, rows)))
+
+    def work(idx):
+        r0, r1 = int(idx[0]), int(idx[-1]) + 1
+        n = r1 - r0
+        p = lambda arr: ctypes.c_void_p(arr[r0:r1].ctypes.data)  # noqa: E731
+        gemm(p(x), ctypes.c_void_p(w.ctypes.data), ctypes.c_void_p(b.ctypes.data), p(y), n, N, K,
+             1.0, 1.0, 2, 1)
+        binary(0, p(y), p(z), p(t1), n * N, -1.0)   # sub = add with -alpha
+        unary(4, p(t1), p(t2), n * N, 0.0)          # exp
+        unary(2, p(t2), p(t1), n * N, 0.0)          # neg
+        unary(3, p(t1), p(t2), n * N, 0.0)          # abs
+
+    t0 = time.perf_counter()
+    with ThreadPoolExecutor(max_workers=len(chunks)) as ex:
+        list(ex.map(work, chunks))
+    return time.perf_counter() - t0, 2.0 * rows * N * K
+
+
+def cpu_baseline_gemm(budget_s: float = 12.0) -> dict:
+    threads = _cpu_cores()
+    rows = max(threads, 8)
+    dt, fl = reference_gemm_chain_rows(rows, threads)
+    # grow the sample toward the time budget
+    rows2 = int(min(M_DEFAULT, max(rows, rows * budget_s / max(dt, 1e-3) * 0.5)))
+    if rows2 > rows:
+        dt, fl = reference_gemm_chain_rows(rows2, threads)
+        rows = rows2
+    return {"value": fl / dt / 1e12, "unit": "TFLOP/s", "cores": threads, "kind": "reference",
+            "sample": f"{rows} of {M_DEFAULT} rows of the GEMM+SiLU and the sub/exp/neg/abs chain, "
+                      f"reference HostKernels.cpp compiled in oracle/_ref, {threads} threads"}
+
+
+# ------------------------------------------------------------------ GPU side
+
+def _device_setup(local_rank: int):
+    import torch
+
+    import torch_tvarant  # noqa: F401
+
+    torch.tvarant.set_device(local_rank)
+    return torch
+
+
+def tf32_peak_tflops(torch) -> float | None:
+    """cuBLAS TF32 GEMM 8192^3 on this GPU (burst, best of 5)."""
+    if not torch.cuda.is_available():
+        return None
+    try:
+        torch.backends.cuda.matmul.allow_tf32 = True
+        n = 8192
+        a = torch.randn(n, n, device="cuda")
+        b = torch.randn(n, n, device="cuda")
+        for _ in range(3):
+            torch.matmul(a, b)
+        best = None
+        for _ in range(5):
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record()
+            torch.matmul(a, b)
+            e1.record()
+            torch.cuda.synchronize()
+            t = e0.elapsed_time(e1) / 1e3
+            best = t if best is None else min(best, t)
+        del a, b
+        torch.cuda.empty_cache()
+        return 2 * n**3 / best / 1e12
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = False
+
+
+class GemmChain:
+    """The fused-GEMM sweep workload as a model compiled by the tvarant compiler."""
+
+    def __init__(self, torch, m: int, mode: str):
+        import torch.nn as nn
+        import torch.nn.functional as F
+
+        import torch_tvarant
+
+        torch.set_float32_matmul_precision("high" if mode == "tf32" else "highest")
+        self.m = m
+
+        class Model(nn.Module):
+            def __init__(self):
+                super().__init__()
+                self.lin = nn.Linear(K_DEFAULT, N_DEFAULT)
+
+            def forward(self, x, z):
+                y = F.silu(self.lin(x))
+                return torch.abs(-torch.exp(y - z))
+
+        g = torch.Generator().manual_seed(0)
+        model = Model()
+        with torch.no_grad():
+            model.lin.weight.uniform_(-1 / 64, 1 / 64, generator=g)
+            model.lin.bias.uniform_(-1 / 64, 1 / 64, generator=g)
+        self.model = torch_tvarant.compiler.compile(model.to("tvarant"))
+        self.fusions = dict(torch_tvarant.compiler.last_log)
+        self.x_host = torch.randn(m, K_DEFAULT, generator=g).pin_memory() if torch.cuda.is_available() else torch.randn(m, K_DEFAULT, generator=g)
+        self.z_host = torch.randn(m, N_DEFAULT, generator=g).pin_memory() if torch.cuda.is_available() else torch.randn(m, N_DEFAULT, generator=g)
+        self.out_host = torch.empty(m, N_DEFAULT).pin_memory() if torch.cuda.is_available() else torch.empty(m, N_DEFAULT)
+        self.x = self.x_host.to("tvarant")
+        self.z = self.z_host.to("tvarant")
+        self.flops = 2.0 * m * N_DEFAULT * K_DEFAULT
+        self.h2d_bytes = (self.x_host.numel() + self.z_host.numel()) * 4
+        self.d2h_bytes = self.out_host.numel() * 4
+
+    def step_resident(self, torch):
+        return self.model(self.x, self.z)
+
+    def step_e2e(self, torch):
+        x = self.x_host.to("tvarant", non_blocking=True)
+        z = self.z_host.to("tvarant", non_blocking=True)
+        y = self.model(x, z)
+        self.out_host.copy_(y, non_blocking=True)
+        return y
+
+
+def _dist_init(world: int):
+    import torch.distributed as dist
+
+    if world > 1 and not dist.is_initialized():
+        import datetime
+
+        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=120))
+    return dist
+
+
+def _max_over_ranks(value: float, world: int) -> float:
+    if world == 1:
+        return value
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([value], dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def _barrier(world: int):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def run_gemm(args, rank, world, local_rank) -> dict | None:
+    torch = _device_setup(local_rank)
+    wl = GemmChain(torch, args.m, args.mode)
+    Event = lambda: torch.Event(device="tvarant", enable_timing=True)  # noqa: E731
+
+    # warm-up
+    for _ in range(args.warmup):
+        wl.step_resident(torch)
+    torch.tvarant.synchronize()
+
+    # kernel timing: events around the GEMM launch inside each step
+    import torch_tvarant
+
+    lin = wl.model.lin if hasattr(wl.model, "lin") else None
+    w = lin.weight if lin is not None else None
+    bias = lin.bias if lin is not None else None
+
+    # resident: K steps bracketed by barrier + synchronize
+    _barrier(world)
+    torch.tvarant.synchronize()
+    with ClockSampler(local_rank) as clocks:
+        h0 = time.perf_counter()
+        e_start, e_end = Event(), Event()
+        e_start.record()
+        for _ in range(args.steps):
+            wl.step_resident(torch)
+        e_end.record()
+        e_end.synchronize()
+        clocks.mark(h0, time.perf_counter())
+        step_ms = e_start.elapsed_time(e_end) / args.steps
+    # The GEMM kernel alone: the same launch K times back to back on the
+    # same stream between two events (the GPU never waits for the host).
+    g0, g1 = Event(), Event()
+    g0.record()
+    for _ in range(args.steps):
+        torch.ops.tvarant.linear_act(wl.x, w, bias, "silu", True)
+    g1.record()
+    g1.synchronize()
+    kernel_ms = g0.elapsed_time(g1) / args.steps
+    torch.tvarant.synchronize()
+    _barrier(world)
+    step_ms = _max_over_ranks(step_ms, world)
+
+    # end to end through the API with host buffers
+    for _ in range(max(1, args.warmup // 2)):
+        wl.step_e2e(torch)
+    torch.tvarant.synchronize()
+    _barrier(world)
+    t0, t1 = Event(), Event()
+    t0.record()
+    for _ in range(args.steps):
+        wl.step_e2e(torch)
+    t1.record()
+    t1.synchronize()
+    e2e_ms = _max_over_ranks(t0.elapsed_time(t1) / args.steps, world)
+    status = torch.tvarant.get_status()
+
+    if rank != 0:
+        return None
+    peaks = _peaks()
+    tf32_peak = tf32_peak_tflops(torch)
+    achieved = wl.flops / (kernel_ms / 1e3) / 1e12
+    peak = tf32_peak if tf32_peak else peaks.get("bf16_tflops", 1590.0) / 2
+    line = {
+        "metric": "fused-GEMM TFLOP/s (% peak); LLM-op GB/s (% HBM); tokens/s at 1/2/4/8 GPU",
+        "value": world * wl.flops / (step_ms / 1e3) / 1e12,
+        "unit": "TFLOP/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": step_ms,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "tf32" if args.mode == "tf32" else "f32 (3xTF32)",
+        "data": "synthetic (seeded N(0,1) activations, U(-1/64,1/64) weights)",
+        "config": {
+            "workload": f"linear+bias+SiLU GEMM M={args.m} K={K_DEFAULT} N={N_DEFAULT} ({args.mode}) "
+                        "+ JIT-fused abs(neg(exp(Y - Z))) chain, compiled by torch_tvarant.compiler",
+            "M": args.m, "K": K_DEFAULT, "N": N_DEFAULT, "mode": args.mode,
+            "parallelism": f"replicas x{world}",
+            "l2": "inputs (X 268 MB + Z 268 MB + W 67 MB) exceed the 126 MB L2",
+            "fusions": wl.fusions,
+        },
+        "e2e": {"value": world * wl.flops / (e2e_ms / 1e3) / 1e12, "unit": "TFLOP/s",
+                "h2d_bytes_per_step": wl.h2d_bytes, "d2h_bytes_per_step": wl.d2h_bytes,
+                "ms_per_step": e2e_ms},
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                     "frac": achieved / peak, "traffic": _traffic(f"gemm_tf32_m{args.m}"),
+                     "kernel": "tvr::tc::gemm_tc_kernel<256, tf32, K-major B>",
+                     "kernel_ms": kernel_ms,
+                     "peak_source": ("cuBLAS TF32 8192^3 measured in this run" if tf32_peak
+                                     else "half of the bf16 peak (no cuBLAS)"),
+                     "frac_of_bf16_measured": achieved / peaks.get("bf16_tflops", 1617.5)},
+        "gpu_launches": args.steps * 2,
+        "clocks": clocks.summary(),
+        "device_status": status,
+    }
+    if not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline_gemm()
+    return line
+
+
+def run_reference(args, rank, world) -> dict | None:
+    if rank != 0:
+        return None
+    threads = _cpu_cores()
+    rows = args.ref_rows or min(args.m, 64 * threads)
+    for _ in range(args.warmup):
+        reference_gemm_chain_rows(rows, threads)
+    times = []
+    fl = 0.0
+    for _ in range(args.steps):
+        dt, fl = reference_gemm_chain_rows(rows, threads)
+        times.append(dt)
+    dt = sum(times) / len(times)
+    value = fl / dt / 1e12
+    return {
+        "metric": "fused-GEMM TFLOP/s (% peak); LLM-op GB/s (% HBM); tokens/s at 1/2/4/8 GPU",
+        "value": value,
+        "unit": "TFLOP/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": dt * 1e3,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic (seeded N(0,1) activations, U(-1/64,1/64) weights)",
+        "config": {
+            "workload": f"linear+bias+SiLU GEMM M={args.m} K={K_DEFAULT} N={N_DEFAULT} "
+                        "+ abs(neg(exp(Y - Z))) chain (eager, as the reference runs it)",
+            "M": args.m, "K": K_DEFAULT, "N": N_DEFAULT, "parallelism": "host threads",
+        },
+        "impl": "reference",
+        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": threads, "kind": "reference",
+                         "sample": f"{rows} rows of {args.m} per step; reference HostKernels.cpp "
+                                   f"(oracle/_ref), {threads} threads"},
+        "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+
+
+def main() -> int:
+    import torch
+
+    with torch.no_grad():
+        return _main()
+
+
+def _main() -> int:
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["tvarant", "reference"], default="tvarant")
+    ap.add_argument("--workload", choices=["gemm", "llm-ops", "mlp"], default="gemm")
+    ap.add_argument("--m", type=int, default=M_DEFAULT)
+    ap.add_argument("--mode", choices=["tf32", "3xtf32"], default="tf32")
+    ap.add_argument("--ref-rows", type=int, default=0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    rank, world, local_rank = _env_rank()
+    if args.impl == "reference":
+        line = run_reference(args, rank, world)
+    else:
+        _dist_init(world)
+        if args.workload == "gemm":
+            line = run_gemm(args, rank, world, local_rank)
+        else:
+            from tvarant_b200 import workloads
+
+            line = workloads.run(args, rank, world, local_rank)
+    if line is not None:
+        print(json.dumps(line), flush=True)
+    if world > 1 and args.impl != "reference":
+        import torch.distributed as dist
+
+        if dist.is_initialized():
+            dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -88,7 +88,8 @@ struct GuardImpl final : public c10::impl::DeviceGuardImplInterface {
                 s.device_index());
     const int prev = exchange_device(s.device_index());
     if (*event == nullptr) {
-      TVR_TRY(tvr_event_create(event, flag == c10::EventFlag::BACKEND_DEFAULT ? 0 : 1));
+      // as for CUDA: BACKEND_DEFAULT records timing, PYTORCH_DEFAULT does not
+      TVR_TRY(tvr_event_create(event, flag == c10::EventFlag::BACKEND_DEFAULT ? 1 : 0));
     }
     TVR_TRY(tvr_event_record(*event, stream_handle(s.device_index(), s.id())));
     if (prev != s.device_index()) set_device(prev);
