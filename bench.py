@@ -486,10 +486,13 @@ def _main() -> int:
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["tvarant", "reference"], default="tvarant")
-    ap.add_argument("--workload", choices=["gemm", "llm-ops", "mlp"], default="gemm")
+    ap.add_argument("--workload", choices=["gemm", "llm-ops", "mlp", "bmm"], default="gemm")
+    ap.add_argument("--batch", type=int, default=256, help="bmm workload: batch size")
     ap.add_argument("--m", type=int, default=M_DEFAULT)
     ap.add_argument("--mode", choices=["tf32", "3xtf32"], default="tf32")
     ap.add_argument("--ref-rows", type=int, default=0)
+    ap.add_argument("--layers", type=int, default=32, help="mlp workload: MLP layers")
+    ap.add_argument("--chunks", type=int, default=2, help="mlp workload: token chunks overlapped with the all-reduce")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:

@@ -1,0 +1,136 @@
+"""The C ABI boundary without a GPU: every symbol declared in
+include/tvarant.h is exported by libtvarant_cuda.so and bound in
+tvarant_b200.capi; argument validation and the pointwise code generator run
+on the host; generated kernels compile for sm_100a.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import re
+import shutil
+import subprocess
+from pathlib import Path
+
+import pytest
+
+from tvarant_b200 import capi
+
+ROOT = Path(__file__).resolve().parents[1]
+HEADER = ROOT / "include" / "tvarant.h"
+
+
+def declared_functions() -> list[str]:
+    text = HEADER.read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(tvr_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_header_declares_the_boundary():
+    names = declared_functions()
+    assert len(names) >= 50
+    for required in ("tvr_gemm_bias_act", "tvr_bmm", "tvr_softmax", "tvr_layer_norm",
+                     "tvr_embedding", "tvr_unary", "tvr_binary", "tvr_pointwise", "tvr_malloc",
+                     "tvr_nccl_all_reduce"):
+        assert required in names
+
+
+def test_library_exports_every_declared_symbol():
+    lib = capi.load()
+    missing = [n for n in declared_functions() if not hasattr(lib, n)]
+    assert not missing, missing
+
+
+def test_binding_covers_every_declared_symbol():
+    bound = set(capi.SIGNATURES) | set(capi._STR_FUNCS)
+    assert set(declared_functions()) == bound
+
+
+def test_library_exports_nothing_else():
+    nm = shutil.which("nm")
+    if nm is None:
+        pytest.skip("nm not available")
+    out = subprocess.run([nm, "-D", "--defined-only", str(capi.LIB_PATH)], capture_output=True,
+                         text=True, check=True).stdout
+    exported = {line.split()[-1] for line in out.splitlines() if " T " in line}
+    assert {n for n in exported if n.startswith("tvr_")} == set(declared_functions())
+
+
+def test_argument_validation_without_device():
+    capi.load()
+    assert capi.try_call("tvr_gemm_bias_act", None, None, None, None, -1, 4, 4, 4, 4, 4, 1.0, 0.0,
+                         0, 1, 1, None) == capi.ERR_INVALID
+    assert "negative" in capi.last_error()
+    assert capi.try_call("tvr_gemm_bias_act", None, None, None, None, 2, 2, 2, 2, 2, 2, 1.0, 0.0,
+                         7, 1, 1, None) == capi.ERR_INVALID
+    assert capi.try_call("tvr_embedding", None, None, 16, None, 1, 1, 1, None) == capi.ERR_INVALID
+    assert capi.try_call("tvr_binary", 0, None, None, None, 9, None, None, None, 1.0,
+                         None) == capi.ERR_INVALID
+    assert capi.try_call("tvr_fill", None, None, 4, 0, None) == capi.OK  # empty is a no-op
+    n = ctypes.c_int(-1)
+    capi.call("tvr_device_count", ctypes.byref(n))
+    assert n.value >= 0
+
+
+CHAIN = [(0, -1, -1, 0, 1, 0), (0, -1, -1, 1, 1, 0), (9, 0, 1, -1, 1, 0), (10, 2, -1, -1, 1, 0),
+         (6, 3, -1, -1, 1, 0), (11, 4, -1, -1, 1, 0)]
+
+
+def _source(nodes, n_inputs) -> str:
+    arr = capi.pw_program(nodes)
+    buf = ctypes.create_string_buffer(1 << 16)
+    ln = ctypes.c_size_t(0)
+    capi.call("tvr_pointwise_source", ctypes.addressof(arr), len(nodes), n_inputs, buf, len(buf),
+              ctypes.byref(ln))
+    assert ln.value == len(buf.value)
+    return buf.value.decode()
+
+
+def test_pointwise_codegen_text():
+    src = _source(CHAIN, 2)
+    assert "tvr_pointwise_kernel" in src
+    assert "expf(v2)" in src and "fabsf(v4)" in src and "(-v3)" in src
+    # sub is a + (-alpha) * b with alpha = 1 embedded by bit pattern (-1.0f = 0xbf800000)
+    assert "__fmul_rn(__int_as_float(0xbf800000), v1)" in src
+
+
+def test_pointwise_codegen_rejects_invalid_programs():
+    arr = capi.pw_program([(0, -1, -1, 2, 1, 0)])
+    assert capi.try_call("tvr_pointwise_source", ctypes.addressof(arr), 1, 1, None, 0,
+                         None) == capi.ERR_INVALID
+    assert "input_id" in capi.last_error()
+    arr = capi.pw_program([(0, -1, -1, 0, 1, 0), (3, 0, 5, -1, 1, 0)])
+    assert capi.try_call("tvr_pointwise_source", ctypes.addressof(arr), 2, 1, None, 0,
+                         None) == capi.ERR_INVALID
+    arr = capi.pw_program([(0, -1, -1, 0, 1, 0), (42, 0, -1, -1, 1, 0)])
+    assert capi.try_call("tvr_pointwise_source", ctypes.addressof(arr), 2, 1, None, 0,
+                         None) == capi.ERR_INVALID
+
+
+@pytest.mark.skipif(shutil.which("nvcc") is None and not Path("/usr/local/cuda/bin/nvcc").exists(),
+                    reason="nvcc not available")
+def test_generated_kernel_compiles_for_sm100a(tmp_path):
+    nvcc = shutil.which("nvcc") or "/usr/local/cuda/bin/nvcc"
+    src = tmp_path / "pw.cu"
+    src.write_text(_source(CHAIN, 2))
+    subprocess.run([nvcc, "-gencode", "arch=compute_100a,code=sm_100a", "-std=c++17", "-c",
+                    str(src), "-o", str(tmp_path / "pw.o")], check=True, capture_output=True)
+
+
+def test_nccl_entry_points_fail_cleanly_without_a_communicator():
+    capi.load()
+    assert capi.try_call("tvr_nccl_all_reduce", None, None, 4, 0, 0, None, None) in (
+        capi.ERR_INVALID, capi.ERR_NCCL)
+
+
+def test_extension_loads_without_gpu():
+    import torch
+
+    import torch_tvarant
+
+    assert torch.utils.backend_registration._privateuse1_backend_name == "tvarant"
+    assert torch_tvarant._C.backend() == "cuda"
+    assert hasattr(torch.ops.tvarant, "linear_act") and hasattr(torch.ops.tvarant, "pointwise")
+    if not torch.cuda.is_available():
+        assert torch.tvarant.is_available() is False
+        assert torch.tvarant.device_count() == 0

@@ -1,0 +1,160 @@
+"""Graph-level tests of the FX passes (no device needed): which nodes the
+GEMM-epilogue and pointwise fusions rewrite, the SSA programs they emit,
+and the counters in ``last_log`` the reference's tests read
+(reference tests/test_compiler.py, torch_tvarant/compiler.py:136-322).
+"""
+
+from __future__ import annotations
+
+import operator
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+import torch_tvarant  # noqa: F401
+from torch_tvarant.compiler import (ABS, ADD, CONST, EXP, LOAD, MUL, NEG, RELU, SCALE, SILU, SUB,
+                                    compile_fx, fuse_gemm_epilogue, fuse_pointwise, last_log,
+                                    trace_module)
+
+
+def _targets(gm):
+    return [n.target for n in gm.graph.nodes if n.op == "call_function"]
+
+
+def test_opcodes_keep_reference_numbering():
+    assert (LOAD, CONST, ADD, MUL, RELU, SILU, NEG, SCALE) == tuple(range(8))
+    assert (SUB, EXP, ABS) == (9, 10, 11)
+
+
+def test_linear_relu_becomes_linear_act():
+    gm = compile_fx(trace_module(nn.Sequential(nn.Linear(768, 768), nn.ReLU())))
+    assert last_log == {"gemm_epilogue": 1, "pointwise_groups": 0}
+    node = [n for n in gm.graph.nodes if n.target is torch.ops.tvarant.linear_act][0]
+    assert node.args[3] == "relu" and node.args[4] is True
+
+
+def test_linear_silu_and_no_bias():
+    gm = compile_fx(trace_module(nn.Sequential(nn.Linear(8, 16, bias=False), nn.SiLU())))
+    node = [n for n in gm.graph.nodes if n.target is torch.ops.tvarant.linear_act][0]
+    assert node.args[3] == "silu"
+    assert last_log["gemm_epilogue"] == 1
+
+
+class MMAdd(nn.Module):
+    def __init__(self):
+        super().__init__()
+        self.w = nn.Parameter(torch.randn(8, 4))
+        self.b = nn.Parameter(torch.randn(4))
+
+    def forward(self, x):
+        return torch.relu(torch.mm(x, self.w) + self.b)
+
+
+def test_mm_plus_bias_relu():
+    gm = compile_fx(trace_module(MMAdd()))
+    assert last_log["gemm_epilogue"] == 1
+    node = [n for n in gm.graph.nodes if n.target is torch.ops.tvarant.linear_act][0]
+    assert node.args[4] is False
+
+
+class Addmm(nn.Module):
+    def __init__(self, alpha=1.0):
+        super().__init__()
+        self.w = nn.Parameter(torch.randn(8, 4))
+        self.b = nn.Parameter(torch.randn(4))
+        self.alpha = alpha
+
+    def forward(self, x):
+        return F.silu(torch.addmm(self.b, x, self.w, alpha=self.alpha))
+
+
+def test_addmm_only_with_unit_scales():
+    compile_fx(trace_module(Addmm()))
+    assert last_log["gemm_epilogue"] == 1
+    compile_fx(trace_module(Addmm(alpha=2.0)))
+    assert last_log["gemm_epilogue"] == 0
+
+
+class SharedGemm(nn.Module):
+    def __init__(self):
+        super().__init__()
+        self.lin = nn.Linear(8, 8)
+
+    def forward(self, x):
+        y = self.lin(x)
+        return torch.relu(y) + y  # the GEMM has two users: no epilogue fusion
+
+
+def test_gemm_with_two_users_is_not_fused():
+    compile_fx(trace_module(SharedGemm()))
+    assert last_log["gemm_epilogue"] == 0
+
+
+class Chain(nn.Module):
+    def forward(self, y, z):
+        return torch.abs(-torch.exp(y - z))
+
+
+def test_sub_exp_neg_abs_chain_is_one_program():
+    gm = compile_fx(trace_module(Chain()))
+    assert last_log == {"gemm_epilogue": 0, "pointwise_groups": 1}
+    node = [n for n in gm.graph.nodes if n.target is torch.ops.tvarant.pointwise][0]
+    inputs, ops, a, b, input_ids, alphas, consts = node.args
+    assert [i.name for i in inputs] == ["y", "z"]
+    assert ops == [LOAD, LOAD, SUB, EXP, NEG, ABS]
+    assert a == [-1, -1, 0, 2, 3, 4] and b == [-1, -1, 1, -1, -1, -1]
+    assert input_ids == [0, 1, -1, -1, -1, -1]
+
+
+class SwiGLU(nn.Module):
+    def __init__(self):
+        super().__init__()
+        self.w1 = nn.Linear(8, 16, bias=False)
+        self.w2 = nn.Linear(8, 16, bias=False)
+
+    def forward(self, x):
+        return F.silu(self.w1(x)) * self.w2(x)
+
+
+def test_swiglu_fuses_gate_epilogue_only():
+    gm = compile_fx(trace_module(SwiGLU()))
+    assert last_log["gemm_epilogue"] == 1
+    assert torch.ops.tvarant.linear_act in _targets(gm)
+
+
+class Consts(nn.Module):
+    def forward(self, x):
+        return torch.sigmoid(x * 0.5 + 1.0)
+
+
+def test_scalar_operands_become_scale_and_const():
+    gm = fuse_pointwise(trace_module(Consts()))
+    node = [n for n in gm.graph.nodes if n.target is torch.ops.tvarant.pointwise][0]
+    _, ops, _, _, _, alphas, consts = node.args
+    assert ops == [LOAD, SCALE, CONST, ADD, 8]
+    assert alphas[1] == 0.5 and consts[2] == 1.0
+
+
+def test_single_op_is_not_fused():
+    class One(nn.Module):
+        def forward(self, x):
+            return torch.relu(x)
+
+    fuse_pointwise(trace_module(One()))
+    assert last_log["pointwise_groups"] == 0
+
+
+def test_operator_add_is_recognised():
+    class Add(nn.Module):
+        def forward(self, x, y):
+            return operator.add(torch.relu(x), y)
+
+    gm = fuse_pointwise(trace_module(Add()))
+    assert torch.ops.tvarant.pointwise in _targets(gm)
+
+
+def test_gemm_pass_then_pointwise_pass_keep_graph_valid():
+    gm = fuse_gemm_epilogue(trace_module(SwiGLU()))
+    gm = fuse_pointwise(gm)
+    gm.graph.lint()

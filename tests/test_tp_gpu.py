@@ -1,0 +1,51 @@
+"""Tensor-parallel MLP stack on 2 GPUs over NCCL equals the unsharded stack.
+
+Launched as two processes with torch.distributed.run; skipped when fewer
+than two GPUs are visible."""
+
+from __future__ import annotations
+
+import os
+import socket
+import subprocess
+import sys
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+from conftest import rel_frobenius
+
+pytestmark = pytest.mark.gpu
+
+HERE = Path(__file__).resolve().parent
+
+
+def _gpus() -> int:
+    try:
+        import torch
+
+        return torch.cuda.device_count()
+    except Exception:
+        return 0
+
+
+def _port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+@pytest.mark.skipif(_gpus() < 2, reason="needs two GPUs")
+@pytest.mark.parametrize("precision,tol", [("highest", 1e-5), ("high", 5e-3)])
+def test_tp2_matches_single_gpu(tmp_path, precision, tol):
+    out = tmp_path / "tp.npz"
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    cmd = ["timeout", "-k", "30", "240", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+           "--nproc-per-node", "2", "--master-addr", "127.0.0.1", "--master-port", str(_port()),
+           str(HERE / "tp_worker.py"), str(out), precision]
+    proc = subprocess.run(cmd, capture_output=True, text=True, env=env)
+    assert proc.returncode == 0, proc.stdout[-3000:] + proc.stderr[-3000:]
+    r = np.load(out)
+    assert int(r["status"]) == 0
+    assert rel_frobenius(r["tp"], r["full"]) <= tol

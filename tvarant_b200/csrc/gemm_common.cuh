@@ -22,6 +22,26 @@ __device__ __forceinline__ float epilogue_value(float acc, float prev, float alp
   return apply_act(__fadd_rn(__fmul_rn(alpha, acc), __fmul_rn(beta, prev)), act);
 }
 
+// The same on four values with the activation fixed at compile time, for
+// the tensor-core epilogue.  SiLU there uses the fast exponential and
+// division intrinsics (a few ulp, inside the GEMM tolerances) so that the
+// epilogue keeps pace with output bandwidth; the CUDA-core kernel keeps the
+// reference's IEEE expression.
+template <int ACT>
+__device__ __forceinline__ float act_fixed(float v) {
+  if constexpr (ACT == 1) return v > 0.f ? v : 0.f;
+  else if constexpr (ACT == 2) return __fdividef(v, 1.f + __expf(-v));
+  else return v;
+}
+
+template <int ACT>
+__device__ __forceinline__ void epilogue4(float4& x, const float4& prev, float alpha, float beta) {
+  x.x = act_fixed<ACT>(__fadd_rn(__fmul_rn(alpha, x.x), __fmul_rn(beta, prev.x)));
+  x.y = act_fixed<ACT>(__fadd_rn(__fmul_rn(alpha, x.y), __fmul_rn(beta, prev.y)));
+  x.z = act_fixed<ACT>(__fadd_rn(__fmul_rn(alpha, x.z), __fmul_rn(beta, prev.z)));
+  x.w = act_fixed<ACT>(__fadd_rn(__fmul_rn(alpha, x.w), __fmul_rn(beta, prev.w)));
+}
+
 // Entry points of the individual GEMM implementations (host side).
 int gemm_simt(const float* a, const float* b, const float* bias, float* c, int64_t m,
               int64_t n, int64_t k, int64_t lda, int64_t ldb, int64_t ldc, int64_t batch,

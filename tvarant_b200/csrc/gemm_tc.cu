@@ -39,11 +39,11 @@ namespace tc {
 
 constexpr int BM = 128;
 constexpr int BK = 32;  // fp32 elements per k-block = 128 bytes = one swizzle row
-constexpr int NUM_THREADS = 192;
-constexpr int EPI_WARPS = 4;
+constexpr int EPI_WARPS = 8;
+constexpr int NUM_THREADS = 64 + 32 * EPI_WARPS;  // producer, MMA, epilogue warps
 constexpr int STAGE_SMEM = 192 * 1024;
 constexpr int EPI_BUF_BYTES = 32 * 32 * 4;                 // one 32 x 32 fp32 sub-tile
-constexpr int EPI_SMEM = EPI_WARPS * 2 * EPI_BUF_BYTES;    // double-buffered per warp
+constexpr int EPI_SMEM = EPI_WARPS * EPI_BUF_BYTES;        // one staging buffer per warp
 constexpr int GROUP_M = 8;                                 // tile raster group height
 constexpr unsigned long long WAIT_TIMEOUT_NS = 2000000000ull;  // 2 s per barrier phase
 constexpr unsigned WAIT_MAX_POLLS = 1u << 30;
@@ -67,7 +67,6 @@ struct Params {
   CUtensorMap tma_b;     // B or B_hi: {K, N, batch} (K-major) or {N, K, batch} (N-major)
   CUtensorMap tma_a_lo;  // 3xTF32 low parts, same geometry
   CUtensorMap tma_b_lo;
-  CUtensorMap tma_c;     // output (or split-K workspace): {N, M, batch | splits}
   const float* bias;
   float* c;
   int64_t ldc;
@@ -76,12 +75,12 @@ struct Params {
   float beta;
   int act;
   int use_prev;
-  int c_tma;        // 1: TMA stores through tma_c; 0: bounds-checked direct stores
+  int c_vec;        // 1: output rows and base allow 16-byte stores
   int m, n, k;
   int batch;
   int b_broadcast;  // every batch entry uses B[0]
   int tiles_m, tiles_n;
-  int splits;       // > 1: split-K, raw partial sums to the workspace in tma_c
+  int splits;       // > 1: split-K, raw partial sums to the workspace at c
   int kb_per_split;
   int num_kb;
   int total_units;
@@ -151,25 +150,6 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map
       : "memory");
 }
 
-__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, uint32_t src, int c0, int c1,
-                                             int c2) {
-  asm volatile(
-      "cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
-          reinterpret_cast<uint64_t>(map)),
-      "r"(src), "r"(c0), "r"(c1), "r"(c2)
-      : "memory");
-}
-
-__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
-__device__ __forceinline__ void bulk_wait_read_1() {
-  asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
-}
-__device__ __forceinline__ void bulk_wait_all() {
-  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
-}
-__device__ __forceinline__ void fence_proxy_async_smem() {
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-}
 
 __device__ __forceinline__ void tc_fence_before() {
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -233,8 +213,9 @@ __device__ __forceinline__ void mma_commit(uint32_t bar) {
 }
 
 // 32 lanes x 32 columns of 32-bit accumulator -> 32 registers per thread
-// (thread t holds TMEM lane base+t, columns col..col+31).
-__device__ __forceinline__ void tmem_load_32(uint32_t taddr, float (&v)[32]) {
+// (thread t holds TMEM lane base+t, columns col..col+31).  Completion is
+// awaited separately with tmem_wait_loads(), so several loads overlap.
+__device__ __forceinline__ void tmem_load_32_async(uint32_t taddr, float* v) {
   uint32_t r[32];
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
@@ -247,9 +228,12 @@ __device__ __forceinline__ void tmem_load_32(uint32_t taddr, float (&v)[32]) {
         "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]),
         "=r"(r[31])
       : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ void tmem_wait_loads() {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
 __device__ __forceinline__ void record_status(int* status, int code) {
@@ -461,12 +445,21 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) gemm_tc_kernel(const __grid_co
     __syncwarp();
   } else {
     // ------------------------------ epilogue ------------------------------
-    const int q = warp & 3;          // TMEM lane quarter this warp may access
-    const int ew = warp - 2;         // epilogue warp index -> staging buffers
-    const uint32_t ebuf0 = epi0 + ew * 2 * EPI_BUF_BYTES;
+    // Eight warps: warp w reads TMEM lane quarter (w % 4) (rows 32q..32q+31
+    // of the tile) and one half of the columns, 32 columns at a time; the
+    // TMEM buffer goes back to the MMA warp after the last chunk is read
+    // (the other buffer keeps the tensor cores busy meanwhile).  Each 32x32
+    // chunk is transposed through a swizzled 4 KB shared buffer so that the
+    // epilogue math works on four consecutive columns per lane and 8 lanes
+    // write one 128-byte row segment.
+    const int q = warp & 3;
+    const int ew = warp - 2;
+    const int half = ew >> 2;
+    constexpr int HC = BN / 2;      // columns per warp
+    constexpr int CH = HC / 32;     // 32-column chunks per warp
+    const uint32_t sbuf = epi0 + ew * EPI_BUF_BYTES;
     int acc = 0;
     uint32_t acc_phase = 0;
-    int buf = 0;
     bool ok = true;
     for (int u = blockIdx.x; u < p.total_units; u += gridDim.x) {
       int b, s, tm, tn;
@@ -477,64 +470,114 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) gemm_tc_kernel(const __grid_co
         break;
       }
       tc_fence_after();
-      const int row_in_tile = 32 * q + lane;
-      const int64_t row = static_cast<int64_t>(tm) * BM + row_in_tile;
+      const uint32_t tcol = tmem_base + (static_cast<uint32_t>(32 * q) << 16) +
+                            static_cast<uint32_t>(acc * BN + half * HC);
       const int zc = p.splits > 1 ? s : b;
-      float* crow = p.c + static_cast<int64_t>(zc) * p.stride_c + row * p.ldc;
-#pragma unroll 1
-      for (int ch = 0; ch < BN / 32; ++ch) {
-        float v[32];
-        tmem_load_32(tmem_base + (static_cast<uint32_t>(32 * q) << 16) +
-                         static_cast<uint32_t>(acc * BN + 32 * ch),
-                     v);
-        if (ch == BN / 32 - 1) {
+      float* cbase = p.c + static_cast<int64_t>(zc) * p.stride_c;
+      const int64_t row0 = static_cast<int64_t>(tm) * BM + 32 * q;
+      const bool finish = p.splits == 1;
+      // chunk c+1 is read from TMEM while chunk c is transposed and stored
+      float v[32];
+      tmem_load_32_async(tcol, v);
+      tmem_wait_loads();
+      const bool plain = p.alpha == 1.f && p.act == TVR_ACT_NONE &&
+                         (p.beta == 0.f || (p.bias == nullptr && !p.use_prev));
+#pragma unroll
+      for (int c = 0; c < CH; ++c) {
+        if (c == CH - 1) {
           // accumulator fully read: hand the TMEM buffer back to the MMA warp
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(tempty_bar + 8 * acc);
-          __syncwarp();
         }
-        const int col0 = tn * BN + 32 * ch;
-        if (p.splits == 1) {
-          const bool row_ok = row < p.m;
+        // stage: thread = row, 16-byte chunk j of row r at chunk j ^ (r & 7)
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            float prev = 0.f;
-            const int col = col0 + j;
-            if (p.bias != nullptr) {
-              prev = col < p.n ? __ldg(p.bias + col) : 0.f;
-            } else if (p.use_prev) {
-              prev = (row_ok && col < p.n) ? crow[col] : 0.f;
+        for (int j = 0; j < 8; ++j) {
+          const uint32_t addr = sbuf + lane * 128 + ((j ^ (lane & 7)) << 4);
+          asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(v[4 * j]),
+                       "f"(v[4 * j + 1]), "f"(v[4 * j + 2]), "f"(v[4 * j + 3])
+                       : "memory");
+        }
+        if (c + 1 < CH) tmem_load_32_async(tcol + 32 * (c + 1), v);
+        __syncwarp();
+        const int jj = lane & 7;
+        const int col = tn * BN + half * HC + 32 * c + 4 * jj;
+        float4 bias4 = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (finish && p.bias != nullptr) {
+          if (p.c_vec && col + 3 < p.n) {
+            bias4 = __ldg(reinterpret_cast<const float4*>(p.bias + col));
+          } else {
+            bias4.x = col < p.n ? __ldg(p.bias + col) : 0.f;
+            bias4.y = col + 1 < p.n ? __ldg(p.bias + col + 1) : 0.f;
+            bias4.z = col + 2 < p.n ? __ldg(p.bias + col + 2) : 0.f;
+            bias4.w = col + 3 < p.n ? __ldg(p.bias + col + 3) : 0.f;
+          }
+        }
+        // All shared-memory reads (and reads of the previous output, when
+        // beta applies to it) are issued before any global store: a warp's
+        // memory instructions drain in order, so a load queued behind a
+        // store would wait for that store.
+        float4 xs[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int rr = 4 * i + (lane >> 3);
+          const uint32_t addr = sbuf + rr * 128 + ((jj ^ (rr & 7)) << 4);
+          asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+                       : "=f"(xs[i].x), "=f"(xs[i].y), "=f"(xs[i].z), "=f"(xs[i].w)
+                       : "r"(addr));
+        }
+        const bool full4 = p.c_vec && col + 3 < p.n;
+        if (finish && !plain) {
+          const bool read_prev = p.bias == nullptr && p.use_prev;
+          float4 prev[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const int64_t row = row0 + 4 * i + (lane >> 3);
+            prev[i] = bias4;
+            if (read_prev && row < p.m && col < p.n) {
+              const float* src = cbase + row * p.ldc + col;
+              if (full4) {
+                prev[i] = *reinterpret_cast<const float4*>(src);
+              } else {
+                prev[i].x = src[0];
+                prev[i].y = col + 1 < p.n ? src[1] : 0.f;
+                prev[i].z = col + 2 < p.n ? src[2] : 0.f;
+                prev[i].w = col + 3 < p.n ? src[3] : 0.f;
+              }
             }
-            v[j] = epilogue_value(v[j], prev, p.alpha, p.beta, p.act);
+          }
+          // One straight-line loop per activation: with the choice inside
+          // the element loop the compiler evaluates the SiLU path for
+          // every element.
+          if (p.act == TVR_ACT_SILU) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) epilogue4<TVR_ACT_SILU>(xs[i], prev[i], p.alpha, p.beta);
+          } else if (p.act == TVR_ACT_RELU) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) epilogue4<TVR_ACT_RELU>(xs[i], prev[i], p.alpha, p.beta);
+          } else {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) epilogue4<TVR_ACT_NONE>(xs[i], prev[i], p.alpha, p.beta);
           }
         }
-        if (p.c_tma) {
-          const uint32_t eb = ebuf0 + buf * EPI_BUF_BYTES;
-          if (lane == 0) bulk_wait_read_1();  // the store issued from this buffer 2 chunks ago
-          __syncwarp();
-          // 128-byte swizzle: 16-byte chunk j of row r lives at chunk j ^ (r & 7)
+        // compiler barrier: keeps the stores below every load above
+        asm volatile("" ::: "memory");
 #pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            const uint32_t addr = eb + lane * 128 + ((j ^ (lane & 7)) << 4);
-            asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(v[4 * j]),
-                         "f"(v[4 * j + 1]), "f"(v[4 * j + 2]), "f"(v[4 * j + 3])
-                         : "memory");
-          }
-          fence_proxy_async_smem();
-          __syncwarp();
-          if (lane == 0) {
-            tma_store_3d(&p.tma_c, eb, col0, tm * BM + 32 * q, zc);
-            bulk_commit();
-          }
-          __syncwarp();
-          buf ^= 1;
-        } else if (row < p.m) {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            if (col0 + j < p.n) crow[col0 + j] = v[j];
+        for (int i = 0; i < 8; ++i) {
+          const int64_t row = row0 + 4 * i + (lane >> 3);
+          if (row >= p.m || col >= p.n) continue;
+          float* dst = cbase + row * p.ldc + col;
+          if (full4) {
+            *reinterpret_cast<float4*>(dst) = xs[i];
+          } else {
+            dst[0] = xs[i].x;
+            if (col + 1 < p.n) dst[1] = xs[i].y;
+            if (col + 2 < p.n) dst[2] = xs[i].z;
+            if (col + 3 < p.n) dst[3] = xs[i].w;
           }
         }
+        if (c + 1 < CH) tmem_wait_loads();
+        __syncwarp();  // the staging buffer is rewritten by the next chunk
       }
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1u;
@@ -543,7 +586,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) gemm_tc_kernel(const __grid_co
       record_status(p.status, TVR_DEV_TIMEOUT_EPILOGUE);
       *const_cast<volatile int*>(abort_flag) = 1;
     }
-    if (lane == 0) bulk_wait_all();
     __syncwarp();
   }
 
@@ -726,9 +768,9 @@ int gemm_tcgen05(const float* a, const float* b, const float* bias, float* c, in
     tiles = t;
     if (t >= (sms * 4) / 5) break;
   }
-  const bool c_tma = al16(c) && ldc % 4 == 0 && (batch == 1 || (sc != 0 && sc % 4 == 0));
+  const bool c_vec = al16(c) && ldc % 4 == 0 && (batch == 1 || sc % 4 == 0);
   int splits = 1;
-  if (batch == 1 && tiles < (sms * 4) / 5 && n % 4 == 0) {
+  if (batch == 1 && tiles < (sms * 4) / 5) {
     int s = static_cast<int>(sms / tiles);
     s = std::min(s, std::max(1, num_kb / 4));
     s = std::min(s, 16);
@@ -799,20 +841,14 @@ int gemm_tcgen05(const float* a, const float* b, const float* bias, float* c, in
   }
   float* out = c;
   int64_t out_ld = ldc, out_bs = sc;
-  int out_tma = c_tma ? 1 : 0;
+  int out_vec = c_vec ? 1 : 0;
   if (splits > 1) {
     const size_t ws_elems = static_cast<size_t>(splits) * m * n;
     if ((rc = workspace.alloc(ws_elems * sizeof(float), dev, stream)) != TVR_OK) return rc;
     out = static_cast<float*>(workspace.ptr);
     out_ld = n;
     out_bs = m * n;
-    out_tma = 1;
-    if ((rc = encode_3d(&p.tma_c, out, n, m, splits, n * 4, static_cast<uint64_t>(m * n) * 4, 32, 32)) != TVR_OK)
-      return rc;
-  } else if (c_tma) {
-    const uint64_t c_bs = static_cast<uint64_t>(batch > 1 ? sc : m * ldc) * 4;
-    if ((rc = encode_3d(&p.tma_c, c, n, m, batch, ldc * 4, c_bs ? c_bs : 16, 32, 32)) != TVR_OK)
-      return rc;
+    out_vec = n % 4 == 0 ? 1 : 0;
   }
   p.bias = bias;
   p.c = out;
@@ -822,7 +858,7 @@ int gemm_tcgen05(const float* a, const float* b, const float* bias, float* c, in
   p.beta = beta;
   p.act = act;
   p.use_prev = (bias == nullptr && beta != 0.f) ? 1 : 0;
-  p.c_tma = out_tma;
+  p.c_vec = out_vec;
   p.m = static_cast<int>(m);
   p.n = static_cast<int>(n);
   p.k = static_cast<int>(k);

@@ -1,0 +1,157 @@
+"""Tensor-parallel gated-SiLU MLP stack on tvarant devices (one process per GPU).
+
+Partitioning (Megatron-style, one exchange per layer):
+
+* gate and up projections ``W_g, W_u [d_ff, d_model]`` are split by rows
+  (column-parallel): rank r holds rows ``[r*s, (r+1)*s)``, ``s = d_ff / p``;
+* the down projection ``W_d [d_model, d_ff]`` is split by columns
+  (row-parallel) over the same range;
+* each rank computes ``y_r = (silu(x W_g,r^T) * (x W_u,r^T)) W_d,r^T`` — the
+  gate GEMM with SiLU fused in its epilogue (``tvarant.linear_act``) — and
+  one NCCL all-reduce (sum) over NVLink gives ``y = sum_r y_r``.
+
+Tokens are independent through the stack, so the batch is cut into chunks
+that run as separate chains: while chunk i is being all-reduced on the
+communication stream, chunk i+1 runs its GEMMs on the compute stream.
+
+The reference has a single device and no collectives; this module is the
+multi-GPU path of its fused-linear MLP.
+"""
+
+from __future__ import annotations
+
+import contextlib
+from dataclasses import dataclass
+
+import torch
+
+
+def shard_rows(w: torch.Tensor, rank: int, world: int) -> torch.Tensor:
+    """Rows [rank*s, (rank+1)*s) of ``w`` (column-parallel shard)."""
+    n = w.shape[0]
+    if n % world:
+        raise ValueError(f"{n} rows do not split over {world} ranks")
+    s = n // world
+    return w[rank * s:(rank + 1) * s].contiguous()
+
+
+def shard_cols(w: torch.Tensor, rank: int, world: int) -> torch.Tensor:
+    """Columns [rank*s, (rank+1)*s) of ``w`` (row-parallel shard)."""
+    n = w.shape[1]
+    if n % world:
+        raise ValueError(f"{n} columns do not split over {world} ranks")
+    s = n // world
+    return w[:, rank * s:(rank + 1) * s].contiguous()
+
+
+def shard_mlp(w_gate: torch.Tensor, w_up: torch.Tensor, w_down: torch.Tensor, rank: int,
+              world: int):
+    """This rank's (gate, up, down) shards of one MLP layer."""
+    return shard_rows(w_gate, rank, world), shard_rows(w_up, rank, world), shard_cols(w_down, rank, world)
+
+
+@dataclass
+class Communicator:
+    """An NCCL communicator of the tvarant extension (handle into _C)."""
+
+    handle: int
+    rank: int
+    world: int
+
+    @classmethod
+    def from_process_group(cls, device: int) -> "Communicator":
+        """Creates the communicator of the current torch.distributed group; the
+        NCCL unique id travels over that group (gloo / TCPStore)."""
+        import torch.distributed as dist
+
+        from tvarant_b200 import _C
+
+        rank, world = dist.get_rank(), dist.get_world_size()
+        box = [_C.nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(box, src=0)
+        handle = _C.nccl_init(world, rank, box[0], device)
+        return cls(handle, rank, world)
+
+    def all_reduce_(self, t: torch.Tensor) -> torch.Tensor:
+        return torch.ops.tvarant.all_reduce_(t, self.handle)
+
+    def destroy(self, abort: bool = False) -> None:
+        from tvarant_b200 import _C
+
+        _C.nccl_destroy(self.handle, abort)
+
+
+@contextlib.contextmanager
+def on_stream(stream: torch.Stream):
+    """Makes ``stream`` the current tvarant stream inside the block."""
+    from tvarant_b200 import _C
+
+    prev = _C.current_stream(stream.device_index)
+    _C.set_stream(stream.device_index, stream.stream_id)
+    try:
+        yield stream
+    finally:
+        _C.set_stream(prev[0], prev[1])
+
+
+def mlp_layer(x: torch.Tensor, w_gate: torch.Tensor, w_up: torch.Tensor,
+              w_down: torch.Tensor) -> torch.Tensor:
+    """``(silu(x W_g^T) * (x W_u^T)) W_d^T`` on this rank's shards (no reduce)."""
+    g = torch.ops.tvarant.linear_act(x, w_gate, None, "silu", True)
+    u = torch.ops.tvarant.linear_act(x, w_up, None, "none", True)
+    return torch.ops.tvarant.linear_act(g * u, w_down, None, "none", True)
+
+
+class TPMLPStack:
+    """A stack of gated-SiLU MLP layers split over the ranks of ``comm``."""
+
+    def __init__(self, layers, comm: Communicator | None, chunks: int = 2):
+        self.layers = layers  # list of (gate, up, down) shards on this device
+        self.comm = comm
+        self.chunks = max(1, chunks)
+        self._streams = None
+
+    def _comm_streams(self, device: int):
+        if self._streams is None:
+            self._streams = (torch.Stream(device=f"tvarant:{device}"),)
+        return self._streams[0]
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        if self.comm is None or self.comm.world == 1:
+            for wg, wu, wd in self.layers:
+                x = mlp_layer(x, wg, wu, wd)
+            return x
+        device = x.device.index or 0
+        comm_stream = self._comm_streams(device)
+        compute = torch.tvarant.current_stream(device)
+        parts = list(x.split((x.shape[0] + self.chunks - 1) // self.chunks, dim=0))
+        ready = [None] * len(parts)  # event: chunk reduced and usable by compute
+        for wg, wu, wd in self.layers:
+            for i, xi in enumerate(parts):
+                if ready[i] is not None:
+                    compute.wait_event(ready[i])
+                y = mlp_layer(xi, wg, wu, wd)
+                done = torch.Event(device=f"tvarant:{device}")
+                done.record(compute)
+                comm_stream.wait_event(done)
+                with on_stream(comm_stream):
+                    self.comm.all_reduce_(y)
+                    ev = torch.Event(device=f"tvarant:{device}")
+                    ev.record(comm_stream)
+                # y was allocated on the compute stream and is used on the comm stream
+                y.record_stream(comm_stream)
+                ready[i] = ev
+                parts[i] = y
+        for ev in ready:
+            if ev is not None:
+                compute.wait_event(ev)
+        if len(parts) == 1:
+            return parts[0]
+        out = torch.empty((x.shape[0],) + tuple(parts[0].shape[1:]), device=x.device)
+        row = 0
+        for p in parts:
+            out[row:row + p.shape[0]].copy_(p)
+            row += p.shape[0]
+        return out
+
+    __call__ = forward

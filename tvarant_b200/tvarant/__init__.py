@@ -92,6 +92,44 @@ def set_rng_state(new_state: torch.Tensor, device: DeviceLike = "tvarant") -> No
     _C.set_rng_state(new_state, _index(device))
 
 
+_PRIVATEUSE1 = 20  # c10::DeviceType::PrivateUse1
+
+
+def current_stream(device: DeviceLike = None) -> torch.Stream:
+    """The current stream of ``device`` as a torch.Stream."""
+    d, sid = _C.current_stream(_index(device))
+    return torch.Stream(stream_id=sid, device_index=d, device_type=_PRIVATEUSE1)
+
+
+def default_stream(device: DeviceLike = None) -> torch.Stream:
+    d = _index(device)
+    d = current_device() if d < 0 else d
+    return torch.Stream(stream_id=0, device_index=d, device_type=_PRIVATEUSE1)
+
+
+def set_stream(stream: torch.Stream) -> None:
+    _C.set_stream(stream.device_index, stream.stream_id)
+
+
+class stream:
+    """Context manager that makes ``s`` the current tvarant stream."""
+
+    def __init__(self, s: torch.Stream | None):
+        self.s = s
+        self.prev = None
+
+    def __enter__(self):
+        if self.s is not None:
+            self.prev = current_stream(self.s.device_index)
+            set_stream(self.s)
+        return self.s
+
+    def __exit__(self, *exc):
+        if self.prev is not None:
+            set_stream(self.prev)
+        return False
+
+
 def current_stream_handle() -> int:
     """The cudaStream_t of the current stream, as an integer."""
     return int(_C.current_stream_handle())

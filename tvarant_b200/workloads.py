@@ -1,0 +1,246 @@
+"""Benchmark workloads beyond the default fused-GEMM sweep (used by bench.py).
+
+* ``llm-ops`` — the memory-bound LLM op set: softmax(dim=-1) on
+  [8, 32, 2048, 2048], layer_norm over [16384, 4096], embedding of int64 ids
+  [16, 2048] from a [32000, 4096] table, and bmm [256, 2048, 128] x
+  [256, 128, 2048].  Value: algorithmic GB/s of one pass over all four.
+* ``mlp`` — the Llama-7B-shaped gated-SiLU MLP stack (32 layers, d_model
+  4096, d_ff 11008, 8192 tokens, TF32), tensor-parallel over the ranks with
+  one NCCL all-reduce per layer.  Value: tokens/s of the whole job.
+
+Inputs are seeded synthetic tensors with the shapes and distributions of
+those workloads.  All work runs through the torch_tvarant device API.
+"""
+
+from __future__ import annotations
+
+import statistics
+import time
+
+import torch
+
+D_MODEL, D_FF, LAYERS, TOKENS = 4096, 11008, 32, 8192
+
+
+def _events():
+    return (torch.Event(device="tvarant", enable_timing=True),
+            torch.Event(device="tvarant", enable_timing=True))
+
+
+def _time_steps(fn, steps: int) -> float:
+    e0, e1 = _events()
+    e0.record()
+    for _ in range(steps):
+        fn()
+    e1.record()
+    e1.synchronize()
+    return e0.elapsed_time(e1) / steps
+
+
+def run(args, rank: int, world: int, local_rank: int):
+    import torch_tvarant  # noqa: F401
+
+    torch.tvarant.set_device(local_rank)
+    if args.workload == "llm-ops":
+        return _llm_ops(args, rank, world, local_rank)
+    if args.workload == "bmm":
+        return _bmm(args, rank, world, local_rank)
+    return _mlp(args, rank, world, local_rank)
+
+
+# ----------------------------------------------------------------------------- bmm
+
+def _bmm(args, rank, world, local_rank):
+    """bmm [batch, 2048, 128] x [batch, 128, 2048] alone (the LLM op set's bmm)."""
+    import bench
+
+    batch = args.batch
+    g = torch.Generator().manual_seed(1)
+    a = torch.randn(batch, 2048, 128, generator=g).to("tvarant")
+    b = torch.randn(batch, 128, 2048, generator=g).to("tvarant")
+    torch.set_float32_matmul_precision("high" if args.mode == "tf32" else "highest")
+    for _ in range(args.warmup):
+        torch.bmm(a, b)
+    torch.tvarant.synchronize()
+    with bench.ClockSampler(local_rank) as clocks:
+        h0 = time.perf_counter()
+        ms = _time_steps(lambda: torch.bmm(a, b), args.steps)
+        clocks.mark(h0, time.perf_counter())
+    ms = bench._max_over_ranks(ms, world)
+    if rank != 0:
+        return None
+    nbytes = 4 * batch * (2048 * 128 * 2 + 2048 * 2048)
+    hbm = bench._peaks().get("hbm_gbs", 6650.0)
+    gbs = nbytes / (ms / 1e3) / 1e9
+    return {
+        "metric": "fused-GEMM TFLOP/s (% peak); LLM-op GB/s (% HBM); tokens/s at 1/2/4/8 GPU",
+        "value": gbs * world, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "tf32" if args.mode == "tf32" else "f32 (3xTF32)",
+        "data": "synthetic N(0,1)",
+        "config": {"workload": f"bmm [{batch},2048,128] x [{batch},128,2048]",
+                   "tflops": 2 * batch * 2048 * 2048 * 128 / (ms / 1e3) / 1e12,
+                   "parallelism": f"replicas x{world}"},
+        "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s",
+                     "frac": gbs / hbm, "traffic": None, "peak_source": "MEASURED_PEAKS.json hbm_gbs"},
+        "clocks": clocks.summary(),
+        "device_status": torch.tvarant.get_status(),
+    }
+
+
+# ----------------------------------------------------------------------------- llm-ops
+
+def _llm_ops(args, rank, world, local_rank):
+    import bench
+
+    g = torch.Generator().manual_seed(1)
+    dev = "tvarant"
+    sm_x = (torch.randn(8, 32, 2048, 2048, generator=g) * 2 ** 0.5).to(dev)
+    ln_x = torch.randn(16384, 4096, generator=g).to(dev)
+    ln = torch.nn.LayerNorm(4096).to(dev)
+    with torch.no_grad():
+        ln.weight.copy_((1 + 0.1 * torch.randn(4096, generator=g)).to(dev))
+        ln.bias.copy_((0.1 * torch.randn(4096, generator=g)).to(dev))
+    table = (0.02 * torch.randn(32000, 4096, generator=g)).to(dev)
+    ids = torch.randint(0, 32000, (16, 2048), generator=g).to(dev)
+    a = torch.randn(256, 2048, 128, generator=g).to(dev)
+    b = torch.randn(256, 128, 2048, generator=g).to(dev)
+    torch.set_float32_matmul_precision("high" if args.mode == "tf32" else "highest")
+    F = torch.nn.functional
+    ops = {
+        "softmax": (lambda: F.softmax(sm_x, dim=-1), 2 * sm_x.numel() * 4),
+        "layer_norm": (lambda: ln(ln_x), 2 * ln_x.numel() * 4 + 2 * 4096 * 4 + 2 * 16384 * 4),
+        "embedding": (lambda: F.embedding(ids, table), 2 * 32768 * 4096 * 4 + 32768 * 8),
+        "bmm": (lambda: torch.bmm(a, b), 4 * 256 * (2048 * 128 * 2 + 2048 * 2048)),
+    }
+    for fn, _ in ops.values():
+        for _ in range(args.warmup):
+            fn()
+    torch.tvarant.synchronize()
+    per = {}
+    for name, (fn, nbytes) in ops.items():
+        ms = _time_steps(fn, args.steps)
+        per[name] = {"ms": ms, "GB/s": nbytes / (ms / 1e3) / 1e9}
+    with bench.ClockSampler(local_rank) as clocks:
+        h0 = time.perf_counter()
+        total_ms = _time_steps(lambda: [fn() for fn, _ in ops.values()], args.steps)
+        clocks.mark(h0, time.perf_counter())
+    total_bytes = sum(nb for _, nb in ops.values())
+    if rank != 0:
+        return None
+    hbm = bench._peaks().get("hbm_gbs", 6650.0)
+    for v in per.values():
+        v["frac_hbm"] = v["GB/s"] / hbm
+    bmm_tflops = 2 * 256 * 2048 * 2048 * 128 / (per["bmm"]["ms"] / 1e3) / 1e12
+    value = total_bytes / (total_ms / 1e3) / 1e9
+    return {
+        "metric": "fused-GEMM TFLOP/s (% peak); LLM-op GB/s (% HBM); tokens/s at 1/2/4/8 GPU",
+        "value": value * world, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": total_ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded, shapes and distributions of the LLM op set)",
+        "config": {"workload": "softmax [8,32,2048,2048] + layer_norm [16384,4096] + embedding "
+                               "[16,2048] from [32000,4096] + bmm [256,2048,128]x[256,128,2048]",
+                   "per_op": per, "bmm_tflops": bmm_tflops, "parallelism": f"replicas x{world}",
+                   "l2": "every operand exceeds the 126 MB L2 except the LN row vectors"},
+        "roofline": {"bound": "hbm", "achieved": value, "peak": hbm, "unit": "GB/s",
+                     "frac": value / hbm, "traffic": None,
+                     "peak_source": "MEASURED_PEAKS.json hbm_gbs"},
+        "clocks": clocks.summary(),
+        "device_status": torch.tvarant.get_status(),
+    }
+
+
+# ----------------------------------------------------------------------------- mlp
+
+def build_stack(rank: int, world: int, device: str, layers: int = LAYERS, seed: int = 0):
+    """This rank's shards of the MLP stack: one seeded draw of the rank's
+    gate/up/down shards, scaled per layer on the device so that every layer
+    has its own weights in HBM without drawing 17 GB on the host."""
+    s = D_FF // world
+    g = torch.Generator().manual_seed(seed * 1000 + rank)
+    base_g = (0.02 * torch.randn(s, D_MODEL, generator=g)).to(device)
+    base_u = (0.02 * torch.randn(s, D_MODEL, generator=g)).to(device)
+    base_d = (0.02 * torch.randn(D_MODEL, s, generator=g)).to(device)
+    out = []
+    for layer in range(layers):
+        f = 1.0 + 1e-3 * layer
+        out.append((base_g * f, base_u * f, base_d * f))
+    return out
+
+
+def _mlp(args, rank, world, local_rank):
+    import bench
+    from tvarant_b200.tp import Communicator, TPMLPStack
+
+    torch.set_float32_matmul_precision("high" if args.mode == "tf32" else "highest")
+    dev = f"tvarant:{local_rank}"
+    layers = build_stack(rank, world, dev, layers=args.layers)
+    comm = Communicator.from_process_group(local_rank) if world > 1 else None
+    stack = TPMLPStack(layers, comm, chunks=args.chunks if world > 1 else 1)
+    g = torch.Generator().manual_seed(7)
+    x_host = torch.randn(TOKENS, D_MODEL, generator=g)
+    if torch.cuda.is_available():
+        x_host = x_host.pin_memory()
+    x = x_host.to(dev)
+    out_host = torch.empty(TOKENS, D_MODEL)
+    if torch.cuda.is_available():
+        out_host = out_host.pin_memory()
+    for _ in range(args.warmup):
+        stack(x)
+    torch.tvarant.synchronize()
+    bench._barrier(world)
+    with bench.ClockSampler(local_rank) as clocks:
+        h0 = time.perf_counter()
+        ms = _time_steps(lambda: stack(x), args.steps)
+        clocks.mark(h0, time.perf_counter())
+    ms = bench._max_over_ranks(ms, world)
+    # the per-layer GEMMs alone (one rank's share of the FLOPs)
+    wg, wu, wd = layers[0]
+    from tvarant_b200.tp import mlp_layer
+
+    layer_ms = _time_steps(lambda: mlp_layer(x, wg, wu, wd), args.steps)
+
+    def e2e_step():
+        xi = x_host.to(dev, non_blocking=True)
+        out_host.copy_(stack(xi), non_blocking=True)
+
+    e2e_step()
+    torch.tvarant.synchronize()
+    bench._barrier(world)
+    e2e_ms = bench._max_over_ranks(_time_steps(e2e_step, args.steps), world)
+    status = torch.tvarant.get_status()
+    if comm is not None:
+        bench._barrier(world)
+        comm.destroy()
+    if rank != 0:
+        return None
+    flops_total = 3 * 2 * TOKENS * D_MODEL * D_FF * args.layers
+    per_rank_flops = flops_total / world
+    peak = bench.tf32_peak_tflops(torch) or 750.0
+    achieved = per_rank_flops / (ms / 1e3) / 1e12
+    nvlink_bytes = (2 * (world - 1) / world) * TOKENS * D_MODEL * 4 * args.layers if world > 1 else 0
+    target_s = max(per_rank_flops / (peak * 1e12), nvlink_bytes / 770e9)
+    return {
+        "metric": "fused-GEMM TFLOP/s (% peak); LLM-op GB/s (% HBM); tokens/s at 1/2/4/8 GPU",
+        "value": TOKENS / (ms / 1e3), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "tf32" if args.mode == "tf32" else "f32 (3xTF32)",
+        "data": "synthetic (N(0,0.02) weights, N(0,1) activations)",
+        "config": {"workload": f"Llama-7B-shaped gated-SiLU MLP stack, {args.layers} layers, "
+                               f"d_model {D_MODEL}, d_ff {D_FF}, {TOKENS} tokens, TP x{world}",
+                   "parallelism": f"tp{world}", "chunks": stack.chunks,
+                   "layer_ms_one_rank_gemms": layer_ms,
+                   "l2": "weights per rank exceed L2 at tp<=4; activations 134 MB"},
+        "e2e": {"value": TOKENS / (e2e_ms / 1e3), "unit": "tokens/s",
+                "h2d_bytes_per_step": TOKENS * D_MODEL * 4,
+                "d2h_bytes_per_step": TOKENS * D_MODEL * 4, "ms_per_step": e2e_ms},
+        "roofline": {"bound": "tensor" if world == 1 else "tensor+nvlink",
+                     "achieved": achieved, "peak": peak, "unit": "TFLOP/s per GPU",
+                     "frac": (target_s * 1e3) / ms,
+                     "traffic": None,
+                     "peak_source": "cuBLAS TF32 8192^3 measured in this run; NVLink 770 GB/s"},
+        "gpu_launches": args.steps * args.layers * (4 * stack.chunks) + (args.steps * args.layers * stack.chunks if world > 1 else 0),
+        "clocks": clocks.summary(),
+        "device_status": status,
+    }
