@@ -176,6 +176,24 @@ int tvr_gemm_bias_act(const float* a, const float* b, const float* bias, float* 
                       float alpha, float beta, int act, int trans_b, int mode,
                       void* stream);
 
+/* tvr_gemm_bias_act in TF32 mode (same arguments, minus the mode) for
+ * callers that cannot allocate device memory during the call: code running
+ * while a CUDA graph is captured, hosts with a fixed device-memory budget,
+ * runtimes that forbid the allocator after start-up.  No counterpart in the
+ * reference.  The only scratch it uses — split-K partial sums — is a fixed
+ * 16 MiB __device__ array inside the library, which every GPU that loads the
+ * library keeps until the process exits; the call makes no allocation.
+ * Limit: m*n <= 4194304 output elements, else TVR_ERR_INVALID.  The first call
+ * on a device looks the array up (cudaGetSymbolAddress); make that first
+ * call before any stream capture.  All calls share the array: two calls that
+ * may run at the same time on the GPU (different streams, different host
+ * threads) race on it and must be ordered by the caller.  Nothing in the
+ * array needs to start at zero: each call writes every element it reads. */
+int tvr_gemm_bias_act_noalloc(const float* a, const float* b, const float* bias, float* c,
+                              int64_t m, int64_t n, int64_t k,
+                              int64_t lda, int64_t ldb, int64_t ldc,
+                              float alpha, float beta, int act, int trans_b, void* stream);
+
 /* Batched C[i] = A[i] * op(B[i]) for i < batch, each as tvr_gemm_bias_act
  * with alpha 1, beta 0, no activation; matrices are dense row-major with the
  * given element strides between batch entries (stride_b may be 0 to

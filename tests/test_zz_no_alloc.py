@@ -1,0 +1,101 @@
+"""tvr_gemm_bias_act_noalloc: the allocation-free GEMM entry point.
+
+It exists for callers that must not allocate device memory during a call
+(work recorded into a CUDA graph, hosts with a fixed memory budget); its
+split-K scratch is a fixed array inside the library.  Its results must match
+tvr_gemm_bias_act in TF32 mode within the TF32 GEMM tolerance, on two calls
+in a row (the second call reuses the scratch the first left behind), and it
+must refuse outputs larger than its scratch limit.
+
+This file sorts last so that a run stopping at the first failure has run
+every other test before it.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+import pytest
+
+from conftest import rel_frobenius
+
+pytestmark = pytest.mark.gpu
+
+TOL_TF32 = 5e-3
+LIMIT = 4 * 1024 * 1024  # output elements
+
+
+@pytest.fixture(scope="module")
+def lib():
+    import torch  # noqa: F401
+
+    from tvarant_b200 import capi
+
+    capi.load()
+    capi.call("tvr_init")
+    return capi
+
+
+def _dev(x):
+    import torch
+
+    return torch.from_numpy(np.ascontiguousarray(x)).cuda()
+
+
+def _p(t):
+    return ctypes.c_void_p(t.data_ptr()) if t is not None else None
+
+
+def _stream():
+    import torch
+
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def _host(t):
+    import torch
+
+    torch.cuda.synchronize()
+    return t.cpu().numpy()
+
+
+@pytest.mark.parametrize("m,n,k,act,trans_b,with_bias", [
+    (64, 1024, 2048, 0, True, False),     # skinny: split-K partials in the fixed scratch
+    (300, 256, 512, 2, True, True),       # bias + SiLU epilogue after the split-K reduction
+    (1000, 1000, 1000, 1, False, True),   # B given as [K, N]; partials fill 4,000,000 floats
+    (2048, 2048, 256, 0, True, False),    # output exactly at the limit, no split needed
+    (37, 29, 53, 2, True, True),          # unaligned rows: CUDA-core kernel, no scratch
+])
+def test_noalloc_matches_gemm_bias_act_twice(lib, m, n, k, act, trans_b, with_bias):
+    rng = np.random.default_rng(m * 7 + n)
+    a = rng.standard_normal((m, k), dtype=np.float32)
+    b = rng.uniform(-1 / np.sqrt(k), 1 / np.sqrt(k), (n, k) if trans_b else (k, n)).astype(np.float32)
+    bias = rng.uniform(-0.1, 0.1, n).astype(np.float32) if with_bias else None
+    da, db = _dev(a), _dev(b)
+    dbias = _dev(bias) if with_bias else None
+    ldb = k if trans_b else n
+    beta = 1.0 if with_bias else 0.0  # without a bias, beta != 0 would read the output buffer
+    ref = _dev(np.zeros((m, n), np.float32))
+    lib.call("tvr_gemm_bias_act", _p(da), _p(db), _p(dbias), _p(ref), m, n, k, k, ldb, n, 1.0,
+             beta, act, int(trans_b), lib.GEMM_TF32, _stream())
+    expected = _host(ref)
+    outs = []
+    for _ in range(2):
+        out = _dev(np.full((m, n), np.nan, np.float32))
+        lib.call("tvr_gemm_bias_act_noalloc", _p(da), _p(db), _p(dbias), _p(out), m, n, k, k,
+                 ldb, n, 1.0, beta, act, int(trans_b), _stream())
+        outs.append(_host(out))
+    for got in outs:
+        assert np.isfinite(got).all()
+        assert rel_frobenius(got, expected) <= TOL_TF32
+    assert np.array_equal(outs[0], outs[1])
+    assert lib.get_status(0) == 0
+
+
+def test_noalloc_rejects_outputs_beyond_its_scratch(lib):
+    m, n = LIMIT // 1024 + 1, 1024
+    rc = lib.try_call("tvr_gemm_bias_act_noalloc", None, None, None, None, m, n, 64, 64, 64, n,
+                      1.0, 0.0, 0, 1, None)
+    assert rc == lib.ERR_INVALID
+    assert "at most" in lib.last_error()

@@ -890,3 +890,179 @@ int gemm_tcgen05(const float* a, const float* b, const float* bias, float* c, in
 }
 
 }  // namespace tvr
+
+// ---- allocation-free variant ----------------------------------------------------
+//
+// Some callers cannot allocate device memory while they run: code that
+// executes while a CUDA graph is being captured (an allocation is not a
+// capturable stream operation), a host that hands the device a fixed memory
+// budget up front, or an embedding runtime that forbids the driver's
+// allocator after start-up.  tvr_gemm_bias_act_noalloc serves them: it is the
+// TF32 tensor-core GEMM of tvr_gemm_bias_act whose only scratch — the split-K
+// partial sums of skinny problems — lives in the fixed device array below
+// instead of coming from tvr_malloc.
+
+namespace tvr {
+namespace tc {
+
+// 16 MiB of split-K partial sums (4 Mi fp32).  A __device__ array is part of
+// the module: every GPU that loads this library holds it until the process
+// exits.  Host code must not use the name as a pointer (on the host it names a
+// stand-in object); its device address comes from cudaGetSymbolAddress.
+constexpr size_t kNoAllocScratchFloats = size_t(4) << 20;
+static __device__ __align__(256) float g_noalloc_scratch[kNoAllocScratchFloats];
+
+constexpr int kNoAllocMaxDevices = 64;
+std::once_flag g_noalloc_once[kNoAllocMaxDevices];
+float* g_noalloc_ptr[kNoAllocMaxDevices] = {nullptr};
+cudaError_t g_noalloc_err[kNoAllocMaxDevices];
+
+// Device address of the scratch array on `dev` (the current device), looked
+// up once per device.
+int noalloc_scratch(int dev, float** out) {
+  if (dev < 0 || dev >= kNoAllocMaxDevices) {
+    return fail(TVR_ERR_INVALID, "tvr_gemm_bias_act_noalloc: device %d out of range", dev);
+  }
+  std::call_once(g_noalloc_once[dev], [dev]() {
+    void* ptr = nullptr;
+    g_noalloc_err[dev] = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+    if (g_noalloc_err[dev] == cudaSuccess) g_noalloc_ptr[dev] = static_cast<float*>(ptr);
+  });
+  if (g_noalloc_err[dev] != cudaSuccess || g_noalloc_ptr[dev] == nullptr) {
+    return fail(TVR_ERR_CUDA, "tvr_gemm_bias_act_noalloc: cudaGetSymbolAddress failed: %s",
+                cudaGetErrorString(g_noalloc_err[dev]));
+  }
+  *out = g_noalloc_ptr[dev];
+  return TVR_OK;
+}
+
+}  // namespace tc
+
+// TF32 tcgen05 GEMM with split-K partials in the fixed scratch.  Returns
+// TVR_ERR_UNSUPPORTED when the operands cannot be described by TMA maps.
+int gemm_tcgen05_noalloc(const float* a, const float* b, const float* bias, float* c, int64_t m,
+                         int64_t n, int64_t k, int64_t lda, int64_t ldb, int64_t ldc,
+                         float alpha, float beta, int act, bool trans_b, cudaStream_t stream) {
+  using namespace tc;
+  if (!al16(a) || !al16(b) || lda % 4 != 0 || ldb % 4 != 0 || k < 1 || m > 0x7fffff00 ||
+      n > 0x7fffff00 || k > 0x7fffff00) {
+    return TVR_ERR_UNSUPPORTED;
+  }
+  const int dev = current_device();
+  float* scratch = nullptr;
+  int rc = noalloc_scratch(dev, &scratch);
+  if (rc != TVR_OK) return rc;
+  const int sms = sm_count(dev);
+  const int num_kb = static_cast<int>(ceil_div(k, BK));
+  int bn = 64;
+  int64_t tiles = 0;
+  const int bn_cap = n > 128 ? 256 : (n > 64 ? 128 : 64);
+  for (int cand : {256, 128, 64}) {
+    if (cand > bn_cap) continue;
+    tiles = ceil_div(m, BM) * ceil_div(n, cand);
+    bn = cand;
+    if (tiles >= (sms * 4) / 5) break;
+  }
+  int splits = 1;
+  if (tiles < (sms * 4) / 5) {
+    int s = static_cast<int>(sms / tiles);
+    s = std::min(s, std::max(1, num_kb / 4));
+    s = std::min(s, 16);
+    if (s > 1) splits = s;
+  }
+  // the partials of every split must fit the fixed scratch
+  while (splits > 1 && static_cast<size_t>(splits) * m * n > kNoAllocScratchFloats) --splits;
+  int kb_per_split = static_cast<int>(ceil_div(num_kb, splits));
+  splits = static_cast<int>(ceil_div(num_kb, kb_per_split));
+
+  Params p;
+  memset(&p, 0, sizeof(p));
+  if ((rc = encode_3d(&p.tma_a, a, k, m, 1, lda * 4, static_cast<uint64_t>(m * lda) * 4, BK, BM)) != TVR_OK)
+    return rc;
+  const int64_t b_rows = trans_b ? n : k;
+  const uint64_t b_bs = static_cast<uint64_t>(b_rows * ldb) * 4;
+  if (trans_b) {
+    if ((rc = encode_3d(&p.tma_b, b, k, n, 1, ldb * 4, b_bs, BK, bn)) != TVR_OK) return rc;
+  } else {
+    if ((rc = encode_3d(&p.tma_b, b, n, k, 1, ldb * 4, b_bs, 32, BK,
+                        CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B)) != TVR_OK)
+      return rc;
+  }
+  const bool c_vec = al16(c) && ldc % 4 == 0;
+  p.bias = bias;
+  p.alpha = alpha;
+  p.beta = beta;
+  p.act = act;
+  p.use_prev = (bias == nullptr && beta != 0.f) ? 1 : 0;
+  if (splits > 1) {
+    // every element of each split's region is written before it is read, so
+    // nothing left in the scratch by an earlier call is ever used
+    p.c = scratch;
+    p.ldc = n;
+    p.stride_c = m * n;
+    p.c_vec = n % 4 == 0 ? 1 : 0;
+  } else {
+    p.c = c;
+    p.ldc = ldc;
+    p.stride_c = 0;
+    p.c_vec = c_vec ? 1 : 0;
+  }
+  p.m = static_cast<int>(m);
+  p.n = static_cast<int>(n);
+  p.k = static_cast<int>(k);
+  p.batch = 1;
+  p.b_broadcast = 0;
+  p.tiles_m = static_cast<int>(ceil_div(m, BM));
+  p.tiles_n = static_cast<int>(ceil_div(n, bn));
+  p.splits = splits;
+  p.kb_per_split = kb_per_split;
+  p.num_kb = num_kb;
+  const int64_t units = static_cast<int64_t>(splits) * p.tiles_m * p.tiles_n;
+  if (units > 0x7fffffff) return TVR_ERR_UNSUPPORTED;
+  p.total_units = static_cast<int>(units);
+  p.status = device_status_ptr_if_ready(dev);  // never sets the device up (no allocation)
+  const int grid = static_cast<int>(std::min<int64_t>(units, sms));
+  switch (bn) {
+    case 256: rc = launch_bn<256>(p, false, !trans_b, grid, stream, dev); break;
+    case 128: rc = launch_bn<128>(p, false, !trans_b, grid, stream, dev); break;
+    default: rc = launch_bn<64>(p, false, !trans_b, grid, stream, dev); break;
+  }
+  if (rc != TVR_OK) return rc;
+  if (splits > 1) {
+    splitk_reduce_kernel<<<elementwise_grid(m * n, 256, dev), 256, 0, stream>>>(
+        scratch, splits, bias, c, m, n, ldc, alpha, beta, act, p.use_prev);
+    TVR_LAUNCH_CHECK();
+  }
+  return TVR_OK;
+}
+
+}  // namespace tvr
+
+extern "C" int tvr_gemm_bias_act_noalloc(const float* a, const float* b, const float* bias,
+                                         float* c, int64_t m, int64_t n, int64_t k, int64_t lda,
+                                         int64_t ldb, int64_t ldc, float alpha, float beta,
+                                         int act, int trans_b, void* stream) {
+  using namespace tvr;
+  TVR_CHECK(m >= 0 && n >= 0 && k >= 0, "gemm: negative size (%lld, %lld, %lld)", (long long)m,
+            (long long)n, (long long)k);
+  TVR_CHECK(act >= 0 && act <= 2, "gemm: unknown activation %d", act);
+  if (m == 0 || n == 0) return TVR_OK;
+  TVR_CHECK(static_cast<size_t>(m) * static_cast<size_t>(n) <= tc::kNoAllocScratchFloats,
+            "tvr_gemm_bias_act_noalloc: the output has %lld elements; this entry point takes at "
+            "most %zu (its fixed 16 MiB scratch); use tvr_gemm_bias_act",
+            (long long)(m * n), tc::kNoAllocScratchFloats);
+  TVR_CHECK(c != nullptr, "gemm: null output");
+  TVR_CHECK(k == 0 || (a != nullptr && b != nullptr), "gemm: null operand");
+  TVR_CHECK(lda >= k && ldc >= n, "gemm: leading dimension too small");
+  TVR_CHECK(trans_b ? ldb >= k : ldb >= n, "gemm: leading dimension of B too small");
+  cudaStream_t s = as_stream(stream);
+  // the same size threshold as tvr_gemm_bias_act in TF32 mode: tiny problems
+  // run on the CUDA cores, which need no scratch either
+  if (m * n * k > (int64_t(1) << 21)) {
+    const int rc = gemm_tcgen05_noalloc(a, b, bias, c, m, n, k, lda, ldb, ldc, alpha, beta, act,
+                                        trans_b != 0, s);
+    if (rc != TVR_ERR_UNSUPPORTED) return rc;
+  }
+  return gemm_simt(a, b, bias, c, m, n, k, lda, ldb, ldc, 1, 0, 0, 0, alpha, beta, act,
+                   trans_b != 0, s);
+}

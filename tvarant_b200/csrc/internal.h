@@ -26,6 +26,9 @@ int current_device();
 // Per-device int in device memory that kernels with bounded waits write a
 // TVR_DEV_* code into.
 int* device_status_ptr(int device);
+// The same word if the device has already been set up, else nullptr; never
+// sets the device up (so never allocates).
+int* device_status_ptr_if_ready(int device);
 
 // Driver API entry points resolved through cudaGetDriverEntryPoint, so the
 // library does not link libcuda directly.

@@ -169,6 +169,11 @@ int* device_status_ptr(int device) {
   return g_status_words[device];
 }
 
+int* device_status_ptr_if_ready(int device) {
+  if (device < 0 || device >= kMaxDevices) return nullptr;
+  return g_status_words[device];
+}
+
 const DriverApi* driver() {
   std::call_once(g_init_once, do_init);
   if (!g_driver_ok) {
