@@ -517,6 +517,16 @@ void host_random(at::Tensor& self, std::optional<at::Generator> gen, Fn&& draw) 
   copy_from(host, self, false);
 }
 
+// A use of `self` on another stream: its block returns to the pool only
+// after the work queued on `s` so far has run.
+void record_stream(at::Tensor& self, c10::Stream s) {
+  TORCH_CHECK(s.device_type() == c10::DeviceType::PrivateUse1,
+              "record_stream: expected a tvarant stream, got ", s);
+  void* base = self.storage().data_ptr().get();
+  if (base == nullptr) return;
+  TVR_TRY(tvr_record_stream(base, stream_handle(s.device_index(), s.id())));
+}
+
 at::Tensor& normal_(at::Tensor& self, double mean, double std, std::optional<at::Generator> gen) {
   host_random(self, gen, [&](at::Tensor& h, std::optional<at::Generator> g) { h.normal_(mean, std, g); });
   return self;
@@ -555,5 +565,6 @@ TORCH_LIBRARY_IMPL(aten, PrivateUse1, m) {
   m.impl("mm", TORCH_FN(tvarant::ops::mm));
   m.impl("addmm", TORCH_FN(tvarant::ops::addmm));
   m.impl("normal_", TORCH_FN(tvarant::ops::normal_));
+  m.impl("record_stream", TORCH_FN(tvarant::ops::record_stream));
   m.impl("uniform_", TORCH_FN(tvarant::ops::uniform_));
 }
