@@ -52,6 +52,7 @@ extern "C" {
 #define TVR_DEV_TIMEOUT_MMA 2      /* MMA issuer gave up waiting for data / TMEM    */
 #define TVR_DEV_TIMEOUT_EPILOGUE 3 /* epilogue gave up waiting for an accumulator   */
 #define TVR_DEV_TIMEOUT_DRAIN 4    /* exit-time drain of async copies gave up       */
+#define TVR_DEV_TIMEOUT_CONVERT 5  /* 3xTF32 converter gave up waiting for a stage  */
 
 /* GEMM precision modes */
 #define TVR_GEMM_AUTO 0    /* TVARANT_GEMM_MODE env, else 3xTF32               */

@@ -151,6 +151,62 @@ def test_gemm_alpha_beta_prev(lib, rng, mode):
         assert rel_frobenius(y, ref) <= tol
 
 
+FEW_ROW_SHAPES = [
+    (1, 4096, 4096),    # one decode row through a 4096-wide linear
+    (2, 512, 1024),     # two rows: the 3xTF32 mode takes the fp32 FMA GEMV
+    (3, 1000, 1028),    # ragged columns, K not a multiple of the 32-float k-block
+    (5, 37, 64),
+    (8, 11008, 512),
+    (13, 768, 3072),
+    (16, 4096, 4096),
+    (16, 50257, 36),    # vocabulary-sized N, K shorter than one k-block
+    (33, 300, 260),
+    (64, 4096, 1024),
+    (128, 1000, 516),
+]
+
+
+@pytest.mark.parametrize("shape", FEW_ROW_SHAPES)
+@pytest.mark.parametrize("mode,tol", [(1, TOL_TF32), (2, TOL_3XTF32)])
+def test_gemm_few_rows(lib, rng, shape, mode, tol):
+    """At most 128 rows: the weight-streaming tensor-core path (split-K over a CTA
+    cluster), or in 3xTF32 mode for one or two rows the fp32 FMA GEMV."""
+    m, n, k = shape
+    a = rng.standard_normal((m, k), dtype=np.float32)
+    w = rng.uniform(-1 / np.sqrt(k), 1 / np.sqrt(k), (n, k)).astype(np.float32)
+    b = rng.uniform(-1 / np.sqrt(k), 1 / np.sqrt(k), n).astype(np.float32)
+    for act, bias in ((0, None), (1, b), (2, b)):
+        beta = 1.0 if bias is not None else 0.0
+        y = _gemm(lib, a, w, bias, act=act, beta=beta, mode=mode)
+        ref = oracle.gemm_bias_act(a, w, bias, act=act, beta=beta)
+        assert rel_frobenius(y, ref) <= tol, (shape, mode, act, rel_frobenius(y, ref))
+    c0 = rng.standard_normal((m, n), dtype=np.float32)
+    y = _gemm(lib, a, w, None, alpha=0.5, beta=-2.0, act=1, mode=mode, c0=c0)
+    ref = oracle.gemm_bias_act(a, w, None, alpha=0.5, beta=-2.0, act=1, c=c0)
+    assert rel_frobenius(y, ref) <= tol
+    # split-K partials are summed in a fixed order: repeated calls agree bit for bit
+    y1 = _gemm(lib, a, w, b, act=2, mode=mode)
+    y2 = _gemm(lib, a, w, b, act=2, mode=mode)
+    assert np.array_equal(y1, y2)
+    _status_ok(lib)
+
+
+@pytest.mark.parametrize("mode,tol", [(1, TOL_TF32), (2, TOL_3XTF32)])
+def test_gemm_few_rows_strided(lib, rng, mode, tol):
+    """Rows of A and C spaced wider than K and N (a slice of a larger buffer)."""
+    m, n, k, lda, ldc = 7, 300, 256, 260, 304
+    a_full = rng.standard_normal((m, lda), dtype=np.float32)
+    w = rng.standard_normal((n, k), dtype=np.float32)
+    c_full = np.full((m, ldc), 7.0, np.float32)
+    da, dw, dc = _dev(a_full), _dev(w), _dev(c_full)
+    lib.call("tvr_gemm_bias_act", _p(da), _p(dw), None, _p(dc), m, n, k, lda, k, ldc, 1.0, 0.0,
+             0, 1, mode, _stream())
+    y = _host(dc)
+    ref = oracle.gemm_bias_act(np.ascontiguousarray(a_full[:, :k]), w, None, beta=0.0)
+    assert rel_frobenius(y[:, :n], ref) <= tol
+    assert np.all(y[:, n:] == 7.0)
+
+
 def test_gemm_known_answer(lib):
     """[[1,2],[3,4]] @ [[5,6],[7,8]] = [[19,22],[43,50]] (reference tests/test_ops.py:40-46)."""
     a = np.array([[1, 2], [3, 4]], np.float32)

@@ -43,7 +43,9 @@ CUDA_SOURCES = [
     "reduce.cu",
     "gemm.cu",
     "gemm_simt.cu",
+    "gemm_skinny.cu",
     "gemm_tc.cu",
+    "gemm_ws.cu",
     "pointwise_jit.cu",
     "nccl.cu",
 ]

@@ -39,9 +39,21 @@ int run(const float* a, const float* b, const float* bias, float* c, int64_t m, 
   if (mode != TVR_GEMM_TF32 && mode != TVR_GEMM_3XTF32 && mode != TVR_GEMM_FP32) {
     return fail(TVR_ERR_INVALID, "gemm: unknown precision mode %d", mode);
   }
+  // At most 128 rows the weight read bounds the time.  One or two rows in
+  // 3xTF32 mode: the fp32 FMA GEMV, as fast and closer to exact; otherwise
+  // the weight-streaming tensor-core kernel, split over K across a CTA
+  // cluster.  FP32 mode keeps the reference's sequential summation order.
+  if (mode == TVR_GEMM_3XTF32 && batch == 1 &&
+      gemm_skinny_applies(a, b, m, n, k, lda, ldb, trans_b)) {
+    return gemm_skinny(a, b, bias, c, m, n, k, lda, ldb, ldc, alpha, beta, act, stream);
+  }
+  if (mode != TVR_GEMM_FP32 && batch == 1 && gemm_ws_applies(a, b, m, n, k, lda, ldb, trans_b)) {
+    return gemm_ws(a, b, bias, c, m, n, k, lda, ldb, ldc, alpha, beta, act,
+                   mode == TVR_GEMM_3XTF32, stream);
+  }
   const int64_t macs = batch * m * n * k;
   bool tensor = mode != TVR_GEMM_FP32 && macs > kSmallMacs;
-  // Skinny 3xTF32 problems are weight-bandwidth bound: the exact CUDA-core
+  // Other skinny 3xTF32 problems (unaligned, batched): the exact CUDA-core
   // kernel reads each operand once and is as accurate.
   if (mode == TVR_GEMM_3XTF32 && m <= 16) tensor = false;
   if (tensor) {

@@ -48,6 +48,23 @@ int gemm_simt(const float* a, const float* b, const float* bias, float* c, int64
               int64_t sa, int64_t sb, int64_t sc, float alpha, float beta, int act,
               bool trans_b, cudaStream_t stream);
 
+// fp32 FMA GEMV for one or two rows against a K-major weight; applies when
+// gemm_skinny_applies() holds (16-byte aligned rows, K % 4 == 0).
+bool gemm_skinny_applies(const float* a, const float* b, int64_t m, int64_t n, int64_t k,
+                         int64_t lda, int64_t ldb, bool trans_b);
+int gemm_skinny(const float* a, const float* b, const float* bias, float* c, int64_t m, int64_t n,
+                int64_t k, int64_t lda, int64_t ldb, int64_t ldc, float alpha, float beta,
+                int act, cudaStream_t stream);
+
+// Weight-streaming tcgen05 GEMM for at most 128 rows against a K-major
+// weight (split-K over a thread-block cluster, reduced in distributed shared
+// memory); applies when gemm_ws_applies() holds.
+bool gemm_ws_applies(const float* x, const float* w, int64_t m, int64_t n, int64_t k,
+                     int64_t ldx, int64_t ldw, bool trans_b);
+int gemm_ws(const float* x, const float* w, const float* bias, float* c, int64_t m, int64_t n,
+            int64_t k, int64_t ldx, int64_t ldw, int64_t ldc, float alpha, float beta, int act,
+            bool split3, cudaStream_t stream);
+
 // Returns TVR_ERR_UNSUPPORTED (without recording an error) when the
 // operands cannot be described by TMA tensor maps; the caller then uses
 // gemm_simt.

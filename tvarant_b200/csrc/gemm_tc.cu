@@ -33,6 +33,7 @@
 #include <mutex>
 
 #include "gemm_common.cuh"
+#include "tc_ptx.cuh"
 
 namespace tvr {
 namespace tc {
@@ -45,8 +46,6 @@ constexpr int STAGE_SMEM = 192 * 1024;
 constexpr int EPI_BUF_BYTES = 32 * 32 * 4;                 // one 32 x 32 fp32 sub-tile
 constexpr int EPI_SMEM = EPI_WARPS * EPI_BUF_BYTES;        // one staging buffer per warp
 constexpr int GROUP_M = 8;                                 // tile raster group height
-constexpr unsigned long long WAIT_TIMEOUT_NS = 2000000000ull;  // 2 s per barrier phase
-constexpr unsigned WAIT_MAX_POLLS = 1u << 30;
 
 template <int BN, bool SPLIT3>
 struct Cfg {
@@ -87,100 +86,6 @@ struct Params {
   int* status;
 };
 
-// ---- PTX wrappers ------------------------------------------------------------
-
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-
-__device__ __forceinline__ unsigned long long global_ns() {
-  unsigned long long t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
-
-__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
-}
-
-__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
-               : "memory");
-}
-
-__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
-}
-
-__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(bar), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-
-// Waits for the phase of `bar` with parity `parity` to complete.  Gives up
-// (returns false) when the CTA abort flag is raised (if `abort` is given) or
-// after WAIT_TIMEOUT_NS / WAIT_MAX_POLLS.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity,
-                                          const volatile int* abort) {
-  if (mbar_try_wait(bar, parity)) return true;
-  const unsigned long long t0 = global_ns();
-  for (unsigned polls = 1; polls < WAIT_MAX_POLLS; ++polls) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((polls & 31u) == 0) {
-      if (abort != nullptr && *abort) return false;
-      if (global_ns() - t0 > WAIT_TIMEOUT_NS) return false;
-    }
-  }
-  return false;
-}
-
-__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, uint32_t bar,
-                                            int c0, int c1, int c2) {
-  asm volatile(
-      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(dst),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1), "r"(c2)
-      : "memory");
-}
-
-
-__device__ __forceinline__ void tc_fence_before() {
-  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-}
-__device__ __forceinline__ void tc_fence_after() {
-  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-}
-
-// Shared-memory matrix descriptors (tcgen05 "matrix descriptor" format):
-// start address >> 4 in bits [0,14), leading byte offset >> 4 in [16,30),
-// stride byte offset >> 4 in [32,46), version 1 in [46,48), layout type in
-// [61,64): 2 = 128-byte swizzle of 16-byte chunks, 1 = 128-byte swizzle of
-// 32-byte chunks (the only N-major layout kind::tf32 accepts).
-__device__ __forceinline__ uint64_t make_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo,
-                                              uint32_t layout) {
-  uint64_t d = 0;
-  d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
-  d |= static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16;
-  d |= static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32;
-  d |= static_cast<uint64_t>(1) << 46;
-  d |= static_cast<uint64_t>(layout) << 61;
-  return d;
-}
-
-// K-major tile: rows of 128 bytes (32 fp32 along K) with 16-byte chunks
-// swizzled over 8 rows; 8-row groups 1024 B apart.  The leading offset is
-// unused for swizzled K-major layouts.
-__device__ __forceinline__ uint64_t desc_kmajor(uint32_t saddr) {
-  return make_desc(saddr, 16, 1024, 2);
-}
-
 // N-major tile: 32-wide N atoms of [BK rows x 128 B] placed BK*128 B apart
 // (leading offset); 32-byte chunks swizzled over 4 rows, so K groups are
 // 4 rows = 512 B apart (stride offset).
@@ -188,56 +93,9 @@ __device__ __forceinline__ uint64_t desc_nmajor(uint32_t saddr) {
   return make_desc(saddr, BK * 128, 512, 1);
 }
 
-// Instruction descriptor for kind::tf32: D f32 (bits 4-5 = 1), A and B tf32
-// (bits 7-9 and 10-12 = 2), B major-ness in bit 16, N >> 3 in bits 17-22,
-// M >> 4 in bits 24-28.
+// Instruction descriptor of the BM x N x 8 MMA.
 __host__ __device__ constexpr uint32_t make_idesc(int n, bool b_nmajor) {
-  return (1u << 4) | (2u << 7) | (2u << 10) | ((b_nmajor ? 1u : 0u) << 16) |
-         (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(BM >> 4) << 24);
-}
-
-__device__ __forceinline__ void mma_tf32(uint32_t d_tmem, uint64_t da, uint64_t db,
-                                         uint32_t idesc, uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(da), "l"(db), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-
-__device__ __forceinline__ void mma_commit(uint32_t bar) {
-  asm volatile(
-      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
-      : "memory");
-}
-
-// 32 lanes x 32 columns of 32-bit accumulator -> 32 registers per thread
-// (thread t holds TMEM lane base+t, columns col..col+31).  Completion is
-// awaited separately with tmem_wait_loads(), so several loads overlap.
-__device__ __forceinline__ void tmem_load_32_async(uint32_t taddr, float* v) {
-  uint32_t r[32];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
-      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
-        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
-        "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]),
-        "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
-        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]),
-        "=r"(r[31])
-      : "r"(taddr));
-#pragma unroll
-  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-}
-
-__device__ __forceinline__ void tmem_wait_loads() {
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-}
-
-__device__ __forceinline__ void record_status(int* status, int code) {
-  if (status != nullptr) atomicCAS(status, TVR_DEV_OK, code);
+  return idesc_tf32(BM, n, b_nmajor);
 }
 
 // Work unit -> (operand batch index, k split, tile row, tile column).
@@ -666,30 +524,6 @@ __global__ void __launch_bounds__(256) splitk_reduce_kernel(
 
 // ---- host side -----------------------------------------------------------------
 
-int encode_3d(CUtensorMap* map, const void* ptr, uint64_t d0, uint64_t d1, uint64_t d2,
-              uint64_t stride1_bytes, uint64_t stride2_bytes, uint32_t box0, uint32_t box1,
-              CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {
-  const DriverApi* drv = driver();
-  if (drv == nullptr) return TVR_ERR_CUDA;
-  const cuuint64_t dims[3] = {d0, d1, d2};
-  const cuuint64_t strides[2] = {stride1_bytes, stride2_bytes};
-  const cuuint32_t box[3] = {box0, box1, 1};
-  const cuuint32_t elem_strides[3] = {1, 1, 1};
-  CUresult r = drv->tensorMapEncodeTiled(
-      map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<void*>(ptr), dims, strides, box,
-      elem_strides, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
-      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) {
-    const char* msg = "?";
-    if (drv->getErrorString) drv->getErrorString(r, &msg);
-    return fail(TVR_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d: %s) dims {%llu, %llu, %llu}",
-                static_cast<int>(r), msg, (unsigned long long)d0, (unsigned long long)d1,
-                (unsigned long long)d2);
-  }
-  return TVR_OK;
-}
-
-inline bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 template <int BN, bool SPLIT3, bool B_NMAJOR>
 int launch_kernel(const Params& p, int grid, cudaStream_t stream, int dev) {
