@@ -17,8 +17,9 @@ chain ``abs(neg(exp(Y - Z)))`` on the output, compiled by
 * ``cpu_baseline``: the reference's own simulator kernels
   (HostKernels.cpp, built into oracle/_ref) on a row sample, all host cores.
 
-Other workloads (``--workload llm-ops | mlp``) report the memory-bound LLM
-ops and the tensor-parallel Llama MLP stack.
+Other workloads (``--workload llm-ops | mlp | bmm | gpt2``) report the
+memory-bound LLM ops, the tensor-parallel Llama MLP stack, the LLM op set's
+bmm alone, and the GPT-2-small-shaped forward split over the ranks by batch.
 
 ``--impl reference`` times the reference's CPU implementation of the same
 workload (rank 0 only) and prints the line with ``"impl": "reference"``.
@@ -486,12 +487,14 @@ def _main() -> int:
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["tvarant", "reference"], default="tvarant")
-    ap.add_argument("--workload", choices=["gemm", "llm-ops", "mlp", "bmm"], default="gemm")
+    ap.add_argument("--workload", choices=["gemm", "llm-ops", "mlp", "bmm", "gpt2"], default="gemm")
     ap.add_argument("--batch", type=int, default=256, help="bmm workload: batch size")
     ap.add_argument("--m", type=int, default=M_DEFAULT)
     ap.add_argument("--mode", choices=["tf32", "3xtf32"], default="tf32")
     ap.add_argument("--ref-rows", type=int, default=0)
     ap.add_argument("--layers", type=int, default=32, help="mlp workload: MLP layers")
+    ap.add_argument("--seq", type=int, default=1024, help="gpt2 workload: sequence length")
+    ap.add_argument("--gpt2-batch", type=int, default=8, help="gpt2 workload: sequences per step (whole job)")
     ap.add_argument("--chunks", type=int, default=2, help="mlp workload: token chunks overlapped with the all-reduce")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()

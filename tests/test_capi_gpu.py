@@ -339,6 +339,7 @@ def test_unary(lib, rng, op, n, offset):
 @pytest.mark.parametrize("a_shape,b_shape", [
     ((3,), (3,)), ((2, 3), (3,)), ((4, 1, 5), (1, 6, 5)), ((8, 12, 64, 64), (64, 64)),
     ((1000, 768), (768,)), ((7, 9), ()), ((), (5, 4)), ((16, 1), (1, 16)), ((2, 3, 4), (2, 1, 4)),
+    ((96, 333, 333), (333, 333)), ((3, 5, 7, 9, 11), (5, 1, 9, 1)), ((6, 1, 10, 1, 14), (1, 7, 1, 13, 1)),
 ])
 @pytest.mark.parametrize("op,alpha", [(0, 1.0), (0, -0.5), (1, 1.0)])
 def test_binary_broadcast(lib, rng, a_shape, b_shape, op, alpha):
@@ -371,6 +372,9 @@ def test_binary_broadcast(lib, rng, a_shape, b_shape, op, alpha):
     ((4, 6, 8), (0, 2, 1), np.float64),
     ((2, 3, 4, 5), (3, 2, 1, 0), np.uint8),
     ((16, 32, 64), (1, 0, 2), np.float32),
+    ((3, 8, 2, 4, 17, 5), (4, 0, 5, 2, 1, 3), np.float32),   # odd extents in every position
+    ((2, 1024, 3, 12, 64), (2, 0, 3, 1, 4), np.float32),     # GPT-2 head split of a fused QKV
+    ((997, 1031), (1, 0), np.float32),
 ])
 def test_strided_copy(lib, rng, shape, perm, dtype):
     import torch

@@ -1,0 +1,107 @@
+"""GPT-2-shaped decoder forward (tvarant_b200.gpt2): the forward built from
+tvarant ops against the same forward composed from the oracle's kernels, and
+the batch sharding used across GPUs."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+import oracle
+from conftest import rel_frobenius
+from oracle import gpt2 as ogpt2
+
+SMALL = dict(n_layer=2, d_model=128, n_head=4, d_ff=512, vocab=1000, n_ctx=64)
+TINY = dict(n_layer=2, d_model=32, n_head=2, d_ff=64, vocab=50, n_ctx=16)
+
+
+def _params(model):
+    n = lambda t: t.detach().cpu().numpy()  # noqa: E731
+    return {"wte": n(model.wte), "wpe": n(model.wpe), "lnf_g": n(model.lnf_g),
+            "lnf_b": n(model.lnf_b),
+            "layers": [{f: n(getattr(L, f)) for f in L.__dataclass_fields__} for L in model.layers]}
+
+
+def _ids(cfg, batch, seq, seed=5):
+    return np.random.default_rng(seed).integers(0, cfg.vocab, (batch, seq), dtype=np.int64)
+
+
+def test_oracle_forward_matches_torch_cpu():
+    """The oracle composition and the torch composition agree in fp32 on the CPU."""
+    import torch
+
+    from tvarant_b200 import gpt2
+
+    cfg = gpt2.GPT2Config(**TINY)
+    model = gpt2.init_gpt2(cfg, seed=1)
+    ids = _ids(cfg, 2, 12)
+    with torch.no_grad():
+        want = gpt2.forward(model, torch.from_numpy(ids)).numpy()
+    got = ogpt2.forward(_params(model), ids, cfg.n_head)
+    assert got.shape == (2, 12, cfg.vocab)
+    assert rel_frobenius(got, want) <= 1e-5
+
+
+def test_flops_per_token_counts_every_gemm():
+    from tvarant_b200 import gpt2
+
+    cfg = gpt2.GPT2Config()
+    d, f = 768, 3072
+    per_layer = 2 * (3 * d * d + d * d + 2 * d * f) + 4 * 1024 * d
+    assert cfg.flops_per_token(1024) == 12 * per_layer + 2 * d * 50257
+
+
+@pytest.mark.parametrize("world", [1, 2, 4, 8])
+def test_shard_batch_covers_the_batch(world):
+    from tvarant_b200 import gpt2
+
+    spans = [gpt2.shard_batch(8, r, world) for r in range(world)]
+    assert spans[0][0] == 0 and spans[-1][1] == 8
+    assert all(a[1] == b[0] for a, b in zip(spans, spans[1:]))
+    with pytest.raises(ValueError):
+        gpt2.shard_batch(8, 0, 3)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("precision,tol", [("highest", 1e-5), ("high", 5e-3)])
+def test_gpt2_forward_on_device_matches_oracle(precision, tol):
+    """3xTF32 ("highest") within 1e-5 and TF32 ("high") within 5e-3 relative
+    Frobenius error on the logits of a 2-layer model."""
+    import torch
+
+    import torch_tvarant  # noqa: F401
+    from tvarant_b200 import gpt2
+
+    cfg = gpt2.GPT2Config(**SMALL)
+    model = gpt2.init_gpt2(cfg, seed=2)
+    ids = _ids(cfg, 2, 64)
+    want = ogpt2.forward(_params(model), ids, cfg.n_head)
+    old = torch.get_float32_matmul_precision()
+    torch.set_float32_matmul_precision(precision)
+    try:
+        with torch.no_grad():
+            got = gpt2.forward(model.to("tvarant"), torch.from_numpy(ids).to("tvarant")).cpu().numpy()
+    finally:
+        torch.set_float32_matmul_precision(old)
+    assert np.isfinite(got).all()
+    assert rel_frobenius(got, want) <= tol, rel_frobenius(got, want)
+    assert torch.tvarant.get_status() == 0
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dim", [8, 1024, 4096, 20000])
+def test_softmax_with_causal_minus_inf(dim):
+    """Rows that hold -inf (an additive causal mask) through every softmax kernel."""
+    import torch
+
+    import torch_tvarant  # noqa: F401
+
+    rng = np.random.default_rng(dim)
+    x = rng.standard_normal((6, dim), dtype=np.float32)
+    for r in range(6):
+        x[r, rng.integers(1, dim):] = -np.inf  # column 0 always finite
+    want = oracle.softmax(x, -1)
+    got = torch.softmax(torch.from_numpy(x).to("tvarant"), -1).cpu().numpy()
+    assert np.isfinite(got).all()
+    assert np.array_equal(got == 0, want == 0)
+    assert rel_frobenius(got, want) <= 1e-5

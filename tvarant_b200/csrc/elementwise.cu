@@ -118,6 +118,37 @@ struct Index8 {
   int64_t sb[TVR_MAX_DIMS];
 };
 
+// Division of n < 2^31 by a divisor d fixed for the launch, by multiplication:
+// the round-up method of Granlund and Montgomery ("Division by Invariant
+// Integers using Multiplication", PLDI 1994, section 4) with N = 32,
+// l = ceil(log2 d), m = floor(2^32 (2^l - d) / d) + 1, q = (umulhi(n, m) + n) >> l.
+// Exact for all n < 2^32 and 1 <= d < 2^31; a 64-bit divide per dimension
+// per element otherwise dominates the index arithmetic of the N-d kernels.
+struct FastDiv {
+  uint32_t d = 1, m = 1, l = 0;
+};
+
+inline FastDiv make_fastdiv(uint32_t d) {
+  FastDiv f;
+  f.d = d;
+  f.l = 0;
+  while ((uint64_t(1) << f.l) < d) ++f.l;
+  f.m = static_cast<uint32_t>((uint64_t(1) << 32) * ((uint64_t(1) << f.l) - d) / d + 1);
+  return f;
+}
+
+__device__ __forceinline__ uint32_t fast_div(uint32_t n, const FastDiv& f) {
+  return static_cast<uint32_t>((static_cast<uint64_t>(__umulhi(n, f.m)) + n) >> f.l);
+}
+
+// Index arithmetic of the N-d kernels when every extent and element offset
+// fits in 32 bits.
+struct Index8Fast {
+  FastDiv div[TVR_MAX_DIMS];
+  uint32_t sa[TVR_MAX_DIMS];
+  uint32_t sb[TVR_MAX_DIMS];
+};
+
 template <int OP>
 __device__ __forceinline__ float binary_op(float a, float b, float alpha) {
   if constexpr (OP == TVR_BINARY_ADD) {
@@ -192,6 +223,44 @@ __global__ void __launch_bounds__(kThreads) binary_nd_kernel(const float* __rest
   }
 }
 
+// The same with 32-bit index arithmetic (FastDiv); dimension d's divisor is
+// its extent (the innermost counted in vectors).
+template <int OP, int VEC>
+__global__ void __launch_bounds__(kThreads) binary_nd_fast_kernel(const float* __restrict__ a,
+                                                                  const float* __restrict__ b,
+                                                                  float* __restrict__ out,
+                                                                  Index8Fast ix, int ndim,
+                                                                  uint32_t n_vec, float alpha) {
+  const uint32_t stride = gridDim.x * blockDim.x;
+  for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n_vec; i += stride) {
+    uint32_t rem = i;
+    uint32_t oa = 0, ob = 0;
+    for (int d = ndim - 1; d >= 0; --d) {
+      const uint32_t q = fast_div(rem, ix.div[d]);
+      const uint32_t c = rem - q * ix.div[d].d;
+      rem = q;
+      oa += c * ix.sa[d];
+      ob += c * ix.sb[d];
+    }
+    if constexpr (VEC == 4) {
+      const bool a_vec = ix.sa[ndim - 1] == VEC, b_vec = ix.sb[ndim - 1] == VEC;
+      float4 x, w;
+      if (a_vec) x = *reinterpret_cast<const float4*>(a + oa);
+      else x = make_float4(a[oa], a[oa], a[oa], a[oa]);
+      if (b_vec) w = *reinterpret_cast<const float4*>(b + ob);
+      else w = make_float4(b[ob], b[ob], b[ob], b[ob]);
+      float4 r;
+      r.x = binary_op<OP>(x.x, w.x, alpha);
+      r.y = binary_op<OP>(x.y, w.y, alpha);
+      r.z = binary_op<OP>(x.z, w.z, alpha);
+      r.w = binary_op<OP>(x.w, w.w, alpha);
+      reinterpret_cast<float4*>(out)[i] = r;
+    } else {
+      out[i] = binary_op<OP>(a[oa], b[ob], alpha);
+    }
+  }
+}
+
 // Collapses adjacent dimensions that are contiguous for the output and for
 // both operands, and drops size-1 dimensions.  Returns the new rank.
 int collapse_binary(int ndim, const int64_t* sizes, const int64_t* sa, const int64_t* sb,
@@ -252,7 +321,34 @@ int launch_binary(const float* a, const float* b, float* out, int ndim, const in
       outer_aligned = false;
     }
   }
-  if (vec_ok && outer_aligned) {
+  const int vec = (vec_ok && outer_aligned) ? 4 : 1;
+  // 32-bit index arithmetic when every element offset fits
+  bool fits = numel / vec < (int64_t(1) << 31);
+  int64_t max_a = 0, max_b = 0;  // largest element offset of each operand
+  for (int d = 0; fits && d < r; ++d) {
+    fits = ix.sa[d] >= 0 && ix.sb[d] >= 0 && ix.size[d] < (int64_t(1) << 31) &&
+           ix.sa[d] < (int64_t(1) << 31) && ix.sb[d] < (int64_t(1) << 31);
+    max_a += (ix.size[d] - 1) * ix.sa[d];
+    max_b += (ix.size[d] - 1) * ix.sb[d];
+  }
+  fits = fits && max_a + 4 < (int64_t(1) << 31) && max_b + 4 < (int64_t(1) << 31);
+  if (fits) {
+    Index8Fast fx;
+    for (int d = 0; d < r; ++d) {
+      const int64_t ext = d == r - 1 ? ix.size[d] / vec : ix.size[d];
+      fx.div[d] = make_fastdiv(static_cast<uint32_t>(ext));
+      fx.sa[d] = static_cast<uint32_t>(d == r - 1 ? ix.sa[d] * vec : ix.sa[d]);
+      fx.sb[d] = static_cast<uint32_t>(d == r - 1 ? ix.sb[d] * vec : ix.sb[d]);
+    }
+    const int64_t nv = numel / vec;
+    if (vec == 4) {
+      binary_nd_fast_kernel<OP, 4><<<elementwise_grid(nv, kThreads, dev), kThreads, 0, stream>>>(
+          a, b, out, fx, r, static_cast<uint32_t>(nv), alpha);
+    } else {
+      binary_nd_fast_kernel<OP, 1><<<elementwise_grid(nv, kThreads, dev), kThreads, 0, stream>>>(
+          a, b, out, fx, r, static_cast<uint32_t>(nv), alpha);
+    }
+  } else if (vec == 4) {
     const int64_t nv = numel / 4;
     binary_nd_kernel<OP, 4><<<elementwise_grid(nv, kThreads, dev), kThreads, 0, stream>>>(
         a, b, out, ix, r, nv, alpha);
@@ -285,6 +381,32 @@ __global__ void __launch_bounds__(kThreads) strided_copy_kernel(T* __restrict__ 
     for (int d = ndim - 1; d >= 0; --d) {
       const int64_t c = rem % ix.size[d];
       rem /= ix.size[d];
+      od += c * ix.sd[d];
+      os += c * ix.ss[d];
+    }
+    dst[od] = src[os];
+  }
+}
+
+struct CopyIndexFast {
+  FastDiv div[TVR_MAX_DIMS];
+  uint32_t sd[TVR_MAX_DIMS];
+  uint32_t ss[TVR_MAX_DIMS];
+};
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads) strided_copy_fast_kernel(T* __restrict__ dst,
+                                                                     const T* __restrict__ src,
+                                                                     CopyIndexFast ix, int ndim,
+                                                                     uint32_t n) {
+  const uint32_t stride = gridDim.x * blockDim.x;
+  for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+    uint32_t rem = i;
+    uint32_t od = 0, os = 0;
+    for (int d = ndim - 1; d >= 0; --d) {
+      const uint32_t q = fast_div(rem, ix.div[d]);
+      const uint32_t c = rem - q * ix.div[d].d;
+      rem = q;
       od += c * ix.sd[d];
       os += c * ix.ss[d];
     }
@@ -340,8 +462,28 @@ int collapse_copy(int ndim, const int64_t* sizes, const int64_t* sd, const int64
 template <typename T>
 int launch_copy(void* dst, const void* src, const CopyIndex& ix, int r, int64_t n,
                 cudaStream_t stream, int dev) {
-  strided_copy_kernel<T><<<elementwise_grid(n, kThreads, dev), kThreads, 0, stream>>>(
-      static_cast<T*>(dst), static_cast<const T*>(src), ix, r, n);
+  bool fits = n < (int64_t(1) << 31);
+  int64_t max_d = 0, max_s = 0;  // largest element offset of each tensor
+  for (int d = 0; fits && d < r; ++d) {
+    fits = ix.sd[d] >= 0 && ix.ss[d] >= 0 && ix.size[d] < (int64_t(1) << 31) &&
+           ix.sd[d] < (int64_t(1) << 31) && ix.ss[d] < (int64_t(1) << 31);
+    max_d += (ix.size[d] - 1) * ix.sd[d];
+    max_s += (ix.size[d] - 1) * ix.ss[d];
+  }
+  fits = fits && max_d < (int64_t(1) << 31) && max_s < (int64_t(1) << 31);
+  if (fits) {
+    CopyIndexFast fx;
+    for (int d = 0; d < r; ++d) {
+      fx.div[d] = make_fastdiv(static_cast<uint32_t>(ix.size[d]));
+      fx.sd[d] = static_cast<uint32_t>(ix.sd[d]);
+      fx.ss[d] = static_cast<uint32_t>(ix.ss[d]);
+    }
+    strided_copy_fast_kernel<T><<<elementwise_grid(n, kThreads, dev), kThreads, 0, stream>>>(
+        static_cast<T*>(dst), static_cast<const T*>(src), fx, r, static_cast<uint32_t>(n));
+  } else {
+    strided_copy_kernel<T><<<elementwise_grid(n, kThreads, dev), kThreads, 0, stream>>>(
+        static_cast<T*>(dst), static_cast<const T*>(src), ix, r, n);
+  }
   TVR_LAUNCH_CHECK();
   return TVR_OK;
 }

@@ -1,0 +1,137 @@
+"""GPT-2-small-shaped decoder forward built only from tvarant ops.
+
+12 layers, d_model 768, 12 heads of 64, pre-LayerNorm, MLP 768 -> 3072 -> 768
+with SiLU through the fused ``tvarant::linear_act`` GEMM, token embedding of a
+50257-entry vocabulary plus learned positions, causal attention as
+bmm + additive mask + softmax + bmm, and the LM head tied to the token
+embedding.  Weights are drawn N(0, 0.02) from a seeded generator (biases 0,
+LayerNorm gamma 1 / beta 0), the usual GPT-2 initialisation.
+
+The same ``forward`` runs on any device: on ``tvarant`` every op dispatches to
+the sm_100a kernels (embedding, broadcast add, layer_norm, linear / linear_act
+GEMMs, strided copies for the head split, bmm, softmax); on the CPU it gives the
+PyTorch fp32 result used to check it.
+
+Multi-GPU: the batch is split over the ranks (``shard_batch``), which splits
+every attention bmm / softmax over batch x heads; weights are replicated and no
+collective runs in the forward.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass, field
+
+import torch
+
+
+@dataclass
+class GPT2Config:
+    n_layer: int = 12
+    d_model: int = 768
+    n_head: int = 12
+    d_ff: int = 3072
+    vocab: int = 50257
+    n_ctx: int = 1024
+
+    def flops_per_token(self, seq: int) -> int:
+        """Multiply-adds x 2 of one token's forward at sequence length ``seq``
+        (attention scores computed for the full square, as bmm does)."""
+        d, f = self.d_model, self.d_ff
+        linear = 2 * (d * 3 * d + d * d + 2 * d * f)
+        attention = 2 * 2 * seq * d
+        return self.n_layer * (linear + attention) + 2 * d * self.vocab
+
+
+@dataclass
+class Layer:
+    ln1_g: torch.Tensor
+    ln1_b: torch.Tensor
+    w_qkv: torch.Tensor
+    b_qkv: torch.Tensor
+    w_proj: torch.Tensor
+    b_proj: torch.Tensor
+    ln2_g: torch.Tensor
+    ln2_b: torch.Tensor
+    w_fc: torch.Tensor
+    b_fc: torch.Tensor
+    w_out: torch.Tensor
+    b_out: torch.Tensor
+
+
+@dataclass
+class GPT2:
+    cfg: GPT2Config
+    wte: torch.Tensor
+    wpe: torch.Tensor
+    layers: list = field(default_factory=list)
+    lnf_g: torch.Tensor | None = None
+    lnf_b: torch.Tensor | None = None
+
+    def to(self, device) -> "GPT2":
+        mv = lambda t: t.to(device)  # noqa: E731
+        return GPT2(self.cfg, mv(self.wte), mv(self.wpe),
+                    [Layer(*[mv(getattr(L, f)) for f in Layer.__dataclass_fields__])
+                     for L in self.layers],
+                    mv(self.lnf_g), mv(self.lnf_b))
+
+
+def init_gpt2(cfg: GPT2Config, seed: int = 0) -> GPT2:
+    """Seeded host-side weights, N(0, 0.02)."""
+    g = torch.Generator().manual_seed(seed)
+    d, f = cfg.d_model, cfg.d_ff
+
+    def w(*shape):
+        return 0.02 * torch.randn(*shape, generator=g)
+
+    layers = [Layer(torch.ones(d), torch.zeros(d), w(3 * d, d), torch.zeros(3 * d),
+                    w(d, d), torch.zeros(d), torch.ones(d), torch.zeros(d),
+                    w(f, d), torch.zeros(f), w(d, f), torch.zeros(d))
+              for _ in range(cfg.n_layer)]
+    return GPT2(cfg, w(cfg.vocab, d), w(cfg.n_ctx, d), layers, torch.ones(d), torch.zeros(d))
+
+
+def causal_mask(seq: int, device) -> torch.Tensor:
+    """[seq, seq] additive mask: 0 on and below the diagonal, -inf above."""
+    m = torch.full((seq, seq), float("-inf")).triu(1)
+    return m.to(device)
+
+
+def _linear_silu(x, w, b):
+    if x.device.type == "tvarant":
+        return torch.ops.tvarant.linear_act(x, w, b, "silu", True)
+    return torch.nn.functional.silu(torch.nn.functional.linear(x, w, b))
+
+
+def forward(model: GPT2, ids: torch.Tensor, mask: torch.Tensor | None = None) -> torch.Tensor:
+    """Logits [B, S, vocab] for token ids [B, S] (int64, on the model's device)."""
+    F = torch.nn.functional
+    cfg = model.cfg
+    B, S = ids.shape
+    d, H = cfg.d_model, cfg.n_head
+    hd = d // H
+    if mask is None:
+        mask = causal_mask(S, ids.device)
+    scale = 1.0 / math.sqrt(hd)
+    x = F.embedding(ids, model.wte) + model.wpe[:S]
+    for L in model.layers:
+        h = F.layer_norm(x, (d,), L.ln1_g, L.ln1_b, 1e-5)
+        qkv = F.linear(h, L.w_qkv, L.b_qkv).view(B, S, 3, H, hd).permute(2, 0, 3, 1, 4)
+        q = (qkv[0] * scale).reshape(B * H, S, hd)
+        k = qkv[1].reshape(B * H, S, hd)
+        v = qkv[2].reshape(B * H, S, hd)
+        att = F.softmax(torch.bmm(q, k.transpose(1, 2)) + mask, dim=-1)
+        o = torch.bmm(att, v).view(B, H, S, hd).permute(0, 2, 1, 3).reshape(B, S, d)
+        x = x + F.linear(o, L.w_proj, L.b_proj)
+        h = F.layer_norm(x, (d,), L.ln2_g, L.ln2_b, 1e-5)
+        x = x + F.linear(_linear_silu(h, L.w_fc, L.b_fc), L.w_out, L.b_out)
+    x = F.layer_norm(x, (d,), model.lnf_g, model.lnf_b, 1e-5)
+    return F.linear(x, model.wte)
+
+
+def shard_batch(batch: int, rank: int, world: int) -> tuple[int, int]:
+    """[begin, end) of the sequences rank ``rank`` of ``world`` processes."""
+    if batch % world != 0:
+        raise ValueError(f"batch {batch} does not split over {world} ranks")
+    per = batch // world
+    return rank * per, (rank + 1) * per

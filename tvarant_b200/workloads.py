@@ -7,6 +7,11 @@
 * ``mlp`` — the Llama-7B-shaped gated-SiLU MLP stack (32 layers, d_model
   4096, d_ff 11008, 8192 tokens, TF32), tensor-parallel over the ranks with
   one NCCL all-reduce per layer.  Value: tokens/s of the whole job.
+* ``gpt2`` — the GPT-2-small-shaped decoder forward (``tvarant_b200.gpt2``:
+  12 layers, d_model 768, 12 heads, SiLU MLP via the fused linear, vocab
+  50257, batch 8 x seq 1024), the batch split over the ranks (so every
+  attention bmm / softmax is split over batch x heads).  Value: tokens/s of
+  the whole job.
 
 Inputs are seeded synthetic tensors with the shapes and distributions of
 those workloads.  All work runs through the torch_tvarant device API.
@@ -45,6 +50,8 @@ def run(args, rank: int, world: int, local_rank: int):
         return _llm_ops(args, rank, world, local_rank)
     if args.workload == "bmm":
         return _bmm(args, rank, world, local_rank)
+    if args.workload == "gpt2":
+        return _gpt2(args, rank, world, local_rank)
     return _mlp(args, rank, world, local_rank)
 
 
@@ -244,3 +251,106 @@ def _mlp(args, rank, world, local_rank):
         "clocks": clocks.summary(),
         "device_status": status,
     }
+
+
+# ----------------------------------------------------------------------------- gpt2
+
+def _gpt2_cpu_baseline(host_model, cfg, seq: int) -> dict:
+    """The reference's compiled kernels (oracle/_ref) running the same forward
+    on one sequence of ``seq`` tokens, one host thread."""
+    import numpy as np
+
+    import oracle
+    from oracle import gpt2 as ogpt2
+
+    impl = "ref" if oracle.available("ref") else "port"
+    n = lambda t: t.numpy()  # noqa: E731
+    params = {"wte": n(host_model.wte), "wpe": n(host_model.wpe), "lnf_g": n(host_model.lnf_g),
+              "lnf_b": n(host_model.lnf_b),
+              "layers": [{f: n(getattr(L, f)) for f in L.__dataclass_fields__} for L in host_model.layers]}
+    ids = np.random.default_rng(3).integers(0, cfg.vocab, (1, seq), dtype=np.int64)
+    t0 = time.perf_counter()
+    ogpt2.forward(params, ids, cfg.n_head, impl=impl)
+    dt = time.perf_counter() - t0
+    return {"value": seq / dt, "unit": "tokens/s", "cores": 1,
+            "kind": "reference" if impl == "ref" else "port",
+            "sample": f"1 sequence x {seq} tokens through all {cfg.n_layer} layers and the LM head "
+                      f"({dt:.1f} s; attention per token is {seq}/1024 of the benchmark's)"}
+
+
+def _gpt2(args, rank, world, local_rank):
+    import bench
+    from tvarant_b200 import gpt2
+
+    torch.set_float32_matmul_precision("high" if args.mode == "tf32" else "highest")
+    dev = f"tvarant:{local_rank}"
+    cfg = gpt2.GPT2Config()
+    seq, batch = args.seq, args.gpt2_batch
+    host_model = gpt2.init_gpt2(cfg, seed=0)
+    model = host_model.to(dev)
+    b0, b1 = gpt2.shard_batch(batch, rank, world)
+    g = torch.Generator().manual_seed(11)
+    ids_all = torch.randint(0, cfg.vocab, (batch, seq), generator=g)
+    ids_host = ids_all[b0:b1].contiguous()
+    last_host = torch.empty(b1 - b0, cfg.vocab)
+    if torch.cuda.is_available():
+        ids_host = ids_host.pin_memory()
+        last_host = last_host.pin_memory()
+    ids = ids_host.to(dev)
+    mask = gpt2.causal_mask(seq, dev)
+    for _ in range(args.warmup):
+        gpt2.forward(model, ids, mask)
+    torch.tvarant.synchronize()
+    bench._barrier(world)
+    with bench.ClockSampler(local_rank) as clocks:
+        h0 = time.perf_counter()
+        ms = _time_steps(lambda: gpt2.forward(model, ids, mask), args.steps)
+        clocks.mark(h0, time.perf_counter())
+    ms = bench._max_over_ranks(ms, world)
+
+    def e2e_step():
+        x = ids_host.to(dev, non_blocking=True)
+        logits = gpt2.forward(model, x, mask)
+        last_host.copy_(logits[:, -1, :], non_blocking=True)
+
+    e2e_step()
+    torch.tvarant.synchronize()
+    bench._barrier(world)
+    e2e_ms = bench._max_over_ranks(_time_steps(e2e_step, args.steps), world)
+    status = torch.tvarant.get_status()
+    # parity on the device-resident result: the last position of every local
+    # sequence is a proper distribution after softmax (finite logits)
+    logits = gpt2.forward(model, ids, mask)
+    finite = bool(torch.isfinite(logits[:, -1, :].cpu()).all())
+    if rank != 0:
+        return None
+    tokens = batch * seq
+    flops_rank = cfg.flops_per_token(seq) * tokens / world
+    peak = bench.tf32_peak_tflops(torch) or 750.0
+    achieved = flops_rank / (ms / 1e3) / 1e12
+    line = {
+        "metric": "fused-GEMM TFLOP/s (% peak); LLM-op GB/s (% HBM); tokens/s at 1/2/4/8 GPU",
+        "value": tokens / (ms / 1e3), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "tf32" if args.mode == "tf32" else "f32 (3xTF32)",
+        "data": "synthetic (N(0,0.02) weights, uniform token ids)",
+        "config": {"workload": f"GPT-2-small-shaped forward, {cfg.n_layer} layers, d_model {cfg.d_model}, "
+                               f"{cfg.n_head} heads, d_ff {cfg.d_ff} SiLU, vocab {cfg.vocab}, "
+                               f"batch {batch} x seq {seq}, causal bmm+softmax attention, tied LM head",
+                   "parallelism": f"batch split over {world} rank(s) (attention split over batch x heads)",
+                   "tflop_per_step": cfg.flops_per_token(seq) * tokens / 1e12,
+                   "last_logits_finite": finite,
+                   "l2": "attention scores 403 MB per layer, weights 497 MB, logits 1.6 GB"},
+        "e2e": {"value": tokens / (e2e_ms / 1e3), "unit": "tokens/s",
+                "h2d_bytes_per_step": batch * seq * 8, "d2h_bytes_per_step": batch * cfg.vocab * 4,
+                "ms_per_step": e2e_ms},
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s per GPU",
+                     "frac": achieved / peak, "traffic": None,
+                     "peak_source": "cuBLAS TF32 8192^3 measured in this run"},
+        "gpu_launches": args.steps * (cfg.n_layer * 17 + 4),
+        "clocks": clocks.summary(),
+        "device_status": status,
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = _gpt2_cpu_baseline(host_model, cfg, 128)
+    return line
