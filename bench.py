@@ -17,7 +17,9 @@ chain ``abs(neg(exp(Y - Z)))`` on the output, compiled by
 * ``cpu_baseline``: the reference's own simulator kernels
   (HostKernels.cpp, built into oracle/_ref) on a row sample, all host cores.
 
-Other workloads (``--workload llm-ops | mlp | bmm | gpt2``) report the
+``--workload sweep`` runs the whole sweep (M in {1, 16, 128, 1024, 4096,
+16384}, TF32 and 3xTF32).  Other workloads (``--workload llm-ops | mlp | bmm |
+gpt2``) report the
 memory-bound LLM ops, the tensor-parallel Llama MLP stack, the LLM op set's
 bmm alone, and the GPT-2-small-shaped forward split over the ranks by batch.
 
@@ -41,6 +43,7 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 M_DEFAULT, K_DEFAULT, N_DEFAULT = 16384, 4096, 4096
+L2_FLUSH_BYTES = 256 << 20  # twice the B200's 126 MB L2
 
 
 def _env_rank():
@@ -72,7 +75,7 @@ class ClockSampler:
     def __init__(self, local_rank: int):
         self.local_rank = local_rank
         self.samples: list[tuple[float, float, float, int]] = []
-        self.window = None
+        self.windows: list[tuple[float, float]] = []
         self._stop = threading.Event()
         self._thread = None
         self._nvml = None
@@ -122,7 +125,8 @@ class ClockSampler:
         return self
 
     def mark(self, start: float, end: float):
-        self.window = (start, end)
+        """Adds a timed window; summary() keeps the samples inside any window."""
+        self.windows.append((start, end))
 
     def __exit__(self, *exc):
         self._stop.set()
@@ -132,8 +136,8 @@ class ClockSampler:
 
     def summary(self) -> dict:
         pts = self.samples
-        if self.window is not None:
-            inside = [p for p in pts if self.window[0] <= p[0] <= self.window[1]]
+        if self.windows:
+            inside = [p for p in pts if any(a <= p[0] <= b for a, b in self.windows)]
             pts = inside or pts[-3:]
         if not pts:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0,
@@ -280,8 +284,20 @@ class GemmChain:
         with torch.no_grad():
             model.lin.weight.uniform_(-1 / 64, 1 / 64, generator=g)
             model.lin.bias.uniform_(-1 / 64, 1 / 64, generator=g)
-        self.model = torch_tvarant.compiler.compile(model.to("tvarant"))
-        self.fusions = dict(torch_tvarant.compiler.last_log)
+        # When one step's own operands fit in L2 (small M), consecutive steps
+        # rotate over copies of the weight in distinct buffers, more than 256 MB
+        # in total, so every step streams its weight from HBM.
+        step_bytes = 4 * (m * K_DEFAULT + 2 * m * N_DEFAULT + N_DEFAULT * K_DEFAULT)
+        w_bytes = 4 * N_DEFAULT * K_DEFAULT
+        self.copies = 1 if step_bytes >= L2_FLUSH_BYTES else -(-L2_FLUSH_BYTES // w_bytes) + 1
+        import copy
+
+        self.models = []
+        for _ in range(self.copies):
+            self.models.append(torch_tvarant.compiler.compile(copy.deepcopy(model).to("tvarant")))
+            self.fusions = dict(torch_tvarant.compiler.last_log)
+        self.model = self.models[0]
+        self.i = 0
         self.x_host = torch.randn(m, K_DEFAULT, generator=g).pin_memory() if torch.cuda.is_available() else torch.randn(m, K_DEFAULT, generator=g)
         self.z_host = torch.randn(m, N_DEFAULT, generator=g).pin_memory() if torch.cuda.is_available() else torch.randn(m, N_DEFAULT, generator=g)
         self.out_host = torch.empty(m, N_DEFAULT).pin_memory() if torch.cuda.is_available() else torch.empty(m, N_DEFAULT)
@@ -291,13 +307,17 @@ class GemmChain:
         self.h2d_bytes = (self.x_host.numel() + self.z_host.numel()) * 4
         self.d2h_bytes = self.out_host.numel() * 4
 
+    def next_model(self):
+        self.i += 1
+        return self.models[self.i % self.copies]
+
     def step_resident(self, torch):
-        return self.model(self.x, self.z)
+        return self.next_model()(self.x, self.z)
 
     def step_e2e(self, torch):
         x = self.x_host.to("tvarant", non_blocking=True)
         z = self.z_host.to("tvarant", non_blocking=True)
-        y = self.model(x, z)
+        y = self.next_model()(x, z)
         self.out_host.copy_(y, non_blocking=True)
         return y
 
@@ -330,77 +350,113 @@ def _barrier(world: int):
         dist.barrier()
 
 
-def run_gemm(args, rank, world, local_rank) -> dict | None:
-    torch = _device_setup(local_rank)
-    wl = GemmChain(torch, args.m, args.mode)
-    Event = lambda: torch.Event(device="tvarant", enable_timing=True)  # noqa: E731
+def gemm_kernel_name(m: int, mode: str) -> tuple[str, str]:
+    """(kernel, bound) that ``tvr_gemm_bias_act`` runs for M rows of the sweep."""
+    if mode == "3xtf32" and m <= 2:
+        return "tvr::gemm_skinny_kernel (fp32 FMA GEMV)", "hbm"
+    if m <= 128:
+        return f"tvr::ws::gemm_ws_kernel ({mode}, weight streaming)", "hbm"
+    return f"tvr::tc::gemm_tc_kernel<256, {mode}, K-major B>", "tensor"
 
-    # warm-up
-    for _ in range(args.warmup):
+
+def measure_gemm_point(torch, m: int, mode: str, steps: int, warmup: int, world: int,
+                       clocks=None) -> dict:
+    """One point of the fused-GEMM sweep: the compiled linear+bias+SiLU +
+    chain step (resident inputs), the GEMM launch alone back to back, and the
+    end-to-end step with host buffers.  Times are max over ranks."""
+    wl = GemmChain(torch, m, mode)
+    Event = lambda: torch.Event(device="tvarant", enable_timing=True)  # noqa: E731
+    for _ in range(warmup):
         wl.step_resident(torch)
     torch.tvarant.synchronize()
-
-    # kernel timing: events around the GEMM launch inside each step
-    import torch_tvarant
-
-    lin = wl.model.lin if hasattr(wl.model, "lin") else None
-    w = lin.weight if lin is not None else None
-    bias = lin.bias if lin is not None else None
-
-    # resident: K steps bracketed by barrier + synchronize
     _barrier(world)
     torch.tvarant.synchronize()
-    with ClockSampler(local_rank) as clocks:
-        h0 = time.perf_counter()
-        e_start, e_end = Event(), Event()
-        e_start.record()
-        for _ in range(args.steps):
-            wl.step_resident(torch)
-        e_end.record()
-        e_end.synchronize()
+    h0 = time.perf_counter()
+    e_start, e_end = Event(), Event()
+    e_start.record()
+    for _ in range(steps):
+        wl.step_resident(torch)
+    e_end.record()
+    e_end.synchronize()
+    if clocks is not None:
         clocks.mark(h0, time.perf_counter())
-        step_ms = e_start.elapsed_time(e_end) / args.steps
-    # The GEMM kernel alone: the same launch K times back to back on the
-    # same stream between two events (the GPU never waits for the host).
+    step_ms = e_start.elapsed_time(e_end) / steps
+    # The GEMM kernel alone: the same launch back to back on the same stream
+    # between two events (the GPU never waits for the host).
+    lins = [mdl.lin for mdl in wl.models]
     g0, g1 = Event(), Event()
     g0.record()
-    for _ in range(args.steps):
-        torch.ops.tvarant.linear_act(wl.x, w, bias, "silu", True)
+    for i in range(steps):
+        li = lins[i % len(lins)]
+        torch.ops.tvarant.linear_act(wl.x, li.weight, li.bias, "silu", True)
     g1.record()
     g1.synchronize()
-    kernel_ms = g0.elapsed_time(g1) / args.steps
+    kernel_ms = g0.elapsed_time(g1) / steps
     torch.tvarant.synchronize()
     _barrier(world)
     step_ms = _max_over_ranks(step_ms, world)
-
-    # end to end through the API with host buffers
-    for _ in range(max(1, args.warmup // 2)):
+    kernel_ms = _max_over_ranks(kernel_ms, world)
+    for _ in range(max(1, warmup // 2)):
         wl.step_e2e(torch)
     torch.tvarant.synchronize()
     _barrier(world)
     t0, t1 = Event(), Event()
     t0.record()
-    for _ in range(args.steps):
+    for _ in range(steps):
         wl.step_e2e(torch)
     t1.record()
     t1.synchronize()
-    e2e_ms = _max_over_ranks(t0.elapsed_time(t1) / args.steps, world)
-    status = torch.tvarant.get_status()
+    e2e_ms = _max_over_ranks(t0.elapsed_time(t1) / steps, world)
+    kernel, bound = gemm_kernel_name(m, mode)
+    gemm_bytes = 4.0 * (N_DEFAULT * K_DEFAULT + m * K_DEFAULT + m * N_DEFAULT + N_DEFAULT)
+    return {"wl": wl, "M": m, "mode": mode, "step_ms": step_ms, "kernel_ms": kernel_ms,
+            "e2e_ms": e2e_ms, "kernel": kernel, "bound": bound, "flops": wl.flops,
+            "gemm_bytes": gemm_bytes,
+            "step_tflops": wl.flops / (step_ms / 1e3) / 1e12,
+            "kernel_tflops": wl.flops / (kernel_ms / 1e3) / 1e12,
+            "kernel_gbs": gemm_bytes / (kernel_ms / 1e3) / 1e9}
 
+
+def _roofline(pt: dict, tf32_peak, peaks: dict) -> dict:
+    if pt["bound"] == "hbm":
+        hbm = peaks.get("hbm_gbs", 6650.0)
+        return {"bound": "hbm", "achieved": pt["kernel_gbs"], "peak": hbm, "unit": "GB/s",
+                "frac": pt["kernel_gbs"] / hbm,
+                "traffic": _traffic(f"gemm_{pt['mode']}_m{pt['M']}"),
+                "kernel": pt["kernel"], "kernel_ms": pt["kernel_ms"],
+                "algorithmic_bytes": pt["gemm_bytes"],
+                "peak_source": "MEASURED_PEAKS.json hbm_gbs"}
+    peak = tf32_peak if tf32_peak else peaks.get("bf16_tflops", 1590.0) / 2
+    if pt["mode"] == "3xtf32":
+        peak = peak / 3  # three TF32 MMAs per k-step
+    return {"bound": "tensor", "achieved": pt["kernel_tflops"], "peak": peak, "unit": "TFLOP/s",
+            "frac": pt["kernel_tflops"] / peak,
+            "traffic": _traffic(f"gemm_{pt['mode']}_m{pt['M']}"),
+            "kernel": pt["kernel"], "kernel_ms": pt["kernel_ms"],
+            "peak_source": ("cuBLAS TF32 8192^3 measured in this run" if tf32_peak
+                            else "half of the bf16 peak (no cuBLAS)")
+            + (" / 3 (3xTF32 issues three TF32 MMAs)" if pt["mode"] == "3xtf32" else ""),
+            "frac_of_bf16_measured": pt["kernel_tflops"] / peaks.get("bf16_tflops", 1617.5)}
+
+
+def run_gemm(args, rank, world, local_rank) -> dict | None:
+    torch = _device_setup(local_rank)
+    with ClockSampler(local_rank) as clocks:
+        pt = measure_gemm_point(torch, args.m, args.mode, args.steps, args.warmup, world, clocks)
+    wl = pt["wl"]
+    status = torch.tvarant.get_status()
     if rank != 0:
         return None
     peaks = _peaks()
     tf32_peak = tf32_peak_tflops(torch)
-    achieved = wl.flops / (kernel_ms / 1e3) / 1e12
-    peak = tf32_peak if tf32_peak else peaks.get("bf16_tflops", 1590.0) / 2
     line = {
         "metric": "fused-GEMM TFLOP/s (% peak); LLM-op GB/s (% HBM); tokens/s at 1/2/4/8 GPU",
-        "value": world * wl.flops / (step_ms / 1e3) / 1e12,
+        "value": world * wl.flops / (pt["step_ms"] / 1e3) / 1e12,
         "unit": "TFLOP/s",
         "n_gpus": world,
         "steps": args.steps,
         "warmup": args.warmup,
-        "ms_per_step": step_ms,
+        "ms_per_step": pt["step_ms"],
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": None,
@@ -411,19 +467,15 @@ def run_gemm(args, rank, world, local_rank) -> dict | None:
                         "+ JIT-fused abs(neg(exp(Y - Z))) chain, compiled by torch_tvarant.compiler",
             "M": args.m, "K": K_DEFAULT, "N": N_DEFAULT, "mode": args.mode,
             "parallelism": f"replicas x{world}",
-            "l2": "inputs (X 268 MB + Z 268 MB + W 67 MB) exceed the 126 MB L2",
+            "l2": ("inputs (X 268 MB + Z 268 MB + W 67 MB) exceed the 126 MB L2" if wl.copies == 1
+                   else f"steps rotate over {wl.copies} weight copies ({wl.copies * 67} MB > L2), "
+                        "so each step reads its weight from HBM"),
             "fusions": wl.fusions,
         },
-        "e2e": {"value": world * wl.flops / (e2e_ms / 1e3) / 1e12, "unit": "TFLOP/s",
+        "e2e": {"value": world * wl.flops / (pt["e2e_ms"] / 1e3) / 1e12, "unit": "TFLOP/s",
                 "h2d_bytes_per_step": wl.h2d_bytes, "d2h_bytes_per_step": wl.d2h_bytes,
-                "ms_per_step": e2e_ms},
-        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                     "frac": achieved / peak, "traffic": _traffic(f"gemm_tf32_m{args.m}"),
-                     "kernel": "tvr::tc::gemm_tc_kernel<256, tf32, K-major B>",
-                     "kernel_ms": kernel_ms,
-                     "peak_source": ("cuBLAS TF32 8192^3 measured in this run" if tf32_peak
-                                     else "half of the bf16 peak (no cuBLAS)"),
-                     "frac_of_bf16_measured": achieved / peaks.get("bf16_tflops", 1617.5)},
+                "ms_per_step": pt["e2e_ms"]},
+        "roofline": _roofline(pt, tf32_peak, peaks),
         "gpu_launches": args.steps * 2,
         "clocks": clocks.summary(),
         "device_status": status,
@@ -431,6 +483,55 @@ def run_gemm(args, rank, world, local_rank) -> dict | None:
     if not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline_gemm()
     return line
+
+
+SWEEP_M = (1, 16, 128, 1024, 4096, 16384)
+
+
+def run_sweep(args, rank, world, local_rank) -> dict | None:
+    """The whole fused-GEMM sweep: M in {1, 16, 128, 1024, 4096, 16384},
+    K = N = 4096, TF32 and 3xTF32, each point the compiled GEMM + chain."""
+    torch = _device_setup(local_rank)
+    points = []
+    with ClockSampler(local_rank) as clocks:
+        for mode in ("tf32", "3xtf32"):
+            for m in SWEEP_M:
+                pt = measure_gemm_point(torch, m, mode, args.steps, args.warmup, world, clocks)
+                pt.pop("wl")
+                points.append(pt)
+                torch.tvarant.empty_cache()
+    status = torch.tvarant.get_status()
+    if rank != 0:
+        return None
+    peaks = _peaks()
+    tf32_peak = tf32_peak_tflops(torch)
+    table = []
+    for pt in points:
+        rl = _roofline(pt, tf32_peak, peaks)
+        table.append({"M": pt["M"], "mode": pt["mode"], "step_ms": pt["step_ms"],
+                      "step_tflops": pt["step_tflops"], "kernel_ms": pt["kernel_ms"],
+                      "kernel": pt["kernel"], "bound": rl["bound"], "achieved": rl["achieved"],
+                      "unit": rl["unit"], "frac": rl["frac"],
+                      "e2e_tflops": pt["flops"] / (pt["e2e_ms"] / 1e3) / 1e12})
+    head = next(p for p in points if p["M"] == SWEEP_M[-1] and p["mode"] == "tf32")
+    return {
+        "metric": "fused-GEMM TFLOP/s (% peak); LLM-op GB/s (% HBM); tokens/s at 1/2/4/8 GPU",
+        "value": world * head["step_tflops"], "unit": "TFLOP/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": head["step_ms"],
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "tf32 and f32 (3xTF32)",
+        "data": "synthetic (seeded N(0,1) activations, U(-1/64,1/64) weights)",
+        "config": {"workload": "fused-GEMM sweep: linear+bias+SiLU M in {1,16,128,1024,4096,16384} "
+                               "K=N=4096 + JIT-fused abs(neg(exp(Y - Z))), TF32 and 3xTF32; "
+                               "value = the M=16384 TF32 point",
+                   "points": table, "parallelism": f"replicas x{world}",
+                   "l2": "points whose operands fit in L2 rotate over weight copies in distinct "
+                         "buffers (> 256 MB in total), so each step reads its weight from HBM"},
+        "roofline": _roofline(head, tf32_peak, peaks),
+        "gpu_launches": 2 * args.steps * len(points) * 2,
+        "clocks": clocks.summary(),
+        "device_status": status,
+    }
 
 
 def run_reference(args, rank, world) -> dict | None:
@@ -487,7 +588,8 @@ def _main() -> int:
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["tvarant", "reference"], default="tvarant")
-    ap.add_argument("--workload", choices=["gemm", "llm-ops", "mlp", "bmm", "gpt2"], default="gemm")
+    ap.add_argument("--workload", choices=["gemm", "sweep", "llm-ops", "mlp", "bmm", "gpt2"],
+                    default="gemm")
     ap.add_argument("--batch", type=int, default=256, help="bmm workload: batch size")
     ap.add_argument("--m", type=int, default=M_DEFAULT)
     ap.add_argument("--mode", choices=["tf32", "3xtf32"], default="tf32")
@@ -507,6 +609,8 @@ def _main() -> int:
         _dist_init(world)
         if args.workload == "gemm":
             line = run_gemm(args, rank, world, local_rank)
+        elif args.workload == "sweep":
+            line = run_sweep(args, rank, world, local_rank)
         else:
             from tvarant_b200 import workloads
 
