@@ -195,6 +195,18 @@ int tvr_gemm_bias_act_noalloc(const float* a, const float* b, const float* bias,
                               int64_t lda, int64_t ldb, int64_t ldc,
                               float alpha, float beta, int act, int trans_b, void* stream);
 
+/* Gated (SwiGLU) projection: out[m, n] = silu(x . Wg^T) * (x . Wu^T), with x
+ * [m, k] (row stride ldx) and both weights in nn.Linear layout [n, k] (row
+ * strides ldw_gate, ldw_up).  No reference counterpart as one call: the
+ * reference computes it as linear_act(x, Wg, None, "silu") * linear(x, Wu)
+ * (csrc/aten/CustomOps.cpp:14-39, csrc/aten/LlmOps.cpp:150-174, Ops.cpp:312-327),
+ * three kernels and two [m, n] round trips.  TVR_GEMM_TF32 runs one tcgen05
+ * pass whose epilogue forms the product; the other modes run that composition
+ * on the device. */
+int tvr_gemm_swiglu(const float* x, const float* w_gate, const float* w_up, float* out,
+                    int64_t m, int64_t n, int64_t k, int64_t ldx, int64_t ldw_gate,
+                    int64_t ldw_up, int64_t ldo, int mode, void* stream);
+
 /* Batched C[i] = A[i] * op(B[i]) for i < batch, each as tvr_gemm_bias_act
  * with alpha 1, beta 0, no activation; matrices are dense row-major with the
  * given element strides between batch entries (stride_b may be 0 to

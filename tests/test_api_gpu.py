@@ -401,3 +401,39 @@ def test_dtype_copies():
 
 def test_status_clean():
     assert torch.tvarant.get_status() == 0
+
+
+@pytest.mark.parametrize("precision,tol", [("high", 5e-3), ("highest", 1e-5)])
+def test_linear_swiglu_op_and_compiled_llama_mlp(tvarant, precision, tol):
+    """tvarant::linear_swiglu and a compiled gate/up/down MLP against PyTorch on the CPU."""
+    torch.set_float32_matmul_precision(precision)
+    try:
+        g = torch.Generator().manual_seed(4)
+        x = torch.randn(3, 100, 256, generator=g)
+        wg = 0.05 * torch.randn(384, 256, generator=g)
+        wu = 0.05 * torch.randn(384, 256, generator=g)
+        want = torch.nn.functional.silu(x @ wg.T) * (x @ wu.T)
+        got = torch.ops.tvarant.linear_swiglu(x.to("tvarant"), wg.to("tvarant"), wu.to("tvarant")).cpu()
+        assert got.shape == want.shape
+        assert (got - want).norm() / want.norm() <= tol
+
+        class MLP(torch.nn.Module):
+            def __init__(self):
+                super().__init__()
+                self.gate = torch.nn.Linear(256, 384, bias=False)
+                self.up = torch.nn.Linear(256, 384, bias=False)
+                self.down = torch.nn.Linear(384, 256, bias=False)
+
+            def forward(self, h):
+                return self.down(torch.nn.functional.silu(self.gate(h)) * self.up(h))
+
+        torch.manual_seed(5)
+        mlp = MLP()
+        with torch.no_grad():
+            want = mlp(x)
+            compiled = tvarant.compiler.compile(mlp.to("tvarant"))
+            assert tvarant.compiler.last_log.get("swiglu") == 1
+            got = compiled(x.to("tvarant")).cpu()
+        assert (got - want).norm() / want.norm() <= tol
+    finally:
+        torch.set_float32_matmul_precision("highest")

@@ -207,6 +207,35 @@ def test_gemm_few_rows_strided(lib, rng, mode, tol):
     assert np.all(y[:, n:] == 7.0)
 
 
+@pytest.mark.parametrize("m,n,k,pad", [
+    (300, 1000, 512, 0),    # one fused tcgen05 pass, ragged tiles
+    (257, 1376, 1024, 0),   # the 8-way tensor-parallel shard of d_ff 11008
+    (513, 264, 260, 8),     # K not a multiple of the k-block; output with a row stride
+    (64, 512, 256, 0),      # few rows: composed from the few-row GEMMs
+    (96, 200, 64, 4),
+])
+@pytest.mark.parametrize("mode,tol", [(1, TOL_TF32), (2, TOL_3XTF32), (3, None)])
+def test_gemm_swiglu(lib, rng, m, n, k, pad, mode, tol):
+    """silu(x Wg^T) * (x Wu^T) against the reference's composition of its ops."""
+    x = rng.standard_normal((m, k), dtype=np.float32)
+    wg = rng.uniform(-1 / np.sqrt(k), 1 / np.sqrt(k), (n, k)).astype(np.float32)
+    wu = rng.uniform(-1 / np.sqrt(k), 1 / np.sqrt(k), (n, k)).astype(np.float32)
+    ldo = n + pad
+    dx, dwg, dwu = _dev(x), _dev(wg), _dev(wu)
+    dout = _dev(np.full((m, ldo), 7.0, np.float32))
+    lib.call("tvr_gemm_swiglu", _p(dx), _p(dwg), _p(dwu), _p(dout), m, n, k, k, k, k, ldo, mode,
+             _stream())
+    got = _host(dout)
+    ref = oracle.binary(1, oracle.gemm_bias_act(x, wg, None, beta=0.0, act=2),
+                        oracle.gemm_bias_act(x, wu, None, beta=0.0))
+    if tol is None:  # FP32 mode: exact GEMMs; expf may differ by an ulp between CUDA and glibc
+        assert max_rel(got[:, :n], ref, 1e-6) <= 1e-6
+    else:
+        assert rel_frobenius(got[:, :n], ref) <= tol, rel_frobenius(got[:, :n], ref)
+    assert np.all(got[:, n:] == 7.0)
+    _status_ok(lib)
+
+
 def test_gemm_known_answer(lib):
     """[[1,2],[3,4]] @ [[5,6],[7,8]] = [[19,22],[43,50]] (reference tests/test_ops.py:40-46)."""
     a = np.array([[1, 2], [3, 4]], np.float32)

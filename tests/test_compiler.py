@@ -117,10 +117,13 @@ class SwiGLU(nn.Module):
         return F.silu(self.w1(x)) * self.w2(x)
 
 
-def test_swiglu_fuses_gate_epilogue_only():
+def test_swiglu_gate_and_up_become_one_gemm():
+    """The reference's SwiGLU-like test model (tests/test_compiler.py:51-66): the silu
+    epilogue fuses first, then the gated product becomes one linear_swiglu."""
     gm = compile_fx(trace_module(SwiGLU()))
     assert last_log["gemm_epilogue"] == 1
-    assert torch.ops.tvarant.linear_act in _targets(gm)
+    assert last_log["swiglu"] == 1
+    assert _targets(gm) == [torch.ops.tvarant.linear_swiglu]
 
 
 class Consts(nn.Module):
@@ -158,3 +161,43 @@ def test_gemm_pass_then_pointwise_pass_keep_graph_valid():
     gm = fuse_gemm_epilogue(trace_module(SwiGLU()))
     gm = fuse_pointwise(gm)
     gm.graph.lint()
+
+
+class _GatedMLP(torch.nn.Module):
+    def __init__(self, d=16, f=24, up_bias=False):
+        super().__init__()
+        self.gate = torch.nn.Linear(d, f, bias=False)
+        self.up = torch.nn.Linear(d, f, bias=up_bias)
+        self.down = torch.nn.Linear(f, d, bias=False)
+
+    def forward(self, x):
+        return self.down(torch.nn.functional.silu(self.gate(x)) * self.up(x))
+
+
+def _targets(gm):
+    return [n.target for n in gm.graph.nodes if n.op == "call_function"]
+
+
+def test_swiglu_fusion_rewrites_gated_projection():
+    """gate / up / down (Llama MLP): the gated projection becomes one linear_swiglu."""
+    gm = compile_fx(trace_module(_GatedMLP()))
+    targets = _targets(gm)
+    assert torch.ops.tvarant.linear_swiglu in targets
+    assert last_log["swiglu"] == 1
+    assert last_log["gemm_epilogue"] == 1
+    assert not any(n.target in (torch.mul, operator.mul) for n in gm.graph.nodes)
+
+
+def test_swiglu_fusion_needs_bias_free_projections():
+    gm = compile_fx(trace_module(_GatedMLP(up_bias=True)))
+    assert torch.ops.tvarant.linear_swiglu not in _targets(gm)
+    assert "swiglu" not in last_log
+
+
+def test_swiglu_fusion_operand_order():
+    class Swapped(_GatedMLP):
+        def forward(self, x):
+            return self.down(self.up(x) * torch.nn.functional.silu(self.gate(x)))
+
+    gm = compile_fx(trace_module(Swapped()))
+    assert torch.ops.tvarant.linear_swiglu in _targets(gm)

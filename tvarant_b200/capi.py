@@ -98,6 +98,7 @@ SIGNATURES: dict[str, list] = {
                           _i32, _i32, _i32, _vp],
     "tvr_gemm_bias_act_noalloc": [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _f32,
                                   _f32, _i32, _i32, _vp],
+    "tvr_gemm_swiglu": [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i32, _vp],
     "tvr_bmm": [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i32, _i32, _vp],
     "tvr_softmax": [_vp, _vp, _i64, _i64, _i64, _vp],
     "tvr_layer_norm": [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _f32, _vp],

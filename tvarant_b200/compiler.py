@@ -15,6 +15,9 @@ Passes:
   followed by ``relu`` / ``silu`` becomes one ``tvarant.linear_act`` — a single
   tcgen05 GEMM with bias and activation in its epilogue
   (reference compiler.py:136-202);
+* ``fuse_swiglu``: ``linear_act(x, Wg, None, "silu") * linear(x, Wu)`` becomes
+  one ``tvarant.linear_swiglu`` (gate and up in one GEMM, the product formed
+  in its epilogue); not a reference pass;
 * ``fuse_pointwise``: a connected group of elementwise nodes whose every
   user is inside the group becomes one ``tvarant.pointwise`` SSA program,
   compiled by NVRTC (reference compiler.py:205-322).  Besides the
@@ -156,6 +159,59 @@ def fuse_gemm_epilogue(gm: torch.fx.GraphModule) -> torch.fx.GraphModule:
     return gm
 
 
+def _projection(node: object, act: str) -> Optional[tuple[object, object]]:
+    """(x, weight) if ``node`` is a bias-free nn.Linear-layout projection with
+    activation ``act`` whose only user is the node being fused."""
+    if not isinstance(node, torch.fx.Node) or len(node.users) != 1:
+        return None
+    if node.op == "call_function" and node.target is torch.ops.tvarant.linear_act:
+        x, w, bias, a, trans_b = (list(node.args) + [False])[:5]
+        if bias is None and a == act and trans_b:
+            return x, w
+        return None
+    if act == "none" and op_name(node) == "linear" and len(node.args) >= 2:
+        bias = node.args[2] if len(node.args) > 2 else node.kwargs.get("bias")
+        if bias is None:
+            return node.args[0], node.args[1]
+    return None
+
+
+def fuse_swiglu(gm: torch.fx.GraphModule) -> torch.fx.GraphModule:
+    """Rewrites ``linear_act(x, Wg, None, "silu", True) * linear(x, Wu)`` (the
+    gated projection of a SwiGLU MLP, in either operand order) into one
+    ``tvarant.linear_swiglu(x, Wg, Wu)``: one GEMM instead of three kernels and
+    two round trips of the [tokens, d_ff] activations.  Runs after
+    ``fuse_gemm_epilogue``; records ``last_log["swiglu"]`` when it fuses."""
+    graph = gm.graph
+    fused = 0
+    for node in list(graph.nodes):
+        if node.op not in ("call_function", "call_method") or op_name(node) not in ("mul", "mul_"):
+            continue
+        if len(node.args) != 2 or node.kwargs:
+            continue
+        for gate_node, up_node in ((node.args[0], node.args[1]), (node.args[1], node.args[0])):
+            gate = _projection(gate_node, "silu")
+            up = _projection(up_node, "none")
+            if gate is None or up is None or gate[0] is not up[0] or gate_node is up_node:
+                continue
+            with graph.inserting_before(node):
+                new = graph.call_function(torch.ops.tvarant.linear_swiglu,
+                                          args=(gate[0], gate[1], up[1]))
+            node.replace_all_uses_with(new)
+            graph.erase_node(node)
+            graph.erase_node(gate_node)
+            graph.erase_node(up_node)
+            fused += 1
+            break
+    graph.lint()
+    gm.recompile()
+    if fused:
+        last_log["swiglu"] = fused
+    else:
+        last_log.pop("swiglu", None)
+    return gm
+
+
 def _pointwise_kind(node: object) -> Optional[tuple[str, int]]:
     """("unary" | "binary" | "scalar", opcode) for fusable elementwise nodes."""
     if not isinstance(node, torch.fx.Node) or node.op not in ("call_function", "call_method"):
@@ -277,9 +333,10 @@ def _build_program(order, members):
 
 
 def compile_fx(gm: torch.fx.GraphModule, example_inputs: Any = None) -> torch.fx.GraphModule:
-    """GEMM-epilogue fusion, then pointwise fusion, in place."""
+    """GEMM-epilogue fusion, SwiGLU fusion, then pointwise fusion, in place."""
     _ = example_inputs
     gm = fuse_gemm_epilogue(gm)
+    gm = fuse_swiglu(gm)
     gm = fuse_pointwise(gm)
     return gm
 

@@ -1,4 +1,5 @@
-// The tvarant operator library: tvarant::linear_act and tvarant::pointwise.
+// The tvarant operator library: tvarant::linear_act, tvarant::pointwise and
+// tvarant::linear_swiglu.
 //
 // Schemas are the reference's, verbatim (csrc/aten/CustomOps.cpp:101-106),
 // so graphs produced by torch_tvarant.compiler run unchanged.  linear_act
@@ -48,6 +49,39 @@ at::Tensor linear_act(const at::Tensor& x, const at::Tensor& weight,
   auto out_sizes = xc.sizes().vec();
   out_sizes.back() = y2.size(1);
   return y2.reshape(out_sizes);
+}
+
+// silu(x . w_gate^T) * (x . w_up^T): the gated projection of a SwiGLU MLP as
+// one GEMM (tvr_gemm_swiglu).  Weights are [N, K] (nn.Linear layout).  Not a
+// reference op: the reference spells it linear_act(x, w_gate, None, "silu",
+// True) * linear(x, w_up), which torch_tvarant.compiler rewrites into this.
+at::Tensor linear_swiglu(const at::Tensor& x, const at::Tensor& w_gate, const at::Tensor& w_up) {
+  check_fp32(x, "linear_swiglu");
+  check_fp32(w_gate, "linear_swiglu");
+  check_fp32(w_up, "linear_swiglu");
+  TORCH_CHECK(x.dim() >= 1 && w_gate.dim() == 2 && w_up.dim() == 2,
+              "linear_swiglu: expected x [..., K] and weights [N, K]");
+  TORCH_CHECK(w_gate.sizes() == w_up.sizes(), "linear_swiglu: gate and up weights differ in shape (",
+              w_gate.sizes(), " vs ", w_up.sizes(), ")");
+  const int64_t k = x.size(-1);
+  TORCH_CHECK(w_gate.size(1) == k, "linear_swiglu: x has ", k, " features, weights expect ",
+              w_gate.size(1));
+  TORCH_CHECK(x.device() == w_gate.device() && x.device() == w_up.device(),
+              "linear_swiglu: operands on different devices");
+  c10::DeviceGuard guard(x.device());
+  at::Tensor xc = x.is_contiguous() ? x : contiguous_copy(x);
+  at::Tensor wg = w_gate.stride(1) == 1 ? w_gate : contiguous_copy(w_gate);
+  at::Tensor wu = w_up.stride(1) == 1 ? w_up : contiguous_copy(w_up);
+  const int64_t n = wg.size(0);
+  const int64_t m = k > 0 ? xc.numel() / k : 0;
+  auto out_sizes = xc.sizes().vec();
+  out_sizes.back() = n;
+  at::Tensor out = empty_device(out_sizes, xc.options());
+  if (m == 0 || n == 0) return out;
+  TVR_TRY(tvr_gemm_swiglu(xc.data_ptr<float>(), wg.data_ptr<float>(), wu.data_ptr<float>(),
+                          out.data_ptr<float>(), m, n, k, k, wg.stride(0), wu.stride(0), n,
+                          gemm_mode(), current_stream_handle()));
+  return out;
 }
 
 at::Tensor pointwise(at::TensorList inputs, at::IntArrayRef ops, at::IntArrayRef a,
@@ -109,9 +143,11 @@ TORCH_LIBRARY(tvarant, m) {
       "pointwise(Tensor[] inputs, int[] ops, int[] a, int[] b, int[] input_ids, float[] alphas, "
       "float[] consts) -> Tensor");
   m.def("all_reduce_(Tensor(a!) self, int comm) -> Tensor(a!)");
+  m.def("linear_swiglu(Tensor x, Tensor w_gate, Tensor w_up) -> Tensor");
 }
 
 TORCH_LIBRARY_IMPL(tvarant, PrivateUse1, m) {
   m.impl("linear_act", TORCH_FN(tvarant::ops::linear_act));
   m.impl("pointwise", TORCH_FN(tvarant::ops::pointwise));
+  m.impl("linear_swiglu", TORCH_FN(tvarant::ops::linear_swiglu));
 }

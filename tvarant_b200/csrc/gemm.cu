@@ -87,6 +87,50 @@ int tvr_gemm_bias_act(const float* a, const float* b, const float* bias, float* 
              mode, as_stream(stream));
 }
 
+int tvr_gemm_swiglu(const float* x, const float* w_gate, const float* w_up, float* out,
+                    int64_t m, int64_t n, int64_t k, int64_t ldx, int64_t ldw_gate,
+                    int64_t ldw_up, int64_t ldo, int mode, void* stream) {
+  TVR_CHECK(m >= 0 && n >= 0 && k >= 0, "gemm_swiglu: negative size (%lld, %lld, %lld)",
+            (long long)m, (long long)n, (long long)k);
+  if (m == 0 || n == 0) return TVR_OK;
+  TVR_CHECK(out != nullptr, "gemm_swiglu: null output");
+  TVR_CHECK(k == 0 || (x != nullptr && w_gate != nullptr && w_up != nullptr),
+            "gemm_swiglu: null operand");
+  TVR_CHECK(ldx >= k && ldw_gate >= k && ldw_up >= k && ldo >= n,
+            "gemm_swiglu: leading dimension too small");
+  mode = resolve_mode(mode);
+  TVR_CHECK(mode == TVR_GEMM_TF32 || mode == TVR_GEMM_3XTF32 || mode == TVR_GEMM_FP32,
+            "gemm_swiglu: unknown precision mode %d", mode);
+  cudaStream_t s = as_stream(stream);
+  if (mode == TVR_GEMM_TF32 && m > 128 && k > 0) {
+    const int rc = gemm_tcgen05_swiglu(x, w_gate, w_up, out, m, n, k, ldx, ldw_gate, ldw_up, ldo, s);
+    if (rc != TVR_ERR_UNSUPPORTED) return rc;
+  }
+  // Composition: gate (with SiLU) and up into scratch, then their product
+  // into out (through a third scratch block when out has a row stride).
+  const bool dense_out = ldo == n;
+  Scratch scratch;
+  const size_t mn = static_cast<size_t>(m * n);
+  int rc = scratch.alloc((dense_out ? 2 : 3) * mn * sizeof(float), current_device(), s);
+  if (rc != TVR_OK) return rc;
+  float* g = static_cast<float*>(scratch.ptr);
+  float* u = g + mn;
+  if ((rc = tvr_gemm_bias_act(x, w_gate, nullptr, g, m, n, k, ldx, ldw_gate, n, 1.f, 0.f,
+                              TVR_ACT_SILU, 1, mode, stream)) != TVR_OK)
+    return rc;
+  if ((rc = tvr_gemm_bias_act(x, w_up, nullptr, u, m, n, k, ldx, ldw_up, n, 1.f, 0.f,
+                              TVR_ACT_NONE, 1, mode, stream)) != TVR_OK)
+    return rc;
+  const int64_t sizes[2] = {m, n};
+  const int64_t dense[2] = {n, 1};
+  const int64_t strided[2] = {ldo, 1};
+  float* prod = dense_out ? out : u + mn;
+  if ((rc = tvr_binary(TVR_BINARY_MUL, g, u, prod, 2, sizes, dense, dense, 1.f, stream)) != TVR_OK)
+    return rc;
+  if (dense_out) return TVR_OK;
+  return tvr_strided_copy(out, prod, 4, 2, sizes, strided, dense, stream);
+}
+
 int tvr_bmm(const float* a, const float* b, float* c, int64_t batch, int64_t m, int64_t n,
             int64_t k, int64_t stride_a, int64_t stride_b, int64_t stride_c, int trans_b,
             int mode, void* stream) {

@@ -65,6 +65,12 @@ int gemm_ws(const float* x, const float* w, const float* bias, float* c, int64_t
             int64_t k, int64_t ldx, int64_t ldw, int64_t ldc, float alpha, float beta, int act,
             bool split3, cudaStream_t stream);
 
+// silu(x . Wg^T) * (x . Wu^T) in one TF32 tcgen05 pass (K-major weights);
+// TVR_ERR_UNSUPPORTED when the operands cannot be described by TMA maps.
+int gemm_tcgen05_swiglu(const float* x, const float* wg, const float* wu, float* out, int64_t m,
+                        int64_t n, int64_t k, int64_t ldx, int64_t ldwg, int64_t ldwu,
+                        int64_t ldo, cudaStream_t stream);
+
 // Returns TVR_ERR_UNSUPPORTED (without recording an error) when the
 // operands cannot be described by TMA tensor maps; the caller then uses
 // gemm_simt.

@@ -65,7 +65,7 @@ struct Params {
   CUtensorMap tma_a;     // A or A_hi: dims {K, M, batch}
   CUtensorMap tma_b;     // B or B_hi: {K, N, batch} (K-major) or {N, K, batch} (N-major)
   CUtensorMap tma_a_lo;  // 3xTF32 low parts, same geometry
-  CUtensorMap tma_b_lo;
+  CUtensorMap tma_b_lo;  // or, for a gated GEMM, the up-projection weight {K, N, 1}
   const float* bias;
   float* c;
   int64_t ldc;
@@ -117,9 +117,15 @@ __device__ __forceinline__ void decode_unit(const Params& p, int u, int& b, int&
   tn = rr / gm;
 }
 
-template <int BN, bool SPLIT3, bool B_NMAJOR>
+// GATED (TF32, K-major weights, BN = 256): the B tile stacks 128 rows of the
+// gate weight (tma_b) over the same 128 rows of the up weight (tma_b_lo), the
+// MMA fills accumulator columns 0..127 with x.Wg^T and 128..255 with x.Wu^T,
+// and the epilogue writes silu(gate) * up: a 128 x 128 output tile.
+template <int BN, bool SPLIT3, bool B_NMAJOR, bool GATED = false>
 __global__ void __launch_bounds__(NUM_THREADS, 1) gemm_tc_kernel(const __grid_constant__ Params p) {
   using Cf = Cfg<BN, SPLIT3>;
+  static_assert(!GATED || (BN == 256 && !SPLIT3 && !B_NMAJOR), "gated GEMM shape");
+  constexpr int OUT_BN = GATED ? BN / 2 : BN;  // output columns per tile
   constexpr int STAGES = Cf::STAGES;
   extern __shared__ uint8_t smem_raw[];
   __shared__ int s_abort;
@@ -190,7 +196,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) gemm_tc_kernel(const __grid_co
           const uint32_t sb = sa + Cf::A_BYTES;
           const int kx = kb * BK;
           tma_load_3d(sa, &p.tma_a, fb, kx, tm * BM, b);
-          if (B_NMAJOR) {
+          if (GATED) {
+            tma_load_3d(sb, &p.tma_b, fb, kx, tn * OUT_BN, zb);
+            tma_load_3d(sb + OUT_BN * BK * 4, &p.tma_b_lo, fb, kx, tn * OUT_BN, zb);
+          } else if (B_NMAJOR) {
 #pragma unroll
             for (int j = 0; j < BN / 32; ++j)
               tma_load_3d(sb + j * (BK * 128), &p.tma_b, fb, tn * BN + 32 * j, kx, zb);
@@ -313,8 +322,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) gemm_tc_kernel(const __grid_co
     const int q = warp & 3;
     const int ew = warp - 2;
     const int half = ew >> 2;
-    constexpr int HC = BN / 2;      // columns per warp
+    constexpr int HC = OUT_BN / 2;  // output columns per warp
     constexpr int CH = HC / 32;     // 32-column chunks per warp
+    constexpr uint32_t UP = BN / 2;  // gated: TMEM column offset of the up half
     const uint32_t sbuf = epi0 + ew * EPI_BUF_BYTES;
     int acc = 0;
     uint32_t acc_phase = 0;
@@ -336,10 +346,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) gemm_tc_kernel(const __grid_co
       const bool finish = p.splits == 1;
       // chunk c+1 is read from TMEM while chunk c is transposed and stored
       float v[32];
+      float up[GATED ? 32 : 1];
       tmem_load_32_async(tcol, v);
+      if constexpr (GATED) tmem_load_32_async(tcol + UP, up);
       tmem_wait_loads();
-      const bool plain = p.alpha == 1.f && p.act == TVR_ACT_NONE &&
-                         (p.beta == 0.f || (p.bias == nullptr && !p.use_prev));
+      if constexpr (GATED) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = act_fixed<TVR_ACT_SILU>(v[i]) * up[i];
+      }
+      const bool plain = GATED || (p.alpha == 1.f && p.act == TVR_ACT_NONE &&
+                                   (p.beta == 0.f || (p.bias == nullptr && !p.use_prev)));
 #pragma unroll
       for (int c = 0; c < CH; ++c) {
         if (c == CH - 1) {
@@ -356,10 +372,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) gemm_tc_kernel(const __grid_co
                        "f"(v[4 * j + 1]), "f"(v[4 * j + 2]), "f"(v[4 * j + 3])
                        : "memory");
         }
-        if (c + 1 < CH) tmem_load_32_async(tcol + 32 * (c + 1), v);
+        if (c + 1 < CH) {
+          tmem_load_32_async(tcol + 32 * (c + 1), v);
+          if constexpr (GATED) tmem_load_32_async(tcol + UP + 32 * (c + 1), up);
+        }
         __syncwarp();
         const int jj = lane & 7;
-        const int col = tn * BN + half * HC + 32 * c + 4 * jj;
+        const int col = tn * OUT_BN + half * HC + 32 * c + 4 * jj;
         float4 bias4 = make_float4(0.f, 0.f, 0.f, 0.f);
         if (finish && p.bias != nullptr) {
           if (p.c_vec && col + 3 < p.n) {
@@ -434,7 +453,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) gemm_tc_kernel(const __grid_co
             if (col + 3 < p.n) dst[3] = xs[i].w;
           }
         }
-        if (c + 1 < CH) tmem_wait_loads();
+        if (c + 1 < CH) {
+          tmem_wait_loads();
+          if constexpr (GATED) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] = act_fixed<TVR_ACT_SILU>(v[i]) * up[i];
+          }
+        }
         __syncwarp();  // the staging buffer is rewritten by the next chunk
       }
       acc ^= 1;
@@ -525,18 +550,18 @@ __global__ void __launch_bounds__(256) splitk_reduce_kernel(
 // ---- host side -----------------------------------------------------------------
 
 
-template <int BN, bool SPLIT3, bool B_NMAJOR>
+template <int BN, bool SPLIT3, bool B_NMAJOR, bool GATED = false>
 int launch_kernel(const Params& p, int grid, cudaStream_t stream, int dev) {
   using Cf = Cfg<BN, SPLIT3>;
   static std::once_flag once[64];
   static cudaError_t attr_err[64];
   std::call_once(once[dev & 63], [&]() {
-    attr_err[dev & 63] = cudaFuncSetAttribute(gemm_tc_kernel<BN, SPLIT3, B_NMAJOR>,
+    attr_err[dev & 63] = cudaFuncSetAttribute(gemm_tc_kernel<BN, SPLIT3, B_NMAJOR, GATED>,
                                               cudaFuncAttributeMaxDynamicSharedMemorySize,
                                               Cf::SMEM_BYTES);
   });
   TVR_CUDA_TRY(attr_err[dev & 63]);
-  gemm_tc_kernel<BN, SPLIT3, B_NMAJOR><<<grid, NUM_THREADS, Cf::SMEM_BYTES, stream>>>(p);
+  gemm_tc_kernel<BN, SPLIT3, B_NMAJOR, GATED><<<grid, NUM_THREADS, Cf::SMEM_BYTES, stream>>>(p);
   TVR_LAUNCH_CHECK();
   return TVR_OK;
 }
@@ -721,6 +746,59 @@ int gemm_tcgen05(const float* a, const float* b, const float* bias, float* c, in
     TVR_LAUNCH_CHECK();
   }
   return TVR_OK;
+}
+
+}  // namespace tvr
+
+// ---- gated (SwiGLU) GEMM ----------------------------------------------------------
+
+namespace tvr {
+
+// out[m, n] = silu(x . Wg^T) * (x . Wu^T) in one TF32 tcgen05 pass: each
+// 128 x 256 accumulator tile holds 128 gate and the matching 128 up columns.
+// Returns TVR_ERR_UNSUPPORTED when the operands cannot be described by TMA maps.
+int gemm_tcgen05_swiglu(const float* x, const float* wg, const float* wu, float* out, int64_t m,
+                        int64_t n, int64_t k, int64_t ldx, int64_t ldwg, int64_t ldwu,
+                        int64_t ldo, cudaStream_t stream) {
+  using namespace tc;
+  if (!al16(x) || !al16(wg) || !al16(wu) || ldx % 4 != 0 || ldwg % 4 != 0 || ldwu % 4 != 0 ||
+      k < 1 || m > 0x7fffff00 || n > 0x7fffff00 || k > 0x7fffff00) {
+    return TVR_ERR_UNSUPPORTED;
+  }
+  const int dev = current_device();
+  const int sms = sm_count(dev);
+  constexpr int kOutBn = 128;
+  Params p;
+  memset(&p, 0, sizeof(p));
+  int rc;
+  if ((rc = encode_3d(&p.tma_a, x, k, m, 1, ldx * 4, m * ldx * 4, BK, BM)) != TVR_OK) return rc;
+  if ((rc = encode_3d(&p.tma_b, wg, k, n, 1, ldwg * 4, n * ldwg * 4, BK, kOutBn)) != TVR_OK) return rc;
+  if ((rc = encode_3d(&p.tma_b_lo, wu, k, n, 1, ldwu * 4, n * ldwu * 4, BK, kOutBn)) != TVR_OK)
+    return rc;
+  p.bias = nullptr;
+  p.c = out;
+  p.ldc = ldo;
+  p.stride_c = m * ldo;
+  p.alpha = 1.f;
+  p.beta = 0.f;
+  p.act = TVR_ACT_NONE;
+  p.use_prev = 0;
+  p.c_vec = (al16(out) && ldo % 4 == 0) ? 1 : 0;
+  p.m = static_cast<int>(m);
+  p.n = static_cast<int>(n);
+  p.k = static_cast<int>(k);
+  p.batch = 1;
+  p.tiles_m = static_cast<int>(ceil_div(m, BM));
+  p.tiles_n = static_cast<int>(ceil_div(n, kOutBn));
+  p.splits = 1;
+  p.num_kb = static_cast<int>(ceil_div(k, BK));
+  p.kb_per_split = p.num_kb;
+  const int64_t units = static_cast<int64_t>(p.tiles_m) * p.tiles_n;
+  if (units > 0x7fffffff) return TVR_ERR_UNSUPPORTED;
+  p.total_units = static_cast<int>(units);
+  p.status = device_status_ptr(dev);
+  const int grid = static_cast<int>(std::min<int64_t>(units, sms));
+  return launch_kernel<256, false, false, true>(p, grid, stream, dev);
 }
 
 }  // namespace tvr

@@ -96,10 +96,10 @@ def on_stream(stream: torch.Stream):
 
 def mlp_layer(x: torch.Tensor, w_gate: torch.Tensor, w_up: torch.Tensor,
               w_down: torch.Tensor) -> torch.Tensor:
-    """``(silu(x W_g^T) * (x W_u^T)) W_d^T`` on this rank's shards (no reduce)."""
-    g = torch.ops.tvarant.linear_act(x, w_gate, None, "silu", True)
-    u = torch.ops.tvarant.linear_act(x, w_up, None, "none", True)
-    return torch.ops.tvarant.linear_act(g * u, w_down, None, "none", True)
+    """``(silu(x W_g^T) * (x W_u^T)) W_d^T`` on this rank's shards (no reduce):
+    the gated projection as one SwiGLU GEMM, then the down projection."""
+    h = torch.ops.tvarant.linear_swiglu(x, w_gate, w_up)
+    return torch.ops.tvarant.linear_act(h, w_down, None, "none", True)
 
 
 class TPMLPStack:
