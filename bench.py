@@ -597,6 +597,9 @@ def _main() -> int:
     ap.add_argument("--layers", type=int, default=32, help="mlp workload: MLP layers")
     ap.add_argument("--seq", type=int, default=1024, help="gpt2 workload: sequence length")
     ap.add_argument("--gpt2-batch", type=int, default=8, help="gpt2 workload: sequences per step (whole job)")
+    ap.add_argument("--attention", choices=["bmm", "sdpa"], default="bmm",
+                    help="gpt2 workload: bmm + mask + softmax + bmm (the config), or the fused "
+                         "F.scaled_dot_product_attention kernel")
     ap.add_argument("--chunks", type=int, default=2, help="mlp workload: token chunks overlapped with the all-reduce")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()

@@ -207,6 +207,22 @@ int tvr_gemm_swiglu(const float* x, const float* w_gate, const float* w_up, floa
                     int64_t m, int64_t n, int64_t k, int64_t ldx, int64_t ldw_gate,
                     int64_t ldw_up, int64_t ldo, int mode, void* stream);
 
+/* Fused attention forward: out = softmax(scale * Q K^T + causal mask) V for
+ * Q [batch, heads, seq_q, head_dim], K and V [batch, heads, seq_k, head_dim],
+ * each given by its element strides over (batch, head, position) with a
+ * contiguous last dimension; out has its own strides; lse (optional, may be
+ * NULL) receives the natural-log log-sum-exp per (batch, head, query) as
+ * [batch, heads, seq_q].  causal != 0 hides key j from query i when j > i
+ * (PyTorch's is_causal).  The kernel computes in TF32 with head_dim 64;
+ * other head dimensions and modes return TVR_ERR_UNSUPPORTED (the caller
+ * then composes bmm / softmax / bmm).  No reference counterpart: the
+ * reference materialises the scores (csrc/aten/LlmOps.cpp:68-148). */
+int tvr_attention_fwd(const float* q, const float* k, const float* v, float* out, float* lse,
+                      int64_t batch, int64_t heads, int64_t seq_q, int64_t seq_k,
+                      int64_t head_dim, const int64_t* q_strides, const int64_t* k_strides,
+                      const int64_t* v_strides, const int64_t* o_strides, float scale,
+                      int causal, int mode, void* stream);
+
 /* Batched C[i] = A[i] * op(B[i]) for i < batch, each as tvr_gemm_bias_act
  * with alpha 1, beta 0, no activation; matrices are dense row-major with the
  * given element strides between batch entries (stride_b may be 0 to
@@ -276,6 +292,21 @@ int tvr_strided_copy(void* dst, const void* src, int64_t elem_size, int ndim,
  * int64 (3), bool/uint8 (4) on contiguous buffers of n elements. */
 int tvr_convert(void* dst, int dst_type, const void* src, int src_type, int64_t n,
                 void* stream);
+
+/* out = cond ? a : b over a dense output of `ndim` dimensions; cond is bool
+ * (1 byte), a / b / out have elements of elem_size bytes (1, 4 or 8); each
+ * input is read through its own element strides (0 broadcasts).  No
+ * reference kernel: the reference runs where / masked_fill on the CPU
+ * through its boxed fallback (csrc/aten/Ops.cpp:499-501). */
+int tvr_where(const void* cond, const void* a, const void* b, void* out, int elem_size, int ndim,
+              const int64_t* sizes, const int64_t* cond_strides, const int64_t* a_strides,
+              const int64_t* b_strides, void* stream);
+
+/* Triangular mask of dense [batch, rows, cols]: out = x where
+ * col - row >= diagonal (upper != 0, triu) or col - row <= diagonal (tril),
+ * else 0.  elem_size 1, 4 or 8.  No reference kernel (CPU fallback there). */
+int tvr_triangle(const void* x, void* out, int elem_size, int64_t batch, int64_t rows,
+                 int64_t cols, int64_t diagonal, int upper, void* stream);
 
 /* ---- pointwise JIT ----------------------------------------------------- */
 

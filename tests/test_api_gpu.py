@@ -437,3 +437,46 @@ def test_linear_swiglu_op_and_compiled_llama_mlp(tvarant, precision, tol):
         assert (got - want).norm() / want.norm() <= tol
     finally:
         torch.set_float32_matmul_precision("highest")
+
+
+# ---- selection ops (native here; CPU fallback in the reference) ---------------
+
+@pytest.mark.parametrize("shape_c,shape_a,shape_b", [
+    ((5, 7), (5, 7), (5, 7)), ((3, 1, 6), (4, 1), (1,)), ((2, 3, 4), (), (3, 4)),
+])
+def test_where_broadcast_bit_exact(shape_c, shape_a, shape_b):
+    g = torch.Generator().manual_seed(11)
+    c = torch.rand(shape_c, generator=g) > 0.5
+    a = torch.randn(shape_a, generator=g)
+    b = torch.randn(shape_b, generator=g)
+    want = torch.where(c, a, b)
+    got = torch.where(c.to("tvarant"), a.to("tvarant"), b.to("tvarant")).cpu()
+    assert torch.equal(got, want)
+    got = torch.where(c.to("tvarant"), a.to("tvarant"), 0.5).cpu()
+    assert torch.equal(got, torch.where(c, a, 0.5))
+
+
+def test_masked_fill_and_logical_not():
+    g = torch.Generator().manual_seed(12)
+    x = torch.randn(6, 9, generator=g)
+    m = torch.rand(9, generator=g) > 0.6
+    want = x.masked_fill(m, float("-inf"))
+    got = x.to("tvarant").masked_fill(m.to("tvarant"), float("-inf")).cpu()
+    assert torch.equal(got, want)
+    y = x.to("tvarant")
+    y.masked_fill_(m.to("tvarant"), torch.tensor(2.5))
+    assert torch.equal(y.cpu(), x.masked_fill(m, 2.5))
+    assert torch.equal(torch.logical_not(m.to("tvarant")).cpu(), torch.logical_not(m))
+
+
+@pytest.mark.parametrize("shape", [(5, 7), (3, 8, 8), (2, 4, 6, 3)])
+@pytest.mark.parametrize("diagonal", [-2, 0, 1, 3])
+def test_tril_triu(shape, diagonal):
+    g = torch.Generator().manual_seed(13)
+    x = torch.randn(shape, generator=g)
+    for fn in (torch.tril, torch.triu):
+        assert torch.equal(fn(x.to("tvarant"), diagonal).cpu(), fn(x, diagonal))
+    b = torch.ones(shape, dtype=torch.bool).to("tvarant")
+    assert torch.equal(torch.tril(b, diagonal).cpu(), torch.tril(torch.ones(shape, dtype=torch.bool), diagonal))
+    t = x.t() if x.dim() == 2 else x.transpose(-1, -2)  # a strided input
+    assert torch.equal(torch.triu(t.to("tvarant"), diagonal).cpu(), torch.triu(t, diagonal))

@@ -42,6 +42,22 @@ def test_oracle_forward_matches_torch_cpu():
     assert rel_frobenius(got, want) <= 1e-5
 
 
+def test_sdpa_attention_matches_bmm_attention_on_cpu():
+    import torch
+
+    from tvarant_b200 import gpt2
+
+    cfg = gpt2.GPT2Config(**TINY)
+    model = gpt2.init_gpt2(cfg, seed=3)
+    ids = torch.from_numpy(_ids(cfg, 2, 12))
+    with torch.no_grad():
+        a = gpt2.forward(model, ids, attention="bmm")
+        b = gpt2.forward(model, ids, attention="sdpa")
+    assert float((a - b).norm() / a.norm()) <= 1e-5
+    with pytest.raises(ValueError):
+        gpt2.forward(model, ids, attention="flash")
+
+
 def test_flops_per_token_counts_every_gemm():
     from tvarant_b200 import gpt2
 
@@ -63,10 +79,13 @@ def test_shard_batch_covers_the_batch(world):
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("attention", ["bmm", "sdpa"])
 @pytest.mark.parametrize("precision,tol", [("highest", 1e-5), ("high", 5e-3)])
-def test_gpt2_forward_on_device_matches_oracle(precision, tol):
+def test_gpt2_forward_on_device_matches_oracle(attention, precision, tol):
     """3xTF32 ("highest") within 1e-5 and TF32 ("high") within 5e-3 relative
-    Frobenius error on the logits of a 2-layer model."""
+    Frobenius error on the logits of a 2-layer model, with attention as the
+    config's bmm formulation or through scaled_dot_product_attention (the fused
+    kernel in TF32; in 3xTF32 the same ops composed on the device)."""
     import torch
 
     import torch_tvarant  # noqa: F401
@@ -80,7 +99,8 @@ def test_gpt2_forward_on_device_matches_oracle(precision, tol):
     torch.set_float32_matmul_precision(precision)
     try:
         with torch.no_grad():
-            got = gpt2.forward(model.to("tvarant"), torch.from_numpy(ids).to("tvarant")).cpu().numpy()
+            got = gpt2.forward(model.to("tvarant"), torch.from_numpy(ids).to("tvarant"),
+                               attention=attention).cpu().numpy()
     finally:
         torch.set_float32_matmul_precision(old)
     assert np.isfinite(got).all()

@@ -40,12 +40,14 @@ ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 CUDA_SOURCES = [
     "runtime.cu",
     "elementwise.cu",
+    "select.cu",
     "reduce.cu",
     "gemm.cu",
     "gemm_simt.cu",
     "gemm_skinny.cu",
     "gemm_tc.cu",
     "gemm_ws.cu",
+    "attention.cu",
     "pointwise_jit.cu",
     "nccl.cu",
 ]
@@ -62,6 +64,8 @@ EXT_SOURCES = [
     "ExtendedOps.cpp",
     "CustomOps.cpp",
     "Collectives.cpp",
+    "Attention.cpp",
+    "Select.cpp",
 ]
 
 

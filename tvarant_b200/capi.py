@@ -99,6 +99,8 @@ SIGNATURES: dict[str, list] = {
     "tvr_gemm_bias_act_noalloc": [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _f32,
                                   _f32, _i32, _i32, _vp],
     "tvr_gemm_swiglu": [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i32, _vp],
+    "tvr_attention_fwd": [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _pi64, _pi64,
+                          _pi64, _pi64, _f32, _i32, _i32, _vp],
     "tvr_bmm": [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i32, _i32, _vp],
     "tvr_softmax": [_vp, _vp, _i64, _i64, _i64, _vp],
     "tvr_layer_norm": [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _f32, _vp],
@@ -108,6 +110,8 @@ SIGNATURES: dict[str, list] = {
     "tvr_binary": [_i32, _vp, _vp, _vp, _i32, _pi64, _pi64, _pi64, _f32, _vp],
     "tvr_strided_copy": [_vp, _vp, _i64, _i32, _pi64, _pi64, _pi64, _vp],
     "tvr_convert": [_vp, _i32, _vp, _i32, _i64, _vp],
+    "tvr_where": [_vp, _vp, _vp, _vp, _i32, _i32, _pi64, _pi64, _pi64, _pi64, _vp],
+    "tvr_triangle": [_vp, _vp, _i32, _i64, _i64, _i64, _i64, _i32, _vp],
     "tvr_pointwise": [_vp, _i32, _i32, _vp, _vp, _i64, _vp],
     "tvr_pointwise_source": [_vp, _i32, _i32, ctypes.c_char_p, _sz, _psz],
     "tvr_nccl_available": [_pi],

@@ -1,0 +1,125 @@
+// F.scaled_dot_product_attention on the tvarant device.
+//
+// PyTorch routes SDPA on an out-of-tree device through two hooks: the
+// `_fused_sdp_choice` dispatch stub picks a backend, and the "overrideable"
+// backend calls aten::_scaled_dot_product_fused_attention_overrideable.  Here
+// every fp32 4-D call without dropout takes the overrideable entry, which runs
+// the fused tcgen05 attention kernel (tvr_attention_fwd: TF32, head dim 64)
+// and otherwise composes the device's own ops — matmul (3xTF32 or TF32
+// GEMMs), the additive causal / attention mask, softmax, matmul — the
+// formulation the reference uses for attention (csrc/aten/LlmOps.cpp:68-148).
+// Forward only.
+#include <ATen/ATen.h>
+#include <ATen/SDPBackend.h>
+#include <ATen/native/DispatchStub.h>
+#include <ATen/native/transformers/attention.h>
+#include <c10/core/DeviceGuard.h>
+#include <torch/library.h>
+
+#include <cmath>
+#include <limits>
+#include <tuple>
+
+#include "TvarantExt.h"
+
+namespace tvarant::ops {
+
+int64_t fused_sdp_choice(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
+                         const std::optional<at::Tensor>& attn_mask, double dropout_p,
+                         bool is_causal, std::optional<double> scale, bool enable_gqa) {
+  (void)attn_mask;
+  (void)is_causal;
+  (void)scale;
+  const bool ok = q.scalar_type() == at::kFloat && k.scalar_type() == at::kFloat &&
+                  v.scalar_type() == at::kFloat && q.dim() == 4 && k.dim() == 4 &&
+                  v.dim() == 4 && dropout_p == 0.0 && (!enable_gqa || k.size(1) == q.size(1));
+  return static_cast<int64_t>(ok ? at::SDPBackend::overrideable : at::SDPBackend::math);
+}
+
+namespace {
+
+// Additive float mask on the device from a bool (true = attend) or float mask.
+at::Tensor additive_mask(const at::Tensor& mask, const at::Tensor& like) {
+  if (mask.scalar_type() == at::kBool) {
+    at::Tensor host = mask.cpu();
+    at::Tensor add = at::zeros(host.sizes(), host.options().dtype(at::kFloat));
+    add.masked_fill_(host.logical_not(), -std::numeric_limits<float>::infinity());
+    return add.to(like.device());
+  }
+  return ensure_fp32(to_device_like(mask, like), "scaled_dot_product_attention");
+}
+
+at::Tensor composed_attention(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
+                              const std::optional<at::Tensor>& attn_bias, bool is_causal,
+                              double scale) {
+  const int64_t L = q.size(2), S = k.size(2);
+  at::Tensor scores = at::matmul(q, k.transpose(-2, -1)) * scale;
+  if (is_causal) {
+    at::Tensor causal = at::full({L, S}, -std::numeric_limits<float>::infinity(),
+                                 at::TensorOptions().dtype(at::kFloat))
+                            .triu(1)
+                            .to(q.device());
+    scores = scores + causal;
+  }
+  if (attn_bias.has_value() && attn_bias->defined()) scores = scores + additive_mask(*attn_bias, q);
+  return at::matmul(at::_softmax(scores, -1, false), v);
+}
+
+std::tuple<at::Tensor, at::Tensor, at::Tensor, at::Tensor, c10::SymInt, c10::SymInt, at::Tensor,
+           at::Tensor, at::Tensor>
+sdpa_overrideable(const at::Tensor& query, const at::Tensor& key, const at::Tensor& value,
+                  const std::optional<at::Tensor>& attn_bias, double dropout_p, bool is_causal,
+                  bool return_debug_mask, std::optional<double> scale) {
+  (void)return_debug_mask;
+  TORCH_CHECK(dropout_p == 0.0,
+              "scaled_dot_product_attention: dropout is not supported on the tvarant device");
+  TORCH_CHECK(query.dim() == 4 && key.dim() == 4 && value.dim() == 4,
+              "scaled_dot_product_attention: expected 4-D query, key and value");
+  check_fp32(query, "scaled_dot_product_attention");
+  check_fp32(key, "scaled_dot_product_attention");
+  check_fp32(value, "scaled_dot_product_attention");
+  const int64_t B = query.size(0), H = query.size(1), L = query.size(2), E = query.size(3);
+  const int64_t S = key.size(2), Ev = value.size(3);
+  TORCH_CHECK(key.size(0) == B && value.size(0) == B && key.size(1) == H && value.size(1) == H &&
+                  value.size(2) == S && key.size(3) == E,
+              "scaled_dot_product_attention: query ", query.sizes(), ", key ", key.sizes(),
+              " and value ", value.sizes(), " do not match");
+  const double sc = scale.has_value() ? *scale : 1.0 / std::sqrt(static_cast<double>(E));
+  c10::DeviceGuard guard(query.device());
+  const at::Tensor none = at::empty({0}, query.options());
+  auto result = [&](const at::Tensor& out, const at::Tensor& lse) {
+    return std::make_tuple(out, lse, none, none, c10::SymInt(L), c10::SymInt(S), none, none, none);
+  };
+  const bool masked = attn_bias.has_value() && attn_bias->defined();
+  if (!masked && E == Ev && L > 0 && S > 0) {
+    auto last_unit = [](const at::Tensor& t) { return t.stride(3) == 1 ? t : contiguous_copy(t); };
+    const at::Tensor q = last_unit(query), k = last_unit(key), v = last_unit(value);
+    // output laid out [B, L, H, E] and returned as the [B, H, L, E] view
+    at::Tensor out_buf = empty_device({B, L, H, Ev}, query.options());
+    at::Tensor out = out_buf.permute({0, 2, 1, 3});
+    at::Tensor lse = empty_device({B, H, L}, query.options());
+    const int64_t qs[3] = {q.stride(0), q.stride(1), q.stride(2)};
+    const int64_t ks[3] = {k.stride(0), k.stride(1), k.stride(2)};
+    const int64_t vs[3] = {v.stride(0), v.stride(1), v.stride(2)};
+    const int64_t os[3] = {out.stride(0), out.stride(1), out.stride(2)};
+    const int rc = tvr_attention_fwd(q.data_ptr<float>(), k.data_ptr<float>(), v.data_ptr<float>(),
+                                     out.data_ptr<float>(), lse.data_ptr<float>(), B, H, L, S, E,
+                                     qs, ks, vs, os, static_cast<float>(sc), is_causal ? 1 : 0,
+                                     gemm_mode(), current_stream_handle());
+    if (rc == TVR_OK) return result(out, lse);
+    TORCH_CHECK(rc == TVR_ERR_UNSUPPORTED, "tvarant: ", tvr_last_error());
+  }
+  return result(composed_attention(query, key, value, attn_bias, is_causal, sc), none);
+}
+
+}  // namespace
+}  // namespace tvarant::ops
+
+TORCH_LIBRARY_IMPL(aten, PrivateUse1, m) {
+  m.impl("_scaled_dot_product_fused_attention_overrideable",
+         TORCH_FN(tvarant::ops::sdpa_overrideable));
+}
+
+namespace at::native {
+REGISTER_PRIVATEUSE1_DISPATCH(_fused_sdp_choice_stub, &tvarant::ops::fused_sdp_choice);
+}  // namespace at::native

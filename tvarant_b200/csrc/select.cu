@@ -1,0 +1,230 @@
+// Selection kernels: where / masked_fill and the triangular masks tril / triu.
+//
+// The reference runs these on the CPU through its boxed fallback
+// (csrc/aten/Ops.cpp:499-501); here they are native so that attention masks
+// (is_causal, boolean attn_mask) and model code that builds them stay on the
+// device.  Both kernels are HBM-bound with 32-bit index arithmetic
+// (fastdiv.cuh) for every tensor whose offsets fit in 31 bits, and a 64-bit
+// path otherwise.
+#include "internal.h"
+
+#include "fastdiv.cuh"
+
+namespace tvr {
+namespace {
+
+constexpr int kThreads = 256;
+
+struct Where8 {
+  int64_t size[TVR_MAX_DIMS];
+  int64_t sc[TVR_MAX_DIMS];
+  int64_t sa[TVR_MAX_DIMS];
+  int64_t sb[TVR_MAX_DIMS];
+};
+
+struct Where8Fast {
+  FastDiv div[TVR_MAX_DIMS];
+  uint32_t sc[TVR_MAX_DIMS];
+  uint32_t sa[TVR_MAX_DIMS];
+  uint32_t sb[TVR_MAX_DIMS];
+};
+
+// out[i] = cond[i] ? a[i] : b[i] over a dense output; each operand is read
+// through its own (possibly zero, i.e. broadcast) strides.
+template <typename T>
+__global__ void __launch_bounds__(kThreads) where_fast_kernel(const uint8_t* __restrict__ c,
+                                                              const T* __restrict__ a,
+                                                              const T* __restrict__ b,
+                                                              T* __restrict__ out, Where8Fast ix,
+                                                              int ndim, uint32_t n) {
+  const uint32_t stride = gridDim.x * blockDim.x;
+  for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+    uint32_t rem = i, oc = 0, oa = 0, ob = 0;
+    for (int d = ndim - 1; d >= 0; --d) {
+      const uint32_t q = fast_div(rem, ix.div[d]);
+      const uint32_t k = rem - q * ix.div[d].d;
+      rem = q;
+      oc += k * ix.sc[d];
+      oa += k * ix.sa[d];
+      ob += k * ix.sb[d];
+    }
+    out[i] = c[oc] ? a[oa] : b[ob];
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads) where_kernel(const uint8_t* __restrict__ c,
+                                                         const T* __restrict__ a,
+                                                         const T* __restrict__ b,
+                                                         T* __restrict__ out, Where8 ix, int ndim,
+                                                         int64_t n) {
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += stride) {
+    int64_t rem = i, oc = 0, oa = 0, ob = 0;
+    for (int d = ndim - 1; d >= 0; --d) {
+      const int64_t k = rem % ix.size[d];
+      rem /= ix.size[d];
+      oc += k * ix.sc[d];
+      oa += k * ix.sa[d];
+      ob += k * ix.sb[d];
+    }
+    out[i] = c[oc] ? a[oa] : b[ob];
+  }
+}
+
+// Merges adjacent dimensions contiguous for the output and all three
+// operands; drops size-1 dimensions.
+int collapse_where(int ndim, const int64_t* sizes, const int64_t* sc, const int64_t* sa,
+                   const int64_t* sb, Where8* ix) {
+  int r = 0;
+  for (int d = 0; d < ndim; ++d) {
+    if (sizes[d] == 1) continue;
+    if (r > 0) {
+      const int p = r - 1;
+      if (ix->sc[p] == sc[d] * sizes[d] && ix->sa[p] == sa[d] * sizes[d] &&
+          ix->sb[p] == sb[d] * sizes[d]) {
+        ix->size[p] *= sizes[d];
+        ix->sc[p] = sc[d];
+        ix->sa[p] = sa[d];
+        ix->sb[p] = sb[d];
+        continue;
+      }
+    }
+    ix->size[r] = sizes[d];
+    ix->sc[r] = sc[d];
+    ix->sa[r] = sa[d];
+    ix->sb[r] = sb[d];
+    ++r;
+  }
+  if (r == 0) {
+    ix->size[0] = 1;
+    ix->sc[0] = ix->sa[0] = ix->sb[0] = 0;
+    r = 1;
+  }
+  return r;
+}
+
+template <typename T>
+int launch_where(const uint8_t* c, const void* a, const void* b, void* out, const Where8& ix,
+                 int r, int64_t n, cudaStream_t s, int dev) {
+  bool fits = n < (int64_t(1) << 31);
+  int64_t mc = 0, ma = 0, mb = 0;
+  for (int d = 0; fits && d < r; ++d) {
+    fits = ix.sc[d] >= 0 && ix.sa[d] >= 0 && ix.sb[d] >= 0 && ix.size[d] < (int64_t(1) << 31) &&
+           ix.sc[d] < (int64_t(1) << 31) && ix.sa[d] < (int64_t(1) << 31) &&
+           ix.sb[d] < (int64_t(1) << 31);
+    mc += (ix.size[d] - 1) * ix.sc[d];
+    ma += (ix.size[d] - 1) * ix.sa[d];
+    mb += (ix.size[d] - 1) * ix.sb[d];
+  }
+  fits = fits && mc < (int64_t(1) << 31) && ma < (int64_t(1) << 31) && mb < (int64_t(1) << 31);
+  const unsigned grid = elementwise_grid(n, kThreads, dev);
+  if (fits) {
+    Where8Fast fx;
+    for (int d = 0; d < r; ++d) {
+      fx.div[d] = make_fastdiv(static_cast<uint32_t>(ix.size[d]));
+      fx.sc[d] = static_cast<uint32_t>(ix.sc[d]);
+      fx.sa[d] = static_cast<uint32_t>(ix.sa[d]);
+      fx.sb[d] = static_cast<uint32_t>(ix.sb[d]);
+    }
+    where_fast_kernel<T><<<grid, kThreads, 0, s>>>(c, static_cast<const T*>(a),
+                                                   static_cast<const T*>(b), static_cast<T*>(out),
+                                                   fx, r, static_cast<uint32_t>(n));
+  } else {
+    where_kernel<T><<<grid, kThreads, 0, s>>>(c, static_cast<const T*>(a),
+                                              static_cast<const T*>(b), static_cast<T*>(out), ix,
+                                              r, n);
+  }
+  TVR_LAUNCH_CHECK();
+  return TVR_OK;
+}
+
+// out[b, i, j] = keep(i, j) ? x[b, i, j] : 0 for dense [batch, rows, cols];
+// keep = j - i >= diagonal (upper) or j - i <= diagonal (lower).
+template <typename T>
+__global__ void __launch_bounds__(kThreads) tri_kernel(const T* __restrict__ x, T* __restrict__ out,
+                                                       int64_t n, int64_t rows, int64_t cols,
+                                                       int64_t diagonal, int upper) {
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t e = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; e < n;
+       e += stride) {
+    const int64_t j = e % cols;
+    const int64_t i = (e / cols) % rows;
+    const bool keep = upper ? (j - i >= diagonal) : (j - i <= diagonal);
+    out[e] = keep ? x[e] : T(0);
+  }
+}
+
+}  // namespace
+}  // namespace tvr
+
+using namespace tvr;
+
+extern "C" {
+
+int tvr_where(const void* cond, const void* a, const void* b, void* out, int elem_size, int ndim,
+              const int64_t* sizes, const int64_t* cond_strides, const int64_t* a_strides,
+              const int64_t* b_strides, void* stream) {
+  TVR_CHECK(ndim >= 0 && ndim <= TVR_MAX_DIMS, "tvr_where: rank %d out of range", ndim);
+  TVR_CHECK(elem_size == 1 || elem_size == 4 || elem_size == 8,
+            "tvr_where: unsupported element size %d", elem_size);
+  int64_t one = 1, zero = 0;
+  if (ndim == 0) {
+    sizes = &one;
+    cond_strides = a_strides = b_strides = &zero;
+    ndim = 1;
+  }
+  TVR_CHECK(sizes && cond_strides && a_strides && b_strides, "tvr_where: null shape");
+  int64_t n = 1;
+  for (int d = 0; d < ndim; ++d) {
+    TVR_CHECK(sizes[d] >= 0, "tvr_where: negative size");
+    n *= sizes[d];
+  }
+  if (n == 0) return TVR_OK;
+  TVR_CHECK(cond && a && b && out, "tvr_where: null pointer");
+  Where8 ix;
+  const int r = collapse_where(ndim, sizes, cond_strides, a_strides, b_strides, &ix);
+  const int dev = current_device();
+  const auto* c = static_cast<const uint8_t*>(cond);
+  cudaStream_t s = as_stream(stream);
+  switch (elem_size) {
+    case 1: return launch_where<uint8_t>(c, a, b, out, ix, r, n, s, dev);
+    case 4: return launch_where<uint32_t>(c, a, b, out, ix, r, n, s, dev);
+    default: return launch_where<unsigned long long>(c, a, b, out, ix, r, n, s, dev);
+  }
+}
+
+int tvr_triangle(const void* x, void* out, int elem_size, int64_t batch, int64_t rows,
+                 int64_t cols, int64_t diagonal, int upper, void* stream) {
+  TVR_CHECK(batch >= 0 && rows >= 0 && cols >= 0, "tvr_triangle: negative size");
+  TVR_CHECK(elem_size == 1 || elem_size == 4 || elem_size == 8,
+            "tvr_triangle: unsupported element size %d", elem_size);
+  const int64_t n = batch * rows * cols;
+  if (n == 0) return TVR_OK;
+  TVR_CHECK(x && out, "tvr_triangle: null pointer");
+  const int dev = current_device();
+  const unsigned grid = elementwise_grid(n, kThreads, dev);
+  cudaStream_t s = as_stream(stream);
+  switch (elem_size) {
+    case 1:
+      tri_kernel<uint8_t><<<grid, kThreads, 0, s>>>(static_cast<const uint8_t*>(x),
+                                                    static_cast<uint8_t*>(out), n, rows, cols,
+                                                    diagonal, upper);
+      break;
+    case 4:
+      tri_kernel<uint32_t><<<grid, kThreads, 0, s>>>(static_cast<const uint32_t*>(x),
+                                                     static_cast<uint32_t*>(out), n, rows, cols,
+                                                     diagonal, upper);
+      break;
+    default:
+      tri_kernel<unsigned long long><<<grid, kThreads, 0, s>>>(
+          static_cast<const unsigned long long*>(x), static_cast<unsigned long long*>(out), n,
+          rows, cols, diagonal, upper);
+      break;
+  }
+  TVR_LAUNCH_CHECK();
+  return TVR_OK;
+}
+
+}  // extern "C"

@@ -76,6 +76,15 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map
 }
 
 
+__device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map, uint32_t bar,
+                                            int c0, int c1, int c2, int c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
+
 __device__ __forceinline__ void tc_fence_before() {
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
 }
@@ -179,6 +188,30 @@ inline int encode_3d(CUtensorMap* map, const void* ptr, uint64_t d0, uint64_t d1
     return fail(TVR_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d: %s) dims {%llu, %llu, %llu}",
                 static_cast<int>(r), msg, (unsigned long long)d0, (unsigned long long)d1,
                 (unsigned long long)d2);
+  }
+  return TVR_OK;
+}
+
+// 4-D fp32 tensor map: dims {d0 (contiguous), d1, d2, d3}, byte strides of
+// d1..d3, box {box0, box1, 1, 1}.
+inline int encode_4d(CUtensorMap* map, const void* ptr, const uint64_t dims[4],
+                     const uint64_t strides_bytes[3], uint32_t box0, uint32_t box1,
+                     CUtensorMapSwizzle swizzle) {
+  const DriverApi* drv = driver();
+  if (drv == nullptr) return TVR_ERR_CUDA;
+  const cuuint64_t d[4] = {dims[0], dims[1], dims[2], dims[3]};
+  const cuuint64_t st[3] = {strides_bytes[0], strides_bytes[1], strides_bytes[2]};
+  const cuuint32_t box[4] = {box0, box1, 1, 1};
+  const cuuint32_t elem_strides[4] = {1, 1, 1, 1};
+  CUresult r = drv->tensorMapEncodeTiled(
+      map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, const_cast<void*>(ptr), d, st, box, elem_strides,
+      CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    const char* msg = "?";
+    if (drv->getErrorString) drv->getErrorString(r, &msg);
+    return fail(TVR_ERR_CUDA, "cuTensorMapEncodeTiled (4-D) failed (%d: %s)", static_cast<int>(r),
+                msg);
   }
   return TVR_OK;
 }

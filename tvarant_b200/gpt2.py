@@ -103,25 +103,37 @@ def _linear_silu(x, w, b):
     return torch.nn.functional.silu(torch.nn.functional.linear(x, w, b))
 
 
-def forward(model: GPT2, ids: torch.Tensor, mask: torch.Tensor | None = None) -> torch.Tensor:
-    """Logits [B, S, vocab] for token ids [B, S] (int64, on the model's device)."""
+def forward(model: GPT2, ids: torch.Tensor, mask: torch.Tensor | None = None,
+            attention: str = "bmm") -> torch.Tensor:
+    """Logits [B, S, vocab] for token ids [B, S] (int64, on the model's device).
+
+    ``attention="bmm"`` is the materialised formulation (bmm, additive causal
+    mask, softmax, bmm); ``"sdpa"`` calls F.scaled_dot_product_attention with
+    ``is_causal=True`` on the heads of the fused QKV projection, which on the
+    tvarant device runs the fused attention kernel in TF32 mode."""
     F = torch.nn.functional
     cfg = model.cfg
     B, S = ids.shape
     d, H = cfg.d_model, cfg.n_head
     hd = d // H
-    if mask is None:
+    if attention not in ("bmm", "sdpa"):
+        raise ValueError(f"attention must be 'bmm' or 'sdpa', got {attention!r}")
+    if mask is None and attention == "bmm":
         mask = causal_mask(S, ids.device)
     scale = 1.0 / math.sqrt(hd)
     x = F.embedding(ids, model.wte) + model.wpe[:S]
     for L in model.layers:
         h = F.layer_norm(x, (d,), L.ln1_g, L.ln1_b, 1e-5)
         qkv = F.linear(h, L.w_qkv, L.b_qkv).view(B, S, 3, H, hd).permute(2, 0, 3, 1, 4)
-        q = (qkv[0] * scale).reshape(B * H, S, hd)
-        k = qkv[1].reshape(B * H, S, hd)
-        v = qkv[2].reshape(B * H, S, hd)
-        att = F.softmax(torch.bmm(q, k.transpose(1, 2)) + mask, dim=-1)
-        o = torch.bmm(att, v).view(B, H, S, hd).permute(0, 2, 1, 3).reshape(B, S, d)
+        if attention == "sdpa":
+            o = F.scaled_dot_product_attention(qkv[0], qkv[1], qkv[2], is_causal=True, scale=scale)
+            o = o.transpose(1, 2).reshape(B, S, d)
+        else:
+            q = (qkv[0] * scale).reshape(B * H, S, hd)
+            k = qkv[1].reshape(B * H, S, hd)
+            v = qkv[2].reshape(B * H, S, hd)
+            att = F.softmax(torch.bmm(q, k.transpose(1, 2)) + mask, dim=-1)
+            o = torch.bmm(att, v).view(B, H, S, hd).permute(0, 2, 1, 3).reshape(B, S, d)
         x = x + F.linear(o, L.w_proj, L.b_proj)
         h = F.layer_norm(x, (d,), L.ln2_g, L.ln2_b, 1e-5)
         x = x + F.linear(_linear_silu(h, L.w_fc, L.b_fc), L.w_out, L.b_out)

@@ -298,19 +298,20 @@ def _gpt2(args, rank, world, local_rank):
         last_host = last_host.pin_memory()
     ids = ids_host.to(dev)
     mask = gpt2.causal_mask(seq, dev)
+    att = args.attention
     for _ in range(args.warmup):
-        gpt2.forward(model, ids, mask)
+        gpt2.forward(model, ids, mask, att)
     torch.tvarant.synchronize()
     bench._barrier(world)
     with bench.ClockSampler(local_rank) as clocks:
         h0 = time.perf_counter()
-        ms = _time_steps(lambda: gpt2.forward(model, ids, mask), args.steps)
+        ms = _time_steps(lambda: gpt2.forward(model, ids, mask, att), args.steps)
         clocks.mark(h0, time.perf_counter())
     ms = bench._max_over_ranks(ms, world)
 
     def e2e_step():
         x = ids_host.to(dev, non_blocking=True)
-        logits = gpt2.forward(model, x, mask)
+        logits = gpt2.forward(model, x, mask, att)
         last_host.copy_(logits[:, -1, :], non_blocking=True)
 
     e2e_step()
@@ -320,7 +321,7 @@ def _gpt2(args, rank, world, local_rank):
     status = torch.tvarant.get_status()
     # parity on the device-resident result: the last position of every local
     # sequence is a proper distribution after softmax (finite logits)
-    logits = gpt2.forward(model, ids, mask)
+    logits = gpt2.forward(model, ids, mask, att)
     finite = bool(torch.isfinite(logits[:, -1, :].cpu()).all())
     if rank != 0:
         return None
@@ -336,7 +337,11 @@ def _gpt2(args, rank, world, local_rank):
         "data": "synthetic (N(0,0.02) weights, uniform token ids)",
         "config": {"workload": f"GPT-2-small-shaped forward, {cfg.n_layer} layers, d_model {cfg.d_model}, "
                                f"{cfg.n_head} heads, d_ff {cfg.d_ff} SiLU, vocab {cfg.vocab}, "
-                               f"batch {batch} x seq {seq}, causal bmm+softmax attention, tied LM head",
+                               f"batch {batch} x seq {seq}, causal attention as "
+                               + ("bmm + mask add + softmax + bmm" if att == "bmm"
+                                  else "fused scaled_dot_product_attention (TF32 kernel)")
+                               + ", tied LM head",
+                   "attention": att,
                    "parallelism": f"batch split over {world} rank(s) (attention split over batch x heads)",
                    "tflop_per_step": cfg.flops_per_token(seq) * tokens / 1e12,
                    "last_logits_finite": finite,
@@ -347,7 +352,7 @@ def _gpt2(args, rank, world, local_rank):
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s per GPU",
                      "frac": achieved / peak, "traffic": None,
                      "peak_source": "cuBLAS TF32 8192^3 measured in this run"},
-        "gpu_launches": args.steps * (cfg.n_layer * 17 + 4),
+        "gpu_launches": args.steps * (cfg.n_layer * (17 if att == "bmm" else 10) + 4),
         "clocks": clocks.summary(),
         "device_status": status,
     }
