@@ -602,6 +602,8 @@ def _main() -> int:
                          "F.scaled_dot_product_attention kernel")
     ap.add_argument("--chunks", type=int, default=2, help="mlp workload: token chunks overlapped with the all-reduce")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-graph", action="store_true",
+                    help="mlp / gpt2 workloads: time the eager calls instead of a CUDA graph replay")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -161,6 +161,20 @@ int tvr_event_synchronize(void* event);
 int tvr_event_query(void* event, int* done);
 int tvr_event_elapsed_ms(void* start, void* end, float* ms);
 
+/* ---- graphs: capture the device work issued on a stream once, replay it
+ * (the reference launches synchronously, one kernel at a time,
+ * csrc/runtime/CpuSimRuntime.cpp:109-218).  Work on other streams joins the
+ * capture through events recorded on the capturing stream and must join back
+ * before tvr_graph_end.  Device memory allocated during the capture
+ * (tvr_malloc is stream-ordered) belongs to the graph: allocations still live
+ * at the end of the capture keep their addresses and are reused by every
+ * replay, so tensors produced by the captured work are rewritten in place. */
+int tvr_graph_begin(void* stream);
+/* Ends the capture begun on `stream` and instantiates it into *graph. */
+int tvr_graph_end(void* stream, void** graph);
+int tvr_graph_launch(void* graph, void* stream);
+int tvr_graph_destroy(void* graph);
+
 /* ---- dense contractions (tensor cores) --------------------------------- */
 
 /* C[m,n] = act(alpha * sum_k A[m,k]*B(k,n) + beta * P[m,n]) where

@@ -37,7 +37,7 @@ def _port() -> int:
 
 
 @pytest.mark.skipif(_gpus() < 2, reason="needs two GPUs")
-@pytest.mark.parametrize("precision,tol", [("highest", 1e-5), ("high", 5e-3)])
+@pytest.mark.parametrize("precision,tol", [("highest", 3e-5), ("high", 5e-3)])
 def test_tp2_matches_single_gpu(tmp_path, precision, tol):
     out = tmp_path / "tp.npz"
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
@@ -48,4 +48,16 @@ def test_tp2_matches_single_gpu(tmp_path, precision, tol):
     assert proc.returncode == 0, proc.stdout[-3000:] + proc.stderr[-3000:]
     r = np.load(out)
     assert int(r["status"]) == 0
-    assert rel_frobenius(r["tp"], r["full"]) <= tol
+    # the TP decomposition adds no error beyond the precision mode: against
+    # the same stack on one GPU in the same mode
+    assert rel_frobenius(r["tp"], r["full"]) <= tol, rel_frobenius(r["tp"], r["full"])
+    if precision == "highest":
+        # and against the float64 stack: 3 layers of 3 GEMMs, the per-GEMM
+        # bound compounding through down projections that cancel (outputs
+        # ~1e-3 from terms ~2.5e-2)
+        assert rel_frobenius(r["tp"], r["exact"]) <= tol, rel_frobenius(r["tp"], r["exact"])
+        assert rel_frobenius(r["full"], r["exact"]) <= tol, rel_frobenius(r["full"], r["exact"])
+    # the captured graph (GEMMs and NCCL all-reduces) replays the eager TP
+    # kernels bit for bit, and follows new inputs written into the captured one
+    assert np.array_equal(r["graph"], r["tp"])
+    assert rel_frobenius(r["graph2"], r["full2"]) <= tol

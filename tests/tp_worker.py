@@ -35,15 +35,36 @@ def main():
     x = torch.randn(tokens, d_model, generator=g)
     shards = [tuple(t.to(dev) for t in shard_mlp(wg, wu, wd, rank, world)) for wg, wu, wd in full]
     comm = Communicator.from_process_group(local)
+    from tvarant_b200.graphs import Graph
+
     with torch.no_grad():
-        y = TPMLPStack(shards, comm, chunks=2)(x.to(dev)).cpu().numpy()
+        stack = TPMLPStack(shards, comm, chunks=2)
+        y = stack(x.to(dev)).cpu().numpy()
+        # the same stack captured as one CUDA graph (GEMMs + NCCL all-reduces),
+        # replayed twice on new inputs written into the captured input
+        xs = x.to(dev)
+        graph = Graph(stack, xs)
+        xs.copy_((2 * x).to(dev))
+        y2 = graph.replay().cpu().numpy()
+        xs.copy_(x.to(dev))
+        yg = graph.replay().cpu().numpy()
+        graph.close()
         if rank == 0:
             ref = TPMLPStack([tuple(t.to(dev) for t in layer) for layer in full], None)(x.to(dev)).cpu().numpy()
+            ref2 = TPMLPStack([tuple(t.to(dev) for t in layer) for layer in full], None)((2 * x).to(dev)).cpu().numpy()
     status = torch.tvarant.get_status()
     dist.barrier()
     comm.destroy()
     if rank == 0:
-        np.savez(sys.argv[1], tp=y, full=ref, status=status)
+        def exact(v):  # the stack in float64 on the host
+            h = v.double().numpy()
+            for wg, wu, wd in full:
+                g, u = h @ wg.double().numpy().T, h @ wu.double().numpy().T
+                h = (g / (1 + np.exp(-g)) * u) @ wd.double().numpy().T
+            return h
+
+        np.savez(sys.argv[1], tp=y, full=ref, graph=yg, graph2=y2, full2=ref2, status=status,
+                 exact=exact(x), exact2=exact(2 * x))
     dist.destroy_process_group()
 
 

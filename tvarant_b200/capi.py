@@ -94,6 +94,10 @@ SIGNATURES: dict[str, list] = {
     "tvr_event_synchronize": [_vp],
     "tvr_event_query": [_vp, _pi],
     "tvr_event_elapsed_ms": [_vp, _vp, _pf],
+    "tvr_graph_begin": [_vp],
+    "tvr_graph_end": [_vp, _pvp],
+    "tvr_graph_launch": [_vp, _vp],
+    "tvr_graph_destroy": [_vp],
     "tvr_gemm_bias_act": [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _f32, _f32,
                           _i32, _i32, _i32, _vp],
     "tvr_gemm_bias_act_noalloc": [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _f32,

@@ -168,6 +168,15 @@ at::Tensor contiguous_copy(const at::Tensor& self) {
 
 at::Tensor to_device_like(const at::Tensor& t, const at::Tensor& like) {
   if (is_device(t)) return t;
+  if (t.dim() == 0) {
+    // A Python number or 0-dim CPU tensor: a fill kernel carries the value as
+    // an argument, so no host buffer is read later by the device (a copy from
+    // a temporary host scalar would be replayed from a dangling address by a
+    // captured graph) and no host-to-device copy is queued.
+    at::Tensor out = empty_device({}, t.options().device(like.device()));
+    fill_scalar(out, t.item());
+    return out;
+  }
   at::Tensor c = t.contiguous();
   at::Tensor out = empty_device(c.sizes(), c.options().device(like.device()));
   copy_h2d(c, out, false);
@@ -273,6 +282,20 @@ at::Tensor binary(const at::Tensor& self, const at::Tensor& other, int op, float
                   const char* name) {
   at::Tensor a = ensure_fp32(self, name);
   at::Tensor b = ensure_fp32(other, name);
+  // tensor (op) Python number: the unary kernels take the number by value,
+  // with the same fp32 rounding as the broadcast binary kernel
+  // (a * s, and a + alpha * s with alpha * s rounded to fp32 first).
+  auto host_scalar = [](const at::Tensor& t) { return !is_device(t) && t.dim() == 0; };
+  if (is_device(a) && host_scalar(b)) {
+    const float s = b.item<float>();
+    if (op == TVR_BINARY_MUL) return unary(a, TVR_UNARY_SCALE, s, name);
+    return unary(a, TVR_UNARY_ADD_SCALAR, alpha * s, name);
+  }
+  if (host_scalar(a) && is_device(b)) {
+    const float s = a.item<float>();
+    if (op == TVR_BINARY_MUL) return unary(b, TVR_UNARY_SCALE, s, name);
+    if (alpha == 1.f) return unary(b, TVR_UNARY_ADD_SCALAR, s, name);
+  }
   const at::Tensor& anchor = is_device(a) ? a : b;
   TORCH_CHECK(is_device(anchor), name, ": expected a tvarant tensor");
   a = to_device_like(a, anchor);

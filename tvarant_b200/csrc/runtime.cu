@@ -547,4 +547,49 @@ int tvr_event_elapsed_ms(void* start, void* end, float* ms) {
   return TVR_OK;
 }
 
+// ---- graphs ----------------------------------------------------------------
+
+int tvr_graph_begin(void* stream) {
+  TVR_CHECK(stream != nullptr, "tvr_graph_begin: capture needs a created stream, not the default");
+  // Relaxed: the allocator's bookkeeping (events for cross-stream uses) may
+  // run while the capture is open.
+  TVR_CUDA_TRY(cudaStreamBeginCapture(as_stream(stream), cudaStreamCaptureModeRelaxed));
+  return TVR_OK;
+}
+
+int tvr_graph_end(void* stream, void** graph) {
+  TVR_CHECK(stream != nullptr && graph != nullptr, "tvr_graph_end: null argument");
+  *graph = nullptr;
+  cudaGraph_t g = nullptr;
+  cudaError_t e = cudaStreamEndCapture(as_stream(stream), &g);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    if (g != nullptr) cudaGraphDestroy(g);
+    return fail(TVR_ERR_CUDA, "tvr_graph_end: capture failed: %s", cudaGetErrorString(e));
+  }
+  cudaGraphExec_t exec = nullptr;
+  // Allocations a launch leaves live are released when the graph is
+  // launched again, so every replay gets the same addresses.
+  e = cudaGraphInstantiateWithFlags(&exec, g, cudaGraphInstantiateFlagAutoFreeOnLaunch);
+  cudaGraphDestroy(g);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return fail(TVR_ERR_CUDA, "tvr_graph_end: instantiation failed: %s", cudaGetErrorString(e));
+  }
+  *graph = exec;
+  return TVR_OK;
+}
+
+int tvr_graph_launch(void* graph, void* stream) {
+  TVR_CHECK(graph != nullptr, "tvr_graph_launch: null graph");
+  TVR_CUDA_TRY(cudaGraphLaunch(reinterpret_cast<cudaGraphExec_t>(graph), as_stream(stream)));
+  return TVR_OK;
+}
+
+int tvr_graph_destroy(void* graph) {
+  if (graph == nullptr) return TVR_OK;
+  TVR_CUDA_TRY(cudaGraphExecDestroy(reinterpret_cast<cudaGraphExec_t>(graph)));
+  return TVR_OK;
+}
+
 }  // extern "C"

@@ -135,6 +135,11 @@ def current_stream_handle() -> int:
     return int(_C.current_stream_handle())
 
 
+def stream_handle(s: torch.Stream) -> int:
+    """The cudaStream_t behind a tvarant torch.Stream, as an integer."""
+    return int(_C.stream_handle(s.device_index, s.stream_id))
+
+
 def memory_stats(device: DeviceLike = None) -> dict:
     reserved, in_use = _C.memory_stats(_index(device))
     return {"reserved_bytes": int(reserved), "allocated_bytes": int(in_use)}

@@ -197,9 +197,20 @@ def _mlp(args, rank, world, local_rank):
         stack(x)
     torch.tvarant.synchronize()
     bench._barrier(world)
+    eager_ms = bench._max_over_ranks(_time_steps(lambda: stack(x), args.steps), world)
+    # the whole stack (GEMMs, events, all-reduces on the side stream) as one
+    # CUDA graph: one launch per step instead of ~6 host-side calls per layer
+    run = stack
+    if not args.no_graph:
+        from tvarant_b200.graphs import Graph
+
+        graph = Graph(stack, x)
+        run = lambda _x: graph.replay()  # noqa: E731
+        torch.tvarant.synchronize()
+        bench._barrier(world)
     with bench.ClockSampler(local_rank) as clocks:
         h0 = time.perf_counter()
-        ms = _time_steps(lambda: stack(x), args.steps)
+        ms = _time_steps(lambda: run(x), args.steps)
         clocks.mark(h0, time.perf_counter())
     ms = bench._max_over_ranks(ms, world)
     # the per-layer GEMMs alone (one rank's share of the FLOPs)
@@ -209,14 +220,16 @@ def _mlp(args, rank, world, local_rank):
     layer_ms = _time_steps(lambda: mlp_layer(x, wg, wu, wd), args.steps)
 
     def e2e_step():
-        xi = x_host.to(dev, non_blocking=True)
-        out_host.copy_(stack(xi), non_blocking=True)
+        x.copy_(x_host, non_blocking=True)
+        out_host.copy_(run(x), non_blocking=True)
 
     e2e_step()
     torch.tvarant.synchronize()
     bench._barrier(world)
     e2e_ms = bench._max_over_ranks(_time_steps(e2e_step, args.steps), world)
     status = torch.tvarant.get_status()
+    if not args.no_graph:
+        graph.close()
     if comm is not None:
         bench._barrier(world)
         comm.destroy()
@@ -237,6 +250,8 @@ def _mlp(args, rank, world, local_rank):
         "config": {"workload": f"Llama-7B-shaped gated-SiLU MLP stack, {args.layers} layers, "
                                f"d_model {D_MODEL}, d_ff {D_FF}, {TOKENS} tokens, TP x{world}",
                    "parallelism": f"tp{world}", "chunks": stack.chunks,
+                   "cuda_graph": not args.no_graph,
+                   "eager_tokens_per_s": TOKENS / (eager_ms / 1e3),
                    "layer_ms_one_rank_gemms": layer_ms,
                    "l2": "weights per rank exceed L2 at tp<=4; activations 134 MB"},
         "e2e": {"value": TOKENS / (e2e_ms / 1e3), "unit": "tokens/s",
@@ -303,15 +318,26 @@ def _gpt2(args, rank, world, local_rank):
         gpt2.forward(model, ids, mask, att)
     torch.tvarant.synchronize()
     bench._barrier(world)
+    eager_ms = bench._max_over_ranks(
+        _time_steps(lambda: gpt2.forward(model, ids, mask, att), args.steps), world)
+    run = lambda: gpt2.forward(model, ids, mask, att)  # noqa: E731
+    graph = None
+    if not args.no_graph:
+        from tvarant_b200.graphs import Graph
+
+        graph = Graph(gpt2.forward, model, ids, mask, att)
+        run = graph.replay
+        torch.tvarant.synchronize()
+        bench._barrier(world)
     with bench.ClockSampler(local_rank) as clocks:
         h0 = time.perf_counter()
-        ms = _time_steps(lambda: gpt2.forward(model, ids, mask, att), args.steps)
+        ms = _time_steps(run, args.steps)
         clocks.mark(h0, time.perf_counter())
     ms = bench._max_over_ranks(ms, world)
 
     def e2e_step():
-        x = ids_host.to(dev, non_blocking=True)
-        logits = gpt2.forward(model, x, mask, att)
+        ids.copy_(ids_host, non_blocking=True)
+        logits = run()
         last_host.copy_(logits[:, -1, :], non_blocking=True)
 
     e2e_step()
@@ -321,8 +347,11 @@ def _gpt2(args, rank, world, local_rank):
     status = torch.tvarant.get_status()
     # parity on the device-resident result: the last position of every local
     # sequence is a proper distribution after softmax (finite logits)
-    logits = gpt2.forward(model, ids, mask, att)
+    logits = run()
     finite = bool(torch.isfinite(logits[:, -1, :].cpu()).all())
+    if graph is not None:
+        del logits
+        graph.close()
     if rank != 0:
         return None
     tokens = batch * seq
@@ -342,6 +371,8 @@ def _gpt2(args, rank, world, local_rank):
                                   else "fused scaled_dot_product_attention (TF32 kernel)")
                                + ", tied LM head",
                    "attention": att,
+                   "cuda_graph": not args.no_graph,
+                   "eager_tokens_per_s": batch * seq / (eager_ms / 1e3),
                    "parallelism": f"batch split over {world} rank(s) (attention split over batch x heads)",
                    "tflop_per_step": cfg.flops_per_token(seq) * tokens / 1e12,
                    "last_logits_finite": finite,
