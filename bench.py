@@ -601,6 +601,8 @@ def _main() -> int:
                     help="gpt2 workload: bmm + mask + softmax + bmm (the config), or the fused "
                          "F.scaled_dot_product_attention kernel")
     ap.add_argument("--chunks", type=int, default=2, help="mlp workload: token chunks overlapped with the all-reduce")
+    ap.add_argument("--nccl-ctas", type=int, default=32,
+                    help="mlp workload: CTAs NCCL may use per collective (the GEMMs leave that many SMs free; 0: no limit)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-graph", action="store_true",
                     help="mlp / gpt2 workloads: time the eager calls instead of a CUDA graph replay")

@@ -209,6 +209,13 @@ int tvr_gemm_bias_act_noalloc(const float* a, const float* b, const float* bias,
                               int64_t lda, int64_t ldb, int64_t ldc,
                               float alpha, float beta, int act, int trans_b, void* stream);
 
+/* Upper bound on the SMs (CTAs) the persistent tensor-core GEMM of this
+ * device occupies; 0 (the default) means all.  Tensor-parallel code keeps a
+ * few SMs free with it so that NCCL kernels overlap the GEMMs instead of
+ * waiting for them.  Applies to launches issued after the call. */
+int tvr_set_gemm_sm_limit(int device, int max_sms);
+int tvr_get_gemm_sm_limit(int device, int* max_sms);
+
 /* Gated (SwiGLU) projection: out[m, n] = silu(x . Wg^T) * (x . Wu^T), with x
  * [m, k] (row stride ldx) and both weights in nn.Linear layout [n, k] (row
  * strides ldw_gate, ldw_up).  No reference counterpart as one call: the
@@ -359,6 +366,12 @@ int tvr_pointwise_source(const tvr_pw_node* nodes, int n_nodes, int n_inputs, ch
 int tvr_nccl_available(int* available);
 int tvr_nccl_get_unique_id(void* id128);
 int tvr_nccl_comm_init(void** comm, int nranks, const void* id128, int rank, int device);
+/* The same, with NCCL's kernels limited to at most max_ctas CTAs per
+ * collective (ncclConfig_t.maxCTAs) when the loaded NCCL supports it
+ * (2.28 and later); max_ctas <= 0 leaves NCCL's choice.  Lets collectives
+ * run beside the persistent GEMM when tvr_set_gemm_sm_limit keeps SMs free. */
+int tvr_nccl_comm_init_ctas(void** comm, int nranks, const void* id128, int rank, int device,
+                            int max_ctas);
 /* dtype: 0 float32; op: 0 sum.  In place when send == recv. */
 int tvr_nccl_all_reduce(const void* send, void* recv, int64_t count, int dtype, int op,
                         void* comm, void* stream);

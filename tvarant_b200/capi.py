@@ -121,6 +121,9 @@ SIGNATURES: dict[str, list] = {
     "tvr_nccl_available": [_pi],
     "tvr_nccl_get_unique_id": [_vp],
     "tvr_nccl_comm_init": [_pvp, _i32, _vp, _i32, _i32],
+    "tvr_nccl_comm_init_ctas": [_pvp, _i32, _vp, _i32, _i32, _i32],
+    "tvr_set_gemm_sm_limit": [_i32, _i32],
+    "tvr_get_gemm_sm_limit": [_i32, _pi],
     "tvr_nccl_all_reduce": [_vp, _vp, _i64, _i32, _i32, _vp, _vp],
     "tvr_nccl_all_gather": [_vp, _vp, _i64, _i32, _vp, _vp],
     "tvr_nccl_comm_destroy": [_vp],

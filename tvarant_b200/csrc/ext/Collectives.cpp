@@ -48,11 +48,13 @@ std::string nccl_unique_id() {
   return id;
 }
 
-int64_t nccl_init(int64_t nranks, int64_t rank, const std::string& id, int64_t device) {
+int64_t nccl_init(int64_t nranks, int64_t rank, const std::string& id, int64_t device,
+                  int64_t max_ctas) {
   TORCH_CHECK(id.size() == 128, "nccl_init: unique id must be 128 bytes");
   void* comm = nullptr;
-  TVR_TRY(tvr_nccl_comm_init(&comm, static_cast<int>(nranks), id.data(), static_cast<int>(rank),
-                             static_cast<int>(device)));
+  TVR_TRY(tvr_nccl_comm_init_ctas(&comm, static_cast<int>(nranks), id.data(),
+                                  static_cast<int>(rank), static_cast<int>(device),
+                                  static_cast<int>(max_ctas)));
   std::lock_guard<std::mutex> lock(g_comm_mutex);
   g_comms.push_back(comm);
   return static_cast<int64_t>(g_comms.size() - 1);

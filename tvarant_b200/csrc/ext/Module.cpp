@@ -17,7 +17,8 @@
 
 namespace tvarant {
 std::string nccl_unique_id();
-int64_t nccl_init(int64_t nranks, int64_t rank, const std::string& id, int64_t device);
+int64_t nccl_init(int64_t nranks, int64_t rank, const std::string& id, int64_t device,
+                  int64_t max_ctas);
 void nccl_destroy(int64_t handle, bool abort);
 void all_gather(const at::Tensor& src, at::Tensor& dst, int64_t comm);
 }  // namespace tvarant
@@ -72,6 +73,19 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     return reinterpret_cast<uintptr_t>(
         tvarant::stream_handle(static_cast<c10::DeviceIndex>(resolve(device)), id));
   });
+  m.def("sm_count", [](int device) {
+    int v = 0;
+    TVR_TRY(tvr_device_sm_count(resolve(device), &v));
+    return v;
+  }, py::arg("device") = -1);
+  m.def("set_gemm_sm_limit", [](int device, int max_sms) {
+    TVR_TRY(tvr_set_gemm_sm_limit(resolve(device), max_sms));
+  });
+  m.def("gemm_sm_limit", [](int device) {
+    int v = 0;
+    TVR_TRY(tvr_get_gemm_sm_limit(resolve(device), &v));
+    return v;
+  });
   m.def("current_stream_handle",
         []() { return reinterpret_cast<uintptr_t>(tvarant::current_stream_handle()); });
 
@@ -96,9 +110,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     return a != 0;
   });
   m.def("nccl_unique_id", []() { return py::bytes(tvarant::nccl_unique_id()); });
-  m.def("nccl_init", [](int64_t nranks, int64_t rank, py::bytes id, int device) {
-    return tvarant::nccl_init(nranks, rank, std::string(id), resolve(device));
-  }, py::arg("nranks"), py::arg("rank"), py::arg("unique_id"), py::arg("device") = -1);
+  m.def("nccl_init", [](int64_t nranks, int64_t rank, py::bytes id, int device, int64_t max_ctas) {
+    return tvarant::nccl_init(nranks, rank, std::string(id), resolve(device), max_ctas);
+  }, py::arg("nranks"), py::arg("rank"), py::arg("unique_id"), py::arg("device") = -1,
+     py::arg("max_ctas") = 0);
   m.def("nccl_destroy", &tvarant::nccl_destroy, py::arg("comm"), py::arg("abort") = false);
   m.def("all_gather", [](const at::Tensor& src, at::Tensor& dst, int64_t comm) {
     tvarant::all_gather(src, dst, comm);

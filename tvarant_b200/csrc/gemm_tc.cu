@@ -30,6 +30,7 @@
 // No TMA load uses cluster multicast.
 #include "internal.h"
 
+#include <atomic>
 #include <mutex>
 
 #include "gemm_common.cuh"
@@ -596,6 +597,14 @@ int split_operand(const float* src, float* hi, float* lo, int64_t rows, int64_t 
   return TVR_OK;
 }
 
+// Per-device cap on the persistent kernel's grid (tvr_set_gemm_sm_limit).
+std::atomic<int> g_sm_limit[64];
+
+int grid_sms(int dev, int sms) {
+  const int lim = g_sm_limit[dev & 63].load(std::memory_order_relaxed);
+  return lim > 0 && lim < sms ? lim : sms;
+}
+
 }  // namespace tc
 
 int gemm_tcgen05(const float* a, const float* b, const float* bias, float* c, int64_t m,
@@ -732,7 +741,7 @@ int gemm_tcgen05(const float* a, const float* b, const float* bias, float* c, in
   if (units > 0x7fffffff) return TVR_ERR_UNSUPPORTED;
   p.total_units = static_cast<int>(units);
   p.status = device_status_ptr(dev);
-  const int grid = static_cast<int>(std::min<int64_t>(units, sms));
+  const int grid = static_cast<int>(std::min<int64_t>(units, grid_sms(dev, sms)));
   const bool b_nmajor = !trans_b;
   switch (bn) {
     case 256: rc = launch_bn<256>(p, split3, b_nmajor, grid, stream, dev); break;
@@ -797,7 +806,7 @@ int gemm_tcgen05_swiglu(const float* x, const float* wg, const float* wu, float*
   if (units > 0x7fffffff) return TVR_ERR_UNSUPPORTED;
   p.total_units = static_cast<int>(units);
   p.status = device_status_ptr(dev);
-  const int grid = static_cast<int>(std::min<int64_t>(units, sms));
+  const int grid = static_cast<int>(std::min<int64_t>(units, tc::grid_sms(dev, sms)));
   return launch_kernel<256, false, false, true>(p, grid, stream, dev);
 }
 
@@ -977,4 +986,17 @@ extern "C" int tvr_gemm_bias_act_noalloc(const float* a, const float* b, const f
   }
   return gemm_simt(a, b, bias, c, m, n, k, lda, ldb, ldc, 1, 0, 0, 0, alpha, beta, act,
                    trans_b != 0, s);
+}
+
+extern "C" int tvr_set_gemm_sm_limit(int device, int max_sms) {
+  TVR_CHECK(device >= 0 && device < 64, "tvr_set_gemm_sm_limit: device %d out of range", device);
+  TVR_CHECK(max_sms >= 0, "tvr_set_gemm_sm_limit: negative limit");
+  tvr::tc::g_sm_limit[device].store(max_sms, std::memory_order_relaxed);
+  return TVR_OK;
+}
+
+extern "C" int tvr_get_gemm_sm_limit(int device, int* max_sms) {
+  TVR_CHECK(device >= 0 && device < 64 && max_sms != nullptr, "tvr_get_gemm_sm_limit: bad argument");
+  *max_sms = tvr::tc::g_sm_limit[device].load(std::memory_order_relaxed);
+  return TVR_OK;
 }

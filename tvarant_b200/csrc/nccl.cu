@@ -9,7 +9,9 @@
 
 #include <dlfcn.h>
 
+#include <climits>
 #include <cstdlib>
+#include <cstring>
 #include <mutex>
 
 namespace tvr {
@@ -21,9 +23,34 @@ struct NcclId {
   char internal[128];
 };
 
+// Layout of ncclConfig_t as NCCL 2.28 defines it (the struct is part of
+// NCCL's ABI: size, magic and version lead, then the tunable fields).
+struct NcclConfig {
+  size_t size;
+  unsigned int magic;
+  unsigned int version;
+  int blocking;
+  int cgaClusterSize;
+  int minCTAs;
+  int maxCTAs;
+  const char* netName;
+  int splitShare;
+  int trafficClass;
+  const char* commName;
+  int collnetEnable;
+  int CTAPolicy;
+  int shrinkShare;
+  int nvlsCTAs;
+  int nChannelsPerNetPeer;
+  int nvlinkCentricSched;
+};
+constexpr int kNcclUndef = INT_MIN;
+
 struct NcclApi {
   nccl_result (*getUniqueId)(NcclId*) = nullptr;
   nccl_result (*commInitRank)(nccl_comm*, int, NcclId, int) = nullptr;
+  nccl_result (*commInitRankConfig)(nccl_comm*, int, NcclId, int, NcclConfig*) = nullptr;
+  nccl_result (*getVersion)(int*) = nullptr;
   nccl_result (*allReduce)(const void*, void*, size_t, int, int, nccl_comm, cudaStream_t) = nullptr;
   nccl_result (*allGather)(const void*, void*, size_t, int, nccl_comm, cudaStream_t) = nullptr;
   nccl_result (*commDestroy)(nccl_comm) = nullptr;
@@ -57,6 +84,10 @@ void load() {
   sym("ncclCommAbort", &g_api.commAbort);
   sym("ncclGetErrorString", &g_api.getErrorString);
   g_ok = ok;
+  // optional: configured communicators (NCCL 2.14+; the 2.28 layout is used)
+  g_api.commInitRankConfig = reinterpret_cast<decltype(g_api.commInitRankConfig)>(
+      dlsym(h, "ncclCommInitRankConfig"));
+  g_api.getVersion = reinterpret_cast<decltype(g_api.getVersion)>(dlsym(h, "ncclGetVersion"));
 }
 
 const NcclApi* api() {
@@ -116,6 +147,40 @@ int tvr_nccl_comm_init(void** comm, int nranks, const void* id128, int rank, int
   nccl_comm c = nullptr;
   nccl_result r = a->commInitRank(&c, nranks, id, rank);
   if (r != 0) return nccl_fail(a, r, "ncclCommInitRank");
+  *comm = c;
+  return TVR_OK;
+}
+
+int tvr_nccl_comm_init_ctas(void** comm, int nranks, const void* id128, int rank, int device,
+                            int max_ctas) {
+  TVR_CHECK(comm != nullptr && id128 != nullptr, "tvr_nccl_comm_init_ctas: null argument");
+  const NcclApi* a = api();
+  if (a == nullptr) return fail(TVR_ERR_NCCL, "NCCL library not found");
+  int version = 0;
+  if (max_ctas <= 0 || a->commInitRankConfig == nullptr || a->getVersion == nullptr ||
+      a->getVersion(&version) != 0 || version < 22800) {
+    return tvr_nccl_comm_init(comm, nranks, id128, rank, device);
+  }
+  TVR_CHECK(nranks > 0 && rank >= 0 && rank < nranks, "tvr_nccl_comm_init_ctas: bad rank %d of %d",
+            rank, nranks);
+  int rc = tvr_set_device(device);
+  if (rc != TVR_OK) return rc;
+  NcclConfig cfg;
+  cfg.size = sizeof(NcclConfig);
+  cfg.magic = 0xcafebeef;
+  cfg.version = static_cast<unsigned int>(version);
+  cfg.blocking = cfg.cgaClusterSize = cfg.minCTAs = kNcclUndef;
+  cfg.maxCTAs = max_ctas;
+  cfg.netName = nullptr;
+  cfg.splitShare = cfg.trafficClass = kNcclUndef;
+  cfg.commName = nullptr;
+  cfg.collnetEnable = cfg.CTAPolicy = cfg.shrinkShare = cfg.nvlsCTAs = kNcclUndef;
+  cfg.nChannelsPerNetPeer = cfg.nvlinkCentricSched = kNcclUndef;
+  NcclId id;
+  memcpy(&id, id128, sizeof(id));
+  nccl_comm c = nullptr;
+  nccl_result r = a->commInitRankConfig(&c, nranks, id, rank, &cfg);
+  if (r != 0) return nccl_fail(a, r, "ncclCommInitRankConfig");
   *comm = c;
   return TVR_OK;
 }

@@ -58,10 +58,14 @@ class Communicator:
     rank: int
     world: int
 
+    max_ctas: int = 0
+
     @classmethod
-    def from_process_group(cls, device: int) -> "Communicator":
+    def from_process_group(cls, device: int, max_ctas: int = 32) -> "Communicator":
         """Creates the communicator of the current torch.distributed group; the
-        NCCL unique id travels over that group (gloo / TCPStore)."""
+        NCCL unique id travels over that group (gloo / TCPStore).  NCCL's
+        kernels are limited to ``max_ctas`` CTAs (0: NCCL's choice) so that
+        they fit beside GEMMs that leave that many SMs free."""
         import torch.distributed as dist
 
         from tvarant_b200 import _C
@@ -69,8 +73,8 @@ class Communicator:
         rank, world = dist.get_rank(), dist.get_world_size()
         box = [_C.nccl_unique_id() if rank == 0 else None]
         dist.broadcast_object_list(box, src=0)
-        handle = _C.nccl_init(world, rank, box[0], device)
-        return cls(handle, rank, world)
+        handle = _C.nccl_init(world, rank, box[0], device, max_ctas)
+        return cls(handle, rank, world, max_ctas)
 
     def all_reduce_(self, t: torch.Tensor) -> torch.Tensor:
         return torch.ops.tvarant.all_reduce_(t, self.handle)
@@ -122,6 +126,20 @@ class TPMLPStack:
                 x = mlp_layer(x, wg, wu, wd)
             return x
         device = x.device.index or 0
+        # The persistent GEMM otherwise holds every SM and the all-reduce of
+        # chunk i would wait for the GEMMs of chunk i+1 instead of overlapping
+        # them: leave NCCL's CTAs their SMs while the stack runs.
+        from tvarant_b200 import _C
+
+        prev_limit = _C.gemm_sm_limit(device)
+        if self.comm.max_ctas > 0:
+            _C.set_gemm_sm_limit(device, max(1, _C.sm_count(device) - self.comm.max_ctas))
+        try:
+            return self._forward_tp(x, device)
+        finally:
+            _C.set_gemm_sm_limit(device, prev_limit)
+
+    def _forward_tp(self, x: torch.Tensor, device: int) -> torch.Tensor:
         comm_stream = self._comm_streams(device)
         compute = torch.tvarant.current_stream(device)
         parts = list(x.split((x.shape[0] + self.chunks - 1) // self.chunks, dim=0))

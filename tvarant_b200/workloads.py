@@ -183,7 +183,7 @@ def _mlp(args, rank, world, local_rank):
     torch.set_float32_matmul_precision("high" if args.mode == "tf32" else "highest")
     dev = f"tvarant:{local_rank}"
     layers = build_stack(rank, world, dev, layers=args.layers)
-    comm = Communicator.from_process_group(local_rank) if world > 1 else None
+    comm = Communicator.from_process_group(local_rank, args.nccl_ctas) if world > 1 else None
     stack = TPMLPStack(layers, comm, chunks=args.chunks if world > 1 else 1)
     g = torch.Generator().manual_seed(7)
     x_host = torch.randn(TOKENS, D_MODEL, generator=g)
@@ -250,6 +250,7 @@ def _mlp(args, rank, world, local_rank):
         "config": {"workload": f"Llama-7B-shaped gated-SiLU MLP stack, {args.layers} layers, "
                                f"d_model {D_MODEL}, d_ff {D_FF}, {TOKENS} tokens, TP x{world}",
                    "parallelism": f"tp{world}", "chunks": stack.chunks,
+                   "nccl_max_ctas": args.nccl_ctas if world > 1 else None,
                    "cuda_graph": not args.no_graph,
                    "eager_tokens_per_s": TOKENS / (eager_ms / 1e3),
                    "layer_ms_one_rank_gemms": layer_ms,
