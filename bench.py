@@ -480,7 +480,7 @@ def run_gemm(args, rank, world, local_rank) -> dict | None:
         "clocks": clocks.summary(),
         "device_status": status,
     }
-    if not args.no_cpu_baseline:
+    if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline_gemm()
     return line
 

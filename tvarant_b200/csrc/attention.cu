@@ -75,6 +75,15 @@ __device__ __forceinline__ uint64_t desc_v(uint32_t saddr) {
   return make_desc(saddr, 32 * 128, 512, 1);
 }
 
+// 2^x with the MUFU approximation (ex2.approx.ftz: about 2 ulp, flushes
+// subnormal results to 0, ex2(-inf) = 0), well inside the TF32 tolerance
+// of the attention output.
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 __device__ __forceinline__ void st_shared4(uint32_t addr, float a, float b, float c, float d) {
   asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(a), "f"(b), "f"(c),
                "f"(d)
@@ -269,42 +278,40 @@ __global__ void __launch_bounds__(THREADS, 1) attn_fwd_kernel(const __grid_const
       int key_end = min(p.seq_k, key0 + BN);
       if (p.causal) key_end = min(key_end, qidx + 1);
       const int nvis = key_end - key0;  // may be <= 0 for padding rows
-      float v[32];
-      float mx = -INFINITY;
+      // the row's 128 scores: four TMEM loads in flight, one wait
+      float sc[BN];
 #pragma unroll
-      for (int c = 0; c < BN / 32; ++c) {
-        tmem_load_32_async(srow + 32 * c, v);
-        tmem_wait_loads();
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          if (32 * c + i < nvis) mx = fmaxf(mx, v[i] * p.scale_log2);
-        }
-      }
-      const float m_new = fmaxf(m, mx);
-      const float m_use = m_new == -INFINITY ? 0.f : m_new;
-      const float alpha = exp2f(m - m_use);
-      float sum = 0.f;
-#pragma unroll
-      for (int c = 0; c < BN / 32; ++c) {
-        tmem_load_32_async(srow + 32 * c, v);
-        tmem_wait_loads();
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const float e = (32 * c + i < nvis) ? exp2f(v[i] * p.scale_log2 - m_use) : 0.f;
-          v[i] = e;
-          sum += e;
-        }
-        const uint32_t row = sp + c * ATOM + t * 128;
-#pragma unroll
-        for (int cc = 0; cc < 8; ++cc) {
-          st_shared4(row + ((cc ^ (t & 7)) << 4), v[4 * cc], v[4 * cc + 1], v[4 * cc + 2],
-                     v[4 * cc + 3]);
-        }
-      }
+      for (int c = 0; c < BN / 32; ++c) tmem_load_32_async(srow + 32 * c, sc + 32 * c);
+      tmem_wait_loads();
       // scores consumed: the buffer may take S_{j+2}
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(s_empty + 8 * sb);
+      float mx = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < BN; ++i) {
+        if (i < nvis) mx = fmaxf(mx, sc[i] * p.scale_log2);
+      }
+      // scores are scaled inside exp2: x * scale_log2 - m in one FMA
+      const float m_new = fmaxf(m, mx);
+      const float m_use = m_new == -INFINITY ? 0.f : m_new;
+      const float alpha = ex2(m - m_use);
+      float sum = 0.f;
+#pragma unroll
+      for (int i = 0; i < BN; ++i) {
+        const float e = i < nvis ? ex2(fmaf(sc[i], p.scale_log2, -m_use)) : 0.f;
+        sc[i] = e;
+        sum += e;
+      }
+#pragma unroll
+      for (int c = 0; c < BN / 32; ++c) {
+        const uint32_t row = sp + c * ATOM + t * 128;
+#pragma unroll
+        for (int cc = 0; cc < 8; ++cc) {
+          const float* q4 = sc + 32 * c + 4 * cc;
+          st_shared4(row + ((cc ^ (t & 7)) << 4), q4[0], q4[1], q4[2], q4[3]);
+        }
+      }
       // P visible to the tensor core
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       __syncwarp();
@@ -317,13 +324,12 @@ __global__ void __launch_bounds__(THREADS, 1) attn_fwd_kernel(const __grid_const
         break;
       }
       tc_fence_after();
+      float pv[D];
 #pragma unroll
-      for (int c = 0; c < D / 32; ++c) {
-        tmem_load_32_async(tmem + lane_off + PV_COL + 32 * c, v);
-        tmem_wait_loads();
+      for (int c = 0; c < D / 32; ++c) tmem_load_32_async(tmem + lane_off + PV_COL + 32 * c, pv + 32 * c);
+      tmem_wait_loads();
 #pragma unroll
-        for (int i = 0; i < 32; ++i) o[32 * c + i] = o[32 * c + i] * alpha + v[i];
-      }
+      for (int i = 0; i < D; ++i) o[i] = fmaf(o[i], alpha, pv[i]);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(pv_empty);
