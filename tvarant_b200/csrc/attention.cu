@@ -6,20 +6,24 @@
 // F.scaled_dot_product_attention on the tvarant device (TF32 mode).
 //
 // One CTA per (128-query tile, batch x head).  Head dimension 64.
-//   warp 0     TMA producer: the Q tile once, then K and V tiles of 128 keys
-//              into a 2-deep ring, straight from strided [B, H, S, 64]
-//              views (no head-split copies);
-//   warp 1     TMEM owner and MMA issuer: S_j = Q K_j^T (M=128, N=128,
-//              K=64) into one of two TMEM score buffers, issued one block
-//              ahead of the softmax; PV_j = P_j V_j (M=128, N=64, K=128)
-//              with V read as an N-major operand;
+//   warp 0     TMA producers: lane 0 loads the Q tile once and the K tile of
+//              each block of 64 keys, lane 1 the V tiles (two buffers each),
+//              straight from strided [B, H, S, 64] views (no head-split
+//              copies);
+//   warp 1     TMEM owner; lane 0 issues S_j = Q K_j^T (M=128, N=64, K=64)
+//              into one of two TMEM score buffers, ahead of the softmax;
+//              lane 1 issues PV_j = P_j V_j (M=128, N=64, K=64) into one of
+//              two TMEM buffers, V read as an N-major operand;
 //   warps 2-5  one thread per query row: online softmax in the log2 domain
-//              over the row's 128 scores (read twice from TMEM: maximum,
-//              then exp2 and the row sum), P written to shared memory in the
-//              128-byte-swizzled K-major layout the MMA reads, and the
-//              output row kept in 64 registers: O = O * exp2(m_old - m_new)
-//              + PV_j.  At the end O / l is stored and the log-sum-exp
-//              (natural log) is written.
+//              over the row's 64 scores of a block (two TMEM loads in flight,
+//              one wait), P_j written to one of two shared-memory tiles in the
+//              128-byte-swizzled K-major layout the MMA reads, and the output
+//              row kept in 64 registers.  The output update trails the
+//              softmax by one block — O = O * exp2(m_{j-2} - m_{j-1}) +
+//              PV_{j-1} runs after the softmax of block j — so the tensor core
+//              computes PV_{j-1} and S_{j+1} while the softmax of block j runs.
+//              At the end O / l is stored and the log-sum-exp (natural log) is
+//              written.
 // Causal masking follows PyTorch's is_causal (key index <= query index,
 // aligned at the top-left); keys at or beyond seq_k are masked.  Every
 // mbarrier wait is bounded (status word + abort flag), as in gemm_tc.  No TMA
@@ -40,25 +44,27 @@ using namespace tc;
 
 constexpr int D = 64;                    // head dimension
 constexpr int BM = 128;                  // queries per CTA (MMA M)
-constexpr int BN = 128;                  // keys per block
-constexpr int ATOM = 128 * 128;          // one [128 rows x 128 B] swizzle block
+constexpr int BN = 64;                   // keys per block
+constexpr int Q_ATOM = BM * 128;         // [128 query rows x 128 B] swizzle block
+constexpr int K_ATOM = BN * 128;         // [64 key rows x 128 B]
 constexpr int Q_BYTES = BM * D * 4;      // D/32 atoms
 constexpr int K_BYTES = BN * D * 4;      // D/32 atoms
-constexpr int V_KB_BYTES = 32 * D * 4;   // one 32-key k-block of V: D/32 atoms of [32 x 128 B]
-constexpr int V_BYTES = BN * D * 4;      // BN/32 k-blocks
-constexpr int P_BYTES = BM * BN * 4;     // BN/32 atoms
-constexpr int STAGES = 2;
+constexpr int V_ATOM = BN * 128;         // one 32-wide slice of the head dimension: [64 keys x 128 B]
+constexpr int V_BYTES = BN * D * 4;      // D/32 atoms
+constexpr int P_BYTES = BM * BN * 4;     // BN/32 atoms of [128 x 128 B]
+constexpr int STAGES = 2;                // K, V, P and both TMEM accumulators are double-buffered
 constexpr int THREADS = 192;
-constexpr uint32_t TMEM_COLS = 512;      // S buffers at 0 and 128, PV at 256
-constexpr uint32_t PV_COL = 256;
-constexpr int BAR_BYTES = 8 * 16;
-constexpr int SMEM_BYTES = 1024 + Q_BYTES + STAGES * (K_BYTES + V_BYTES) + P_BYTES + BAR_BYTES;
+constexpr uint32_t TMEM_COLS = 256;      // S buffers at 0 and 64, PV buffers at 128 and 192
+constexpr uint32_t PV_COL = 2 * BN;
+constexpr int BAR_BYTES = 8 * 24;
+constexpr int SMEM_BYTES =
+    1024 + Q_BYTES + STAGES * (K_BYTES + V_BYTES + P_BYTES) + BAR_BYTES;
 static_assert(SMEM_BYTES <= 232448, "shared memory budget");
 
 struct Params {
   CUtensorMap tma_q;  // {D, seq_q, heads, batch}, box {32, 128}
-  CUtensorMap tma_k;  // {D, seq_k, heads, batch}, box {32, 128}
-  CUtensorMap tma_v;  // {D, seq_k, heads, batch}, box {32, 32}, 32-byte-atom swizzle
+  CUtensorMap tma_k;  // {D, seq_k, heads, batch}, box {32, 64}
+  CUtensorMap tma_v;  // {D, seq_k, heads, batch}, box {32, 64}, 32-byte-atom swizzle
   float* out;
   int64_t o_sb, o_sh, o_ss;  // output element strides (last dimension contiguous)
   float* lse;                // [batch, heads, seq_q] or null
@@ -68,11 +74,11 @@ struct Params {
   int* status;
 };
 
-// N-major V operand: 32-wide atoms (of the head dimension) [32 keys x 128 B]
-// placed V_KB/2 bytes apart within a k-block; 32-byte chunks swizzled over
-// 4 rows, so K groups of 4 keys are 512 B apart.
+// N-major V operand: 32-wide atoms of the head dimension, each [64 keys x
+// 128 B] and V_ATOM bytes apart (leading offset); 32-byte chunks swizzled
+// over 4 rows, so K groups of 4 keys are 512 B apart (stride offset).
 __device__ __forceinline__ uint64_t desc_v(uint32_t saddr) {
-  return make_desc(saddr, 32 * 128, 512, 1);
+  return make_desc(saddr, V_ATOM, 512, 1);
 }
 
 // 2^x with the MUFU approximation (ex2.approx.ftz: about 2 ulp, flushes
@@ -93,26 +99,26 @@ __device__ __forceinline__ void st_shared4(uint32_t addr, float a, float b, floa
 __global__ void __launch_bounds__(THREADS, 1) attn_fwd_kernel(const __grid_constant__ Params p) {
   extern __shared__ uint8_t smem_raw[];
   __shared__ int s_abort;
+  __shared__ uint64_t s_drain;
+  __shared__ uint32_t s_tmem;
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
   const uint32_t sq = base;
-  const uint32_t sk = sq + Q_BYTES;                  // [STAGES][K_BYTES]
-  const uint32_t sv = sk + STAGES * K_BYTES;         // [STAGES][V_BYTES]
-  const uint32_t sp = sv + STAGES * V_BYTES;         // P tile
-  // mbarriers, one 8-byte slot each
-  const uint32_t bar = sp + P_BYTES;
-  const uint32_t q_full = bar;              // slot 0
-  const uint32_t k_full = bar + 8;          // slots 1-2, one per stage
-  const uint32_t k_empty = bar + 24;        // slots 3-4
-  const uint32_t v_full = bar + 40;         // slots 5-6
-  const uint32_t v_empty = bar + 56;        // slots 7-8
-  const uint32_t s_full = bar + 72;         // slots 9-10, one per score buffer
-  const uint32_t s_empty = bar + 88;        // slots 11-12
-  const uint32_t p_full = bar + 104;        // slot 13
-  const uint32_t pv_full = bar + 112;       // slot 14
-  const uint32_t pv_empty = bar + 120;      // slot 15
-  __shared__ uint64_t s_drain;
-  __shared__ uint32_t s_tmem;
+  const uint32_t sk = sq + Q_BYTES;                 // [2] K tiles
+  const uint32_t sv = sk + STAGES * K_BYTES;        // [2] V tiles
+  const uint32_t sp = sv + STAGES * V_BYTES;        // [2] P tiles
+  // mbarriers, one 8-byte slot each; [2] = one per buffer
+  const uint32_t bar = sp + STAGES * P_BYTES;
+  const uint32_t q_full = bar;
+  const uint32_t k_full = bar + 8;       // [2]
+  const uint32_t k_empty = bar + 24;     // [2]
+  const uint32_t v_full = bar + 40;      // [2]
+  const uint32_t v_empty = bar + 56;     // [2]
+  const uint32_t s_full = bar + 72;      // [2]
+  const uint32_t s_empty = bar + 88;     // [2]
+  const uint32_t p_full = bar + 104;     // [2]
+  const uint32_t pv_full = bar + 120;    // [2]
+  const uint32_t pv_empty = bar + 136;   // [2]
   const uint32_t drain = smem_u32(&s_drain);
 
   const int warp = threadIdx.x >> 5;
@@ -129,18 +135,18 @@ __global__ void __launch_bounds__(THREADS, 1) attn_fwd_kernel(const __grid_const
   if (threadIdx.x == 0) {
     s_abort = 0;
     mbar_init(q_full, 1);
-    for (int s = 0; s < 2; ++s) {
-      mbar_init(k_full + 8 * s, 1);
-      mbar_init(k_empty + 8 * s, 1);
-      mbar_init(v_full + 8 * s, 1);
-      mbar_init(v_empty + 8 * s, 1);
-      mbar_init(s_full + 8 * s, 1);
-      mbar_init(s_empty + 8 * s, 4);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(k_full + 8 * i, 1);
+      mbar_init(k_empty + 8 * i, 1);
+      mbar_init(v_full + 8 * i, 1);
+      mbar_init(v_empty + 8 * i, 1);
+      mbar_init(s_full + 8 * i, 1);
+      mbar_init(s_empty + 8 * i, 4);
+      mbar_init(p_full + 8 * i, 4);
+      mbar_init(pv_full + 8 * i, 1);
+      mbar_init(pv_empty + 8 * i, 4);
     }
-    mbar_init(p_full, 4);
-    mbar_init(pv_full, 1);
-    mbar_init(pv_empty, 4);
-    mbar_init(drain, 1);
+    mbar_init(drain, 2);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 1) {
@@ -156,102 +162,113 @@ __global__ void __launch_bounds__(THREADS, 1) attn_fwd_kernel(const __grid_const
   const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(&s_tmem);
 
   if (warp == 0) {
-    // ------------------------------ TMA producer ------------------------------
-    if (lane == 0) {
+    // ------------------------------ TMA producers ------------------------------
+    // lane 0: Q, then K_j into K buffer j & 1 once S_{j-2} has consumed it;
+    // lane 1: V_j into V buffer j & 1 once PV_{j-2} has consumed it.
+    if (lane < 2) {
+      const bool is_k = lane == 0;
+      const uint32_t full = is_k ? k_full : v_full;
+      const uint32_t empty = is_k ? k_empty : v_empty;
       bool ok = true;
-      uint32_t k_issued = 0, v_issued = 0, k_par = 0, v_par = 0;
-      mbar_expect_tx(q_full, Q_BYTES);
-      for (int a = 0; a < D / 32; ++a) tma_load_4d(sq + a * ATOM, &p.tma_q, q_full, 32 * a, q0, h, b);
-      for (int j = 0; ok && j < nkb; ++j) {
+      int issued = 0;
+      if (is_k) {
+        mbar_expect_tx(q_full, Q_BYTES);
+        for (int a = 0; a < D / 32; ++a) tma_load_4d(sq + a * Q_ATOM, &p.tma_q, q_full, 32 * a, q0, h, b);
+      }
+      for (int j = 0; j < nkb; ++j) {
         const int st = j & 1;
-        const uint32_t ph = (j >> 1) & 1;
-        if (!mbar_wait(k_empty + 8 * st, ph ^ 1u, abort_flag)) { ok = false; break; }
-        mbar_expect_tx(k_full + 8 * st, K_BYTES);
-        for (int a = 0; a < D / 32; ++a)
-          tma_load_4d(sk + st * K_BYTES + a * ATOM, &p.tma_k, k_full + 8 * st, 32 * a, j * BN, h, b);
-        k_issued |= 1u << st;
-        k_par = (k_par & ~(1u << st)) | (ph << st);
-        if (!mbar_wait(v_empty + 8 * st, ph ^ 1u, abort_flag)) { ok = false; break; }
-        mbar_expect_tx(v_full + 8 * st, V_BYTES);
-        for (int kb = 0; kb < BN / 32; ++kb)
+        if (j >= 2 && !mbar_wait(empty + 8 * st, ((j >> 1) - 1) & 1, abort_flag)) {
+          ok = false;
+          break;
+        }
+        const uint32_t fb = full + 8 * st;
+        if (is_k) {
+          mbar_expect_tx(fb, K_BYTES);
           for (int a = 0; a < D / 32; ++a)
-            tma_load_4d(sv + st * V_BYTES + kb * V_KB_BYTES + a * (32 * 128), &p.tma_v,
-                        v_full + 8 * st, 32 * a, j * BN + 32 * kb, h, b);
-        v_issued |= 1u << st;
-        v_par = (v_par & ~(1u << st)) | (ph << st);
+            tma_load_4d(sk + st * K_BYTES + a * K_ATOM, &p.tma_k, fb, 32 * a, j * BN, h, b);
+        } else {
+          mbar_expect_tx(fb, V_BYTES);
+          for (int a = 0; a < D / 32; ++a)
+            tma_load_4d(sv + st * V_BYTES + a * V_ATOM, &p.tma_v, fb, 32 * a, j * BN, h, b);
+        }
+        issued = j + 1;
       }
       if (!ok) {
         record_status(p.status, TVR_DEV_TIMEOUT_PRODUCER);
         *const_cast<volatile int*>(abort_flag) = 1;
       }
       // every issued load lands before the CTA may exit
-      if (!mbar_wait(q_full, 0, nullptr)) record_status(p.status, TVR_DEV_TIMEOUT_DRAIN);
-      for (int st = 0; st < 2; ++st) {
-        if ((k_issued >> st) & 1u)
-          if (!mbar_wait(k_full + 8 * st, (k_par >> st) & 1u, nullptr)) record_status(p.status, TVR_DEV_TIMEOUT_DRAIN);
-        if ((v_issued >> st) & 1u)
-          if (!mbar_wait(v_full + 8 * st, (v_par >> st) & 1u, nullptr)) record_status(p.status, TVR_DEV_TIMEOUT_DRAIN);
+      if (is_k && !mbar_wait(q_full, 0, nullptr)) record_status(p.status, TVR_DEV_TIMEOUT_DRAIN);
+      for (int j = max(0, issued - 2); j < issued; ++j) {
+        if (!mbar_wait(full + 8 * (j & 1), (j >> 1) & 1, nullptr)) record_status(p.status, TVR_DEV_TIMEOUT_DRAIN);
       }
     }
     __syncwarp();
   } else if (warp == 1) {
-    // ------------------------------ MMA issuer ------------------------------
-    if (lane == 0) {
+    // ------------------------------ MMA issuers ------------------------------
+    // Two threads issue independently, so that neither stream of MMAs waits
+    // behind the other's operands: lane 0 the scores S_i = Q K_i^T into score
+    // buffer i & 1 (free once the softmax of i-2 read it), lane 1 the products
+    // PV_j = P_j V_j into PV buffer j & 1 (free once the output update of j-2
+    // read it).  Each commits its own barriers and, at the end, the drain
+    // barrier (count 2) that TMEM release waits for.
+    if (lane < 2) {
       constexpr uint32_t idesc_s = idesc_tf32(BM, BN, false);
       constexpr uint32_t idesc_pv = idesc_tf32(BM, D, true);
-      bool ok = mbar_wait(q_full, 0, abort_flag);
-      bool issued = false;
-      // S_i = Q K_i^T into score buffer i & 1
-      auto issue_s = [&](int i) -> bool {
-        const int st = i & 1;
-        if (!mbar_wait(k_full + 8 * st, (i >> 1) & 1, abort_flag)) return false;
-        if (i >= 2 && !mbar_wait(s_empty + 8 * st, ((i >> 1) - 1) & 1, abort_flag)) return false;
-        tc_fence_after();
-        const uint32_t d = tmem + static_cast<uint32_t>(st * BN);
+      bool ok = true;
+      if (lane == 0) {
+        ok = mbar_wait(q_full, 0, abort_flag);
+        for (int i = 0; ok && i < nkb; ++i) {
+          const int sb = i & 1;
+          if (!mbar_wait(k_full + 8 * sb, (i >> 1) & 1, abort_flag) ||
+              (i >= 2 && !mbar_wait(s_empty + 8 * sb, ((i >> 1) - 1) & 1, abort_flag))) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t d = tmem + static_cast<uint32_t>(sb * BN);
 #pragma unroll
-        for (int x = 0; x < D / 8; ++x) {
-          const uint32_t off = (x >> 2) * ATOM + (x & 3) * 32;
-          mma_tf32(d, desc_kmajor(sq + off), desc_kmajor(sk + st * K_BYTES + off), idesc_s,
-                   x > 0 ? 1u : 0u);
+          for (int x = 0; x < D / 8; ++x) {
+            const uint32_t k32 = (x & 3) * 32;
+            mma_tf32(d, desc_kmajor(sq + (x >> 2) * Q_ATOM + k32),
+                     desc_kmajor(sk + sb * K_BYTES + (x >> 2) * K_ATOM + k32), idesc_s,
+                     x > 0 ? 1u : 0u);
+          }
+          mma_commit(k_empty + 8 * sb);
+          mma_commit(s_full + 8 * sb);
         }
-        mma_commit(k_empty + 8 * st);
-        mma_commit(s_full + 8 * st);
-        return true;
-      };
-      if (ok && nkb > 0) {
-        ok = issue_s(0);
-        issued = ok;
-      }
-      for (int j = 0; ok && j < nkb; ++j) {
-        if (j + 1 < nkb && !(ok = issue_s(j + 1))) break;
-        // PV_j = P_j V_j
-        const int st = j & 1;
-        if (!mbar_wait(p_full, j & 1, abort_flag) ||
-            !mbar_wait(v_full + 8 * st, (j >> 1) & 1, abort_flag) ||
-            (j >= 1 && !mbar_wait(pv_empty, (j - 1) & 1, abort_flag))) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
+      } else {
+        for (int j = 0; ok && j < nkb; ++j) {
+          const int pb = j & 1;
+          if (!mbar_wait(p_full + 8 * pb, (j >> 1) & 1, abort_flag) ||
+              !mbar_wait(v_full + 8 * pb, (j >> 1) & 1, abort_flag) ||
+              (j >= 2 && !mbar_wait(pv_empty + 8 * pb, ((j >> 1) - 1) & 1, abort_flag))) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t d = tmem + PV_COL + static_cast<uint32_t>(pb * D);
+          const uint32_t pt = sp + pb * P_BYTES;
 #pragma unroll
-        for (int x = 0; x < BN / 8; ++x) {
-          const int kb = x >> 2, kk = x & 3;
-          mma_tf32(tmem + PV_COL, desc_kmajor(sp + kb * ATOM + kk * 32),
-                   desc_v(sv + st * V_BYTES + kb * V_KB_BYTES + kk * 1024), idesc_pv,
-                   x > 0 ? 1u : 0u);
+          for (int x = 0; x < BN / 8; ++x) {
+            // K step x covers keys 8x .. 8x+7: P atom x / 4 (32 keys), +32 B
+            // per step inside it; V rows 8x.., 8 rows of 128 B = 1024 B per step
+            mma_tf32(d, desc_kmajor(pt + (x >> 2) * Q_ATOM + (x & 3) * 32),
+                     desc_v(sv + pb * V_BYTES + x * 1024), idesc_pv, x > 0 ? 1u : 0u);
+          }
+          mma_commit(v_empty + 8 * pb);
+          mma_commit(pv_full + 8 * pb);
         }
-        mma_commit(v_empty + 8 * st);
-        mma_commit(pv_full);
       }
       if (!ok) {
         record_status(p.status, TVR_DEV_TIMEOUT_MMA);
         *const_cast<volatile int*>(abort_flag) = 1;
       }
-      if (issued) {
-        mma_commit(drain);
-        if (!mbar_wait(drain, 0, nullptr)) record_status(p.status, TVR_DEV_TIMEOUT_DRAIN);
-      }
+      // arrives once every MMA this thread issued has retired (at once if none)
+      mma_commit(drain);
     }
+    __syncwarp();
+    if (lane == 0 && !mbar_wait(drain, 0, nullptr)) record_status(p.status, TVR_DEV_TIMEOUT_DRAIN);
     __syncwarp();
   } else {
     // ------------------------------ softmax rows ------------------------------
@@ -263,7 +280,26 @@ __global__ void __launch_bounds__(THREADS, 1) attn_fwd_kernel(const __grid_const
 #pragma unroll
     for (int i = 0; i < D; ++i) o[i] = 0.f;
     float m = -INFINITY, l = 0.f;
+    float alpha_prev = 1.f;  // rescale factor that goes with PV_{j-1}
     bool ok = true;
+    // O = O * alpha + PV_j, then PV buffer j & 1 is free again
+    auto update_o = [&](int j, float alpha) -> bool {
+      const bool got = mbar_wait(pv_full + 8 * (j & 1), (j >> 1) & 1, abort_flag);
+      if (!__all_sync(0xffffffffu, got)) return false;
+      tc_fence_after();
+      float pv[D];
+#pragma unroll
+      for (int c = 0; c < D / 32; ++c)
+        tmem_load_32_async(tmem + lane_off + PV_COL + static_cast<uint32_t>((j & 1) * D + 32 * c),
+                           pv + 32 * c);
+      tmem_wait_loads();
+#pragma unroll
+      for (int i = 0; i < D; ++i) o[i] = fmaf(o[i], alpha, pv[i]);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(pv_empty + 8 * (j & 1));
+      return true;
+    };
     for (int j = 0; j < nkb; ++j) {
       const int sb = j & 1;
       const bool got = mbar_wait(s_full + 8 * sb, (j >> 1) & 1, abort_flag);
@@ -278,7 +314,7 @@ __global__ void __launch_bounds__(THREADS, 1) attn_fwd_kernel(const __grid_const
       int key_end = min(p.seq_k, key0 + BN);
       if (p.causal) key_end = min(key_end, qidx + 1);
       const int nvis = key_end - key0;  // may be <= 0 for padding rows
-      // the row's 128 scores: four TMEM loads in flight, one wait
+      // the row's BN scores: all TMEM loads in flight, one wait
       float sc[BN];
 #pragma unroll
       for (int c = 0; c < BN / 32; ++c) tmem_load_32_async(srow + 32 * c, sc + 32 * c);
@@ -303,9 +339,11 @@ __global__ void __launch_bounds__(THREADS, 1) attn_fwd_kernel(const __grid_const
         sc[i] = e;
         sum += e;
       }
+      // P tile j & 1 is free: PV_{j-2} was consumed by the output update of j-2
+      const uint32_t pt = sp + sb * P_BYTES;
 #pragma unroll
       for (int c = 0; c < BN / 32; ++c) {
-        const uint32_t row = sp + c * ATOM + t * 128;
+        const uint32_t row = pt + c * Q_ATOM + t * 128;
 #pragma unroll
         for (int cc = 0; cc < 8; ++cc) {
           const float* q4 = sc + 32 * c + 4 * cc;
@@ -315,25 +353,17 @@ __global__ void __launch_bounds__(THREADS, 1) attn_fwd_kernel(const __grid_const
       // P visible to the tensor core
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       __syncwarp();
-      if (lane == 0) mbar_arrive(p_full);
+      if (lane == 0) mbar_arrive(p_full + 8 * sb);
       l = l * alpha + sum;
       m = m_new;
-      const bool got_pv = mbar_wait(pv_full, j & 1, abort_flag);
-      if (!__all_sync(0xffffffffu, got_pv)) {
+      // the previous block's output contribution, while PV_j runs
+      if (j >= 1 && !update_o(j - 1, alpha_prev)) {
         ok = false;
         break;
       }
-      tc_fence_after();
-      float pv[D];
-#pragma unroll
-      for (int c = 0; c < D / 32; ++c) tmem_load_32_async(tmem + lane_off + PV_COL + 32 * c, pv + 32 * c);
-      tmem_wait_loads();
-#pragma unroll
-      for (int i = 0; i < D; ++i) o[i] = fmaf(o[i], alpha, pv[i]);
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(pv_empty);
+      alpha_prev = alpha;
     }
+    if (ok && nkb > 0 && !update_o(nkb - 1, alpha_prev)) ok = false;
     if (!ok) {
       if (lane == 0) {
         record_status(p.status, TVR_DEV_TIMEOUT_EPILOGUE);
@@ -422,7 +452,7 @@ extern "C" int tvr_attention_fwd(const float* q, const float* k, const float* v,
   };
   if ((rc = enc(&p.tma_q, q, seq_q, q_strides, BM, CU_TENSOR_MAP_SWIZZLE_128B)) != TVR_OK) return rc;
   if ((rc = enc(&p.tma_k, k, seq_k, k_strides, BN, CU_TENSOR_MAP_SWIZZLE_128B)) != TVR_OK) return rc;
-  if ((rc = enc(&p.tma_v, v, seq_k, v_strides, 32, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B)) != TVR_OK)
+  if ((rc = enc(&p.tma_v, v, seq_k, v_strides, BN, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B)) != TVR_OK)
     return rc;
   p.out = out;
   p.o_sb = o_strides[0];
