@@ -314,11 +314,58 @@ class GemmChain:
     def step_resident(self, torch):
         return self.next_model()(self.x, self.z)
 
+    # End-to-end steps with host buffers.  Inputs are copied in on one stream,
+    # the compiled model runs on the current stream and its output is copied
+    # out on a third; the device inputs are double-buffered, so step i+1's
+    # inputs cross PCIe towards the GPU while step i's output crosses back
+    # (the link is full duplex) and step i computes.  Every step still moves
+    # all of its inputs and its whole output inside the timed region.
+    def e2e_begin(self, torch):
+        """Orders the copy streams after the work queued so far (the start
+        event of a timed region)."""
+        if not hasattr(self, "s_in"):
+            self.s_in = torch.Stream(device="tvarant")
+            self.s_out = torch.Stream(device="tvarant")
+            self.x_dev = [torch.empty_like(self.x) for _ in range(2)]
+            self.z_dev = [torch.empty_like(self.z) for _ in range(2)]
+            pin = torch.cuda.is_available()
+            spare = torch.empty_like(self.out_host)
+            self.out_hosts = [self.out_host, spare.pin_memory() if pin else spare]
+            self.j = 0
+        self.consumed = [None, None]
+        start = torch.Event(device="tvarant")
+        start.record(torch.tvarant.current_stream())
+        self.s_in.wait_event(start)
+        self.s_out.wait_event(start)
+
+    def e2e_end(self, torch):
+        """Orders the current stream after both copy streams."""
+        compute = torch.tvarant.current_stream()
+        for s in (self.s_in, self.s_out):
+            ev = torch.Event(device="tvarant")
+            ev.record(s)
+            compute.wait_event(ev)
+
     def step_e2e(self, torch):
-        x = self.x_host.to("tvarant", non_blocking=True)
-        z = self.z_host.to("tvarant", non_blocking=True)
-        y = self.next_model()(x, z)
-        self.out_host.copy_(y, non_blocking=True)
+        k = self.j & 1
+        self.j += 1
+        compute = torch.tvarant.current_stream()
+        if self.consumed[k] is not None:
+            self.s_in.wait_event(self.consumed[k])  # step i-2 has read buffer k
+        with torch.tvarant.stream(self.s_in):
+            self.x_dev[k].copy_(self.x_host, non_blocking=True)
+            self.z_dev[k].copy_(self.z_host, non_blocking=True)
+            landed = torch.Event(device="tvarant")
+            landed.record(self.s_in)
+        compute.wait_event(landed)
+        y = self.next_model()(self.x_dev[k], self.z_dev[k])
+        done = torch.Event(device="tvarant")
+        done.record(compute)
+        self.consumed[k] = done
+        self.s_out.wait_event(done)
+        with torch.tvarant.stream(self.s_out):
+            self.out_hosts[k].copy_(y, non_blocking=True)
+        y.record_stream(self.s_out)
         return y
 
 
@@ -350,20 +397,36 @@ def _barrier(world: int):
         dist.barrier()
 
 
-def gemm_kernel_name(m: int, mode: str) -> tuple[str, str]:
-    """(kernel, bound) that ``tvr_gemm_bias_act`` runs for M rows of the sweep."""
+def gemm_kernel_name(m: int, mode: str, program_in_epilogue: bool = False) -> tuple[str, str]:
+    """(kernel, bound) that the GEMM of the sweep runs for M rows."""
     if mode == "3xtf32" and m <= 2:
         return "tvr::gemm_skinny_kernel (fp32 FMA GEMV)", "hbm"
     if m <= 128:
         return f"tvr::ws::gemm_ws_kernel ({mode}, weight streaming)", "hbm"
+    if program_in_epilogue:
+        return (f"tvr::tc::gemm_tc_kernel<256, {mode}, K-major B, PROG> "
+                "(abs(neg(exp(Y - Z))) in the epilogue)", "tensor")
     return f"tvr::tc::gemm_tc_kernel<256, {mode}, K-major B>", "tensor"
+
+
+def program_in_epilogue(m: int, fusions: dict, sms: int = 148) -> bool:
+    """Whether the compiled step is one tensor-core launch with the pointwise
+    program in its epilogue: the compiler fused the program into the GEMM
+    (tvarant::linear_pointwise) and the GEMM has enough 128 x 256 tiles
+    (4/5 of a wave) to run without split-K."""
+    tiles = -(-m // 128) * -(-N_DEFAULT // 256)
+    return bool(fusions.get("gemm_pointwise")) and m > 128 and tiles >= (sms * 4) // 5
 
 
 def measure_gemm_point(torch, m: int, mode: str, steps: int, warmup: int, world: int,
                        clocks=None) -> dict:
     """One point of the fused-GEMM sweep: the compiled linear+bias+SiLU +
     chain step (resident inputs), the GEMM launch alone back to back, and the
-    end-to-end step with host buffers.  Times are max over ranks."""
+    end-to-end step with host buffers.  Times are max over ranks.
+
+    When the compiler put the chain into the GEMM's epilogue, a step is that
+    one kernel: its time is the kernel's duration (back-to-back launches on
+    one stream), and the plain GEMM (linear_act alone) is timed beside it."""
     wl = GemmChain(torch, m, mode)
     Event = lambda: torch.Event(device="tvarant", enable_timing=True)  # noqa: E731
     for _ in range(warmup):
@@ -391,25 +454,38 @@ def measure_gemm_point(torch, m: int, mode: str, steps: int, warmup: int, world:
         torch.ops.tvarant.linear_act(wl.x, li.weight, li.bias, "silu", True)
     g1.record()
     g1.synchronize()
-    kernel_ms = g0.elapsed_time(g1) / steps
+    plain_gemm_ms = g0.elapsed_time(g1) / steps
     torch.tvarant.synchronize()
     _barrier(world)
     step_ms = _max_over_ranks(step_ms, world)
-    kernel_ms = _max_over_ranks(kernel_ms, world)
+    plain_gemm_ms = _max_over_ranks(plain_gemm_ms, world)
+    from tvarant_b200 import _C
+
+    fused = program_in_epilogue(m, wl.fusions, _C.sm_count(torch.tvarant.current_device()))
+    kernel_ms = step_ms if fused else plain_gemm_ms
+    wl.e2e_begin(torch)
     for _ in range(max(1, warmup // 2)):
         wl.step_e2e(torch)
+    wl.e2e_end(torch)
     torch.tvarant.synchronize()
     _barrier(world)
     t0, t1 = Event(), Event()
     t0.record()
+    wl.e2e_begin(torch)
     for _ in range(steps):
         wl.step_e2e(torch)
+    wl.e2e_end(torch)
     t1.record()
     t1.synchronize()
     e2e_ms = _max_over_ranks(t0.elapsed_time(t1) / steps, world)
-    kernel, bound = gemm_kernel_name(m, mode)
-    gemm_bytes = 4.0 * (N_DEFAULT * K_DEFAULT + m * K_DEFAULT + m * N_DEFAULT + N_DEFAULT)
+    kernel, bound = gemm_kernel_name(m, mode, fused)
+    # algorithmic bytes of the timed kernel: W, X, bias and the output, plus Z
+    # when the chain runs in its epilogue
+    gemm_bytes = 4.0 * (N_DEFAULT * K_DEFAULT + m * K_DEFAULT + m * N_DEFAULT + N_DEFAULT
+                        + (m * N_DEFAULT if fused else 0))
     return {"wl": wl, "M": m, "mode": mode, "step_ms": step_ms, "kernel_ms": kernel_ms,
+            "plain_gemm_ms": plain_gemm_ms, "program_in_epilogue": fused,
+            "launches_per_step": 1 if fused else 2,
             "e2e_ms": e2e_ms, "kernel": kernel, "bound": bound, "flops": wl.flops,
             "gemm_bytes": gemm_bytes,
             "step_tflops": wl.flops / (step_ms / 1e3) / 1e12,
@@ -417,12 +493,18 @@ def measure_gemm_point(torch, m: int, mode: str, steps: int, warmup: int, world:
             "kernel_gbs": gemm_bytes / (kernel_ms / 1e3) / 1e9}
 
 
+def _traffic_key(pt: dict) -> str:
+    """Key of the timed kernel's ncu DRAM traffic in profiles/ncu_traffic.json."""
+    prefix = "gemm_pw" if pt.get("program_in_epilogue") else "gemm"
+    return f"{prefix}_{pt['mode']}_m{pt['M']}"
+
+
 def _roofline(pt: dict, tf32_peak, peaks: dict) -> dict:
     if pt["bound"] == "hbm":
         hbm = peaks.get("hbm_gbs", 6650.0)
         return {"bound": "hbm", "achieved": pt["kernel_gbs"], "peak": hbm, "unit": "GB/s",
                 "frac": pt["kernel_gbs"] / hbm,
-                "traffic": _traffic(f"gemm_{pt['mode']}_m{pt['M']}"),
+                "traffic": _traffic(_traffic_key(pt)),
                 "kernel": pt["kernel"], "kernel_ms": pt["kernel_ms"],
                 "algorithmic_bytes": pt["gemm_bytes"],
                 "peak_source": "MEASURED_PEAKS.json hbm_gbs"}
@@ -431,7 +513,7 @@ def _roofline(pt: dict, tf32_peak, peaks: dict) -> dict:
         peak = peak / 3  # three TF32 MMAs per k-step
     return {"bound": "tensor", "achieved": pt["kernel_tflops"], "peak": peak, "unit": "TFLOP/s",
             "frac": pt["kernel_tflops"] / peak,
-            "traffic": _traffic(f"gemm_{pt['mode']}_m{pt['M']}"),
+            "traffic": _traffic(_traffic_key(pt)),
             "kernel": pt["kernel"], "kernel_ms": pt["kernel_ms"],
             "peak_source": ("cuBLAS TF32 8192^3 measured in this run" if tf32_peak
                             else "half of the bf16 peak (no cuBLAS)")
@@ -464,7 +546,10 @@ def run_gemm(args, rank, world, local_rank) -> dict | None:
         "data": "synthetic (seeded N(0,1) activations, U(-1/64,1/64) weights)",
         "config": {
             "workload": f"linear+bias+SiLU GEMM M={args.m} K={K_DEFAULT} N={N_DEFAULT} ({args.mode}) "
-                        "+ JIT-fused abs(neg(exp(Y - Z))) chain, compiled by torch_tvarant.compiler",
+                        "+ abs(neg(exp(Y - Z))) chain, compiled by torch_tvarant.compiler "
+                        + ("(chain in the GEMM epilogue: one kernel per step)"
+                           if pt["program_in_epilogue"] else "(chain as a second kernel)"),
+            "plain_gemm_ms": pt["plain_gemm_ms"],
             "M": args.m, "K": K_DEFAULT, "N": N_DEFAULT, "mode": args.mode,
             "parallelism": f"replicas x{world}",
             "l2": ("inputs (X 268 MB + Z 268 MB + W 67 MB) exceed the 126 MB L2" if wl.copies == 1
@@ -474,9 +559,12 @@ def run_gemm(args, rank, world, local_rank) -> dict | None:
         },
         "e2e": {"value": world * wl.flops / (pt["e2e_ms"] / 1e3) / 1e12, "unit": "TFLOP/s",
                 "h2d_bytes_per_step": wl.h2d_bytes, "d2h_bytes_per_step": wl.d2h_bytes,
-                "ms_per_step": pt["e2e_ms"]},
+                "ms_per_step": pt["e2e_ms"],
+                "pipeline": "pinned host X, Z in on a copy stream, compiled model on the "
+                            "compute stream, Y out on another copy stream; double-buffered "
+                            "device inputs, so consecutive steps overlap"},
         "roofline": _roofline(pt, tf32_peak, peaks),
-        "gpu_launches": args.steps * 2,
+        "gpu_launches": args.steps * pt["launches_per_step"],
         "clocks": clocks.summary(),
         "device_status": status,
     }
@@ -510,6 +598,7 @@ def run_sweep(args, rank, world, local_rank) -> dict | None:
         rl = _roofline(pt, tf32_peak, peaks)
         table.append({"M": pt["M"], "mode": pt["mode"], "step_ms": pt["step_ms"],
                       "step_tflops": pt["step_tflops"], "kernel_ms": pt["kernel_ms"],
+                      "plain_gemm_ms": pt["plain_gemm_ms"],
                       "kernel": pt["kernel"], "bound": rl["bound"], "achieved": rl["achieved"],
                       "unit": rl["unit"], "frac": rl["frac"],
                       "e2e_tflops": pt["flops"] / (pt["e2e_ms"] / 1e3) / 1e12})
@@ -528,7 +617,7 @@ def run_sweep(args, rank, world, local_rank) -> dict | None:
                    "l2": "points whose operands fit in L2 rotate over weight copies in distinct "
                          "buffers (> 256 MB in total), so each step reads its weight from HBM"},
         "roofline": _roofline(head, tf32_peak, peaks),
-        "gpu_launches": 2 * args.steps * len(points) * 2,
+        "gpu_launches": sum(args.steps * p["launches_per_step"] for p in points),
         "clocks": clocks.summary(),
         "device_status": status,
     }

@@ -359,6 +359,25 @@ int tvr_pointwise(const tvr_pw_node* nodes, int n_nodes, int n_inputs,
 int tvr_pointwise_source(const tvr_pw_node* nodes, int n_nodes, int n_inputs, char* buf,
                          size_t cap, size_t* len);
 
+/* GEMM with a pointwise program on its output:
+ *   y = act(alpha * A . op(B) + beta * bias)      (as tvr_gemm_bias_act)
+ *   c[r, j] = program(input gemm_input = y[r, j], input i = inputs[i][r * input_ld[i] + j])
+ * The program is a tvr_pointwise SSA program of at most 12 nodes over at most
+ * three inputs, one of them (gemm_input) the GEMM result; inputs[gemm_input]
+ * is ignored.  The other inputs are [m, n] fp32 with row stride input_ld[i]
+ * (>= n), or 0 for one row of n values broadcast over all rows; they must not
+ * overlap c.  The tensor-core GEMM runs the program in its epilogue, so y is
+ * never written to memory; other GEMM kernels are followed by one in-place
+ * pass.  Either way the result equals tvr_gemm_bias_act followed by
+ * tvr_pointwise on the same program.  No reference counterpart as one call:
+ * the reference's compiler emits linear_act followed by a pointwise program
+ * (torch_tvarant/compiler.py, csrc/aten/CustomOps.cpp:14-89). */
+int tvr_gemm_pointwise(const float* a, const float* b, const float* bias, float* c, int64_t m,
+                       int64_t n, int64_t k, int64_t lda, int64_t ldb, int64_t ldc, float alpha,
+                       float beta, int act, int trans_b, int mode, const tvr_pw_node* nodes,
+                       int n_nodes, int n_inputs, int gemm_input, const float* const* inputs,
+                       const int64_t* input_ld, void* stream);
+
 /* ---- NCCL (no counterpart in the reference, which has one device) ------ */
 
 /* NCCL is loaded at run time; these return TVR_ERR_NCCL when it is absent.

@@ -201,3 +201,53 @@ def test_swiglu_fusion_operand_order():
 
     gm = compile_fx(trace_module(Swapped()))
     assert torch.ops.tvarant.linear_swiglu in _targets(gm)
+
+
+class _LinearChain(nn.Module):
+    """The fused-GEMM benchmark model: linear + SiLU, then abs(-exp(y - z))."""
+
+    def __init__(self, act=True):
+        super().__init__()
+        self.lin = nn.Linear(8, 16)
+        self.act = act
+
+    def forward(self, x, z):
+        y = self.lin(x)
+        if self.act:
+            y = F.silu(y)
+        return torch.abs(-torch.exp(y - z))
+
+
+def test_pointwise_program_joins_the_gemm_epilogue():
+    gm = compile_fx(trace_module(_LinearChain()))
+    assert last_log["gemm_epilogue"] == 1 and last_log["gemm_pointwise"] == 1
+    targets = _targets(gm)
+    assert torch.ops.tvarant.linear_pointwise in targets
+    assert torch.ops.tvarant.pointwise not in targets
+    assert torch.ops.tvarant.linear_act not in targets
+    node = [n for n in gm.graph.nodes if n.target is torch.ops.tvarant.linear_pointwise][0]
+    x, w, bias, act, trans_b, gemm_input, extras, ops, a, b, input_ids, alphas, consts = node.args
+    assert act == "silu" and trans_b is True and gemm_input == 0
+    assert [t.name for t in extras] == ["z"]
+    assert ops == [LOAD, LOAD, SUB, EXP, NEG, ABS]
+    assert input_ids == [0, 1, -1, -1, -1, -1]
+
+
+def test_pointwise_program_joins_a_plain_linear():
+    gm = compile_fx(trace_module(_LinearChain(act=False)))
+    node = [n for n in gm.graph.nodes if n.target is torch.ops.tvarant.linear_pointwise][0]
+    assert node.args[3] == "none" and node.args[4] is True
+    assert "linear" not in [str(n.target) for n in gm.graph.nodes]
+
+
+def test_gemm_with_other_users_keeps_its_output():
+    class Both(_LinearChain):
+        def forward(self, x, z):
+            y = F.silu(self.lin(x))
+            return torch.abs(-torch.exp(y - z)), y
+
+    gm = compile_fx(trace_module(Both()))
+    targets = _targets(gm)
+    assert torch.ops.tvarant.linear_act in targets and torch.ops.tvarant.pointwise in targets
+    assert torch.ops.tvarant.linear_pointwise not in targets
+    assert "gemm_pointwise" not in last_log

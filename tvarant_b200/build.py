@@ -43,6 +43,7 @@ CUDA_SOURCES = [
     "select.cu",
     "reduce.cu",
     "gemm.cu",
+    "gemm_epilogue.cu",
     "gemm_simt.cu",
     "gemm_skinny.cu",
     "gemm_tc.cu",

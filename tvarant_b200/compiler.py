@@ -5,7 +5,7 @@ Entry points (the reference's torch_tvarant/compiler.py API):
 * ``compile(module)`` — FX-trace the module (inlining Linear, activations,
   norms, ...) and fuse; falls back to ``torch.compile(backend="tvarant")``
   when FX tracing fails (reference compiler.py:377-399);
-* ``compile_fx(gm, example_inputs)`` — run both passes on a GraphModule;
+* ``compile_fx(gm, example_inputs)`` — run the passes on a GraphModule;
 * ``torch.compile(model, backend="tvarant")`` — the Dynamo backend,
   registered on import.
 
@@ -23,7 +23,10 @@ Passes:
   compiled by NVRTC (reference compiler.py:205-322).  Besides the
   reference's relu / silu / neg / sigmoid / add / mul / scalar-mul, the
   group may contain sub, exp and abs (opcodes appended after the
-  reference's 0-8).
+  reference's 0-8);
+* ``fuse_gemm_pointwise``: a pointwise program fed by a GEMM that nothing
+  else uses becomes one ``tvarant.linear_pointwise`` — the program is
+  evaluated in the GEMM's epilogue; not a reference pass.
 
 ``last_log`` records the counts of the last run of each pass.
 """
@@ -332,12 +335,70 @@ def _build_program(order, members):
     return inputs, ops, a, b, input_ids, alphas, consts
 
 
+def _gemm_source(node: object):
+    """(x, weight, bias, act, trans_b) if ``node`` is a GEMM whose output
+    only feeds the pointwise program being fused, else None."""
+    if not isinstance(node, torch.fx.Node) or len(node.users) != 1:
+        return None
+    if node.op == "call_function" and node.target is torch.ops.tvarant.linear_act:
+        x, w, bias, act, trans_b = (list(node.args) + [False])[:5]
+        return x, w, bias, act, bool(trans_b)
+    if op_name(node) in ("linear", "addmm", "mm"):
+        match = _gemm_operands(node)
+        if match is not None:
+            x, w, bias, trans_b, _ = match
+            return x, w, bias, "none", trans_b
+    return None
+
+
+def fuse_gemm_pointwise(gm: torch.fx.GraphModule) -> torch.fx.GraphModule:
+    """Rewrites a ``tvarant.pointwise`` program one of whose inputs is a GEMM
+    (``linear_act`` or an unfused linear / addmm / mm) used only by that
+    program into one ``tvarant.linear_pointwise``: the program runs in the
+    GEMM's epilogue and the GEMM's output never reaches memory.  Runs after
+    ``fuse_pointwise``; not a reference pass.  Records
+    ``last_log["gemm_pointwise"]`` when it fuses."""
+    graph = gm.graph
+    fused = 0
+    for node in list(graph.nodes):
+        if node.op != "call_function" or node.target is not torch.ops.tvarant.pointwise:
+            continue
+        inputs, ops, a, b, input_ids, alphas, consts = node.args
+        if len(ops) > 12 or len(inputs) > 3:
+            continue  # beyond the epilogue program's limits
+        for gi, src in enumerate(inputs):
+            gemm = _gemm_source(src)
+            if gemm is None:
+                continue
+            x, w, bias, act, trans_b = gemm
+            extras = [t for i, t in enumerate(inputs) if i != gi]
+            with graph.inserting_before(node):
+                new = graph.call_function(
+                    torch.ops.tvarant.linear_pointwise,
+                    args=(x, w, bias, act, trans_b, gi, extras, ops, a, b, input_ids, alphas,
+                          consts))
+            node.replace_all_uses_with(new)
+            graph.erase_node(node)
+            graph.erase_node(src)
+            fused += 1
+            break
+    graph.lint()
+    gm.recompile()
+    if fused:
+        last_log["gemm_pointwise"] = fused
+    else:
+        last_log.pop("gemm_pointwise", None)
+    return gm
+
+
 def compile_fx(gm: torch.fx.GraphModule, example_inputs: Any = None) -> torch.fx.GraphModule:
-    """GEMM-epilogue fusion, SwiGLU fusion, then pointwise fusion, in place."""
+    """GEMM-epilogue fusion, SwiGLU fusion, pointwise fusion, then pointwise
+    programs into GEMM epilogues, in place."""
     _ = example_inputs
     gm = fuse_gemm_epilogue(gm)
     gm = fuse_swiglu(gm)
     gm = fuse_pointwise(gm)
+    gm = fuse_gemm_pointwise(gm)
     return gm
 
 

@@ -1,5 +1,5 @@
-// The tvarant operator library: tvarant::linear_act, tvarant::pointwise and
-// tvarant::linear_swiglu.
+// The tvarant operator library: tvarant::linear_act, tvarant::pointwise,
+// tvarant::linear_swiglu and tvarant::linear_pointwise.
 //
 // Schemas are the reference's, verbatim (csrc/aten/CustomOps.cpp:101-106),
 // so graphs produced by torch_tvarant.compiler run unchanged.  linear_act
@@ -134,6 +134,90 @@ at::Tensor pointwise(at::TensorList inputs, at::IntArrayRef ops, at::IntArrayRef
   return out;
 }
 
+// pointwise(inputs', program) where inputs' is `inputs` with
+// linear_act(x, weight, bias, act, trans_b) inserted at position gemm_input:
+// the GEMM -> pointwise pair torch_tvarant.compiler emits, as one call.  The
+// program runs in the GEMM's epilogue (tvr_gemm_pointwise) when its other
+// inputs are the GEMM output's size (contiguous) or one broadcast row of it;
+// otherwise the two ops run as written.
+at::Tensor linear_pointwise(const at::Tensor& x, const at::Tensor& weight,
+                            const std::optional<at::Tensor>& bias, std::string act, bool trans_b,
+                            int64_t gemm_input, at::TensorList inputs, at::IntArrayRef ops,
+                            at::IntArrayRef a, at::IntArrayRef b, at::IntArrayRef input_ids,
+                            at::ArrayRef<double> alphas, at::ArrayRef<double> consts) {
+  check_fp32(x, "linear_pointwise");
+  check_fp32(weight, "linear_pointwise");
+  TORCH_CHECK(gemm_input >= 0 && gemm_input <= static_cast<int64_t>(inputs.size()),
+              "linear_pointwise: gemm_input ", gemm_input, " out of range");
+  TORCH_CHECK(x.dim() >= 1 && weight.dim() == 2, "linear_pointwise: expected x [..., K], weight 2D");
+  const size_t n_nodes = ops.size();
+  TORCH_CHECK(a.size() == n_nodes && b.size() == n_nodes && input_ids.size() == n_nodes &&
+                  alphas.size() == n_nodes && consts.size() == n_nodes,
+              "linear_pointwise: SSA arrays must all have the same length");
+  c10::DeviceGuard guard(x.device());
+  const int64_t n = trans_b ? weight.size(0) : weight.size(1);
+  auto y_sizes = x.sizes().vec();
+  y_sizes.back() = n;
+  const int64_t numel = c10::multiply_integers(y_sizes);
+  const int64_t m = n > 0 ? numel / n : 0;
+
+  // Can the program run in the epilogue?  Every other input must be the
+  // GEMM output's size (taken element by element, as tvarant::pointwise
+  // does) or one row of n values that broadcasts to it.
+  bool fused = n_nodes <= 12 && inputs.size() <= 2 && n_nodes > 0;
+  bool same_numel = true;
+  std::vector<int64_t> shape = y_sizes;
+  for (const auto& t : inputs) {
+    fused = fused && t.defined() && t.scalar_type() == at::kFloat && is_device(t) &&
+            t.device() == x.device() && t.is_contiguous();
+    if (!fused) break;
+    if (t.numel() == numel) continue;
+    same_numel = false;
+    fused = t.numel() == n && at::infer_size(y_sizes, t.sizes()) == y_sizes;
+  }
+  if (fused) {
+    // output shape: input 0's when all sizes agree, else the broadcast shape
+    if (same_numel && gemm_input != 0) shape = inputs[0].sizes().vec();
+    GemmProgram prog;
+    prog.gemm_input = static_cast<int>(gemm_input);
+    prog.nodes.resize(n_nodes);
+    for (size_t i = 0; i < n_nodes; ++i) {
+      prog.nodes[i].op = static_cast<int32_t>(ops[i]);
+      prog.nodes[i].a = static_cast<int32_t>(a[i]);
+      prog.nodes[i].b = static_cast<int32_t>(b[i]);
+      prog.nodes[i].input_id = static_cast<int32_t>(input_ids[i]);
+      prog.nodes[i].alpha = static_cast<float>(alphas[i]);
+      prog.nodes[i].c = static_cast<float>(consts[i]);
+    }
+    size_t e = 0;
+    for (int64_t i = 0; i <= static_cast<int64_t>(inputs.size()); ++i) {
+      if (i == gemm_input) {
+        prog.inputs.push_back(nullptr);
+        prog.ld.push_back(0);
+        continue;
+      }
+      const at::Tensor& t = inputs[e++];
+      prog.inputs.push_back(static_cast<const float*>(t.data_ptr()));
+      prog.ld.push_back(t.numel() == numel ? n : 0);
+    }
+    at::Tensor xc = x.is_contiguous() ? x : contiguous_copy(x);
+    const int64_t k = xc.size(-1);
+    const at::Tensor* bptr = nullptr;
+    at::Tensor bstore;
+    if (bias.has_value() && bias->defined()) {
+      check_fp32(*bias, "linear_pointwise");
+      bstore = *bias;
+      bptr = &bstore;
+    }
+    at::Tensor y2 = gemm_bias_act(xc.reshape({m, k}), weight, bptr, 1.f, 1.f, parse_act(act),
+                                  trans_b, &prog);
+    return y2.reshape(shape);
+  }
+  std::vector<at::Tensor> all(inputs.begin(), inputs.end());
+  all.insert(all.begin() + gemm_input, linear_act(x, weight, bias, act, trans_b));
+  return pointwise(all, ops, a, b, input_ids, alphas, consts);
+}
+
 }  // namespace
 }  // namespace tvarant::ops
 
@@ -144,10 +228,15 @@ TORCH_LIBRARY(tvarant, m) {
       "float[] consts) -> Tensor");
   m.def("all_reduce_(Tensor(a!) self, int comm) -> Tensor(a!)");
   m.def("linear_swiglu(Tensor x, Tensor w_gate, Tensor w_up) -> Tensor");
+  m.def(
+      "linear_pointwise(Tensor x, Tensor weight, Tensor? bias, str act, bool trans_b, "
+      "int gemm_input, Tensor[] inputs, int[] ops, int[] a, int[] b, int[] input_ids, "
+      "float[] alphas, float[] consts) -> Tensor");
 }
 
 TORCH_LIBRARY_IMPL(tvarant, PrivateUse1, m) {
   m.impl("linear_act", TORCH_FN(tvarant::ops::linear_act));
   m.impl("pointwise", TORCH_FN(tvarant::ops::pointwise));
   m.impl("linear_swiglu", TORCH_FN(tvarant::ops::linear_swiglu));
+  m.impl("linear_pointwise", TORCH_FN(tvarant::ops::linear_pointwise));
 }

@@ -192,7 +192,7 @@ int gemm_mode() {
 }
 
 at::Tensor gemm_bias_act(const at::Tensor& a_in, const at::Tensor& b_in, const at::Tensor* bias,
-                         float alpha, float beta, int act, bool trans_b) {
+                         float alpha, float beta, int act, bool trans_b, const GemmProgram* prog) {
   TORCH_CHECK(a_in.dim() == 2 && b_in.dim() == 2, "gemm: expected 2D tensors");
   c10::DeviceGuard guard(a_in.device());
   at::Tensor a = a_in;
@@ -235,6 +235,15 @@ at::Tensor gemm_bias_act(const at::Tensor& a_in, const at::Tensor& b_in, const a
   }
   at::Tensor out = empty_device({m, n}, a.options());
   if (m == 0 || n == 0) return out;
+  if (prog != nullptr) {
+    TVR_TRY(tvr_gemm_pointwise(
+        static_cast<const float*>(a.data_ptr()), static_cast<const float*>(b.data_ptr()),
+        static_cast<const float*>(bias_ptr), static_cast<float*>(out.data_ptr()), m, n, k, lda, ldb,
+        n, alpha, beta_use, act, trans ? 1 : 0, gemm_mode(), prog->nodes.data(),
+        static_cast<int>(prog->nodes.size()), static_cast<int>(prog->inputs.size()),
+        prog->gemm_input, prog->inputs.data(), prog->ld.data(), current_stream_handle()));
+    return out;
+  }
   TVR_TRY(tvr_gemm_bias_act(static_cast<const float*>(a.data_ptr()),
                             static_cast<const float*>(b.data_ptr()),
                             static_cast<const float*>(bias_ptr),

@@ -65,8 +65,18 @@ int gemm_mode();
 // C[m,n] = act(alpha * A[m,k] @ op(B) + beta * bias) — the reference's
 // ops::gemm_bias_act (csrc/aten/AtenCommon.h:33-86).  B is [k,n], or [n,k]
 // when trans_b.  A transposed B view is consumed without a copy.
+// With `prog`, the pointwise program runs on the GEMM's output
+// (tvr_gemm_pointwise): prog->inputs[prog->gemm_input] is unused and the
+// other inputs are [m, n] with row strides prog->ld (0: broadcast row).
+struct GemmProgram {
+  std::vector<tvr_pw_node> nodes;
+  int gemm_input = 0;
+  std::vector<const float*> inputs;
+  std::vector<int64_t> ld;
+};
 at::Tensor gemm_bias_act(const at::Tensor& a, const at::Tensor& b, const at::Tensor* bias,
-                         float alpha, float beta, int act, bool trans_b);
+                         float alpha, float beta, int act, bool trans_b,
+                         const GemmProgram* prog = nullptr);
 
 at::Tensor empty_like_contig(const at::Tensor& like, at::IntArrayRef sizes);
 at::Tensor empty_device(at::IntArrayRef sizes, const at::TensorOptions& opts);

@@ -34,8 +34,14 @@ constexpr int64_t kSmallMacs = int64_t(1) << 21;
 int run(const float* a, const float* b, const float* bias, float* c, int64_t m, int64_t n,
         int64_t k, int64_t lda, int64_t ldb, int64_t ldc, int64_t batch, int64_t sa,
         int64_t sb, int64_t sc, float alpha, float beta, int act, bool trans_b, int mode,
-        cudaStream_t stream) {
+        cudaStream_t stream, const EpiProg* prog = nullptr) {
   mode = resolve_mode(mode);
+  // A pointwise program on the output: the tensor-core kernel applies it in
+  // its epilogue; after the other kernels it runs as an in-place pass.
+  auto then_prog = [&](int rc) {
+    if (rc != TVR_OK || prog == nullptr) return rc;
+    return epi_prog_inplace(*prog, c, ldc, m, n, stream);
+  };
   if (mode != TVR_GEMM_TF32 && mode != TVR_GEMM_3XTF32 && mode != TVR_GEMM_FP32) {
     return fail(TVR_ERR_INVALID, "gemm: unknown precision mode %d", mode);
   }
@@ -45,11 +51,11 @@ int run(const float* a, const float* b, const float* bias, float* c, int64_t m, 
   // cluster.  FP32 mode keeps the reference's sequential summation order.
   if (mode == TVR_GEMM_3XTF32 && batch == 1 &&
       gemm_skinny_applies(a, b, m, n, k, lda, ldb, trans_b)) {
-    return gemm_skinny(a, b, bias, c, m, n, k, lda, ldb, ldc, alpha, beta, act, stream);
+    return then_prog(gemm_skinny(a, b, bias, c, m, n, k, lda, ldb, ldc, alpha, beta, act, stream));
   }
   if (mode != TVR_GEMM_FP32 && batch == 1 && gemm_ws_applies(a, b, m, n, k, lda, ldb, trans_b)) {
-    return gemm_ws(a, b, bias, c, m, n, k, lda, ldb, ldc, alpha, beta, act,
-                   mode == TVR_GEMM_3XTF32, stream);
+    return then_prog(gemm_ws(a, b, bias, c, m, n, k, lda, ldb, ldc, alpha, beta, act,
+                             mode == TVR_GEMM_3XTF32, stream));
   }
   const int64_t macs = batch * m * n * k;
   bool tensor = mode != TVR_GEMM_FP32 && macs > kSmallMacs;
@@ -58,11 +64,11 @@ int run(const float* a, const float* b, const float* bias, float* c, int64_t m, 
   if (mode == TVR_GEMM_3XTF32 && m <= 16) tensor = false;
   if (tensor) {
     const int rc = gemm_tcgen05(a, b, bias, c, m, n, k, lda, ldb, ldc, batch, sa, sb, sc, alpha,
-                                beta, act, trans_b, mode == TVR_GEMM_3XTF32, stream);
+                                beta, act, trans_b, mode == TVR_GEMM_3XTF32, stream, prog);
     if (rc != TVR_ERR_UNSUPPORTED) return rc;
   }
-  return gemm_simt(a, b, bias, c, m, n, k, lda, ldb, ldc, batch, sa, sb, sc, alpha, beta, act,
-                   trans_b, stream);
+  return then_prog(gemm_simt(a, b, bias, c, m, n, k, lda, ldb, ldc, batch, sa, sb, sc, alpha,
+                             beta, act, trans_b, stream));
 }
 
 }  // namespace
@@ -85,6 +91,27 @@ int tvr_gemm_bias_act(const float* a, const float* b, const float* bias, float* 
   TVR_CHECK(trans_b ? ldb >= k : ldb >= n, "gemm: leading dimension of B too small");
   return run(a, b, bias, c, m, n, k, lda, ldb, ldc, 1, 0, 0, 0, alpha, beta, act, trans_b != 0,
              mode, as_stream(stream));
+}
+
+int tvr_gemm_pointwise(const float* a, const float* b, const float* bias, float* c, int64_t m,
+                       int64_t n, int64_t k, int64_t lda, int64_t ldb, int64_t ldc, float alpha,
+                       float beta, int act, int trans_b, int mode, const tvr_pw_node* nodes,
+                       int n_nodes, int n_inputs, int gemm_input, const float* const* inputs,
+                       const int64_t* input_ld, void* stream) {
+  TVR_CHECK(m >= 0 && n >= 0 && k >= 0, "gemm_pointwise: negative size (%lld, %lld, %lld)",
+            (long long)m, (long long)n, (long long)k);
+  TVR_CHECK(act >= 0 && act <= 2, "gemm_pointwise: unknown activation %d", act);
+  if (m == 0 || n == 0) return TVR_OK;
+  TVR_CHECK(c != nullptr, "gemm_pointwise: null output");
+  TVR_CHECK(k == 0 || (a != nullptr && b != nullptr), "gemm_pointwise: null operand");
+  TVR_CHECK(lda >= k && ldc >= n, "gemm_pointwise: leading dimension too small");
+  TVR_CHECK(trans_b ? ldb >= k : ldb >= n, "gemm_pointwise: leading dimension of B too small");
+  EpiProg prog;
+  const int rc = build_epi_prog(nodes, n_nodes, n_inputs, gemm_input, inputs, input_ld, c, m, n,
+                                ldc, &prog);
+  if (rc != TVR_OK) return rc;
+  return run(a, b, bias, c, m, n, k, lda, ldb, ldc, 1, 0, 0, 0, alpha, beta, act, trans_b != 0,
+             mode, as_stream(stream), &prog);
 }
 
 int tvr_gemm_swiglu(const float* x, const float* w_gate, const float* w_up, float* out,

@@ -1,6 +1,8 @@
 // Epilogue arithmetic shared by the GEMM kernels.
 #pragma once
 
+#include "epilogue_prog.cuh"
+
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -73,10 +75,24 @@ int gemm_tcgen05_swiglu(const float* x, const float* wg, const float* wu, float*
 
 // Returns TVR_ERR_UNSUPPORTED (without recording an error) when the
 // operands cannot be described by TMA tensor maps; the caller then uses
-// gemm_simt.
+// gemm_simt.  With a pointwise program (prog non-null with nodes), the
+// program is applied to the output: in the epilogue when possible, else by
+// epi_prog_inplace after the GEMM.
 int gemm_tcgen05(const float* a, const float* b, const float* bias, float* c, int64_t m,
                  int64_t n, int64_t k, int64_t lda, int64_t ldb, int64_t ldc, int64_t batch,
                  int64_t sa, int64_t sb, int64_t sc, float alpha, float beta, int act,
-                 bool trans_b, bool split3, cudaStream_t stream);
+                 bool trans_b, bool split3, cudaStream_t stream, const EpiProg* prog = nullptr);
+
+// c[r, j] = program(c[r, j], extra inputs at (r, j)) over [m, n] (row stride
+// ldc), in place (gemm_epilogue.cu).
+int epi_prog_inplace(const EpiProg& prog, float* c, int64_t ldc, int64_t m, int64_t n,
+                     cudaStream_t stream);
+
+// Checks a tvr_pw_node program whose input gemm_input is the GEMM result and
+// whose other inputs are [m, n] fp32 with row strides input_ld (0: one row
+// broadcast), none overlapping the output c, and packs it (gemm_epilogue.cu).
+int build_epi_prog(const tvr_pw_node* nodes, int n_nodes, int n_inputs, int gemm_input,
+                   const float* const* inputs, const int64_t* input_ld, const float* c,
+                   int64_t m, int64_t n, int64_t ldc, EpiProg* out);
 
 }  // namespace tvr

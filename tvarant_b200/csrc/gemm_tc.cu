@@ -33,6 +33,7 @@
 #include <atomic>
 #include <mutex>
 
+#include "epilogue_prog.cuh"
 #include "gemm_common.cuh"
 #include "tc_ptx.cuh"
 
@@ -85,6 +86,7 @@ struct Params {
   int num_kb;
   int total_units;
   int* status;
+  EpiProg prog;  // PROG kernels: pointwise program applied to each output element
 };
 
 // N-major tile: 32-wide N atoms of [BK rows x 128 B] placed BK*128 B apart
@@ -122,10 +124,15 @@ __device__ __forceinline__ void decode_unit(const Params& p, int u, int& b, int&
 // gate weight (tma_b) over the same 128 rows of the up weight (tma_b_lo), the
 // MMA fills accumulator columns 0..127 with x.Wg^T and 128..255 with x.Wu^T,
 // and the epilogue writes silu(gate) * up: a 128 x 128 output tile.
-template <int BN, bool SPLIT3, bool B_NMAJOR, bool GATED = false>
+//
+// PROG (K-major weights, no split-K): after bias and activation, the epilogue
+// runs the pointwise program p.prog on each output element, reading the
+// program's other inputs at the element's position, and stores its result.
+template <int BN, bool SPLIT3, bool B_NMAJOR, bool GATED = false, bool PROG = false>
 __global__ void __launch_bounds__(NUM_THREADS, 1) gemm_tc_kernel(const __grid_constant__ Params p) {
   using Cf = Cfg<BN, SPLIT3>;
   static_assert(!GATED || (BN == 256 && !SPLIT3 && !B_NMAJOR), "gated GEMM shape");
+  static_assert(!PROG || (!GATED && !B_NMAJOR), "pointwise-epilogue GEMM shape");
   constexpr int OUT_BN = GATED ? BN / 2 : BN;  // output columns per tile
   constexpr int STAGES = Cf::STAGES;
   extern __shared__ uint8_t smem_raw[];
@@ -357,7 +364,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) gemm_tc_kernel(const __grid_co
       }
       const bool plain = GATED || (p.alpha == 1.f && p.act == TVR_ACT_NONE &&
                                    (p.beta == 0.f || (p.bias == nullptr && !p.use_prev)));
-#pragma unroll
+      // A pointwise program makes each chunk's code long: keep one copy of
+      // it (instruction-cache misses otherwise stall every warp of the CTA).
+      constexpr int CH_UNROLL = PROG ? 1 : CH;
+#pragma unroll CH_UNROLL
       for (int c = 0; c < CH; ++c) {
         if (c == CH - 1) {
           // accumulator fully read: hand the TMEM buffer back to the MMA warp
@@ -373,7 +383,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) gemm_tc_kernel(const __grid_co
                        "f"(v[4 * j + 1]), "f"(v[4 * j + 2]), "f"(v[4 * j + 3])
                        : "memory");
         }
-        if (c + 1 < CH) {
+        // (with a program, the next chunk is read after this one is stored:
+        // its 32 registers hold the program's prefetched input meanwhile)
+        if (!PROG && c + 1 < CH) {
           tmem_load_32_async(tcol + 32 * (c + 1), v);
           if constexpr (GATED) tmem_load_32_async(tcol + UP + 32 * (c + 1), up);
         }
@@ -391,69 +403,209 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) gemm_tc_kernel(const __grid_co
             bias4.w = col + 3 < p.n ? __ldg(p.bias + col + 3) : 0.f;
           }
         }
-        // All shared-memory reads (and reads of the previous output, when
-        // beta applies to it) are issued before any global store: a warp's
-        // memory instructions drain in order, so a load queued behind a
-        // store would wait for that store.
-        float4 xs[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const int rr = 4 * i + (lane >> 3);
-          const uint32_t addr = sbuf + rr * 128 + ((jj ^ (rr & 7)) << 4);
-          asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
-                       : "=f"(xs[i].x), "=f"(xs[i].y), "=f"(xs[i].z), "=f"(xs[i].w)
-                       : "r"(addr));
-        }
         const bool full4 = p.c_vec && col + 3 < p.n;
-        if (finish && !plain) {
-          const bool read_prev = p.bias == nullptr && p.use_prev;
-          float4 prev[8];
+        if constexpr (PROG) {
+          // The program as stack code (EpiProg::sop), each operation applied
+          // to 16 values of this lane at once: rows row0 + 4i + lane/8 for
+          // i in [4h, 4h + 4), columns col..col+3, for the two halves h of
+          // the chunk.  Slot 0 ends as the result.
+          const bool read_prev = finish && p.bias == nullptr && p.use_prev;
+#pragma unroll 1
+          for (int h = 0; h < 2; ++h) {
+            float s0[16], s1[16];
 #pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const int64_t row = row0 + 4 * i + (lane >> 3);
-            prev[i] = bias4;
-            if (read_prev && row < p.m && col < p.n) {
-              const float* src = cbase + row * p.ldc + col;
+            for (int j = 0; j < 16; ++j) s0[j] = s1[j] = 0.f;
+#pragma unroll 1
+            for (int pc = 0; pc < p.prog.n_ops; ++pc) {
+              const int op = p.prog.sop[pc];
+              const float sv = p.prog.sval[pc];
+              const bool rv = p.prog.rev[pc] != 0;
+              if (op <= kStPushC) {
+#pragma unroll
+                for (int j = 0; j < 16; ++j) s1[j] = s0[j];
+              }
+              switch (op) {
+                case kStPushY: {
+                  // one row at a time: no temporaries beside the two slots
+#pragma unroll
+                  for (int i = 0; i < 4; ++i) {
+                    const int rr = 4 * (4 * h + i) + (lane >> 3);
+                    const uint32_t addr = sbuf + rr * 128 + ((jj ^ (rr & 7)) << 4);
+                    float4 x;
+                    asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+                                 : "=f"(x.x), "=f"(x.y), "=f"(x.z), "=f"(x.w)
+                                 : "r"(addr));
+                    if (finish && !plain) {
+                      float4 prev = bias4;
+                      const int64_t row = row0 + rr;
+                      if (read_prev && row < p.m && col < p.n) {
+                        const float* src = cbase + row * p.ldc + col;
+                        if (full4) {
+                          prev = *reinterpret_cast<const float4*>(src);
+                        } else {
+                          prev.x = src[0];
+                          prev.y = col + 1 < p.n ? src[1] : 0.f;
+                          prev.z = col + 2 < p.n ? src[2] : 0.f;
+                          prev.w = col + 3 < p.n ? src[3] : 0.f;
+                        }
+                      }
+                      if (p.act == TVR_ACT_SILU) epilogue4<TVR_ACT_SILU>(x, prev, p.alpha, p.beta);
+                      else if (p.act == TVR_ACT_RELU) epilogue4<TVR_ACT_RELU>(x, prev, p.alpha, p.beta);
+                      else epilogue4<TVR_ACT_NONE>(x, prev, p.alpha, p.beta);
+                    }
+                    s0[4 * i] = x.x;
+                    s0[4 * i + 1] = x.y;
+                    s0[4 * i + 2] = x.z;
+                    s0[4 * i + 3] = x.w;
+                  }
+                  break;
+                }
+                case kStPushX:
+#pragma unroll
+                  for (int i = 0; i < 4; ++i) {
+                    const float4 e =
+                        epi_load4(p.prog, 0, row0 + 4 * (4 * h + i) + (lane >> 3), col, p.m, p.n);
+                    s0[4 * i] = e.x;
+                    s0[4 * i + 1] = e.y;
+                    s0[4 * i + 2] = e.z;
+                    s0[4 * i + 3] = e.w;
+                  }
+                  break;
+                case kStPushC:
+#pragma unroll
+                  for (int j = 0; j < 16; ++j) s0[j] = sv;
+                  break;
+                case kStAdd:
+#pragma unroll
+                  for (int j = 0; j < 16; ++j) {
+                    const float a = rv ? s0[j] : s1[j], b = rv ? s1[j] : s0[j];
+                    s0[j] = __fadd_rn(a, __fmul_rn(sv, b));
+                  }
+                  break;
+                case kStSub:
+#pragma unroll
+                  for (int j = 0; j < 16; ++j) {
+                    const float a = rv ? s0[j] : s1[j], b = rv ? s1[j] : s0[j];
+                    s0[j] = __fadd_rn(a, __fmul_rn(-sv, b));
+                  }
+                  break;
+                case kStMul:
+#pragma unroll
+                  for (int j = 0; j < 16; ++j) s0[j] = __fmul_rn(s1[j], s0[j]);
+                  break;
+                case kStRelu:
+#pragma unroll
+                  for (int j = 0; j < 16; ++j) s0[j] = s0[j] > 0.f ? s0[j] : 0.f;
+                  break;
+                case kStSilu:
+#pragma unroll
+                  for (int j = 0; j < 16; ++j) s0[j] = s0[j] / (1.f + expf(-s0[j]));
+                  break;
+                case kStNeg:
+#pragma unroll
+                  for (int j = 0; j < 16; ++j) s0[j] = -s0[j];
+                  break;
+                case kStScale:
+#pragma unroll
+                  for (int j = 0; j < 16; ++j) s0[j] = __fmul_rn(sv, s0[j]);
+                  break;
+                case kStSigmoid:
+#pragma unroll
+                  for (int j = 0; j < 16; ++j) s0[j] = 1.f / (1.f + expf(-s0[j]));
+                  break;
+                case kStExp:
+#pragma unroll
+                  for (int j = 0; j < 16; ++j) s0[j] = expf(s0[j]);
+                  break;
+                default:  // kStAbs
+#pragma unroll
+                  for (int j = 0; j < 16; ++j) s0[j] = fabsf(s0[j]);
+                  break;
+              }
+            }
+            // compiler barrier: keeps the stores below every load above
+            asm volatile("" ::: "memory");
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const int64_t row = row0 + 4 * (4 * h + i) + (lane >> 3);
+              if (row >= p.m || col >= p.n) continue;
+              float* dst = cbase + row * p.ldc + col;
               if (full4) {
-                prev[i] = *reinterpret_cast<const float4*>(src);
+                *reinterpret_cast<float4*>(dst) =
+                    make_float4(s0[4 * i], s0[4 * i + 1], s0[4 * i + 2], s0[4 * i + 3]);
               } else {
-                prev[i].x = src[0];
-                prev[i].y = col + 1 < p.n ? src[1] : 0.f;
-                prev[i].z = col + 2 < p.n ? src[2] : 0.f;
-                prev[i].w = col + 3 < p.n ? src[3] : 0.f;
+                dst[0] = s0[4 * i];
+                if (col + 1 < p.n) dst[1] = s0[4 * i + 1];
+                if (col + 2 < p.n) dst[2] = s0[4 * i + 2];
+                if (col + 3 < p.n) dst[3] = s0[4 * i + 3];
               }
             }
           }
-          // One straight-line loop per activation: with the choice inside
-          // the element loop the compiler evaluates the SiLU path for
-          // every element.
-          if (p.act == TVR_ACT_SILU) {
+        } else {
+          // All shared-memory reads (and reads of the previous output, when
+          // beta applies to it) are issued before any global store: a warp's
+          // memory instructions drain in order, so a load queued behind a
+          // store would wait for that store.
+          float4 xs[8];
 #pragma unroll
-            for (int i = 0; i < 8; ++i) epilogue4<TVR_ACT_SILU>(xs[i], prev[i], p.alpha, p.beta);
-          } else if (p.act == TVR_ACT_RELU) {
+          for (int i = 0; i < 8; ++i) {
+            const int rr = 4 * i + (lane >> 3);
+            const uint32_t addr = sbuf + rr * 128 + ((jj ^ (rr & 7)) << 4);
+            asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+                         : "=f"(xs[i].x), "=f"(xs[i].y), "=f"(xs[i].z), "=f"(xs[i].w)
+                         : "r"(addr));
+          }
+          if (finish && !plain) {
+            const bool read_prev = p.bias == nullptr && p.use_prev;
+            float4 prev[8];
 #pragma unroll
-            for (int i = 0; i < 8; ++i) epilogue4<TVR_ACT_RELU>(xs[i], prev[i], p.alpha, p.beta);
-          } else {
+            for (int i = 0; i < 8; ++i) {
+              const int64_t row = row0 + 4 * i + (lane >> 3);
+              prev[i] = bias4;
+              if (read_prev && row < p.m && col < p.n) {
+                const float* src = cbase + row * p.ldc + col;
+                if (full4) {
+                  prev[i] = *reinterpret_cast<const float4*>(src);
+                } else {
+                  prev[i].x = src[0];
+                  prev[i].y = col + 1 < p.n ? src[1] : 0.f;
+                  prev[i].z = col + 2 < p.n ? src[2] : 0.f;
+                  prev[i].w = col + 3 < p.n ? src[3] : 0.f;
+                }
+              }
+            }
+            // One straight-line loop per activation: with the choice inside
+            // the element loop the compiler evaluates the SiLU path for
+            // every element.
+            if (p.act == TVR_ACT_SILU) {
 #pragma unroll
-            for (int i = 0; i < 8; ++i) epilogue4<TVR_ACT_NONE>(xs[i], prev[i], p.alpha, p.beta);
+              for (int i = 0; i < 8; ++i) epilogue4<TVR_ACT_SILU>(xs[i], prev[i], p.alpha, p.beta);
+            } else if (p.act == TVR_ACT_RELU) {
+#pragma unroll
+              for (int i = 0; i < 8; ++i) epilogue4<TVR_ACT_RELU>(xs[i], prev[i], p.alpha, p.beta);
+            } else {
+#pragma unroll
+              for (int i = 0; i < 8; ++i) epilogue4<TVR_ACT_NONE>(xs[i], prev[i], p.alpha, p.beta);
+            }
+          }
+          // compiler barrier: keeps the stores below every load above
+          asm volatile("" ::: "memory");
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const int64_t row = row0 + 4 * i + (lane >> 3);
+            if (row >= p.m || col >= p.n) continue;
+            float* dst = cbase + row * p.ldc + col;
+            if (full4) {
+              *reinterpret_cast<float4*>(dst) = xs[i];
+            } else {
+              dst[0] = xs[i].x;
+              if (col + 1 < p.n) dst[1] = xs[i].y;
+              if (col + 2 < p.n) dst[2] = xs[i].z;
+              if (col + 3 < p.n) dst[3] = xs[i].w;
+            }
           }
         }
-        // compiler barrier: keeps the stores below every load above
-        asm volatile("" ::: "memory");
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const int64_t row = row0 + 4 * i + (lane >> 3);
-          if (row >= p.m || col >= p.n) continue;
-          float* dst = cbase + row * p.ldc + col;
-          if (full4) {
-            *reinterpret_cast<float4*>(dst) = xs[i];
-          } else {
-            dst[0] = xs[i].x;
-            if (col + 1 < p.n) dst[1] = xs[i].y;
-            if (col + 2 < p.n) dst[2] = xs[i].z;
-            if (col + 3 < p.n) dst[3] = xs[i].w;
-          }
-        }
+        if (PROG && c + 1 < CH) tmem_load_32_async(tcol + 32 * (c + 1), v);
         if (c + 1 < CH) {
           tmem_wait_loads();
           if constexpr (GATED) {
@@ -551,24 +703,30 @@ __global__ void __launch_bounds__(256) splitk_reduce_kernel(
 // ---- host side -----------------------------------------------------------------
 
 
-template <int BN, bool SPLIT3, bool B_NMAJOR, bool GATED = false>
+template <int BN, bool SPLIT3, bool B_NMAJOR, bool GATED = false, bool PROG = false>
 int launch_kernel(const Params& p, int grid, cudaStream_t stream, int dev) {
   using Cf = Cfg<BN, SPLIT3>;
   static std::once_flag once[64];
   static cudaError_t attr_err[64];
   std::call_once(once[dev & 63], [&]() {
-    attr_err[dev & 63] = cudaFuncSetAttribute(gemm_tc_kernel<BN, SPLIT3, B_NMAJOR, GATED>,
+    attr_err[dev & 63] = cudaFuncSetAttribute(gemm_tc_kernel<BN, SPLIT3, B_NMAJOR, GATED, PROG>,
                                               cudaFuncAttributeMaxDynamicSharedMemorySize,
                                               Cf::SMEM_BYTES);
   });
   TVR_CUDA_TRY(attr_err[dev & 63]);
-  gemm_tc_kernel<BN, SPLIT3, B_NMAJOR, GATED><<<grid, NUM_THREADS, Cf::SMEM_BYTES, stream>>>(p);
+  gemm_tc_kernel<BN, SPLIT3, B_NMAJOR, GATED, PROG>
+      <<<grid, NUM_THREADS, Cf::SMEM_BYTES, stream>>>(p);
   TVR_LAUNCH_CHECK();
   return TVR_OK;
 }
 
 template <int BN>
-int launch_bn(const Params& p, bool split3, bool b_nmajor, int grid, cudaStream_t s, int dev) {
+int launch_bn(const Params& p, bool split3, bool b_nmajor, int grid, cudaStream_t s, int dev,
+              bool prog = false) {
+  if (prog) {  // K-major weights only
+    return split3 ? launch_kernel<BN, true, false, false, true>(p, grid, s, dev)
+                  : launch_kernel<BN, false, false, false, true>(p, grid, s, dev);
+  }
   if (split3) {
     return b_nmajor ? launch_kernel<BN, true, true>(p, grid, s, dev)
                     : launch_kernel<BN, true, false>(p, grid, s, dev);
@@ -610,7 +768,7 @@ int grid_sms(int dev, int sms) {
 int gemm_tcgen05(const float* a, const float* b, const float* bias, float* c, int64_t m,
                  int64_t n, int64_t k, int64_t lda, int64_t ldb, int64_t ldc, int64_t batch,
                  int64_t sa, int64_t sb, int64_t sc, float alpha, float beta, int act,
-                 bool trans_b, bool split3, cudaStream_t stream) {
+                 bool trans_b, bool split3, cudaStream_t stream, const EpiProg* prog) {
   using namespace tc;
   // TMA addressability: 16-byte aligned bases, row and batch strides in
   // multiples of 16 bytes, extents that fit the 32-bit coordinates.
@@ -743,10 +901,17 @@ int gemm_tcgen05(const float* a, const float* b, const float* bias, float* c, in
   p.status = device_status_ptr(dev);
   const int grid = static_cast<int>(std::min<int64_t>(units, grid_sms(dev, sms)));
   const bool b_nmajor = !trans_b;
+  // A pointwise program runs in the epilogue when each output element is
+  // final there (no split-K, one batch entry, K-major weights); otherwise it
+  // runs as a pass over the finished output.
+  const bool has_prog = prog != nullptr && prog->n_nodes > 0;
+  const bool prog_in_kernel = has_prog && splits == 1 && batch == 1 && trans_b &&
+                              prog->n_ops > 0;
+  if (prog_in_kernel) p.prog = *prog;
   switch (bn) {
-    case 256: rc = launch_bn<256>(p, split3, b_nmajor, grid, stream, dev); break;
-    case 128: rc = launch_bn<128>(p, split3, b_nmajor, grid, stream, dev); break;
-    default: rc = launch_bn<64>(p, split3, b_nmajor, grid, stream, dev); break;
+    case 256: rc = launch_bn<256>(p, split3, b_nmajor, grid, stream, dev, prog_in_kernel); break;
+    case 128: rc = launch_bn<128>(p, split3, b_nmajor, grid, stream, dev, prog_in_kernel); break;
+    default: rc = launch_bn<64>(p, split3, b_nmajor, grid, stream, dev, prog_in_kernel); break;
   }
   if (rc != TVR_OK) return rc;
   if (splits > 1) {
@@ -754,6 +919,7 @@ int gemm_tcgen05(const float* a, const float* b, const float* bias, float* c, in
         out, splits, bias, c, m, n, ldc, alpha, beta, act, p.use_prev);
     TVR_LAUNCH_CHECK();
   }
+  if (has_prog && !prog_in_kernel) return epi_prog_inplace(*prog, c, ldc, m, n, stream);
   return TVR_OK;
 }
 
