@@ -9,8 +9,9 @@ LayerNorm gamma 1 / beta 0), the usual GPT-2 initialisation.
 
 The same ``forward`` runs on any device: on ``tvarant`` every op dispatches to
 the sm_100a kernels (embedding, broadcast add, layer_norm, linear / linear_act
-GEMMs, strided copies for the head split, bmm, softmax); on the CPU it gives the
-PyTorch fp32 result used to check it.
+GEMMs, the output projections with their residual add in the GEMM epilogue
+(linear_pointwise), strided copies for the head split, bmm, softmax); on the
+CPU it gives the PyTorch fp32 result used to check it.
 
 Multi-GPU: the batch is split over the ranks (``shard_batch``), which splits
 every attention bmm / softmax over batch x heads; weights are replicated and no
@@ -103,6 +104,23 @@ def _linear_silu(x, w, b):
     return torch.nn.functional.silu(torch.nn.functional.linear(x, w, b))
 
 
+# y + r with y = the GEMM result (input 0) and r the residual (input 1):
+# Load, Load, Add(alpha 1) in the pointwise opcodes (IEEE addition commutes,
+# so this is exactly r + y)
+_RESIDUAL_PROGRAM = ([0, 0, 2], [-1, -1, 0], [-1, -1, 1], [0, 1, -1], [1.0, 1.0, 1.0],
+                     [0.0, 0.0, 0.0])
+
+
+def _linear_residual(r, x, w, b):
+    """r + linear(x, w, b); on the tvarant device the residual add runs in the
+    GEMM's epilogue (tvarant::linear_pointwise), so the projection's output
+    never makes a round trip through memory."""
+    if x.device.type == "tvarant":
+        return torch.ops.tvarant.linear_pointwise(x, w, b, "none", True, 0, [r],
+                                                  *_RESIDUAL_PROGRAM)
+    return r + torch.nn.functional.linear(x, w, b)
+
+
 def forward(model: GPT2, ids: torch.Tensor, mask: torch.Tensor | None = None,
             attention: str = "bmm") -> torch.Tensor:
     """Logits [B, S, vocab] for token ids [B, S] (int64, on the model's device).
@@ -134,9 +152,9 @@ def forward(model: GPT2, ids: torch.Tensor, mask: torch.Tensor | None = None,
             v = qkv[2].reshape(B * H, S, hd)
             att = F.softmax(torch.bmm(q, k.transpose(1, 2)) + mask, dim=-1)
             o = torch.bmm(att, v).view(B, H, S, hd).permute(0, 2, 1, 3).reshape(B, S, d)
-        x = x + F.linear(o, L.w_proj, L.b_proj)
+        x = _linear_residual(x, o, L.w_proj, L.b_proj)
         h = F.layer_norm(x, (d,), L.ln2_g, L.ln2_b, 1e-5)
-        x = x + F.linear(_linear_silu(h, L.w_fc, L.b_fc), L.w_out, L.b_out)
+        x = _linear_residual(x, _linear_silu(h, L.w_fc, L.b_fc), L.w_out, L.b_out)
     x = F.layer_norm(x, (d,), model.lnf_g, model.lnf_b, 1e-5)
     return F.linear(x, model.wte)
 
