@@ -690,6 +690,11 @@ def _main() -> int:
                     help="gpt2 workload: bmm + mask + softmax + bmm (the config), or the fused "
                          "F.scaled_dot_product_attention kernel")
     ap.add_argument("--chunks", type=int, default=2, help="mlp workload: token chunks overlapped with the all-reduce")
+    ap.add_argument("--comm", choices=["nccl", "nvls"], default="nccl",
+                    help="mlp workload at N>1: NCCL all-reduce, or this library's NVLink SHARP "
+                         "all-reduce over symmetric memory")
+    ap.add_argument("--nvls-blocks", type=int, default=32,
+                    help="mlp workload, --comm nvls: CTAs of the all-reduce kernel")
     ap.add_argument("--nccl-ctas", type=int, default=32,
                     help="mlp workload: CTAs NCCL may use per collective (the GEMMs leave that many SMs free; 0: no limit)")
     ap.add_argument("--no-cpu-baseline", action="store_true")

@@ -53,6 +53,7 @@ extern "C" {
 #define TVR_DEV_TIMEOUT_EPILOGUE 3 /* epilogue gave up waiting for an accumulator   */
 #define TVR_DEV_TIMEOUT_DRAIN 4    /* exit-time drain of async copies gave up       */
 #define TVR_DEV_TIMEOUT_CONVERT 5  /* 3xTF32 converter gave up waiting for a stage  */
+#define TVR_DEV_TIMEOUT_PEER 6     /* a cross-rank barrier gave up waiting for a rank */
 
 /* GEMM precision modes */
 #define TVR_GEMM_AUTO 0    /* TVARANT_GEMM_MODE env, else 3xTF32               */
@@ -398,6 +399,32 @@ int tvr_nccl_all_gather(const void* send, void* recv, int64_t send_count, int dt
                         void* comm, void* stream);
 int tvr_nccl_comm_destroy(void* comm);
 int tvr_nccl_comm_abort(void* comm);
+
+/* ---- NVLink SHARP all-reduce (no counterpart in the reference) -------- */
+
+#define TVR_NVLS_MAX_RANKS 8
+#define TVR_NVLS_MAX_BLOCKS 64
+/* uint32 words of one rank's flag array */
+#define TVR_NVLS_FLAG_WORDS (2 * TVR_NVLS_MAX_BLOCKS * TVR_NVLS_MAX_RANKS)
+
+/* In-place sum of `count` fp32 values over `world` ranks (one process per
+ * GPU) of a buffer bound to an NVLink multicast object: `multicast` is the
+ * buffer's multicast address on this rank, peer_flags[r] the address (on this
+ * rank) of rank r's flag array of TVR_NVLS_FLAG_WORDS uint32 (zero when
+ * first used; mapped peer memory, e.g. from a symmetric-memory rendezvous).
+ * Rank r reduces slice r through the switch (multimem.ld_reduce) and stores
+ * it to every rank (multimem.st); two barriers on the flags order the call
+ * after every rank's writes of the input and before every rank's next use.
+ * epoch_counter is one uint32 in this rank's device memory, zero before the
+ * first call with these flag arrays; each call first advances it on the
+ * stream (so a captured CUDA graph uses a fresh value on every replay) and
+ * the barriers wait for that value.  Every rank makes the same sequence of
+ * calls with the same count and blocks.  count must be a multiple of
+ * 4 x world.  A barrier wait that expires (2 s; a rank that never arrives)
+ * sets TVR_DEV_TIMEOUT_PEER in the device status word and the kernel
+ * returns: check tvr_get_status after synchronizing. */
+int tvr_nvls_all_reduce_f32(void* multicast, int64_t count, void* const* peer_flags, int rank,
+                            int world, uint32_t* epoch_counter, int blocks, void* stream);
 
 #if defined(__GNUC__)
 #pragma GCC visibility pop

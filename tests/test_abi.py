@@ -123,6 +123,29 @@ def test_nccl_entry_points_fail_cleanly_without_a_communicator():
         capi.ERR_INVALID, capi.ERR_NCCL)
 
 
+def test_nvls_all_reduce_validates_before_touching_a_device():
+    import ctypes
+
+    capi.load()
+    flags = (ctypes.c_void_p * 2)(16, 32)
+    counter = ctypes.c_void_p(64)
+    mc = ctypes.c_void_p(256)
+
+    def call(count=64, world=2, rank=0, blocks=8, mc=mc, counter=counter):
+        return capi.try_call("tvr_nvls_all_reduce_f32", mc, count, ctypes.addressof(flags), rank,
+                             world, counter, blocks, None)
+
+    assert call(world=1) == capi.ERR_INVALID  # one rank: nothing to reduce with
+    assert call(world=9) == capi.ERR_INVALID
+    assert call(rank=2) == capi.ERR_INVALID
+    assert call(count=36) == capi.ERR_INVALID  # not a multiple of 4 x 2 ranks
+    assert "multiple of 4" in capi.last_error()
+    assert call(blocks=65) == capi.ERR_INVALID
+    assert call(mc=ctypes.c_void_p(8)) == capi.ERR_INVALID  # unaligned multicast address
+    assert call(counter=None) == capi.ERR_INVALID
+    assert call(count=0) == capi.OK  # nothing to do: no launch, no device needed
+
+
 def test_extension_loads_without_gpu():
     import torch
 

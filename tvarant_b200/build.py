@@ -51,6 +51,7 @@ CUDA_SOURCES = [
     "attention.cu",
     "pointwise_jit.cu",
     "nccl.cu",
+    "nvls.cu",
 ]
 
 EXT_SOURCES = [

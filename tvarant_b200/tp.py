@@ -14,6 +14,12 @@ Tokens are independent through the stack, so the batch is cut into chunks
 that run as separate chains: while chunk i is being all-reduced on the
 communication stream, chunk i+1 runs its GEMMs on the compute stream.
 
+The exchange is either NCCL's all-reduce (``Communicator``) or this
+library's NVLink SHARP all-reduce (``nvls.NvlsAllReduce``, one symmetric
+buffer per chunk): the down projection writes its partial sums straight into
+the symmetric buffer and the switch reduces them in place, so each GPU sends
+and receives the activations once instead of twice.
+
 The reference has a single device and no collectives; this module is the
 multi-GPU path of its fused-linear MLP.
 """
@@ -106,13 +112,22 @@ def mlp_layer(x: torch.Tensor, w_gate: torch.Tensor, w_up: torch.Tensor,
     return torch.ops.tvarant.linear_act(h, w_down, None, "none", True)
 
 
-class TPMLPStack:
-    """A stack of gated-SiLU MLP layers split over the ranks of ``comm``."""
+def _gemm_mode() -> int:
+    """The GEMM precision mode the tvarant ops use (float32 matmul precision)."""
+    from tvarant_b200 import capi
 
-    def __init__(self, layers, comm: Communicator | None, chunks: int = 2):
+    return capi.GEMM_3XTF32 if torch.get_float32_matmul_precision() == "highest" else capi.GEMM_TF32
+
+
+class TPMLPStack:
+    """A stack of gated-SiLU MLP layers split over the ranks of ``comm``
+    (NCCL) or of ``nvls`` (one ``NvlsAllReduce`` per token chunk)."""
+
+    def __init__(self, layers, comm: Communicator | None, chunks: int = 2, nvls=None):
         self.layers = layers  # list of (gate, up, down) shards on this device
         self.comm = comm
-        self.chunks = max(1, chunks)
+        self.nvls = list(nvls) if nvls else None
+        self.chunks = len(self.nvls) if self.nvls else max(1, chunks)
         self._streams = None
 
     def _comm_streams(self, device: int):
@@ -121,23 +136,89 @@ class TPMLPStack:
         return self._streams[0]
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
-        if self.comm is None or self.comm.world == 1:
+        if self.nvls is None and (self.comm is None or self.comm.world == 1):
             for wg, wu, wd in self.layers:
                 x = mlp_layer(x, wg, wu, wd)
             return x
         device = x.device.index or 0
         # The persistent GEMM otherwise holds every SM and the all-reduce of
         # chunk i would wait for the GEMMs of chunk i+1 instead of overlapping
-        # them: leave NCCL's CTAs their SMs while the stack runs.
+        # them: leave the collective's CTAs their SMs while the stack runs.
         from tvarant_b200 import _C
 
         prev_limit = _C.gemm_sm_limit(device)
-        if self.comm.max_ctas > 0:
-            _C.set_gemm_sm_limit(device, max(1, _C.sm_count(device) - self.comm.max_ctas))
+        ctas = self.nvls[0].blocks if self.nvls else self.comm.max_ctas
+        if ctas > 0 and self.chunks > 1:
+            _C.set_gemm_sm_limit(device, max(1, _C.sm_count(device) - ctas))
         try:
+            if self.nvls:
+                return self._forward_nvls(x, device)
             return self._forward_tp(x, device)
         finally:
             _C.set_gemm_sm_limit(device, prev_limit)
+
+    def _forward_nvls(self, x: torch.Tensor, device: int) -> torch.Tensor:
+        """The stack over raw device pointers: per chunk and layer, the SwiGLU
+        GEMM (reading the previous layer's reduced activations in place), the
+        down projection into the chunk's symmetric buffer, and the in-place
+        NVLS all-reduce on the communication stream."""
+        import ctypes
+
+        from tvarant_b200 import capi
+
+        if x.dim() != 2 or not x.is_contiguous():
+            raise ValueError("the NVLS stack takes a contiguous [tokens, d_model] input")
+        T, d = x.shape
+        n = len(self.nvls)
+        rows = -(-T // n)
+        f = self.layers[0][0].shape[0]
+        if rows * d > self.nvls[0].numel:
+            raise ValueError(f"a chunk of {rows} x {d} exceeds the symmetric buffers")
+        mode = _gemm_mode()
+        compute = torch.tvarant.current_stream(device)
+        comm_stream = self._comm_streams(device)
+        c_h = torch.tvarant.stream_handle(compute)
+        m_h = torch.tvarant.stream_handle(comm_stream) if n > 1 else c_h
+        vp = ctypes.c_void_p
+        h = torch.empty((rows, f), device=x.device)
+        ready = [None] * n
+        for li, (wg, wu, wd) in enumerate(self.layers):
+            for c in range(n):
+                r0 = c * rows
+                rc = min(rows, T - r0)
+                if rc <= 0:
+                    continue
+                src = x.data_ptr() + 4 * r0 * d if li == 0 else self.nvls[c].data_ptr
+                if ready[c] is not None:
+                    compute.wait_event(ready[c])
+                capi.call("tvr_gemm_swiglu", vp(src), vp(wg.data_ptr()), vp(wu.data_ptr()),
+                          vp(h.data_ptr()), rc, f, d, d, wg.stride(0), wu.stride(0), f, mode,
+                          vp(c_h))
+                capi.call("tvr_gemm_bias_act", vp(h.data_ptr()), vp(wd.data_ptr()), None,
+                          vp(self.nvls[c].data_ptr), rc, d, f, f, wd.stride(0), d, 1.0, 0.0, 0,
+                          1, mode, vp(c_h))
+                if n == 1:
+                    self.nvls[c].all_reduce(rc * d, c_h)
+                    continue
+                done = torch.Event(device=f"tvarant:{device}")
+                done.record(compute)
+                comm_stream.wait_event(done)
+                self.nvls[c].all_reduce(rc * d, m_h)
+                ev = torch.Event(device=f"tvarant:{device}")
+                ev.record(comm_stream)
+                ready[c] = ev
+        for ev in ready:
+            if ev is not None:
+                compute.wait_event(ev)
+        out = torch.empty((T, d), device=x.device)
+        for c in range(n):
+            rc = min(rows, T - c * rows)
+            if rc > 0:
+                capi.call("tvr_memcpy_d2d", vp(out.data_ptr() + 4 * c * rows * d),
+                          vp(self.nvls[c].data_ptr), 4 * rc * d, vp(c_h))
+        # h was allocated on the compute stream; the GEMMs that use it are
+        # all on that stream
+        return out
 
     def _forward_tp(self, x: torch.Tensor, device: int) -> torch.Tensor:
         comm_stream = self._comm_streams(device)

@@ -183,8 +183,18 @@ def _mlp(args, rank, world, local_rank):
     torch.set_float32_matmul_precision("high" if args.mode == "tf32" else "highest")
     dev = f"tvarant:{local_rank}"
     layers = build_stack(rank, world, dev, layers=args.layers)
-    comm = Communicator.from_process_group(local_rank, args.nccl_ctas) if world > 1 else None
-    stack = TPMLPStack(layers, comm, chunks=args.chunks if world > 1 else 1)
+    comm, nvls = None, None
+    use_nvls = world > 1 and args.comm == "nvls"
+    if use_nvls:
+        from tvarant_b200.nvls import NvlsAllReduce
+
+        chunks = max(1, args.chunks)
+        rows = -(-TOKENS // chunks)
+        nvls = [NvlsAllReduce(rows * D_MODEL, local_rank, blocks=args.nvls_blocks)
+                for _ in range(chunks)]
+    elif world > 1:
+        comm = Communicator.from_process_group(local_rank, args.nccl_ctas)
+    stack = TPMLPStack(layers, comm, chunks=args.chunks if world > 1 else 1, nvls=nvls)
     g = torch.Generator().manual_seed(7)
     x_host = torch.randn(TOKENS, D_MODEL, generator=g)
     if torch.cuda.is_available():
@@ -233,6 +243,11 @@ def _mlp(args, rank, world, local_rank):
     if comm is not None:
         bench._barrier(world)
         comm.destroy()
+    if nvls is not None:
+        bench._barrier(world)
+        for buf in nvls:
+            buf.close()
+        bench._barrier(world)
     if rank != 0:
         return None
     flops_total = 3 * 2 * TOKENS * D_MODEL * D_FF * args.layers
@@ -250,7 +265,10 @@ def _mlp(args, rank, world, local_rank):
         "config": {"workload": f"Llama-7B-shaped gated-SiLU MLP stack, {args.layers} layers, "
                                f"d_model {D_MODEL}, d_ff {D_FF}, {TOKENS} tokens, TP x{world}",
                    "parallelism": f"tp{world}", "chunks": stack.chunks,
-                   "nccl_max_ctas": args.nccl_ctas if world > 1 else None,
+                   "exchange": ("NVLS all-reduce (multimem, this library's kernel, "
+                                f"{args.nvls_blocks} CTAs)" if use_nvls
+                                else ("NCCL all-reduce" if world > 1 else None)),
+                   "nccl_max_ctas": args.nccl_ctas if comm is not None else None,
                    "cuda_graph": not args.no_graph,
                    "eager_tokens_per_s": TOKENS / (eager_ms / 1e3),
                    "layer_ms_one_rank_gemms": layer_ms,
@@ -263,7 +281,9 @@ def _mlp(args, rank, world, local_rank):
                      "frac": (target_s * 1e3) / ms,
                      "traffic": None,
                      "peak_source": "cuBLAS TF32 8192^3 measured in this run; NVLink 770 GB/s"},
-        "gpu_launches": args.steps * args.layers * (4 * stack.chunks) + (args.steps * args.layers * stack.chunks if world > 1 else 0),
+        # per layer and chunk: the SwiGLU GEMM and the down GEMM, plus the
+        # epoch step and the all-reduce kernel with NVLS (NCCL's are not ours)
+        "gpu_launches": args.steps * args.layers * stack.chunks * (4 if use_nvls else 2),
         "clocks": clocks.summary(),
         "device_status": status,
     }
