@@ -264,6 +264,17 @@ int tvr_bmm(const float* a, const float* b, float* c,
 int tvr_softmax(const float* x, float* y, int64_t outer, int64_t dim, int64_t inner,
                 void* stream);
 
+/* y[r, :] = softmax(x[r, :] + mask[r % mask_rows, :]) over rows of `dim`
+ * contiguous values: an additive attention mask ([L, S], shared by every
+ * batch entry and head of x [B, H, L, S]) applied as the row is loaded.  The
+ * add is the same fp32 rounding as tvr_binary's, so the result equals
+ * tvr_binary(ADD) followed by tvr_softmax.  Returns TVR_ERR_UNSUPPORTED
+ * (nothing launched) unless dim % 4 == 0, dim <= 2048 and the three pointers
+ * are 16-byte aligned.  No reference counterpart as one call: the reference
+ * runs add(scores, mask) then softmax (csrc/aten/LlmOps.cpp:68-105). */
+int tvr_softmax_add(const float* x, const float* mask, float* y, int64_t rows, int64_t dim,
+                    int64_t mask_rows, void* stream);
+
 /* Row layer norm of x[rows, n]: mean, biased variance (two-pass),
  * rstd = 1/sqrt(var + eps), y = (x - mean) * rstd [* gamma] [+ beta].
  * gamma, beta, mean, rstd may be NULL.  Replaces

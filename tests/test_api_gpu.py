@@ -480,3 +480,25 @@ def test_tril_triu(shape, diagonal):
     assert torch.equal(torch.tril(b, diagonal).cpu(), torch.tril(torch.ones(shape, dtype=torch.bool), diagonal))
     t = x.t() if x.dim() == 2 else x.transpose(-1, -2)  # a strided input
     assert torch.equal(torch.triu(t.to("tvarant"), diagonal).cpu(), torch.triu(t, diagonal))
+
+
+@pytest.mark.parametrize("mask_shape", ["LS", "BHLS", "B11S"])
+def test_softmax_add_op(tvarant, mask_shape):
+    """tvarant::softmax_add against PyTorch's softmax(x + mask) on the CPU: a
+    trailing [L, S] mask (fused kernel), a full-shape mask (fused, one mask row
+    per score row), and a [B, 1, 1, S] mask (broadcast that is not a trailing
+    block: the add and the softmax run as written)."""
+    g = torch.Generator().manual_seed(11)
+    B, H, L, S = 2, 3, 40, 256
+    x = torch.randn(B, H, L, S, generator=g)
+    if mask_shape == "LS":
+        mask = torch.full((L, S), float("-inf")).triu(1 + S - L)
+    elif mask_shape == "BHLS":
+        mask = torch.randn(B, H, L, S, generator=g)
+    else:
+        mask = torch.randn(B, 1, 1, S, generator=g)
+    want = torch.softmax(x + mask, dim=-1)
+    got = torch.ops.tvarant.softmax_add(x.to("tvarant"), mask.to("tvarant")).cpu()
+    assert got.shape == want.shape
+    assert torch.allclose(got, want, rtol=1e-5, atol=1e-7)
+    assert torch.tvarant.get_status() == 0

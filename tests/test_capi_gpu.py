@@ -310,6 +310,41 @@ def test_softmax(lib, rng, shape, dim):
     assert max_rel(y, ref, 1e-30) <= TOL_POINTWISE
 
 
+@pytest.mark.parametrize("batch,L,S", [(6, 128, 1024), (2, 64, 64), (3, 5, 2048), (1, 7, 4)])
+def test_softmax_add_causal_mask(lib, rng, batch, L, S):
+    """softmax(scores + mask) with an [L, S] mask shared by every batch row:
+    the same bits as the device's add followed by its softmax, and the
+    reference's add + softmax (oracle) within the pointwise tolerance."""
+    import torch
+
+    x = (rng.standard_normal((batch, L, S)) * 2).astype(np.float32)
+    mask = np.triu(np.full((L, S), -np.inf, np.float32), 1 + max(S - L, 0))
+    mask[:, :2] += rng.standard_normal((L, 2)).astype(np.float32)  # finite, not only 0 / -inf
+    dx, dm = _dev(x), _dev(mask)
+    dy = torch.empty_like(dx)
+    lib.call("tvr_softmax_add", _p(dx), _p(dm), _p(dy), batch * L, S, L, _stream())
+    got = _host(dy)
+    summed = torch.empty_like(dx)
+    sizes = lib.int64_array([batch, L, S])
+    lib.call("tvr_binary", lib.BINARY_ADD, _p(dx), _p(dm), _p(summed), 3, sizes,
+             lib.int64_array([L * S, S, 1]), lib.int64_array([0, S, 1]), 1.0, _stream())
+    two_step = torch.empty_like(dx)
+    lib.call("tvr_softmax", _p(summed), _p(two_step), batch * L, S, 1, _stream())
+    assert np.array_equal(got, _host(two_step))
+    ref = oracle.softmax(oracle.binary(0, x, np.broadcast_to(mask, x.shape).copy()), -1)
+    assert max_rel(got, ref, 1e-30) <= TOL_POINTWISE
+
+
+def test_softmax_add_declines_rows_it_does_not_take(lib):
+    import torch
+
+    x = torch.zeros(4, 1002, device="cuda")  # 1002 % 4 != 0
+    assert lib.try_call("tvr_softmax_add", _p(x), _p(x), _p(x), 4, 1002, 1, _stream()) == \
+        lib.ERR_UNSUPPORTED
+    assert lib.try_call("tvr_softmax_add", _p(x), _p(x), _p(x), 4, 1002, 3, _stream()) == \
+        lib.ERR_INVALID  # 4 rows are not a whole number of 3 mask rows
+
+
 @pytest.mark.parametrize("rows,n", [(2, 8), (16, 768), (33, 4096), (5, 1000), (4, 1001), (3, 20000)])
 @pytest.mark.parametrize("affine", [True, False])
 def test_layer_norm(lib, rng, rows, n, affine):

@@ -1,5 +1,5 @@
 // The tvarant operator library: tvarant::linear_act, tvarant::pointwise,
-// tvarant::linear_swiglu and tvarant::linear_pointwise.
+// tvarant::linear_swiglu, tvarant::linear_pointwise and tvarant::softmax_add.
 //
 // Schemas are the reference's, verbatim (csrc/aten/CustomOps.cpp:101-106),
 // so graphs produced by torch_tvarant.compiler run unchanged.  linear_act
@@ -218,6 +218,37 @@ at::Tensor linear_pointwise(const at::Tensor& x, const at::Tensor& weight,
   return pointwise(all, ops, a, b, input_ids, alphas, consts);
 }
 
+// softmax(x + mask, dim=-1) with the additive mask applied as each row is
+// loaded (tvr_softmax_add): the attention-scores pattern
+// softmax(q k^T * scale + mask) without the [.., L, S] round trip of the add.
+// The mask must be a contiguous trailing block of x's shape (e.g. [L, S] for
+// scores [B, H, L, S]); other shapes, and rows the fused kernel does not
+// take, run the add and the softmax as written.
+at::Tensor softmax_add(const at::Tensor& x, const at::Tensor& mask) {
+  check_fp32(x, "softmax_add");
+  TORCH_CHECK(x.dim() >= 1, "softmax_add: expected at least 1D scores");
+  c10::DeviceGuard guard(x.device());
+  at::Tensor m = to_device_like(mask, x);
+  check_fp32(m, "softmax_add");
+  const int64_t dim = x.size(-1);
+  const int64_t k = x.dim() - m.dim();
+  bool trailing = k >= 0 && m.dim() >= 1 && m.is_contiguous();
+  for (int64_t i = 0; trailing && i < m.dim(); ++i) trailing = m.size(i) == x.size(k + i);
+  if (trailing && dim > 0 && x.numel() > 0) {
+    at::Tensor xc = x.is_contiguous() ? x : contiguous_copy(x);
+    at::Tensor out = empty_device(xc.sizes(), xc.options());
+    const int64_t rows = xc.numel() / dim;
+    const int64_t mask_rows = m.numel() / dim;
+    const int rc = tvr_softmax_add(static_cast<const float*>(xc.data_ptr()),
+                                   static_cast<const float*>(m.data_ptr()),
+                                   static_cast<float*>(out.data_ptr()), rows, dim, mask_rows,
+                                   current_stream_handle());
+    if (rc == TVR_OK) return out;
+    TORCH_CHECK(rc == TVR_ERR_UNSUPPORTED, "tvarant: ", tvr_last_error());
+  }
+  return at::_softmax(at::add(x, m), -1, false);
+}
+
 }  // namespace
 }  // namespace tvarant::ops
 
@@ -232,6 +263,7 @@ TORCH_LIBRARY(tvarant, m) {
       "linear_pointwise(Tensor x, Tensor weight, Tensor? bias, str act, bool trans_b, "
       "int gemm_input, Tensor[] inputs, int[] ops, int[] a, int[] b, int[] input_ids, "
       "float[] alphas, float[] consts) -> Tensor");
+  m.def("softmax_add(Tensor x, Tensor mask) -> Tensor");
 }
 
 TORCH_LIBRARY_IMPL(tvarant, PrivateUse1, m) {
@@ -239,4 +271,5 @@ TORCH_LIBRARY_IMPL(tvarant, PrivateUse1, m) {
   m.impl("pointwise", TORCH_FN(tvarant::ops::pointwise));
   m.impl("linear_swiglu", TORCH_FN(tvarant::ops::linear_swiglu));
   m.impl("linear_pointwise", TORCH_FN(tvarant::ops::linear_pointwise));
+  m.impl("softmax_add", TORCH_FN(tvarant::ops::softmax_add));
 }

@@ -55,17 +55,23 @@ __device__ __forceinline__ float block_max(float v, float* red) {
 
 // ---- softmax: one warp per row, the row held in registers ---------------------
 // VPL float4 per lane; requires dim % 4 == 0, 16-byte aligned rows,
-// dim <= 128 * VPL.
-template <int VPL>
+// dim <= 128 * VPL.  MASK: softmax(x + mask[row % mask_rows]) — the additive
+// mask (e.g. a causal mask shared by every batch entry and head) is added as
+// the row is loaded, with the same single fp32 rounding as a separate add.
+template <int VPL, bool MASK = false>
 __global__ void __launch_bounds__(256) softmax_warp_kernel(const float* __restrict__ x,
                                                            float* __restrict__ y, int64_t rows,
-                                                           int dim) {
+                                                           int dim,
+                                                           const float* __restrict__ mask = nullptr,
+                                                           int64_t mask_rows = 1) {
   const int lane = threadIdx.x & 31;
   const int64_t warps_total = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
   const int n4 = dim >> 2;
   for (int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
        row < rows; row += warps_total) {
     const float4* xr = reinterpret_cast<const float4*>(x + row * dim);
+    const float4* mr = MASK ? reinterpret_cast<const float4*>(mask + (row % mask_rows) * dim)
+                            : nullptr;
     float4 v[VPL];
     float m = -INFINITY;
 #pragma unroll
@@ -73,6 +79,13 @@ __global__ void __launch_bounds__(256) softmax_warp_kernel(const float* __restri
       const int c = lane + 32 * j;
       if (c < n4) {
         v[j] = __ldcs(xr + c);
+        if constexpr (MASK) {
+          const float4 a = __ldg(mr + c);
+          v[j].x = __fadd_rn(v[j].x, a.x);
+          v[j].y = __fadd_rn(v[j].y, a.y);
+          v[j].z = __fadd_rn(v[j].z, a.z);
+          v[j].w = __fadd_rn(v[j].w, a.w);
+        }
         m = fmaxf(m, fmaxf(fmaxf(v[j].x, v[j].y), fmaxf(v[j].z, v[j].w)));
       }
     }
@@ -204,13 +217,18 @@ __global__ void __launch_bounds__(1024) softmax_long_row_kernel(const float* __r
 
 template <int VPL>
 void launch_softmax_warp(const float* x, float* y, int64_t rows, int dim, cudaStream_t s,
-                         int dev) {
+                         int dev, const float* mask = nullptr, int64_t mask_rows = 1) {
   const int warps_per_block = 8;
   int64_t blocks = ceil_div(rows, warps_per_block);
   const int64_t cap = static_cast<int64_t>(sm_count(dev)) * 32;
   if (blocks > cap) blocks = cap;
-  softmax_warp_kernel<VPL><<<static_cast<unsigned>(blocks), 32 * warps_per_block, 0, s>>>(
-      x, y, rows, dim);
+  if (mask != nullptr) {
+    softmax_warp_kernel<VPL, true><<<static_cast<unsigned>(blocks), 32 * warps_per_block, 0, s>>>(
+        x, y, rows, dim, mask, mask_rows);
+  } else {
+    softmax_warp_kernel<VPL><<<static_cast<unsigned>(blocks), 32 * warps_per_block, 0, s>>>(
+        x, y, rows, dim);
+  }
 }
 
 // ---- layer norm: one block per row, the row held in registers ---------------
@@ -414,6 +432,31 @@ int tvr_softmax(const float* x, float* y, int64_t outer, int64_t dim, int64_t in
   }
   softmax_generic_kernel<<<elementwise_grid(outer * inner, 256, dev), 256, 0, s>>>(
       x, y, outer, dim, inner);
+  TVR_LAUNCH_CHECK();
+  return TVR_OK;
+}
+
+int tvr_softmax_add(const float* x, const float* mask, float* y, int64_t rows, int64_t dim,
+                    int64_t mask_rows, void* stream) {
+  TVR_CHECK(rows >= 0 && dim >= 0, "tvr_softmax_add: negative size");
+  TVR_CHECK(mask_rows >= 1 && rows % mask_rows == 0,
+            "tvr_softmax_add: %lld rows are not a whole number of %lld mask rows",
+            (long long)rows, (long long)mask_rows);
+  if (rows == 0 || dim == 0) return TVR_OK;
+  TVR_CHECK(x && mask && y, "tvr_softmax_add: null pointer");
+  if (!(dim % 4 == 0 && dim <= 2048 && aligned16(x) && aligned16(y) && aligned16(mask))) {
+    return TVR_ERR_UNSUPPORTED;  // the caller adds, then calls tvr_softmax
+  }
+  const int dev = current_device();
+  cudaStream_t s = as_stream(stream);
+  const int d = static_cast<int>(dim);
+  switch (static_cast<int>(ceil_div(dim, 128))) {
+    case 1: launch_softmax_warp<1>(x, y, rows, d, s, dev, mask, mask_rows); break;
+    case 2: launch_softmax_warp<2>(x, y, rows, d, s, dev, mask, mask_rows); break;
+    case 3: case 4: launch_softmax_warp<4>(x, y, rows, d, s, dev, mask, mask_rows); break;
+    case 5: case 6: case 7: case 8: launch_softmax_warp<8>(x, y, rows, d, s, dev, mask, mask_rows); break;
+    default: launch_softmax_warp<16>(x, y, rows, d, s, dev, mask, mask_rows); break;
+  }
   TVR_LAUNCH_CHECK();
   return TVR_OK;
 }

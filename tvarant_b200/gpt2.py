@@ -10,7 +10,8 @@ LayerNorm gamma 1 / beta 0), the usual GPT-2 initialisation.
 The same ``forward`` runs on any device: on ``tvarant`` every op dispatches to
 the sm_100a kernels (embedding, broadcast add, layer_norm, linear / linear_act
 GEMMs, the output projections with their residual add in the GEMM epilogue
-(linear_pointwise), strided copies for the head split, bmm, softmax); on the
+(linear_pointwise), strided copies for the head split, bmm, softmax with the
+causal mask added as the scores are loaded (softmax_add)); on the
 CPU it gives the PyTorch fp32 result used to check it.
 
 Multi-GPU: the batch is split over the ranks (``shard_batch``), which splits
@@ -111,6 +112,15 @@ _RESIDUAL_PROGRAM = ([0, 0, 2], [-1, -1, 0], [-1, -1, 1], [0, 1, -1], [1.0, 1.0,
                      [0.0, 0.0, 0.0])
 
 
+def _softmax_masked(scores, mask):
+    """softmax(scores + mask, -1); on the tvarant device the additive mask is
+    applied inside the softmax kernel (tvarant::softmax_add), so the scores
+    make one round trip through memory instead of two."""
+    if scores.device.type == "tvarant":
+        return torch.ops.tvarant.softmax_add(scores, mask)
+    return torch.nn.functional.softmax(scores + mask, dim=-1)
+
+
 def _linear_residual(r, x, w, b):
     """r + linear(x, w, b); on the tvarant device the residual add runs in the
     GEMM's epilogue (tvarant::linear_pointwise), so the projection's output
@@ -150,7 +160,7 @@ def forward(model: GPT2, ids: torch.Tensor, mask: torch.Tensor | None = None,
             q = (qkv[0] * scale).reshape(B * H, S, hd)
             k = qkv[1].reshape(B * H, S, hd)
             v = qkv[2].reshape(B * H, S, hd)
-            att = F.softmax(torch.bmm(q, k.transpose(1, 2)) + mask, dim=-1)
+            att = _softmax_masked(torch.bmm(q, k.transpose(1, 2)), mask)
             o = torch.bmm(att, v).view(B, H, S, hd).permute(0, 2, 1, 3).reshape(B, S, d)
         x = _linear_residual(x, o, L.w_proj, L.b_proj)
         h = F.layer_norm(x, (d,), L.ln2_g, L.ln2_b, 1e-5)
