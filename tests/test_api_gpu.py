@@ -502,3 +502,38 @@ def test_softmax_add_op(tvarant, mask_shape):
     assert got.shape == want.shape
     assert torch.allclose(got, want, rtol=1e-5, atol=1e-7)
     assert torch.tvarant.get_status() == 0
+
+
+@pytest.mark.parametrize("precision,tol", [("high", 5e-3), ("highest", 1e-5)])
+def test_compiled_residual_and_masked_attention(tvarant, precision, tol):
+    """A compiled block with a residual projection (linear + r in the GEMM
+    epilogue) and masked attention scores (softmax_add) against PyTorch on
+    the CPU."""
+    import torch.nn as nn
+
+    class Block(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.proj = nn.Linear(64, 64)
+
+        def forward(self, q, k, v, mask, r):
+            att = torch.softmax(q @ k.transpose(-1, -2) + mask, dim=-1) @ v
+            return self.proj(att) + r
+
+    g = torch.Generator().manual_seed(4)
+    B, L, D = 3, 96, 64
+    q, k, v, r = (torch.randn(B, L, D, generator=g) for _ in range(4))
+    mask = torch.full((L, L), float("-inf")).triu(1)
+    model = Block()
+    with torch.no_grad():
+        want = model(q, k, v, mask, r)
+        torch.set_float32_matmul_precision(precision)
+        try:
+            compiled = tvarant.compiler.compile(model.to("tvarant"))
+            assert tvarant.compiler.last_log.get("softmax_mask") == 1
+            assert tvarant.compiler.last_log.get("gemm_pointwise") == 1
+            dev = [t.to("tvarant") for t in (q, k, v, mask, r)]
+            got = compiled(*dev).cpu()
+        finally:
+            torch.set_float32_matmul_precision("highest")
+    assert float((got - want).norm() / want.norm()) <= tol

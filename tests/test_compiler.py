@@ -251,3 +251,68 @@ def test_gemm_with_other_users_keeps_its_output():
     assert torch.ops.tvarant.linear_act in targets and torch.ops.tvarant.pointwise in targets
     assert torch.ops.tvarant.linear_pointwise not in targets
     assert "gemm_pointwise" not in last_log
+
+
+def test_single_add_after_linear_joins_the_epilogue():
+    """linear(x) + r (a residual): one elementwise op, which fuse_pointwise
+    leaves alone, still moves into the GEMM's epilogue."""
+    class Residual(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.lin = nn.Linear(8, 8)
+
+        def forward(self, x, r):
+            return self.lin(x) + r
+
+    gm = compile_fx(trace_module(Residual()))
+    assert last_log["gemm_pointwise"] == 1 and last_log["pointwise_groups"] == 0
+    node = [n for n in gm.graph.nodes if n.target is torch.ops.tvarant.linear_pointwise][0]
+    x, w, bias, act, trans_b, gemm_input, extras, ops, a, b, input_ids, alphas, consts = node.args
+    assert act == "none" and gemm_input == 0 and [t.name for t in extras] == ["r"]
+    assert ops == [LOAD, LOAD, ADD] and input_ids == [0, 1, -1]
+    assert not any(n.target is operator.add for n in gm.graph.nodes)
+
+
+def test_scaled_linear_needs_no_extra_input():
+    class Scaled(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.lin = nn.Linear(8, 8)
+
+        def forward(self, x):
+            return F.silu(self.lin(x)) * 0.5
+
+    gm = compile_fx(trace_module(Scaled()))
+    node = [n for n in gm.graph.nodes if n.target is torch.ops.tvarant.linear_pointwise][0]
+    assert node.args[3] == "silu" and node.args[6] == [] and node.args[7] == [LOAD, SCALE]
+
+
+class _Attention(nn.Module):
+    def forward(self, q, k, v, mask):
+        return torch.softmax(q @ k.transpose(-1, -2) + mask, dim=-1) @ v
+
+
+def test_softmax_of_masked_scores_becomes_softmax_add():
+    gm = compile_fx(trace_module(_Attention()))
+    assert last_log["softmax_mask"] == 1
+    targets = _targets(gm)
+    assert torch.ops.tvarant.softmax_add in targets
+    assert not any("softmax" in str(t) and t is not torch.ops.tvarant.softmax_add for t in targets)
+    node = [n for n in gm.graph.nodes if n.target is torch.ops.tvarant.softmax_add][0]
+    assert node.args[1].name == "mask"
+
+
+def test_softmax_over_another_dim_or_shared_add_is_left_alone():
+    class Dim0(nn.Module):
+        def forward(self, s, mask):
+            return torch.softmax(s + mask, dim=0)
+
+    class Shared(nn.Module):
+        def forward(self, s, mask):
+            t = s + mask
+            return torch.softmax(t, dim=-1), t
+
+    for model in (Dim0(), Shared()):
+        gm = compile_fx(trace_module(model))
+        assert torch.ops.tvarant.softmax_add not in _targets(gm)
+        assert "softmax_mask" not in last_log

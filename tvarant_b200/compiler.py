@@ -24,9 +24,12 @@ Passes:
   reference's relu / silu / neg / sigmoid / add / mul / scalar-mul, the
   group may contain sub, exp and abs (opcodes appended after the
   reference's 0-8);
-* ``fuse_gemm_pointwise``: a pointwise program fed by a GEMM that nothing
-  else uses becomes one ``tvarant.linear_pointwise`` — the program is
-  evaluated in the GEMM's epilogue; not a reference pass.
+* ``fuse_softmax_mask``: ``softmax(scores + mask, dim=-1)`` becomes one
+  ``tvarant.softmax_add`` (the mask added as rows load); not a reference pass;
+* ``fuse_gemm_pointwise``: a pointwise program (or a single elementwise op)
+  fed by a GEMM that nothing else uses becomes one
+  ``tvarant.linear_pointwise`` — the program is evaluated in the GEMM's
+  epilogue; not a reference pass.
 
 ``last_log`` records the counts of the last run of each pass.
 """
@@ -352,18 +355,28 @@ def _gemm_source(node: object):
 
 
 def fuse_gemm_pointwise(gm: torch.fx.GraphModule) -> torch.fx.GraphModule:
-    """Rewrites a ``tvarant.pointwise`` program one of whose inputs is a GEMM
-    (``linear_act`` or an unfused linear / addmm / mm) used only by that
-    program into one ``tvarant.linear_pointwise``: the program runs in the
-    GEMM's epilogue and the GEMM's output never reaches memory.  Runs after
-    ``fuse_pointwise``; not a reference pass.  Records
+    """Rewrites a ``tvarant.pointwise`` program — or a single elementwise op,
+    which ``fuse_pointwise`` leaves alone (``linear(x) + residual``) — one of
+    whose inputs is a GEMM (``linear_act`` or an unfused linear / addmm / mm)
+    used only by it into one ``tvarant.linear_pointwise``: the program runs
+    in the GEMM's epilogue and the GEMM's output never reaches memory.  Runs
+    after ``fuse_pointwise``; not a reference pass.  Records
     ``last_log["gemm_pointwise"]`` when it fuses."""
     graph = gm.graph
     fused = 0
     for node in list(graph.nodes):
-        if node.op != "call_function" or node.target is not torch.ops.tvarant.pointwise:
+        if node.op not in ("call_function", "call_method"):
             continue
-        inputs, ops, a, b, input_ids, alphas, consts = node.args
+        if node.target is torch.ops.tvarant.pointwise:
+            inputs, ops, a, b, input_ids, alphas, consts = node.args
+        elif _pointwise_kind(node) is not None and any(
+                _gemm_source(v) is not None for v in node.args[:2]):
+            program = _build_program([node], {node})
+            if program is None:
+                continue
+            inputs, ops, a, b, input_ids, alphas, consts = program
+        else:
+            continue
         if len(ops) > 12 or len(inputs) > 3:
             continue  # beyond the epilogue program's limits
         for gi, src in enumerate(inputs):
@@ -391,12 +404,52 @@ def fuse_gemm_pointwise(gm: torch.fx.GraphModule) -> torch.fx.GraphModule:
     return gm
 
 
+def _last_dim(node: torch.fx.Node) -> bool:
+    """Whether a softmax node normalises over the last dimension."""
+    dim = node.kwargs.get("dim", node.args[1] if len(node.args) > 1 else None)
+    return dim == -1
+
+
+def fuse_softmax_mask(gm: torch.fx.GraphModule) -> torch.fx.GraphModule:
+    """Rewrites ``softmax(scores + mask, dim=-1)`` — the additive attention
+    mask — into ``tvarant.softmax_add(scores, mask)``: the mask is added as
+    each row is loaded, so the scores make one round trip through memory
+    instead of two.  The add must have no other user.  Not a reference pass;
+    records ``last_log["softmax_mask"]`` when it fuses."""
+    graph = gm.graph
+    fused = 0
+    for node in list(graph.nodes):
+        if node.op not in ("call_function", "call_method") or op_name(node) != "softmax":
+            continue
+        if not node.args or not _last_dim(node):
+            continue
+        src = node.args[0]
+        if (not isinstance(src, torch.fx.Node) or len(src.users) != 1 or op_name(src) != "add"
+                or len(src.args) != 2 or not _is_one(src.kwargs.get("alpha", 1))
+                or not all(isinstance(v, torch.fx.Node) for v in src.args)):
+            continue
+        with graph.inserting_before(node):
+            new = graph.call_function(torch.ops.tvarant.softmax_add, args=tuple(src.args))
+        node.replace_all_uses_with(new)
+        graph.erase_node(node)
+        graph.erase_node(src)
+        fused += 1
+    graph.lint()
+    gm.recompile()
+    if fused:
+        last_log["softmax_mask"] = fused
+    else:
+        last_log.pop("softmax_mask", None)
+    return gm
+
+
 def compile_fx(gm: torch.fx.GraphModule, example_inputs: Any = None) -> torch.fx.GraphModule:
-    """GEMM-epilogue fusion, SwiGLU fusion, pointwise fusion, then pointwise
-    programs into GEMM epilogues, in place."""
+    """GEMM-epilogue fusion, SwiGLU fusion, masked-softmax fusion, pointwise
+    fusion, then pointwise programs into GEMM epilogues, in place."""
     _ = example_inputs
     gm = fuse_gemm_epilogue(gm)
     gm = fuse_swiglu(gm)
+    gm = fuse_softmax_mask(gm)
     gm = fuse_pointwise(gm)
     gm = fuse_gemm_pointwise(gm)
     return gm
