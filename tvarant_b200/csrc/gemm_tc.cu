@@ -68,6 +68,7 @@ struct Params {
   CUtensorMap tma_b;     // B or B_hi: {K, N, batch} (K-major) or {N, K, batch} (N-major)
   CUtensorMap tma_a_lo;  // 3xTF32 low parts, same geometry
   CUtensorMap tma_b_lo;  // or, for a gated GEMM, the up-projection weight {K, N, 1}
+  CUtensorMap tma_c;     // TMA_C kernels: the output {N, M, batch}, 32 x 32 boxes, 128B swizzle
   const float* bias;
   float* c;
   int64_t ldc;
@@ -128,11 +129,20 @@ __device__ __forceinline__ void decode_unit(const Params& p, int u, int& b, int&
 // PROG (K-major weights, no split-K): after bias and activation, the epilogue
 // runs the pointwise program p.prog on each output element, reading the
 // program's other inputs at the element's position, and stores its result.
-template <int BN, bool SPLIT3, bool B_NMAJOR, bool GATED = false, bool PROG = false>
+//
+// TMA_C (no split-K, no program, output not read back): bias and activation
+// are applied to each thread's row in registers, the 32 x 32 chunk is staged
+// in the 128-byte-swizzled layout a TMA box of the output has, and one lane
+// stores it with cp.async.bulk.tensor — no warp issues global stores.  This
+// is what small-K GEMMs (batched attention scores, K = 64..128), whose time
+// is the output stream, need.
+template <int BN, bool SPLIT3, bool B_NMAJOR, bool GATED = false, bool PROG = false,
+          bool TMA_C = false>
 __global__ void __launch_bounds__(NUM_THREADS, 1) gemm_tc_kernel(const __grid_constant__ Params p) {
   using Cf = Cfg<BN, SPLIT3>;
   static_assert(!GATED || (BN == 256 && !SPLIT3 && !B_NMAJOR), "gated GEMM shape");
   static_assert(!PROG || (!GATED && !B_NMAJOR), "pointwise-epilogue GEMM shape");
+  static_assert(!TMA_C || (!GATED && !PROG), "TMA-store epilogue");
   constexpr int OUT_BN = GATED ? BN / 2 : BN;  // output columns per tile
   constexpr int STAGES = Cf::STAGES;
   extern __shared__ uint8_t smem_raw[];
@@ -374,6 +384,53 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) gemm_tc_kernel(const __grid_co
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(tempty_bar + 8 * acc);
+        }
+        if constexpr (TMA_C) {
+          const int col0 = tn * OUT_BN + half * HC + 32 * c;
+          if (!plain) {
+            // act(alpha * acc + beta * bias): epilogue4's arithmetic, per
+            // element; one straight-line loop per activation (with the choice
+            // inside the loop every element would pay for the SiLU path)
+            float bv[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              bv[j] = p.bias != nullptr && col0 + j < p.n ? __ldg(p.bias + col0 + j) : 0.f;
+            }
+            if (p.act == TVR_ACT_SILU) {
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                v[j] = act_fixed<TVR_ACT_SILU>(__fadd_rn(__fmul_rn(p.alpha, v[j]), __fmul_rn(p.beta, bv[j])));
+            } else if (p.act == TVR_ACT_RELU) {
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                v[j] = act_fixed<TVR_ACT_RELU>(__fadd_rn(__fmul_rn(p.alpha, v[j]), __fmul_rn(p.beta, bv[j])));
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                v[j] = __fadd_rn(__fmul_rn(p.alpha, v[j]), __fmul_rn(p.beta, bv[j]));
+            }
+          }
+          // the previous chunk's store must have read the staging buffer
+          if (lane == 0) bulk_wait_read();
+          __syncwarp();
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const uint32_t addr = sbuf + lane * 128 + ((j ^ (lane & 7)) << 4);
+            asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(v[4 * j]),
+                         "f"(v[4 * j + 1]), "f"(v[4 * j + 2]), "f"(v[4 * j + 3])
+                         : "memory");
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0 && col0 < p.n && row0 < p.m) {  // (boxes past the edge are clipped)
+            tma_store_3d(&p.tma_c, sbuf, col0, static_cast<int>(row0), zc);
+            bulk_commit();
+          }
+          if (c + 1 < CH) {
+            tmem_load_32_async(tcol + 32 * (c + 1), v);
+            tmem_wait_loads();
+          }
+          continue;
         }
         // stage: thread = row, 16-byte chunk j of row r at chunk j ^ (r & 7)
 #pragma unroll
@@ -618,6 +675,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) gemm_tc_kernel(const __grid_co
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1u;
     }
+    // every store this warp issued is complete before the CTA exits
+    if (TMA_C && lane == 0) bulk_wait_all();
+    __syncwarp();
     if (!ok) {
       record_status(p.status, TVR_DEV_TIMEOUT_EPILOGUE);
       *const_cast<volatile int*>(abort_flag) = 1;
@@ -703,18 +763,19 @@ __global__ void __launch_bounds__(256) splitk_reduce_kernel(
 // ---- host side -----------------------------------------------------------------
 
 
-template <int BN, bool SPLIT3, bool B_NMAJOR, bool GATED = false, bool PROG = false>
+template <int BN, bool SPLIT3, bool B_NMAJOR, bool GATED = false, bool PROG = false,
+          bool TMA_C = false>
 int launch_kernel(const Params& p, int grid, cudaStream_t stream, int dev) {
   using Cf = Cfg<BN, SPLIT3>;
   static std::once_flag once[64];
   static cudaError_t attr_err[64];
   std::call_once(once[dev & 63], [&]() {
-    attr_err[dev & 63] = cudaFuncSetAttribute(gemm_tc_kernel<BN, SPLIT3, B_NMAJOR, GATED, PROG>,
-                                              cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                              Cf::SMEM_BYTES);
+    attr_err[dev & 63] =
+        cudaFuncSetAttribute(gemm_tc_kernel<BN, SPLIT3, B_NMAJOR, GATED, PROG, TMA_C>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, Cf::SMEM_BYTES);
   });
   TVR_CUDA_TRY(attr_err[dev & 63]);
-  gemm_tc_kernel<BN, SPLIT3, B_NMAJOR, GATED, PROG>
+  gemm_tc_kernel<BN, SPLIT3, B_NMAJOR, GATED, PROG, TMA_C>
       <<<grid, NUM_THREADS, Cf::SMEM_BYTES, stream>>>(p);
   TVR_LAUNCH_CHECK();
   return TVR_OK;
@@ -722,10 +783,18 @@ int launch_kernel(const Params& p, int grid, cudaStream_t stream, int dev) {
 
 template <int BN>
 int launch_bn(const Params& p, bool split3, bool b_nmajor, int grid, cudaStream_t s, int dev,
-              bool prog = false) {
+              bool prog = false, bool tma_c = false) {
   if (prog) {  // K-major weights only
     return split3 ? launch_kernel<BN, true, false, false, true>(p, grid, s, dev)
                   : launch_kernel<BN, false, false, false, true>(p, grid, s, dev);
+  }
+  if (tma_c) {
+    if (split3) {
+      return b_nmajor ? launch_kernel<BN, true, true, false, false, true>(p, grid, s, dev)
+                      : launch_kernel<BN, true, false, false, false, true>(p, grid, s, dev);
+    }
+    return b_nmajor ? launch_kernel<BN, false, true, false, false, true>(p, grid, s, dev)
+                    : launch_kernel<BN, false, false, false, false, true>(p, grid, s, dev);
   }
   if (split3) {
     return b_nmajor ? launch_kernel<BN, true, true>(p, grid, s, dev)
@@ -908,10 +977,24 @@ int gemm_tcgen05(const float* a, const float* b, const float* bias, float* c, in
   const bool prog_in_kernel = has_prog && splits == 1 && batch == 1 && trans_b &&
                               prog->n_ops > 0;
   if (prog_in_kernel) p.prog = *prog;
+  // Output through TMA stores: whole-K tiles whose output is not read back,
+  // describable by a tensor map (16-byte aligned rows and batches), and at
+  // least one 32 x 32 box wide.
+  const bool tma_c = !prog_in_kernel && splits == 1 && p.use_prev == 0 && c_vec && n >= 32 &&
+                     m >= 32 && ldc <= (int64_t(1) << 36) / 4;
+  if (tma_c) {
+    const uint64_t c_bs = static_cast<uint64_t>(batch > 1 ? sc : m * ldc) * 4;
+    if ((rc = encode_3d(&p.tma_c, c, n, m, batch, ldc * 4, c_bs ? c_bs : 16, 32, 32)) != TVR_OK)
+      return rc;
+  }
   switch (bn) {
-    case 256: rc = launch_bn<256>(p, split3, b_nmajor, grid, stream, dev, prog_in_kernel); break;
-    case 128: rc = launch_bn<128>(p, split3, b_nmajor, grid, stream, dev, prog_in_kernel); break;
-    default: rc = launch_bn<64>(p, split3, b_nmajor, grid, stream, dev, prog_in_kernel); break;
+    case 256:
+      rc = launch_bn<256>(p, split3, b_nmajor, grid, stream, dev, prog_in_kernel, tma_c);
+      break;
+    case 128:
+      rc = launch_bn<128>(p, split3, b_nmajor, grid, stream, dev, prog_in_kernel, tma_c);
+      break;
+    default: rc = launch_bn<64>(p, split3, b_nmajor, grid, stream, dev, prog_in_kernel, tma_c); break;
   }
   if (rc != TVR_OK) return rc;
   if (splits > 1) {
