@@ -37,6 +37,10 @@
 #include "gemm_common.cuh"
 #include "tc_ptx.cuh"
 
+// TMA_C instances leave the chunk loop early (`continue`), so the register-
+// store epilogue after it is unreachable there by design.
+#pragma nv_diag_suppress 128
+
 namespace tvr {
 namespace tc {
 
@@ -432,6 +436,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) gemm_tc_kernel(const __grid_co
           }
           continue;
         }
+        if constexpr (PROG) {
+          // the previous chunk's TMA store must have read the staging buffer
+          if (lane == 0) bulk_wait_read();
+          __syncwarp();
+        }
         // stage: thread = row, 16-byte chunk j of row r at chunk j ^ (r & 7)
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
@@ -580,23 +589,23 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) gemm_tc_kernel(const __grid_co
                   break;
               }
             }
-            // compiler barrier: keeps the stores below every load above
-            asm volatile("" ::: "memory");
+            // results back into the staged chunk (these rows' PushY reads
+            // are done); the chunk leaves through one TMA store below
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
-              const int64_t row = row0 + 4 * (4 * h + i) + (lane >> 3);
-              if (row >= p.m || col >= p.n) continue;
-              float* dst = cbase + row * p.ldc + col;
-              if (full4) {
-                *reinterpret_cast<float4*>(dst) =
-                    make_float4(s0[4 * i], s0[4 * i + 1], s0[4 * i + 2], s0[4 * i + 3]);
-              } else {
-                dst[0] = s0[4 * i];
-                if (col + 1 < p.n) dst[1] = s0[4 * i + 1];
-                if (col + 2 < p.n) dst[2] = s0[4 * i + 2];
-                if (col + 3 < p.n) dst[3] = s0[4 * i + 3];
-              }
+              const int rr = 4 * (4 * h + i) + (lane >> 3);
+              const uint32_t addr = sbuf + rr * 128 + ((jj ^ (rr & 7)) << 4);
+              asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(s0[4 * i]),
+                           "f"(s0[4 * i + 1]), "f"(s0[4 * i + 2]), "f"(s0[4 * i + 3])
+                           : "memory");
             }
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          const int col0 = tn * OUT_BN + half * HC + 32 * c;
+          if (lane == 0 && col0 < p.n && row0 < p.m) {  // (boxes past the edge are clipped)
+            tma_store_3d(&p.tma_c, sbuf, col0, static_cast<int>(row0), zc);
+            bulk_commit();
           }
         } else {
           // All shared-memory reads (and reads of the previous output, when
@@ -676,7 +685,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) gemm_tc_kernel(const __grid_co
       if (acc == 0) acc_phase ^= 1u;
     }
     // every store this warp issued is complete before the CTA exits
-    if (TMA_C && lane == 0) bulk_wait_all();
+    if ((TMA_C || PROG) && lane == 0) bulk_wait_all();
     __syncwarp();
     if (!ok) {
       record_status(p.status, TVR_DEV_TIMEOUT_EPILOGUE);
@@ -974,15 +983,15 @@ int gemm_tcgen05(const float* a, const float* b, const float* bias, float* c, in
   // final there (no split-K, one batch entry, K-major weights); otherwise it
   // runs as a pass over the finished output.
   const bool has_prog = prog != nullptr && prog->n_nodes > 0;
-  const bool prog_in_kernel = has_prog && splits == 1 && batch == 1 && trans_b &&
-                              prog->n_ops > 0;
-  if (prog_in_kernel) p.prog = *prog;
   // Output through TMA stores: whole-K tiles whose output is not read back,
   // describable by a tensor map (16-byte aligned rows and batches), and at
-  // least one 32 x 32 box wide.
-  const bool tma_c = !prog_in_kernel && splits == 1 && p.use_prev == 0 && c_vec && n >= 32 &&
-                     m >= 32 && ldc <= (int64_t(1) << 36) / 4;
-  if (tma_c) {
+  // least one 32 x 32 box wide.  A program runs in the epilogue only then.
+  const bool tma_ok = splits == 1 && p.use_prev == 0 && c_vec && n >= 32 && m >= 32 &&
+                      ldc <= (int64_t(1) << 36) / 4;
+  const bool prog_in_kernel = has_prog && tma_ok && batch == 1 && trans_b && prog->n_ops > 0;
+  if (prog_in_kernel) p.prog = *prog;
+  const bool tma_c = tma_ok && !has_prog;
+  if (tma_c || prog_in_kernel) {
     const uint64_t c_bs = static_cast<uint64_t>(batch > 1 ? sc : m * ldc) * 4;
     if ((rc = encode_3d(&p.tma_c, c, n, m, batch, ldc * 4, c_bs ? c_bs : 16, 32, 32)) != TVR_OK)
       return rc;
