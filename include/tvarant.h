@@ -390,6 +390,19 @@ int tvr_gemm_pointwise(const float* a, const float* b, const float* bias, float*
                        int n_nodes, int n_inputs, int gemm_input, const float* const* inputs,
                        const int64_t* input_ld, void* stream);
 
+/* How tvr_gemm_pointwise runs a program (host only, no device): *n_ops
+ * receives the length of the two-slot stack code the tensor-core GEMM's
+ * epilogue evaluates, 0 when the program runs as a pass over the GEMM's
+ * output instead (it needs more than two stack slots or reads two extra
+ * inputs).  Up to cap operations are written to ops / rev / vals: the stack
+ * opcode (0 push GEMM result, 1 push the extra input, 2 push constant vals[i],
+ * 3 add a + vals[i]*b, 4 sub a - vals[i]*b, 5 mul, 6 relu, 7 silu, 8 neg,
+ * 9 scale vals[i]*a, 10 sigmoid, 11 exp, 12 abs; binary operations take
+ * a = slot 1, b = slot 0, or the reverse when rev[i] is 1).  The program is
+ * checked as tvr_gemm_pointwise checks it. */
+int tvr_gemm_pointwise_plan(const tvr_pw_node* nodes, int n_nodes, int n_inputs, int gemm_input,
+                            int* n_ops, int8_t* ops, int8_t* rev, float* vals, int cap);
+
 /* ---- NCCL (no counterpart in the reference, which has one device) ------ */
 
 /* NCCL is loaded at run time; these return TVR_ERR_NCCL when it is absent.

@@ -119,6 +119,7 @@ SIGNATURES: dict[str, list] = {
     "tvr_triangle": [_vp, _vp, _i32, _i64, _i64, _i64, _i64, _i32, _vp],
     "tvr_pointwise": [_vp, _i32, _i32, _vp, _vp, _i64, _vp],
     "tvr_pointwise_source": [_vp, _i32, _i32, ctypes.c_char_p, _sz, _psz],
+    "tvr_gemm_pointwise_plan": [_vp, _i32, _i32, _i32, _pi, _vp, _vp, _vp, _i32],
     "tvr_gemm_pointwise": [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _f32, _f32,
                            _i32, _i32, _i32, _vp, _i32, _i32, _i32, _vp, _pi64, _vp],
     "tvr_nvls_all_reduce_f32": [_vp, _i64, _vp, _i32, _i32, _vp, _i32, _vp],

@@ -224,3 +224,31 @@ int build_epi_prog(const tvr_pw_node* nodes, int n_nodes, int n_inputs, int gemm
 }
 
 }  // namespace tvr
+
+extern "C" int tvr_gemm_pointwise_plan(const tvr_pw_node* nodes, int n_nodes, int n_inputs,
+                                       int gemm_input, int* n_ops, int8_t* ops, int8_t* rev,
+                                       float* vals, int cap) {
+  using namespace tvr;
+  TVR_CHECK(n_ops != nullptr, "gemm_pointwise_plan: null output count");
+  TVR_CHECK(cap >= 0 && (cap == 0 || (ops && rev && vals)), "gemm_pointwise_plan: bad buffers");
+  // the checks and the translation of build_epi_prog, with stand-in input
+  // addresses (one row each, far from the stand-in output)
+  static const float stand_in[2][4] = {};
+  const float* inputs[EPI_MAX_EXTRA + 1] = {stand_in[0], stand_in[1], stand_in[1]};
+  const int64_t lds[EPI_MAX_EXTRA + 1] = {0, 0, 0};
+  static float out_stand_in[4];
+  TVR_CHECK(n_inputs >= 1 && n_inputs <= EPI_MAX_EXTRA + 1,
+            "gemm_pointwise_plan: %d inputs (the GEMM result and at most %d more)", n_inputs,
+            EPI_MAX_EXTRA);
+  EpiProg g;
+  const int rc = build_epi_prog(nodes, n_nodes, n_inputs, gemm_input, inputs, lds, out_stand_in,
+                                1, 4, 4, &g);
+  if (rc != TVR_OK) return rc;
+  *n_ops = g.n_ops;
+  for (int i = 0; i < g.n_ops && i < cap; ++i) {
+    ops[i] = g.sop[i];
+    rev[i] = g.rev[i];
+    vals[i] = g.sval[i];
+  }
+  return TVR_OK;
+}
