@@ -2,18 +2,20 @@
 """Benchmark of the tvarant B200 backend (one JSON line on rank 0).
 
 Default workload — the fused-GEMM sweep's largest point: ``nn.Linear(4096,
-4096)`` + SiLU on X [16384, 4096] (TF32 tensor cores), then the JIT-fused
-chain ``abs(neg(exp(Y - Z)))`` on the output, compiled by
-``torch_tvarant.compiler.compile`` into one ``tvarant.linear_act`` and one
-``tvarant.pointwise``.  A step is one pass of that graph over one batch.
+4096)`` + SiLU on X [16384, 4096] (TF32 tensor cores), then the chain
+``abs(neg(exp(Y - Z)))`` on the output, compiled by
+``torch_tvarant.compiler.compile`` into one ``tvarant.linear_pointwise``
+(the chain runs in the GEMM's epilogue).  A step is one pass of that graph
+over one batch.
 
 * ``value``: TFLOP/s of the GEMM (2*M*N*K per step) over the whole step with
   inputs resident in HBM, summed over ranks (weak scaling: every rank runs
   its own replica; this path has no exchange step).
 * ``e2e``: the same metric through the same API with host buffers: X and Z
-  copied from pinned host memory and the result copied back every step.
-* ``roofline``: the tcgen05 GEMM kernel, timed with events on the stream it
-  runs on, against the TF32 dense peak measured with cuBLAS in this run.
+  copied from pinned host memory and the result copied back every step
+  (consecutive steps' copies overlap on two copy streams).
+* ``roofline``: the step's kernel, timed with events on the stream it runs
+  on, against the TF32 dense peak measured with cuBLAS in this run.
 * ``cpu_baseline``: the reference's own simulator kernels
   (HostKernels.cpp, built into oracle/_ref) on a row sample, all host cores.
 
@@ -611,7 +613,8 @@ def run_sweep(args, rank, world, local_rank) -> dict | None:
         "dtype": "tf32 and f32 (3xTF32)",
         "data": "synthetic (seeded N(0,1) activations, U(-1/64,1/64) weights)",
         "config": {"workload": "fused-GEMM sweep: linear+bias+SiLU M in {1,16,128,1024,4096,16384} "
-                               "K=N=4096 + JIT-fused abs(neg(exp(Y - Z))), TF32 and 3xTF32; "
+                               "K=N=4096 + abs(neg(exp(Y - Z))) compiled into the GEMM epilogue "
+                               "(M > 128) or a program pass (M <= 128), TF32 and 3xTF32; "
                                "value = the M=16384 TF32 point",
                    "points": table, "parallelism": f"replicas x{world}",
                    "l2": "points whose operands fit in L2 rotate over weight copies in distinct "

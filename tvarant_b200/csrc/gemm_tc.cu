@@ -10,9 +10,13 @@
 //               k-block into a STAGES-deep ring (mbarrier full/empty pairs)
 //   warp 1      allocates TMEM; one lane issues the MMAs (4 x K=8 per
 //               k-block, 12 in 3xTF32 mode) and commits each stage back
-//   warps 2-5   epilogue: tcgen05.ld of the 128 x BN accumulator, bias /
-//               alpha / beta / activation, staged through swizzled shared
-//               memory and written with TMA stores
+//   warps 2-9   epilogue: tcgen05.ld of the 128 x BN accumulator in 32 x 32
+//               chunks, each staged through a 128-byte-swizzled shared
+//               buffer; bias / alpha / beta / activation, and optionally a
+//               pointwise program (PROG), applied on the way; the chunk
+//               leaves through one TMA bulk-tensor store (TMA_C, PROG) or
+//               coalesced register stores (split-K partials, outputs read
+//               back as beta * C, outputs a tensor map cannot describe)
 // The accumulator is double-buffered in TMEM (2 x BN columns) so the
 // epilogue of tile i overlaps the main loop of tile i+1.
 //
