@@ -680,7 +680,8 @@ def _main() -> int:
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["tvarant", "reference"], default="tvarant")
-    ap.add_argument("--workload", choices=["gemm", "sweep", "llm-ops", "mlp", "bmm", "gpt2"],
+    ap.add_argument("--workload", choices=["gemm", "sweep", "llm-ops", "llama-ops", "mlp", "bmm",
+                                           "gpt2"],
                     default="gemm")
     ap.add_argument("--batch", type=int, default=256, help="bmm workload: batch size")
     ap.add_argument("--m", type=int, default=M_DEFAULT)

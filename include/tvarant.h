@@ -341,6 +341,27 @@ int tvr_where(const void* cond, const void* a, const void* b, void* out, int ele
 int tvr_triangle(const void* x, void* out, int elem_size, int64_t batch, int64_t rows,
                  int64_t cols, int64_t diagonal, int upper, void* stream);
 
+/* RMSNorm over rows of n contiguous values: y = x / sqrt(mean(x^2) + eps)
+ * [* weight] (weight [n] or null); rstd[row] = 1 / sqrt(mean(x^2) + eps)
+ * when rstd is not null.  y must not overlap x.  No reference counterpart
+ * (the reference has no RMSNorm; F.rms_norm decomposes into pow / mean /
+ * rsqrt / mul there). */
+int tvr_rms_norm(const float* x, const float* weight, float* y, float* rstd, int64_t rows,
+                 int64_t n, float eps, void* stream);
+
+/* Rotary position embedding of [batch, seq, heads] vectors of `dim` values
+ * (dim contiguous; x_strides / y_strides give the batch, position and head
+ * strides in elements): for each rotation pair (a, b) — (i, i + dim/2), or
+ * (2i, 2i + 1) when interleaved — with c = cos_table[p][i], s =
+ * sin_table[p][i] at position p = pos_offset + position:
+ *   a' = a*c - b*s,  b' = b*c + a*s   (products and sums rounded separately).
+ * The tables have table_rows rows of table_stride >= dim/2 values.  x and y
+ * may be the same buffer with the same strides.  No reference counterpart. */
+int tvr_rope(const float* x, float* y, const float* cos_table, const float* sin_table,
+             int64_t batch, int64_t seq, int64_t heads, int64_t dim, const int64_t* x_strides,
+             const int64_t* y_strides, int64_t table_rows, int64_t table_stride,
+             int64_t pos_offset, int interleaved, void* stream);
+
 /* ---- pointwise JIT ----------------------------------------------------- */
 
 /* One SSA node.  Opcodes 0-8 keep the reference numbering

@@ -146,6 +146,22 @@ def test_nvls_all_reduce_validates_before_touching_a_device():
     assert call(count=0) == capi.OK  # nothing to do: no launch, no device needed
 
 
+def test_rms_norm_and_rope_validate_arguments():
+    import ctypes
+
+    capi.load()
+    assert capi.try_call("tvr_rms_norm", None, None, None, None, 4, 0, 1e-6, None) == capi.ERR_INVALID
+    assert capi.try_call("tvr_rms_norm", None, None, None, None, 0, 8, 1e-6, None) == capi.OK
+    st = capi.int64_array([0, 0, 0])
+    # odd head dim
+    assert capi.try_call("tvr_rope", None, None, None, None, 1, 1, 1, 7, st, st, 4, 4, 0, 0,
+                         None) == capi.ERR_INVALID
+    # positions past the end of the angle tables
+    assert capi.try_call("tvr_rope", None, None, None, None, 1, 8, 1, 8, st, st, 10, 4, 3, 0,
+                         None) == capi.ERR_INVALID
+    assert "exceed" in capi.last_error()
+
+
 def test_extension_loads_without_gpu():
     import torch
 

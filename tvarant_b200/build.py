@@ -52,6 +52,7 @@ CUDA_SOURCES = [
     "pointwise_jit.cu",
     "nccl.cu",
     "nvls.cu",
+    "llama_ops.cu",
 ]
 
 EXT_SOURCES = [
@@ -68,6 +69,7 @@ EXT_SOURCES = [
     "Collectives.cpp",
     "Attention.cpp",
     "Select.cpp",
+    "LlamaOps.cpp",
 ]
 
 

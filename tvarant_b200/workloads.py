@@ -52,7 +52,71 @@ def run(args, rank: int, world: int, local_rank: int):
         return _bmm(args, rank, world, local_rank)
     if args.workload == "gpt2":
         return _gpt2(args, rank, world, local_rank)
+    if args.workload == "llama-ops":
+        return _llama_ops(args, rank, world, local_rank)
     return _mlp(args, rank, world, local_rank)
+
+
+# ----------------------------------------------------------------------------- llama ops
+
+def _llama_ops(args, rank, world, local_rank):
+    """The row ops a Llama-style decoder adds to the LLM op set, at Llama-7B
+    shapes over 8192 tokens: RMSNorm of the [8192, 4096] hidden states, and
+    RoPE of the query heads [1, 32, 8192, 128] (Hugging Face layout, [T, 128]
+    angle tables).  Both are HBM-bound: GB/s against the measured copy rate."""
+    import bench
+
+    g = torch.Generator().manual_seed(1)
+    dev = "tvarant"
+    x = torch.randn(8192, 4096, generator=g).to(dev)
+    w = (1 + 0.1 * torch.randn(4096, generator=g)).to(dev)
+    q = torch.randn(1, 32, 8192, 128, generator=g).to(dev)
+    inv = 1.0 / (10000 ** (torch.arange(0, 128, 2, dtype=torch.float32) / 128))
+    ang = torch.arange(8192, dtype=torch.float32)[:, None] * inv[None, :]
+    cos = torch.cat([ang.cos(), ang.cos()], -1).to(dev)
+    sin = torch.cat([ang.sin(), ang.sin()], -1).to(dev)
+    F = torch.nn.functional
+    ops = {
+        "rms_norm": (lambda: F.rms_norm(x, (4096,), w, 1e-6), 2 * x.numel() * 4 + 4096 * 4),
+        # q in and out; the half-width tables are read once per position
+        "rope": (lambda: torch.ops.tvarant.rope(q, cos, sin), 2 * q.numel() * 4 + 2 * 8192 * 64 * 4),
+    }
+    for fn, _ in ops.values():
+        for _ in range(args.warmup):
+            fn()
+    torch.tvarant.synchronize()
+    per = {}
+    for name, (fn, nbytes) in ops.items():
+        ms = _time_steps(fn, args.steps)
+        per[name] = {"ms": ms, "GB/s": nbytes / (ms / 1e3) / 1e9}
+    with bench.ClockSampler(local_rank) as clocks:
+        h0 = time.perf_counter()
+        total_ms = _time_steps(lambda: [fn() for fn, _ in ops.values()], args.steps)
+        clocks.mark(h0, time.perf_counter())
+    total_bytes = sum(nb for _, nb in ops.values())
+    if rank != 0:
+        return None
+    hbm = bench._peaks().get("hbm_gbs", 6650.0)
+    for v in per.values():
+        v["frac_hbm"] = v["GB/s"] / hbm
+    value = total_bytes / (total_ms / 1e3) / 1e9
+    return {
+        "metric": "fused-GEMM TFLOP/s (% peak); LLM-op GB/s (% HBM); tokens/s at 1/2/4/8 GPU",
+        "value": value * world, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": total_ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded N(0,1) activations, Llama-7B shapes)",
+        "config": {"workload": "rms_norm [8192,4096] + rope q [1,32,8192,128] (rotate-half, "
+                               "[T,128] tables)",
+                   "per_op": per, "parallelism": f"replicas x{world}",
+                   "l2": "each operand (134 MB) exceeds the 126 MB L2"},
+        "roofline": {"bound": "hbm", "achieved": value, "peak": hbm, "unit": "GB/s",
+                     "frac": value / hbm, "traffic": None,
+                     "peak_source": "MEASURED_PEAKS.json hbm_gbs"},
+        "gpu_launches": 2 * args.steps,
+        "clocks": clocks.summary(),
+        "device_status": torch.tvarant.get_status(),
+    }
 
 
 # ----------------------------------------------------------------------------- bmm
