@@ -18,6 +18,8 @@
 
 #include <cmath>
 
+#include "fastdiv.cuh"
+
 namespace tvr {
 namespace {
 
@@ -141,6 +143,49 @@ __global__ void __launch_bounds__(256) rope_kernel(const float* x, float* y,
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// Rotate-half with 4 pairs per thread: float4 loads of both halves and of the
+// tables (half % 4 == 0, every stride and base 16-byte aligned), 32-bit
+// index arithmetic (fewer than 2^31 quads, offsets below 2^31).
+struct RopeVec {
+  FastDiv quads, heads, seq;
+  uint32_t half;
+  uint32_t xs_b, xs_s, xs_h, ys_b, ys_s, ys_h;
+  uint32_t pos_offset, table_stride;
+};
+
+__global__ void __launch_bounds__(256) rope_half_vec_kernel(const float* x, float* y,
+                                                            const float* __restrict__ cos_t,
+                                                            const float* __restrict__ sin_t,
+                                                            RopeVec d, uint32_t total) {
+  const uint32_t stride = gridDim.x * blockDim.x;
+  for (uint32_t t = blockIdx.x * blockDim.x + threadIdx.x; t < total; t += stride) {
+    uint32_t r = fast_div(t, d.quads);
+    const uint32_t i = 4 * (t - r * d.quads.d);
+    const uint32_t r2 = fast_div(r, d.heads);
+    const uint32_t h = r - r2 * d.heads.d;
+    const uint32_t b = fast_div(r2, d.seq);
+    const uint32_t s = r2 - b * d.seq.d;
+    const float* xv = x + b * d.xs_b + s * d.xs_s + h * d.xs_h;
+    float* yv = y + b * d.ys_b + s * d.ys_s + h * d.ys_h;
+    const uint32_t ti = (s + d.pos_offset) * d.table_stride + i;
+    const float4 a = *reinterpret_cast<const float4*>(xv + i);
+    const float4 bb = *reinterpret_cast<const float4*>(xv + i + d.half);
+    const float4 c = __ldg(reinterpret_cast<const float4*>(cos_t + ti));
+    const float4 sn = __ldg(reinterpret_cast<const float4*>(sin_t + ti));
+    float4 oa, ob;
+    oa.x = __fsub_rn(__fmul_rn(a.x, c.x), __fmul_rn(bb.x, sn.x));
+    oa.y = __fsub_rn(__fmul_rn(a.y, c.y), __fmul_rn(bb.y, sn.y));
+    oa.z = __fsub_rn(__fmul_rn(a.z, c.z), __fmul_rn(bb.z, sn.z));
+    oa.w = __fsub_rn(__fmul_rn(a.w, c.w), __fmul_rn(bb.w, sn.w));
+    ob.x = __fadd_rn(__fmul_rn(bb.x, c.x), __fmul_rn(a.x, sn.x));
+    ob.y = __fadd_rn(__fmul_rn(bb.y, c.y), __fmul_rn(a.y, sn.y));
+    ob.z = __fadd_rn(__fmul_rn(bb.z, c.z), __fmul_rn(a.z, sn.z));
+    ob.w = __fadd_rn(__fmul_rn(bb.w, c.w), __fmul_rn(a.w, sn.w));
+    *reinterpret_cast<float4*>(yv + i) = oa;
+    *reinterpret_cast<float4*>(yv + i + d.half) = ob;
+  }
+}
+
 }  // namespace
 }  // namespace tvr
 
@@ -159,14 +204,19 @@ int tvr_rms_norm(const float* x, const float* weight, float* y, float* rstd, int
   const unsigned blocks = static_cast<unsigned>(rows);
   const bool vec = n % 4 == 0 && aligned16(x) && aligned16(y) && (!weight || aligned16(weight));
   if (vec && n <= 16 * 4 * 1024) {
+    // up to 256 threads, more float4 per thread as rows grow (as for layer norm)
     const int ni = static_cast<int>(n);
-    const int threads = static_cast<int>(std::min<int64_t>(1024, std::max<int64_t>(32, (n / 4 + 31) / 32 * 32)));
-    const int vpt = static_cast<int>(ceil_div(n / 4, threads));
-    if (vpt <= 1) rms_norm_kernel<1><<<blocks, threads, 0, s>>>(x, weight, y, rstd, ni, eps);
-    else if (vpt <= 2) rms_norm_kernel<2><<<blocks, threads, 0, s>>>(x, weight, y, rstd, ni, eps);
-    else if (vpt <= 4) rms_norm_kernel<4><<<blocks, threads, 0, s>>>(x, weight, y, rstd, ni, eps);
-    else if (vpt <= 8) rms_norm_kernel<8><<<blocks, threads, 0, s>>>(x, weight, y, rstd, ni, eps);
-    else rms_norm_kernel<16><<<blocks, threads, 0, s>>>(x, weight, y, rstd, ni, eps);
+    const int64_t n4 = n / 4;
+    int vpt = 1;
+    while (vpt < 16 && ceil_div(n4, vpt) > 256) vpt *= 2;
+    const int threads = static_cast<int>(ceil_div(ceil_div(n4, vpt), 32) * 32);
+    switch (vpt) {
+      case 1: rms_norm_kernel<1><<<blocks, threads, 0, s>>>(x, weight, y, rstd, ni, eps); break;
+      case 2: rms_norm_kernel<2><<<blocks, threads, 0, s>>>(x, weight, y, rstd, ni, eps); break;
+      case 4: rms_norm_kernel<4><<<blocks, threads, 0, s>>>(x, weight, y, rstd, ni, eps); break;
+      case 8: rms_norm_kernel<8><<<blocks, threads, 0, s>>>(x, weight, y, rstd, ni, eps); break;
+      default: rms_norm_kernel<16><<<blocks, threads, 0, s>>>(x, weight, y, rstd, ni, eps); break;
+    }
   } else {
     rms_norm_generic_kernel<<<blocks, 256, 0, s>>>(x, weight, y, rstd, n, eps);
   }
@@ -192,6 +242,38 @@ int tvr_rope(const float* x, float* y, const float* cos_table, const float* sin_
              y_strides[1], y_strides[2], pos_offset, table_stride};
   const int dev = current_device();
   cudaStream_t s = as_stream(stream);
+  const int64_t half = dim / 2;
+  auto fits = [](int64_t v) { return v >= 0 && v < (int64_t(1) << 31); };
+  const int64_t x_span = (batch - 1) * x_strides[0] + (seq - 1) * x_strides[1] +
+                         (heads - 1) * x_strides[2] + dim;
+  const int64_t y_span = (batch - 1) * y_strides[0] + (seq - 1) * y_strides[1] +
+                         (heads - 1) * y_strides[2] + dim;
+  bool vec = !interleaved && half % 4 == 0 && table_stride % 4 == 0 && aligned16(x) &&
+             aligned16(y) && aligned16(cos_table) && aligned16(sin_table) &&
+             fits(total / 4) && fits(x_span) && fits(y_span) && fits(table_rows * table_stride);
+  for (int k = 0; vec && k < 3; ++k) {
+    vec = x_strides[k] % 4 == 0 && y_strides[k] % 4 == 0 && x_strides[k] >= 0 && y_strides[k] >= 0;
+  }
+  if (vec) {
+    RopeVec v;
+    v.quads = make_fastdiv(static_cast<uint32_t>(half / 4));
+    v.heads = make_fastdiv(static_cast<uint32_t>(heads));
+    v.seq = make_fastdiv(static_cast<uint32_t>(seq));
+    v.half = static_cast<uint32_t>(half);
+    v.xs_b = static_cast<uint32_t>(x_strides[0]);
+    v.xs_s = static_cast<uint32_t>(x_strides[1]);
+    v.xs_h = static_cast<uint32_t>(x_strides[2]);
+    v.ys_b = static_cast<uint32_t>(y_strides[0]);
+    v.ys_s = static_cast<uint32_t>(y_strides[1]);
+    v.ys_h = static_cast<uint32_t>(y_strides[2]);
+    v.pos_offset = static_cast<uint32_t>(pos_offset);
+    v.table_stride = static_cast<uint32_t>(table_stride);
+    const uint32_t quads = static_cast<uint32_t>(total / 4);
+    rope_half_vec_kernel<<<elementwise_grid(quads, 256, dev), 256, 0, s>>>(x, y, cos_table,
+                                                                           sin_table, v, quads);
+    TVR_LAUNCH_CHECK();
+    return TVR_OK;
+  }
   const unsigned grid = elementwise_grid(total, 256, dev);
   if (interleaved) rope_kernel<true><<<grid, 256, 0, s>>>(x, y, cos_table, sin_table, d, total);
   else rope_kernel<false><<<grid, 256, 0, s>>>(x, y, cos_table, sin_table, d, total);
