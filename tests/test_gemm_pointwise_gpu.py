@@ -300,3 +300,38 @@ def test_linear_pointwise_op_falls_back_for_other_shapes():
     want = (x @ w.t()) * col
     assert got.shape == want.shape
     assert float((got - want).norm() / want.norm()) <= 1e-5
+
+
+@pytest.mark.parametrize("mode", [TF32, X3])
+def test_full_size_chain_equals_the_two_kernel_path(lib, mode):
+    """The benchmark's full size, M = 16384, K = N = 4096 (the fused launch
+    with the chain in the epilogue): equal to the GEMM followed by the
+    pointwise kernel on the device within 1e-6 per element, and the output
+    has the chain's range (abs(-exp(.)) lies in (0, inf))."""
+    import torch
+
+    g = torch.Generator(device="cuda").manual_seed(5)
+    m = 16384 if mode == TF32 else 4096  # 3xTF32 at a quarter of the rows (3x the MMAs)
+    n, k = 4096, 4096
+    a = torch.randn(m, k, device="cuda", generator=g)
+    w = (torch.rand(n, k, device="cuda", generator=g) * 2 - 1) / 64
+    b = (torch.rand(n, device="cuda", generator=g) * 2 - 1) / 64
+    z = torch.randn(m, n, device="cuda", generator=g)
+    c = torch.empty(m, n, device="cuda")
+    prog = lib.pw_program(CHAIN)
+    parr = (ctypes.c_void_p * 2)(None, z.data_ptr())
+    lib.call("tvr_gemm_pointwise", _p(a), _p(w), _p(b), _p(c), m, n, k, k, k, n, 1.0, 1.0, 2, 1,
+             mode, ctypes.addressof(prog), len(CHAIN), 2, 0, ctypes.addressof(parr),
+             lib.int64_array([0, n]), _stream())
+    y = torch.empty(m, n, device="cuda")
+    lib.call("tvr_gemm_bias_act", _p(a), _p(w), _p(b), _p(y), m, n, k, k, k, n, 1.0, 1.0, 2, 1,
+             mode, _stream())
+    two = torch.empty(m, n, device="cuda")
+    pin = (ctypes.c_void_p * 2)(y.data_ptr(), z.data_ptr())
+    lib.call("tvr_pointwise", ctypes.addressof(prog), len(CHAIN), 2, ctypes.addressof(pin), _p(two),
+             m * n, _stream())
+    torch.cuda.synchronize()
+    rel = ((c - two).abs() / two.abs().clamp_min(1e-6)).max().item()
+    assert rel <= 1e-6, rel
+    assert bool((c > 0).all()) and bool(torch.isfinite(c).all())
+    assert lib.get_status(0) == 0

@@ -85,14 +85,16 @@ def _llama_ops(args, rank, world, local_rank):
         for _ in range(args.warmup):
             fn()
     torch.tvarant.synchronize()
+    # Each op is timed back to back on its own: at ~50 us per launch, a step
+    # that alternates the two ops from Python would time the host.
     per = {}
-    for name, (fn, nbytes) in ops.items():
-        ms = _time_steps(fn, args.steps)
-        per[name] = {"ms": ms, "GB/s": nbytes / (ms / 1e3) / 1e9}
     with bench.ClockSampler(local_rank) as clocks:
         h0 = time.perf_counter()
-        total_ms = _time_steps(lambda: [fn() for fn, _ in ops.values()], args.steps)
+        for name, (fn, nbytes) in ops.items():
+            ms = bench._max_over_ranks(_time_steps(fn, args.steps), world)
+            per[name] = {"ms": ms, "GB/s": nbytes / (ms / 1e3) / 1e9}
         clocks.mark(h0, time.perf_counter())
+    total_ms = sum(v["ms"] for v in per.values())
     total_bytes = sum(nb for _, nb in ops.values())
     if rank != 0:
         return None
