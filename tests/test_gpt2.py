@@ -125,3 +125,64 @@ def test_softmax_with_causal_minus_inf(dim):
     assert np.isfinite(got).all()
     assert np.array_equal(got == 0, want == 0)
     assert rel_frobenius(got, want) <= 1e-5
+
+
+def _small_model():
+    from tvarant_b200.gpt2 import GPT2Config, init_gpt2
+
+    cfg = GPT2Config(n_layer=2, d_model=128, n_head=2, d_ff=256, vocab=500, n_ctx=64)
+    return cfg, init_gpt2(cfg, seed=3)
+
+
+def test_kv_cache_decode_reproduces_the_full_forward_on_cpu():
+    """Prefill 12 tokens, then decode 4 one at a time, then a 3-token chunk
+    after the cache is non-empty: the logits of every step equal the full
+    forward's at the same positions (CPU, float32)."""
+    import torch
+
+    from tvarant_b200.gpt2 import forward, forward_step, new_cache
+
+    cfg, model = _small_model()
+    g = torch.Generator().manual_seed(8)
+    ids = torch.randint(0, cfg.vocab, (2, 19), generator=g)
+    with torch.no_grad():
+        full = forward(model, ids, attention="sdpa")
+        cache = new_cache(model, 2, 32, "cpu")
+        steps = [forward_step(model, ids[:, :12], cache)]
+        for t in range(12, 16):
+            steps.append(forward_step(model, ids[:, t:t + 1], cache))
+        steps.append(forward_step(model, ids[:, 16:19], cache))
+    got = torch.cat(steps, dim=1)
+    assert cache.length == 19
+    assert torch.allclose(got, full, rtol=1e-4, atol=1e-5), (got - full).abs().max()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("precision,tol", [("high", 5e-3), ("highest", 1e-5)])
+def test_kv_cache_decode_on_the_device(precision, tol):
+    """The same prefill + decode on the tvarant device against the CPU: few-row
+    GEMMs, cached-key attention (the fused kernel in TF32 mode), in-place cache
+    writes."""
+    import torch
+
+    import torch_tvarant  # noqa: F401
+    from tvarant_b200.gpt2 import forward_step, new_cache
+
+    cfg, model = _small_model()
+    g = torch.Generator().manual_seed(9)
+    ids = torch.randint(0, cfg.vocab, (2, 16), generator=g)
+    dmodel = model.to("tvarant")
+    torch.set_float32_matmul_precision(precision)
+    try:
+        with torch.no_grad():
+            c_cpu, c_dev = new_cache(model, 2, 32, "cpu"), new_cache(dmodel, 2, 32, "tvarant")
+            want = [forward_step(model, ids[:, :10], c_cpu)]
+            got = [forward_step(dmodel, ids[:, :10].to("tvarant"), c_dev).cpu()]
+            for t in range(10, 16):
+                want.append(forward_step(model, ids[:, t:t + 1], c_cpu))
+                got.append(forward_step(dmodel, ids[:, t:t + 1].to("tvarant"), c_dev).cpu())
+    finally:
+        torch.set_float32_matmul_precision("highest")
+    for w, gt in zip(want, got):
+        assert float((gt - w).norm() / w.norm()) <= tol
+    assert torch.tvarant.get_status() == 0

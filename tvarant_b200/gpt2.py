@@ -169,6 +169,73 @@ def forward(model: GPT2, ids: torch.Tensor, mask: torch.Tensor | None = None,
     return F.linear(x, model.wte)
 
 
+@dataclass
+class KVCache:
+    """Keys and values of every layer for positions [0, length): per layer
+    [B, H, max_len, head_dim] buffers, written in place as tokens arrive."""
+
+    k: list
+    v: list
+    length: int = 0
+
+    @property
+    def max_len(self) -> int:
+        return self.k[0].shape[2]
+
+
+def new_cache(model: GPT2, batch: int, max_len: int, device) -> KVCache:
+    """An empty cache for ``batch`` sequences of up to ``max_len`` tokens."""
+    cfg = model.cfg
+    hd = cfg.d_model // cfg.n_head
+    shape = (batch, cfg.n_head, max_len, hd)
+    return KVCache([torch.zeros(shape, device=device) for _ in model.layers],
+                   [torch.zeros(shape, device=device) for _ in model.layers])
+
+
+def forward_step(model: GPT2, ids: torch.Tensor, cache: KVCache) -> torch.Tensor:
+    """Logits [B, S, vocab] for the next S tokens ``ids`` [B, S] at positions
+    cache.length .. cache.length + S - 1, attending to every cached position
+    and causally among themselves; their keys and values are appended to the
+    cache.  A prompt (prefill, S > 1, empty cache) followed by one token at a
+    time (decode, S = 1) gives the logits ``forward`` gives for the whole
+    sequence.  Attention is F.scaled_dot_product_attention on the heads of the
+    fused QKV projection and the cache views, so on the tvarant device a
+    decode step is few-row GEMMs plus the fused attention kernel over the
+    cached keys (TF32 mode)."""
+    F = torch.nn.functional
+    cfg = model.cfg
+    B, S = ids.shape
+    d, H = cfg.d_model, cfg.n_head
+    hd = d // H
+    p0 = cache.length
+    if p0 + S > cache.max_len:
+        raise ValueError(f"{p0 + S} positions exceed the cache's {cache.max_len}")
+    scale = 1.0 / math.sqrt(hd)
+    mask = None
+    if S > 1 and p0 > 0:
+        # query j (position p0 + j) sees keys up to position p0 + j
+        mask = torch.full((S, p0 + S), float("-inf")).triu(p0 + 1).to(ids.device)
+    x = F.embedding(ids, model.wte) + model.wpe[p0:p0 + S]
+    for li, L in enumerate(model.layers):
+        h = F.layer_norm(x, (d,), L.ln1_g, L.ln1_b, 1e-5)
+        qkv = F.linear(h, L.w_qkv, L.b_qkv).view(B, S, 3, H, hd).permute(2, 0, 3, 1, 4)
+        cache.k[li][:, :, p0:p0 + S].copy_(qkv[1])
+        cache.v[li][:, :, p0:p0 + S].copy_(qkv[2])
+        k = cache.k[li][:, :, :p0 + S]
+        v = cache.v[li][:, :, :p0 + S]
+        if mask is not None:
+            o = F.scaled_dot_product_attention(qkv[0], k, v, attn_mask=mask, scale=scale)
+        else:
+            o = F.scaled_dot_product_attention(qkv[0], k, v, is_causal=S > 1, scale=scale)
+        o = o.transpose(1, 2).reshape(B, S, d)
+        x = _linear_residual(x, o, L.w_proj, L.b_proj)
+        h = F.layer_norm(x, (d,), L.ln2_g, L.ln2_b, 1e-5)
+        x = _linear_residual(x, _linear_silu(h, L.w_fc, L.b_fc), L.w_out, L.b_out)
+    cache.length = p0 + S
+    x = F.layer_norm(x, (d,), model.lnf_g, model.lnf_b, 1e-5)
+    return F.linear(x, model.wte)
+
+
 def shard_batch(batch: int, rank: int, world: int) -> tuple[int, int]:
     """[begin, end) of the sequences rank ``rank`` of ``world`` processes."""
     if batch % world != 0:
