@@ -22,7 +22,8 @@ try:
     from . import _C
 except ImportError as exc:  # pragma: no cover - exercised only without a build
     raise ImportError(
-        "tvarant_b200._C is not built; run `python -m tvarant_b200.build` "
+        "tvarant_b200._C is not built; run `python tvarant_b200/build.py` (or "
+        "`python __graft_entry__.py`) from the repository root "
         f"(underlying error: {exc})"
     ) from exc
 
