@@ -681,7 +681,7 @@ def _main() -> int:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["tvarant", "reference"], default="tvarant")
     ap.add_argument("--workload", choices=["gemm", "sweep", "llm-ops", "llama-ops", "mlp", "bmm",
-                                           "gpt2"],
+                                           "gpt2", "gpt2-decode"],
                     default="gemm")
     ap.add_argument("--batch", type=int, default=256, help="bmm workload: batch size")
     ap.add_argument("--m", type=int, default=M_DEFAULT)

@@ -335,6 +335,12 @@ int tvr_where(const void* cond, const void* a, const void* b, void* out, int ele
               const int64_t* sizes, const int64_t* cond_strides, const int64_t* a_strides,
               const int64_t* b_strides, void* stream);
 
+/* out[r] = index of the largest of the n contiguous values of row r (int64):
+ * the first on ties, a NaN counting as the largest (PyTorch's argmax rule).
+ * No reference kernel: the reference runs argmax on the CPU through its
+ * boxed fallback (csrc/aten/Ops.cpp:499-501). */
+int tvr_argmax_rows(const float* x, int64_t* out, int64_t rows, int64_t n, void* stream);
+
 /* Triangular mask of dense [batch, rows, cols]: out = x where
  * col - row >= diagonal (upper != 0, triu) or col - row <= diagonal (tril),
  * else 0.  elem_size 1, 4 or 8.  No reference kernel (CPU fallback there). */

@@ -537,3 +537,23 @@ def test_compiled_residual_and_masked_attention(tvarant, precision, tol):
         finally:
             torch.set_float32_matmul_precision("highest")
     assert float((got - want).norm() / want.norm()) <= tol
+
+
+@pytest.mark.parametrize("shape,dim,keepdim", [((8, 50257), -1, False), ((3, 7, 129), 1, True),
+                                               ((5, 1000), 0, False), ((4, 6, 10), None, False),
+                                               ((4, 6, 10), None, True), ((1,), 0, False)])
+def test_argmax_matches_torch(tvarant, shape, dim, keepdim):
+    """argmax on the device (tvr_argmax_rows) against PyTorch on the CPU, with
+    ties (first index wins), a NaN (counts as the largest) and a row of -inf."""
+    g = torch.Generator().manual_seed(len(shape))
+    x = torch.randint(-3, 4, shape, generator=g).float()  # many ties
+    flat = x.view(-1)
+    if flat.numel() > 20:
+        flat[17] = float("nan")
+    if x.dim() == 2 and x.shape[0] > 2:
+        x[2] = float("-inf")
+    want = x.argmax() if dim is None and not keepdim else x.argmax(dim=dim, keepdim=keepdim)
+    got = (x.to("tvarant").argmax() if dim is None and not keepdim
+           else x.to("tvarant").argmax(dim=dim, keepdim=keepdim)).cpu()
+    assert got.dtype == torch.int64 and got.shape == want.shape
+    assert torch.equal(got, want)

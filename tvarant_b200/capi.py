@@ -108,6 +108,7 @@ SIGNATURES: dict[str, list] = {
     "tvr_bmm": [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i32, _i32, _vp],
     "tvr_softmax": [_vp, _vp, _i64, _i64, _i64, _vp],
     "tvr_softmax_add": [_vp, _vp, _vp, _i64, _i64, _i64, _vp],
+    "tvr_argmax_rows": [_vp, _vp, _i64, _i64, _vp],
     "tvr_rms_norm": [_vp, _vp, _vp, _vp, _i64, _i64, _f32, _vp],
     "tvr_rope": [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _pi64, _pi64, _i64, _i64, _i64, _i32, _vp],
     "tvr_layer_norm": [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _f32, _vp],

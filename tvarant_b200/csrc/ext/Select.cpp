@@ -1,4 +1,4 @@
-// where / masked_fill / tril / triu on the tvarant device.
+// where / masked_fill / tril / triu / argmax on the tvarant device.
 //
 // The reference has no kernels for these and runs them on the CPU through its
 // boxed fallback (csrc/aten/Ops.cpp:499-501); this backend has no fallback,
@@ -109,6 +109,37 @@ at::Tensor& triu_(at::Tensor& self, int64_t diagonal) {
   return self;
 }
 
+// argmax over one dimension (or the flattened tensor when dim is None): the
+// reduced dimension is made the last, contiguous one, then one row per
+// remaining index (tvr_argmax_rows).
+at::Tensor argmax(const at::Tensor& self, std::optional<int64_t> dim, bool keepdim) {
+  check_fp32(self, "argmax");
+  c10::DeviceGuard guard(self.device());
+  TORCH_CHECK(self.numel() > 0, "argmax(): Expected reduction dim to be specified for input.numel() == 0.");
+  at::Tensor x;
+  std::vector<int64_t> out_shape;
+  if (!dim.has_value()) {
+    x = (self.is_contiguous() ? self : contiguous_copy(self)).reshape({1, self.numel()});
+    if (keepdim) out_shape.assign(self.dim(), 1);
+  } else {
+    const int64_t d = at::maybe_wrap_dim(*dim, self.dim());
+    at::Tensor moved = self.dim() == 0 ? self.reshape({1}) : self.movedim(d, -1);
+    at::Tensor c = moved.is_contiguous() ? moved : contiguous_copy(moved);
+    const int64_t n = c.dim() == 0 ? 1 : c.size(-1);
+    x = c.reshape({c.numel() / n, n});
+    out_shape = self.sizes().vec();
+    if (self.dim() > 0) {
+      if (keepdim) out_shape[d] = 1;
+      else out_shape.erase(out_shape.begin() + d);
+    }
+  }
+  at::Tensor out = empty_device({x.size(0)}, x.options().dtype(at::kLong));
+  TVR_TRY(tvr_argmax_rows(static_cast<const float*>(x.data_ptr()),
+                          static_cast<int64_t*>(out.data_ptr()), x.size(0), x.size(1),
+                          current_stream_handle()));
+  return out.reshape(out_shape);
+}
+
 at::Tensor logical_not(const at::Tensor& self) {
   c10::DeviceGuard guard(self.device());
   at::Tensor b = as_type_on(self, at::kBool, self);
@@ -129,4 +160,5 @@ TORCH_LIBRARY_IMPL(aten, PrivateUse1, m) {
   m.impl("tril_", TORCH_FN(tvarant::ops::tril_));
   m.impl("triu_", TORCH_FN(tvarant::ops::triu_));
   m.impl("logical_not", TORCH_FN(tvarant::ops::logical_not));
+  m.impl("argmax", TORCH_FN(tvarant::ops::argmax));
 }

@@ -1,4 +1,5 @@
-// Selection kernels: where / masked_fill and the triangular masks tril / triu.
+// Selection kernels: where / masked_fill, the triangular masks tril / triu,
+// and row argmax (greedy token choice).
 //
 // The reference runs these on the CPU through its boxed fallback
 // (csrc/aten/Ops.cpp:499-501); here they are native so that attention masks
@@ -9,6 +10,10 @@
 #include "internal.h"
 
 #include "fastdiv.cuh"
+
+#include <cfloat>
+#include <climits>
+#include <cmath>
 
 namespace tvr {
 namespace {
@@ -156,6 +161,57 @@ __global__ void __launch_bounds__(kThreads) tri_kernel(const T* __restrict__ x, 
   }
 }
 
+// Row argmax: index of the largest value of each row of n contiguous values,
+// the first one on ties, NaN counting as larger than any number (PyTorch's
+// rule).  One block per row; each thread scans a strided slice, then a
+// (value, index) reduction across the block.
+__device__ __forceinline__ bool argmax_better(float v, int64_t i, float bv, int64_t bi) {
+  const bool vn = v != v, bn = bv != bv;
+  if (vn != bn) return vn;                    // a NaN beats a number
+  if (!vn && v != bv) return v > bv;          // larger number
+  return i < bi;                              // equal (or both NaN): first index
+}
+
+__global__ void __launch_bounds__(256) argmax_rows_kernel(const float* __restrict__ x,
+                                                          int64_t* __restrict__ out, int64_t n) {
+  __shared__ float sv[8];
+  __shared__ int64_t si[8];
+  const float* xr = x + static_cast<int64_t>(blockIdx.x) * n;
+  float bv = -INFINITY;
+  int64_t bi = INT64_MAX;
+  for (int64_t i = threadIdx.x; i < n; i += blockDim.x) {
+    const float v = xr[i];
+    if (argmax_better(v, i, bv, bi)) {
+      bv = v;
+      bi = i;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+    const int64_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (argmax_better(ov, oi, bv, bi)) {
+      bv = ov;
+      bi = oi;
+    }
+  }
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (lane == 0) {
+    sv[warp] = bv;
+    si[warp] = bi;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < static_cast<int>(blockDim.x >> 5); ++w) {
+      if (argmax_better(sv[w], si[w], bv, bi)) {
+        bv = sv[w];
+        bi = si[w];
+      }
+    }
+    out[blockIdx.x] = bi;
+  }
+}
+
 }  // namespace
 }  // namespace tvr
 
@@ -193,6 +249,17 @@ int tvr_where(const void* cond, const void* a, const void* b, void* out, int ele
     case 4: return launch_where<uint32_t>(c, a, b, out, ix, r, n, s, dev);
     default: return launch_where<unsigned long long>(c, a, b, out, ix, r, n, s, dev);
   }
+}
+
+int tvr_argmax_rows(const float* x, int64_t* out, int64_t rows, int64_t n, void* stream) {
+  TVR_CHECK(rows >= 0 && n >= 1, "tvr_argmax_rows: invalid shape rows=%lld n=%lld",
+            (long long)rows, (long long)n);
+  TVR_CHECK(rows <= 0x7fffffff, "tvr_argmax_rows: too many rows");
+  if (rows == 0) return TVR_OK;
+  TVR_CHECK(x && out, "tvr_argmax_rows: null pointer");
+  argmax_rows_kernel<<<static_cast<unsigned>(rows), 256, 0, as_stream(stream)>>>(x, out, n);
+  TVR_LAUNCH_CHECK();
+  return TVR_OK;
 }
 
 int tvr_triangle(const void* x, void* out, int elem_size, int64_t batch, int64_t rows,

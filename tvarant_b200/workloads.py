@@ -54,6 +54,8 @@ def run(args, rank: int, world: int, local_rank: int):
         return _gpt2(args, rank, world, local_rank)
     if args.workload == "llama-ops":
         return _llama_ops(args, rank, world, local_rank)
+    if args.workload == "gpt2-decode":
+        return _gpt2_decode(args, rank, world, local_rank)
     return _mlp(args, rank, world, local_rank)
 
 
@@ -378,6 +380,78 @@ def _gpt2_cpu_baseline(host_model, cfg, seq: int) -> dict:
             "kind": "reference" if impl == "ref" else "port",
             "sample": f"1 sequence x {seq} tokens through all {cfg.n_layer} layers and the LM head "
                       f"({dt:.1f} s; attention per token is {seq}/1024 of the benchmark's)"}
+
+
+def _gpt2_decode(args, rank, world, local_rank):
+    """GPT-2-small generation with a KV cache: a prompt of ``--seq`` tokens
+    per sequence (prefill), then one token per sequence per step (decode).
+    A step is one ``forward_step`` over [batch, 1] new tokens: few-row GEMMs
+    (batch rows), attention of one query per head over the cached keys, and
+    the LM head.  Steps run eagerly (the cache views grow by one position a
+    step); the decode tokens are the model's greedy choices, so nothing of a
+    step is precomputed.  ``value`` = batch / step time."""
+    import bench
+    from tvarant_b200 import gpt2
+
+    torch.set_float32_matmul_precision("high" if args.mode == "tf32" else "highest")
+    dev = f"tvarant:{local_rank}"
+    cfg = gpt2.GPT2Config()
+    batch, prompt = args.gpt2_batch, args.seq
+    steps = args.steps
+    if prompt + args.warmup + steps > cfg.n_ctx:
+        raise ValueError(f"prompt {prompt} + {args.warmup + steps} steps exceed {cfg.n_ctx} positions")
+    model = gpt2.init_gpt2(cfg, seed=0).to(dev)
+    g = torch.Generator().manual_seed(12)
+    ids = torch.randint(0, cfg.vocab, (batch, prompt), generator=g).to(dev)
+    cache = gpt2.new_cache(model, batch, cfg.n_ctx, dev)
+    t0, t1 = _events()
+    t0.record()
+    logits = gpt2.forward_step(model, ids, cache)
+    t1.record()
+    t1.synchronize()
+    prefill_ms = t0.elapsed_time(t1)
+    nxt = logits[:, -1:].argmax(-1)
+    for _ in range(args.warmup):
+        nxt = gpt2.forward_step(model, nxt, cache)[:, -1:].argmax(-1)
+    torch.tvarant.synchronize()
+    bench._barrier(world)
+
+    def step():
+        nonlocal nxt
+        nxt = gpt2.forward_step(model, nxt, cache)[:, -1:].argmax(-1)
+
+    with bench.ClockSampler(local_rank) as clocks:
+        h0 = time.perf_counter()
+        ms = _time_steps(step, steps)
+        clocks.mark(h0, time.perf_counter())
+    ms = bench._max_over_ranks(ms, world)
+    status = torch.tvarant.get_status()
+    if rank != 0:
+        return None
+    weight_bytes = 4 * (cfg.n_layer * (4 * cfg.d_model ** 2 + 2 * cfg.d_model * cfg.d_ff)
+                        + cfg.vocab * cfg.d_model)
+    return {
+        "metric": "fused-GEMM TFLOP/s (% peak); LLM-op GB/s (% HBM); tokens/s at 1/2/4/8 GPU",
+        "value": world * batch / (ms / 1e3), "unit": "tokens/s (decode)", "n_gpus": world,
+        "steps": steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None,
+        "dtype": "tf32" if args.mode == "tf32" else "f32 (3xTF32)",
+        "data": "synthetic (N(0,0.02) weights, uniform prompt ids, greedy decode tokens)",
+        "config": {"workload": f"GPT-2-small decode with a KV cache: batch {batch}, prompt {prompt}, "
+                               f"{steps} timed single-token steps (eager)",
+                   "prefill_ms": prefill_ms, "parallelism": f"replicas x{world}",
+                   "weights_mb": weight_bytes / 1e6,
+                   "l2": "the 0.5 GB of weights exceed L2; every step streams them"},
+        "roofline": {"bound": "hbm", "achieved": weight_bytes / (ms / 1e3) / 1e9,
+                     "peak": bench._peaks().get("hbm_gbs", 6650.0), "unit": "GB/s",
+                     "frac": weight_bytes / (ms / 1e3) / 1e9 / bench._peaks().get("hbm_gbs", 6650.0),
+                     "traffic": None,
+                     "note": "weight bytes per step over the step time: a step that is host-bound "
+                             "(eager launches) reads far below the HBM rate"},
+        "gpu_launches": None,
+        "clocks": clocks.summary(),
+        "device_status": status,
+    }
 
 
 def _gpt2(args, rank, world, local_rank):
