@@ -54,6 +54,7 @@ extern "C" {
 #define TVR_DEV_TIMEOUT_DRAIN 4    /* exit-time drain of async copies gave up       */
 #define TVR_DEV_TIMEOUT_CONVERT 5  /* 3xTF32 converter gave up waiting for a stage  */
 #define TVR_DEV_TIMEOUT_PEER 6     /* a cross-rank barrier gave up waiting for a rank */
+#define TVR_DEV_CACHE_FULL 7       /* a KV-cache append past the cache's capacity was dropped */
 
 /* GEMM precision modes */
 #define TVR_GEMM_AUTO 0    /* TVARANT_GEMM_MODE env, else 3xTF32               */
@@ -244,6 +245,32 @@ int tvr_attention_fwd(const float* q, const float* k, const float* v, float* out
                       int64_t head_dim, const int64_t* q_strides, const int64_t* k_strides,
                       const int64_t* v_strides, const int64_t* o_strides, float scale,
                       int causal, int mode, void* stream);
+
+/* The same attention (no mask, no lse) over K / V buffers of seq_k positions
+ * of which only the first clamp(*key_len + key_len_add, 1, seq_k) are
+ * attended: key_len is an int64 in device memory written by earlier work on
+ * the stream, so a step captured in a CUDA graph attends to a growing KV
+ * cache without being captured again.  TF32 mode only (TVR_ERR_UNSUPPORTED
+ * otherwise, as for tvr_attention_fwd).  No reference counterpart. */
+int tvr_attention_fwd_keylen(const float* q, const float* k, const float* v, float* out,
+                             int64_t batch, int64_t heads, int64_t seq_q, int64_t seq_k,
+                             int64_t head_dim, const int64_t* q_strides,
+                             const int64_t* k_strides, const int64_t* v_strides,
+                             const int64_t* o_strides, float scale, const int64_t* key_len,
+                             int key_len_add, int mode, void* stream);
+
+/* KV-cache append: src [batch, heads, seq_new, dim] (strides src_strides for
+ * batch, head, position; dim contiguous) is written into cache positions
+ * *pos .. *pos + seq_new - 1 (cache strides cache_strides, dim contiguous).
+ * *pos is an int64 in device memory; positions at or past max_len are
+ * dropped and TVR_DEV_CACHE_FULL is set in the device status word.  The
+ * position does not advance (tvr_counter_add).  No reference counterpart. */
+int tvr_kv_append(float* cache, const float* src, int64_t batch, int64_t heads, int64_t seq_new,
+                  int64_t dim, int64_t max_len, const int64_t* cache_strides,
+                  const int64_t* src_strides, const int64_t* pos, void* stream);
+
+/* *counter += delta on the stream (an int64 in device memory). */
+int tvr_counter_add(int64_t* counter, int64_t delta, void* stream);
 
 /* Batched C[i] = A[i] * op(B[i]) for i < batch, each as tvr_gemm_bias_act
  * with alpha 1, beta 0, no activation; matrices are dense row-major with the

@@ -186,3 +186,50 @@ def test_kv_cache_decode_on_the_device(precision, tol):
     for w, gt in zip(want, got):
         assert float((gt - w).norm() / w.norm()) <= tol
     assert torch.tvarant.get_status() == 0
+
+
+@pytest.mark.gpu
+def test_graph_decode_matches_eager_decode():
+    """decode_step (fixed shapes, key count and cache position on the device)
+    captured once as a CUDA graph and replayed per token produces the same
+    greedy tokens as the eager forward_step decode, and leaves the position
+    on the device at the number of tokens."""
+    import torch
+
+    import torch_tvarant  # noqa: F401
+    from tvarant_b200.gpt2 import decode_step, forward_step, new_cache
+    from tvarant_b200.graphs import Graph
+
+    cfg, model = _small_model()
+    dmodel = model.to("tvarant")
+    g = torch.Generator().manual_seed(10)
+    prompt = torch.randint(0, cfg.vocab, (2, 10), generator=g).to("tvarant")
+    torch.set_float32_matmul_precision("high")
+    try:
+        with torch.no_grad():
+            eager = new_cache(dmodel, 2, 32, "tvarant")
+            nxt = forward_step(dmodel, prompt, eager)[:, -1:].argmax(-1)
+            first = nxt.clone()
+            want = []
+            for _ in range(6):
+                nxt = forward_step(dmodel, nxt, eager)[:, -1:].argmax(-1)
+                want.append(nxt.cpu())
+            cache = new_cache(dmodel, 2, 32, "tvarant")
+            forward_step(dmodel, prompt, cache)
+            ids = first.clone()
+            pos = torch.full((1,), 10, dtype=torch.int64).to("tvarant")
+            graph = Graph(decode_step, dmodel, ids, cache, pos, warmup=1)
+            # building the graph ran the step three times: restart from the prompt
+            pos.copy_(torch.full((1,), 10, dtype=torch.int64))
+            ids.copy_(first)
+            got = []
+            for _ in range(6):
+                got.append(graph.replay().cpu())
+            final_pos = int(pos.cpu())
+            graph.close()
+    finally:
+        torch.set_float32_matmul_precision("highest")
+    assert final_pos == 16
+    for w, gt in zip(want, got):
+        assert torch.equal(w, gt)
+    assert torch.tvarant.get_status() == 0

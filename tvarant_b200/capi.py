@@ -103,6 +103,10 @@ SIGNATURES: dict[str, list] = {
     "tvr_gemm_bias_act_noalloc": [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _f32,
                                   _f32, _i32, _i32, _vp],
     "tvr_gemm_swiglu": [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i32, _vp],
+    "tvr_attention_fwd_keylen": [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _pi64, _pi64,
+                                 _pi64, _pi64, _f32, _vp, _i32, _i32, _vp],
+    "tvr_kv_append": [_vp, _vp, _i64, _i64, _i64, _i64, _i64, _pi64, _pi64, _vp, _vp],
+    "tvr_counter_add": [_vp, _i64, _vp],
     "tvr_attention_fwd": [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _pi64, _pi64,
                           _pi64, _pi64, _f32, _i32, _i32, _vp],
     "tvr_bmm": [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i32, _i32, _vp],

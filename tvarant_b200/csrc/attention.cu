@@ -72,6 +72,8 @@ struct Params {
   float scale_log2;          // softmax scale * log2(e)
   int causal;
   int* status;
+  const int64_t* key_len;    // non-null: attend to clamp(*key_len + key_len_add, 1, seq_k) keys
+  int key_len_add;
 };
 
 // N-major V operand: 32-wide atoms of the head dimension, each [64 keys x
@@ -129,7 +131,12 @@ __global__ void __launch_bounds__(THREADS, 1) attn_fwd_kernel(const __grid_const
   const int h = bh - b * p.heads;
   const int qt = static_cast<int>(gridDim.x) - 1 - static_cast<int>(blockIdx.x);  // heavy tiles first
   const int q0 = qt * BM;
-  const int kblocks = (p.seq_k + BN - 1) / BN;
+  // the key count: the buffers' extent, or a length held in device memory
+  // (written by earlier work on the stream, e.g. a KV cache's fill level)
+  const int seq_k = p.key_len != nullptr
+                        ? max(1, min(p.seq_k, static_cast<int>(*p.key_len) + p.key_len_add))
+                        : p.seq_k;
+  const int kblocks = (seq_k + BN - 1) / BN;
   const int nkb = p.causal ? min(kblocks, (min(q0 + BM, p.seq_q) - 1) / BN + 1) : kblocks;
 
   if (threadIdx.x == 0) {
@@ -311,7 +318,7 @@ __global__ void __launch_bounds__(THREADS, 1) attn_fwd_kernel(const __grid_const
       const uint32_t srow = tmem + lane_off + static_cast<uint32_t>(sb * BN);
       const int key0 = j * BN;
       // keys [key0, key_end) are visible to this row
-      int key_end = min(p.seq_k, key0 + BN);
+      int key_end = min(seq_k, key0 + BN);
       if (p.causal) key_end = min(key_end, qidx + 1);
       const int nvis = key_end - key0;  // may be <= 0 for padding rows
       // the row's BN scores: all TMEM loads in flight, one wait
@@ -404,12 +411,13 @@ __global__ void __launch_bounds__(THREADS, 1) attn_fwd_kernel(const __grid_const
 
 using namespace tvr;
 
-extern "C" int tvr_attention_fwd(const float* q, const float* k, const float* v, float* out,
-                                 float* lse, int64_t batch, int64_t heads, int64_t seq_q,
-                                 int64_t seq_k, int64_t head_dim, const int64_t* q_strides,
-                                 const int64_t* k_strides, const int64_t* v_strides,
-                                 const int64_t* o_strides, float scale, int causal, int mode,
-                                 void* stream) {
+namespace {
+
+int attention_impl(const float* q, const float* k, const float* v, float* out, float* lse,
+                   int64_t batch, int64_t heads, int64_t seq_q, int64_t seq_k, int64_t head_dim,
+                   const int64_t* q_strides, const int64_t* k_strides, const int64_t* v_strides,
+                   const int64_t* o_strides, float scale, int causal, int mode,
+                   const int64_t* key_len, int key_len_add, void* stream) {
   using namespace attn;
   TVR_CHECK(batch >= 0 && heads >= 0 && seq_q >= 0 && seq_k >= 0, "attention: negative size");
   if (batch == 0 || heads == 0 || seq_q == 0) return TVR_OK;
@@ -465,6 +473,8 @@ extern "C" int tvr_attention_fwd(const float* q, const float* k, const float* v,
   p.scale_log2 = scale * 1.4426950408889634f;
   p.causal = causal ? 1 : 0;
   p.status = device_status_ptr(dev);
+  p.key_len = key_len;
+  p.key_len_add = key_len_add;
   static std::once_flag once[64];
   static cudaError_t attr_err[64];
   std::call_once(once[dev & 63], [&]() {
@@ -475,6 +485,91 @@ extern "C" int tvr_attention_fwd(const float* q, const float* k, const float* v,
   TVR_CUDA_TRY(attr_err[dev & 63]);
   const dim3 grid(static_cast<unsigned>(ceil_div(seq_q, BM)), static_cast<unsigned>(batch * heads));
   attn_fwd_kernel<<<grid, THREADS, SMEM_BYTES, as_stream(stream)>>>(p);
+  TVR_LAUNCH_CHECK();
+  return TVR_OK;
+}
+
+// Writes src [batch, heads, seq_new, dim] into cache positions
+// *pos .. *pos + seq_new - 1; positions at or past max_len are dropped and
+// reported in the status word.
+__global__ void __launch_bounds__(256) kv_append_kernel(float* cache, const float* src,
+                                                        int64_t heads, int64_t seq_new,
+                                                        int64_t dim, int64_t max_len,
+                                                        int64_t cb, int64_t ch, int64_t cs,
+                                                        int64_t sb, int64_t sh, int64_t ss,
+                                                        const int64_t* pos, int64_t total,
+                                                        int* status) {
+  const int64_t p0 = *pos;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; t < total;
+       t += stride) {
+    const int64_t d = t % dim;
+    int64_t r = t / dim;
+    const int64_t s = r % seq_new;
+    r /= seq_new;
+    const int64_t h = r % heads;
+    const int64_t b = r / heads;
+    const int64_t at = p0 + s;
+    if (at < 0 || at >= max_len) {
+      if (status != nullptr) atomicCAS(status, TVR_DEV_OK, TVR_DEV_CACHE_FULL);
+      continue;
+    }
+    cache[b * cb + h * ch + at * cs + d] = src[b * sb + h * sh + s * ss + d];
+  }
+}
+
+__global__ void counter_add_kernel(int64_t* counter, int64_t delta) { *counter += delta; }
+
+}  // namespace
+
+extern "C" int tvr_attention_fwd(const float* q, const float* k, const float* v, float* out,
+                                 float* lse, int64_t batch, int64_t heads, int64_t seq_q,
+                                 int64_t seq_k, int64_t head_dim, const int64_t* q_strides,
+                                 const int64_t* k_strides, const int64_t* v_strides,
+                                 const int64_t* o_strides, float scale, int causal, int mode,
+                                 void* stream) {
+  return attention_impl(q, k, v, out, lse, batch, heads, seq_q, seq_k, head_dim, q_strides,
+                        k_strides, v_strides, o_strides, scale, causal, mode, nullptr, 0,
+                        stream);
+}
+
+extern "C" int tvr_attention_fwd_keylen(const float* q, const float* k, const float* v,
+                                        float* out, int64_t batch, int64_t heads, int64_t seq_q,
+                                        int64_t seq_k, int64_t head_dim,
+                                        const int64_t* q_strides, const int64_t* k_strides,
+                                        const int64_t* v_strides, const int64_t* o_strides,
+                                        float scale, const int64_t* key_len, int key_len_add,
+                                        int mode, void* stream) {
+  TVR_CHECK(key_len != nullptr && reinterpret_cast<uintptr_t>(key_len) % 8 == 0,
+            "attention_keylen: null or unaligned key length");
+  return attention_impl(q, k, v, out, nullptr, batch, heads, seq_q, seq_k, head_dim, q_strides,
+                        k_strides, v_strides, o_strides, scale, 0, mode, key_len, key_len_add,
+                        stream);
+}
+
+extern "C" int tvr_kv_append(float* cache, const float* src, int64_t batch, int64_t heads,
+                             int64_t seq_new, int64_t dim, int64_t max_len,
+                             const int64_t* cache_strides, const int64_t* src_strides,
+                             const int64_t* pos, void* stream) {
+  TVR_CHECK(batch >= 0 && heads >= 0 && seq_new >= 0 && dim >= 0 && max_len >= 0,
+            "kv_append: negative size");
+  const int64_t total = batch * heads * seq_new * dim;
+  if (total == 0) return TVR_OK;
+  TVR_CHECK(cache && src && cache_strides && src_strides && pos, "kv_append: null pointer");
+  TVR_CHECK(reinterpret_cast<uintptr_t>(pos) % 8 == 0, "kv_append: unaligned position");
+  const int dev = current_device();
+  kv_append_kernel<<<elementwise_grid(total, 256, dev), 256, 0, as_stream(stream)>>>(
+      cache, src, heads, seq_new, dim, max_len, cache_strides[0], cache_strides[1],
+      cache_strides[2], src_strides[0], src_strides[1], src_strides[2], pos, total,
+      device_status_ptr(dev));
+  TVR_LAUNCH_CHECK();
+  return TVR_OK;
+}
+
+extern "C" int tvr_counter_add(int64_t* counter, int64_t delta, void* stream) {
+  TVR_CHECK(counter != nullptr && reinterpret_cast<uintptr_t>(counter) % 8 == 0,
+            "counter_add: null or unaligned counter");
+  counter_add_kernel<<<1, 1, 0, as_stream(stream)>>>(counter, delta);
   TVR_LAUNCH_CHECK();
   return TVR_OK;
 }

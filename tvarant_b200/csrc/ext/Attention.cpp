@@ -16,6 +16,7 @@
 #include <c10/core/DeviceGuard.h>
 #include <torch/library.h>
 
+#include <array>
 #include <cmath>
 #include <limits>
 #include <tuple>
@@ -112,8 +113,90 @@ sdpa_overrideable(const at::Tensor& query, const at::Tensor& key, const at::Tens
   return result(composed_attention(query, key, value, attn_bias, is_causal, sc), none);
 }
 
+// ---- KV-cache decode pieces ----------------------------------------------
+// Shapes stay fixed from step to step (the whole cache buffer, a position
+// held in device memory), so a decode step can be captured once in a CUDA
+// graph and replayed per token.
+
+void check_pos(const at::Tensor& pos, const at::Tensor& like, const char* op) {
+  TORCH_CHECK(pos.device() == like.device() && pos.scalar_type() == at::kLong && pos.numel() == 1,
+              op, ": the position must be a one-element int64 tensor on the same device");
+}
+
+// cache[:, :, pos:pos+S] = src for cache [B, H, T, D] and src [B, H, S, D]
+// (D contiguous in both), pos an int64 device scalar.
+at::Tensor& kv_append_(at::Tensor& cache, const at::Tensor& src, const at::Tensor& pos) {
+  check_fp32(cache, "kv_append_");
+  check_fp32(src, "kv_append_");
+  TORCH_CHECK(cache.dim() == 4 && src.dim() == 4 && cache.size(0) == src.size(0) &&
+                  cache.size(1) == src.size(1) && cache.size(3) == src.size(3),
+              "kv_append_: cache ", cache.sizes(), " and new entries ", src.sizes(),
+              " must be [B, H, T, D] and [B, H, S, D]");
+  TORCH_CHECK(cache.stride(3) == 1, "kv_append_: the cache's last dimension must be contiguous");
+  check_pos(pos, cache, "kv_append_");
+  c10::DeviceGuard guard(cache.device());
+  at::Tensor s = src.stride(3) == 1 ? src : contiguous_copy(src);
+  const int64_t cs[3] = {cache.stride(0), cache.stride(1), cache.stride(2)};
+  const int64_t ss[3] = {s.stride(0), s.stride(1), s.stride(2)};
+  TVR_TRY(tvr_kv_append(static_cast<float*>(cache.data_ptr()), static_cast<const float*>(s.data_ptr()),
+                        s.size(0), s.size(1), s.size(2), s.size(3), cache.size(2), cs, ss,
+                        static_cast<const int64_t*>(pos.data_ptr()), current_stream_handle()));
+  return cache;
+}
+
+// Attention of q [B, H, Sq, D] to the first *key_len + key_len_add keys of
+// k / v [B, H, T, D] (no mask; the fused TF32 kernel).
+at::Tensor attention_keylen(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
+                            const at::Tensor& key_len, int64_t key_len_add, double scale) {
+  for (const auto* t : {&q, &k, &v}) check_fp32(*t, "attention_keylen");
+  TORCH_CHECK(q.dim() == 4 && k.dim() == 4 && v.sizes() == k.sizes() && q.size(0) == k.size(0) &&
+                  q.size(1) == k.size(1) && q.size(3) == k.size(3),
+              "attention_keylen: expected q [B, H, Sq, D] and k, v [B, H, T, D]");
+  check_pos(key_len, q, "attention_keylen");
+  TORCH_CHECK(gemm_mode() == TVR_GEMM_TF32,
+              "attention_keylen runs the fused TF32 attention kernel: call "
+              "torch.set_float32_matmul_precision('high')");
+  c10::DeviceGuard guard(q.device());
+  const int64_t B = q.size(0), H = q.size(1), L = q.size(2), E = q.size(3);
+  at::Tensor out_buf = empty_device({B, L, H, E}, q.options());
+  at::Tensor out = out_buf.permute({0, 2, 1, 3});
+  auto st = [](const at::Tensor& t) {
+    return std::array<int64_t, 3>{t.stride(0), t.stride(1), t.stride(2)};
+  };
+  const auto qs = st(q), ks = st(k), vs = st(v), os = st(out);
+  TVR_TRY(tvr_attention_fwd_keylen(
+      static_cast<const float*>(q.data_ptr()), static_cast<const float*>(k.data_ptr()),
+      static_cast<const float*>(v.data_ptr()), static_cast<float*>(out.data_ptr()), B, H, L,
+      k.size(2), E, qs.data(), ks.data(), vs.data(), os.data(), static_cast<float>(scale),
+      static_cast<const int64_t*>(key_len.data_ptr()), static_cast<int>(key_len_add),
+      TVR_GEMM_TF32, current_stream_handle()));
+  return out;
+}
+
+at::Tensor& counter_add_(at::Tensor& counter, int64_t delta) {
+  TORCH_CHECK(is_device(counter) && counter.scalar_type() == at::kLong && counter.numel() == 1,
+              "counter_add_: expected a one-element int64 tvarant tensor");
+  c10::DeviceGuard guard(counter.device());
+  TVR_TRY(tvr_counter_add(static_cast<int64_t*>(counter.data_ptr()), delta,
+                          current_stream_handle()));
+  return counter;
+}
+
 }  // namespace
 }  // namespace tvarant::ops
+
+TORCH_LIBRARY_FRAGMENT(tvarant, m) {
+  m.def("kv_append_(Tensor(a!) cache, Tensor src, Tensor pos) -> Tensor(a!)");
+  m.def("attention_keylen(Tensor q, Tensor k, Tensor v, Tensor key_len, int key_len_add, "
+        "float scale) -> Tensor");
+  m.def("counter_add_(Tensor(a!) counter, int delta) -> Tensor(a!)");
+}
+
+TORCH_LIBRARY_IMPL(tvarant, PrivateUse1, m) {
+  m.impl("kv_append_", TORCH_FN(tvarant::ops::kv_append_));
+  m.impl("attention_keylen", TORCH_FN(tvarant::ops::attention_keylen));
+  m.impl("counter_add_", TORCH_FN(tvarant::ops::counter_add_));
+}
 
 TORCH_LIBRARY_IMPL(aten, PrivateUse1, m) {
   m.impl("_scaled_dot_product_fused_attention_overrideable",

@@ -236,6 +236,41 @@ def forward_step(model: GPT2, ids: torch.Tensor, cache: KVCache) -> torch.Tensor
     return F.linear(x, model.wte)
 
 
+def decode_step(model: GPT2, ids: torch.Tensor, cache: KVCache, pos: torch.Tensor) -> torch.Tensor:
+    """One greedy decode step with fixed shapes, for the tvarant device in TF32
+    mode: ``ids`` [B, 1] (int64, device) holds the current token of every
+    sequence and ``pos`` (one int64, device) the number of cached positions.
+    The step appends this position's keys and values to the cache at ``pos``,
+    attends to positions 0..pos over the whole cache buffer (the key count is
+    read from ``pos`` on the device), writes the greedy next token into
+    ``ids`` and advances ``pos``.  Nothing in it depends on host values, so it
+    can be captured once as a CUDA graph and replayed once per token
+    (``tvarant_b200.graphs.Graph``); ``cache.length`` is not updated.
+    Returns ``ids``."""
+    F = torch.nn.functional
+    cfg = model.cfg
+    B = ids.shape[0]
+    d, H = cfg.d_model, cfg.n_head
+    hd = d // H
+    scale = 1.0 / math.sqrt(hd)
+    x = F.embedding(ids, model.wte) + F.embedding(pos.view(1, 1), model.wpe)
+    for li, L in enumerate(model.layers):
+        h = F.layer_norm(x, (d,), L.ln1_g, L.ln1_b, 1e-5)
+        qkv = F.linear(h, L.w_qkv, L.b_qkv).view(B, 1, 3, H, hd).permute(2, 0, 3, 1, 4)
+        torch.ops.tvarant.kv_append_(cache.k[li], qkv[1], pos)
+        torch.ops.tvarant.kv_append_(cache.v[li], qkv[2], pos)
+        o = torch.ops.tvarant.attention_keylen(qkv[0], cache.k[li], cache.v[li], pos, 1, scale)
+        o = o.transpose(1, 2).reshape(B, 1, d)
+        x = _linear_residual(x, o, L.w_proj, L.b_proj)
+        h = F.layer_norm(x, (d,), L.ln2_g, L.ln2_b, 1e-5)
+        x = _linear_residual(x, _linear_silu(h, L.w_fc, L.b_fc), L.w_out, L.b_out)
+    x = F.layer_norm(x, (d,), model.lnf_g, model.lnf_b, 1e-5)
+    nxt = F.linear(x, model.wte)[:, -1].argmax(-1, keepdim=True)
+    torch.ops.tvarant.counter_add_(pos, 1)
+    ids.copy_(nxt)
+    return ids
+
+
 def shard_batch(batch: int, rank: int, world: int) -> tuple[int, int]:
     """[begin, end) of the sequences rank ``rank`` of ``world`` processes."""
     if batch % world != 0:
