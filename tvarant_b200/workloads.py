@@ -387,9 +387,11 @@ def _gpt2_decode(args, rank, world, local_rank):
     per sequence (prefill), then one token per sequence per step (decode).
     A step is one ``forward_step`` over [batch, 1] new tokens: few-row GEMMs
     (batch rows), attention of one query per head over the cached keys, and
-    the LM head.  Steps run eagerly (the cache views grow by one position a
-    step); the decode tokens are the model's greedy choices, so nothing of a
-    step is precomputed.  ``value`` = batch / step time."""
+    the LM head; the decode tokens are the model's greedy choices, so nothing
+    of a step is precomputed.  ``value`` = batch / step time, for the step
+    captured as a CUDA graph (TF32: ``gpt2.decode_step``, position and key
+    count on the device) unless ``--no-graph``; the eager step (the cache
+    views grow by one position a step) is timed beside it."""
     import bench
     from tvarant_b200 import gpt2
 
@@ -398,8 +400,9 @@ def _gpt2_decode(args, rank, world, local_rank):
     cfg = gpt2.GPT2Config()
     batch, prompt = args.gpt2_batch, args.seq
     steps = args.steps
-    if prompt + args.warmup + steps > cfg.n_ctx:
-        raise ValueError(f"prompt {prompt} + {args.warmup + steps} steps exceed {cfg.n_ctx} positions")
+    if prompt + args.warmup + 2 * steps + 3 > cfg.n_ctx:
+        raise ValueError(f"prompt {prompt} + {args.warmup + 2 * steps + 3} steps exceed "
+                         f"{cfg.n_ctx} positions")
     model = gpt2.init_gpt2(cfg, seed=0).to(dev)
     g = torch.Generator().manual_seed(12)
     ids = torch.randint(0, cfg.vocab, (batch, prompt), generator=g).to(dev)
@@ -411,6 +414,7 @@ def _gpt2_decode(args, rank, world, local_rank):
     t1.synchronize()
     prefill_ms = t0.elapsed_time(t1)
     nxt = logits[:, -1:].argmax(-1)
+    first = nxt.clone()
     for _ in range(args.warmup):
         nxt = gpt2.forward_step(model, nxt, cache)[:, -1:].argmax(-1)
     torch.tvarant.synchronize()
@@ -420,11 +424,28 @@ def _gpt2_decode(args, rank, world, local_rank):
         nonlocal nxt
         nxt = gpt2.forward_step(model, nxt, cache)[:, -1:].argmax(-1)
 
+    eager_ms = bench._max_over_ranks(_time_steps(step, steps), world)
+    run, graph = step, None
+    if not args.no_graph and args.mode == "tf32":
+        # the fixed-shape step (cache position and key count on the device)
+        # captured once; each replay decodes one token per sequence
+        from tvarant_b200.graphs import Graph
+
+        ids = first.clone()
+        pos = torch.full((1,), prompt, dtype=torch.int64).to(dev)
+        graph = Graph(gpt2.decode_step, model, ids, cache, pos, warmup=1)
+        pos.copy_(torch.full((1,), prompt, dtype=torch.int64))
+        ids.copy_(first)
+        run = graph.replay
+        torch.tvarant.synchronize()
+        bench._barrier(world)
     with bench.ClockSampler(local_rank) as clocks:
         h0 = time.perf_counter()
-        ms = _time_steps(step, steps)
+        ms = _time_steps(run, steps)
         clocks.mark(h0, time.perf_counter())
     ms = bench._max_over_ranks(ms, world)
+    if graph is not None:
+        graph.close()
     status = torch.tvarant.get_status()
     if rank != 0:
         return None
@@ -438,7 +459,11 @@ def _gpt2_decode(args, rank, world, local_rank):
         "dtype": "tf32" if args.mode == "tf32" else "f32 (3xTF32)",
         "data": "synthetic (N(0,0.02) weights, uniform prompt ids, greedy decode tokens)",
         "config": {"workload": f"GPT-2-small decode with a KV cache: batch {batch}, prompt {prompt}, "
-                               f"{steps} timed single-token steps (eager)",
+                               f"{steps} timed single-token steps "
+                               + ("(CUDA graph of the fixed-shape step)" if graph is not None
+                                  else "(eager)"),
+                   "eager_ms_per_step": eager_ms,
+                   "eager_tokens_per_s": world * batch / (eager_ms / 1e3),
                    "prefill_ms": prefill_ms, "parallelism": f"replicas x{world}",
                    "weights_mb": weight_bytes / 1e6,
                    "l2": "the 0.5 GB of weights exceed L2; every step streams them"},
