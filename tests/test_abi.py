@@ -162,6 +162,23 @@ def test_rms_norm_and_rope_validate_arguments():
     assert "exceed" in capi.last_error()
 
 
+def test_decode_entry_points_validate_arguments():
+    import ctypes
+
+    capi.load()
+    st = capi.int64_array([0, 0, 0])
+    assert capi.try_call("tvr_kv_append", None, None, -1, 1, 1, 8, 4, st, st, None,
+                         None) == capi.ERR_INVALID
+    assert capi.try_call("tvr_kv_append", None, None, 0, 1, 1, 8, 4, st, st, None,
+                         None) == capi.OK  # nothing to append
+    assert capi.try_call("tvr_kv_append", ctypes.c_void_p(16), ctypes.c_void_p(16), 1, 1, 1, 8, 4,
+                         st, st, ctypes.c_void_p(12), None) == capi.ERR_INVALID  # unaligned position
+    assert capi.try_call("tvr_counter_add", None, 1, None) == capi.ERR_INVALID
+    assert capi.try_call("tvr_attention_fwd_keylen", None, None, None, None, 1, 1, 1, 8, 64, st, st,
+                         st, st, 1.0, None, 1, capi.GEMM_TF32, None) == capi.ERR_INVALID
+    assert "key length" in capi.last_error()
+
+
 def test_extension_loads_without_gpu():
     import torch
 
