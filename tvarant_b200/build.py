@@ -11,7 +11,9 @@ Two shared objects are produced in-tree, next to this file:
   the C ABI above.
 
 Builds are incremental (object files are rebuilt when a source or header is
-newer) and run compilers in parallel.  Usage: ``python -m tvarant_b200.build``.
+newer) and run compilers in parallel.  Usage, from the repository root:
+``python tvarant_b200/build.py [--force] [--clean]`` (run as a script: importing the
+package needs the extension this builds).
 """
 
 from __future__ import annotations

@@ -155,7 +155,7 @@ def load(path: str | os.PathLike | None = None) -> ctypes.CDLL:
     if not p.exists():
         raise ImportError(
             f"{p} is missing: the tvarant CUDA library has not been built "
-            "(python -m tvarant_b200.build)"
+            "(python tvarant_b200/build.py from the repository root)"
         )
     lib = ctypes.CDLL(str(p), mode=ctypes.RTLD_GLOBAL)
     for name, args in SIGNATURES.items():
