@@ -194,10 +194,11 @@ int tvr_gemm_bias_act(const float* a, const float* b, const float* bias, float* 
                       void* stream);
 
 /* tvr_gemm_bias_act in TF32 mode (same arguments, minus the mode) for
- * callers that cannot allocate device memory during the call: code running
- * while a CUDA graph is captured, hosts with a fixed device-memory budget,
- * runtimes that forbid the allocator after start-up.  No counterpart in the
- * reference.  The only scratch it uses — split-K partial sums — is a fixed
+ * callers that cannot allocate device memory during the call: a host that
+ * hands out all device memory itself from a budget fixed at start-up, or a
+ * runtime that forbids the CUDA allocator once it is serving (an allocation
+ * can synchronize the device and its latency is unbounded).  No counterpart
+ * in the reference.  The only scratch it uses — split-K partial sums — is a fixed
  * 16 MiB __device__ array inside the library, which every GPU that loads the
  * library keeps until the process exits; the call makes no allocation.
  * Limit: m*n <= 4194304 output elements, else TVR_ERR_INVALID.  The first call

@@ -1,7 +1,8 @@
 """tvr_gemm_bias_act_noalloc: the allocation-free GEMM entry point.
 
 It exists for callers that must not allocate device memory during a call
-(work recorded into a CUDA graph, hosts with a fixed memory budget); its
+(hosts with a fixed device-memory budget they hand out themselves, runtimes
+that forbid the allocator while serving); its
 split-K scratch is a fixed array inside the library.  Its results must match
 tvr_gemm_bias_act in TF32 mode within the TF32 GEMM tolerance, on two calls
 in a row (the second call reuses the scratch the first left behind), and it

@@ -1076,11 +1076,11 @@ int gemm_tcgen05_swiglu(const float* x, const float* wg, const float* wu, float*
 
 // ---- allocation-free variant ----------------------------------------------------
 //
-// Some callers cannot allocate device memory while they run: code that
-// executes while a CUDA graph is being captured (an allocation is not a
-// capturable stream operation), a host that hands the device a fixed memory
-// budget up front, or an embedding runtime that forbids the driver's
-// allocator after start-up.  tvr_gemm_bias_act_noalloc serves them: it is the
+// Some callers cannot allocate device memory while they run: a host that
+// hands out all device memory itself from a budget fixed at start-up, or an
+// embedding runtime that forbids the CUDA allocator once it is serving (an
+// allocation can synchronize the device, and its latency is unbounded).
+// tvr_gemm_bias_act_noalloc serves them: it is the
 // TF32 tensor-core GEMM of tvr_gemm_bias_act whose only scratch — the split-K
 // partial sums of skinny problems — lives in the fixed device array below
 // instead of coming from tvr_malloc.
