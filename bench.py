@@ -689,6 +689,8 @@ def _main() -> int:
     ap.add_argument("--ref-rows", type=int, default=0)
     ap.add_argument("--layers", type=int, default=32, help="mlp workload: MLP layers")
     ap.add_argument("--seq", type=int, default=1024, help="gpt2 workload: sequence length")
+    ap.add_argument("--prompt", type=int, default=512,
+                    help="gpt2-decode workload: prompt tokens per sequence before decoding")
     ap.add_argument("--gpt2-batch", type=int, default=8, help="gpt2 workload: sequences per step (whole job)")
     ap.add_argument("--attention", choices=["bmm", "sdpa"], default="bmm",
                     help="gpt2 workload: bmm + mask + softmax + bmm (the config), or the fused "

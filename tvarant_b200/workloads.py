@@ -383,7 +383,7 @@ def _gpt2_cpu_baseline(host_model, cfg, seq: int) -> dict:
 
 
 def _gpt2_decode(args, rank, world, local_rank):
-    """GPT-2-small generation with a KV cache: a prompt of ``--seq`` tokens
+    """GPT-2-small generation with a KV cache: a prompt of ``--prompt`` tokens
     per sequence (prefill), then one token per sequence per step (decode).
     A step is one ``forward_step`` over [batch, 1] new tokens: few-row GEMMs
     (batch rows), attention of one query per head over the cached keys, and
@@ -398,7 +398,7 @@ def _gpt2_decode(args, rank, world, local_rank):
     torch.set_float32_matmul_precision("high" if args.mode == "tf32" else "highest")
     dev = f"tvarant:{local_rank}"
     cfg = gpt2.GPT2Config()
-    batch, prompt = args.gpt2_batch, args.seq
+    batch, prompt = args.gpt2_batch, args.prompt
     steps = args.steps
     if prompt + args.warmup + 2 * steps + 3 > cfg.n_ctx:
         raise ValueError(f"prompt {prompt} + {args.warmup + 2 * steps + 3} steps exceed "
