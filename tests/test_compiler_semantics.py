@@ -154,11 +154,15 @@ def _model(spec):
 @settings(max_examples=150, deadline=None)
 @given(chains())
 def test_compiled_graph_means_what_the_model_means(spec):
+    # float64: a chain such as exp(exp(y + z)) multiplies a rounding
+    # difference of its argument by about 80, so in float32 a different but
+    # equally valid evaluation order of the fused program could exceed the
+    # tolerance; what is checked here is the program's meaning, not rounding
     torch.manual_seed(0)
-    model = _model(spec).eval()
+    model = _model(spec).double().eval()
     g = torch.Generator().manual_seed(1)
-    x = torch.randn(5, 16, generator=g) * 0.5
-    z = torch.randn(5, 24, generator=g) * 0.5
+    x = (torch.randn(5, 16, generator=g) * 0.5).double()
+    z = (torch.randn(5, 24, generator=g) * 0.5).double()
     with torch.no_grad():
         want = model(x, z)
         gm = compile_fx(trace_module(model))

@@ -56,10 +56,16 @@ constexpr int STAGES = 2;                // K, V, P and both TMEM accumulators a
 constexpr int THREADS = 192;
 constexpr uint32_t TMEM_COLS = 256;      // S buffers at 0 and 64, PV buffers at 128 and 192
 constexpr uint32_t PV_COL = 2 * BN;
+constexpr float kLazyLog2 = 8.f;         // P_TMEM: raise the running maximum past 2^8 growth
 constexpr int BAR_BYTES = 8 * 24;
-constexpr int SMEM_BYTES =
-    1024 + Q_BYTES + STAGES * (K_BYTES + V_BYTES + P_BYTES) + BAR_BYTES;
-static_assert(SMEM_BYTES <= 232448, "shared memory budget");
+// P_j in shared memory (the A operand of PV_j read through a descriptor), or
+// written back over S_j in tensor memory and read from there (P_TMEM): the
+// second form needs no P tiles, so two CTAs fit on one SM.
+constexpr int smem_bytes(bool p_tmem) {
+  return 1024 + Q_BYTES + STAGES * (K_BYTES + V_BYTES + (p_tmem ? 0 : P_BYTES)) + BAR_BYTES;
+}
+static_assert(smem_bytes(false) <= 232448, "shared memory budget");
+static_assert(2 * (smem_bytes(true) + 1024 + 64) <= 233472, "two CTAs per SM with P in TMEM");
 
 struct Params {
   CUtensorMap tma_q;  // {D, seq_q, heads, batch}, box {32, 128}
@@ -92,13 +98,37 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
+// Row qidx of the output (O / l) and its log-sum-exp (natural log), from the
+// unnormalised O and the log2-domain running maximum m and sum l.
+__device__ __forceinline__ void store_row(const Params& p, int b, int h, int qidx, const float* o,
+                                          float m, float l) {
+  const float inv = l > 0.f ? 1.f / l : 0.f;
+  float* dst = p.out + b * p.o_sb + h * p.o_sh + static_cast<int64_t>(qidx) * p.o_ss;
+  if ((reinterpret_cast<uintptr_t>(dst) & 15u) == 0) {
+#pragma unroll
+    for (int i = 0; i < D / 4; ++i) {
+      reinterpret_cast<float4*>(dst)[i] =
+          make_float4(o[4 * i] * inv, o[4 * i + 1] * inv, o[4 * i + 2] * inv, o[4 * i + 3] * inv);
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < D; ++i) dst[i] = o[i] * inv;
+  }
+  if (p.lse != nullptr) {
+    p.lse[(static_cast<int64_t>(b) * p.heads + h) * p.seq_q + qidx] =
+        m * 0.69314718055994531f + logf(l);
+  }
+}
+
 __device__ __forceinline__ void st_shared4(uint32_t addr, float a, float b, float c, float d) {
   asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(a), "f"(b), "f"(c),
                "f"(d)
                : "memory");
 }
 
-__global__ void __launch_bounds__(THREADS, 1) attn_fwd_kernel(const __grid_constant__ Params p) {
+template <bool P_TMEM>
+__global__ void __launch_bounds__(THREADS, P_TMEM ? 2 : 1)
+    attn_fwd_kernel(const __grid_constant__ Params p) {
   extern __shared__ uint8_t smem_raw[];
   __shared__ int s_abort;
   __shared__ uint64_t s_drain;
@@ -108,9 +138,9 @@ __global__ void __launch_bounds__(THREADS, 1) attn_fwd_kernel(const __grid_const
   const uint32_t sq = base;
   const uint32_t sk = sq + Q_BYTES;                 // [2] K tiles
   const uint32_t sv = sk + STAGES * K_BYTES;        // [2] V tiles
-  const uint32_t sp = sv + STAGES * V_BYTES;        // [2] P tiles
+  const uint32_t sp = sv + STAGES * V_BYTES;        // [2] P tiles (unless P_TMEM)
   // mbarriers, one 8-byte slot each; [2] = one per buffer
-  const uint32_t bar = sp + STAGES * P_BYTES;
+  const uint32_t bar = sp + (P_TMEM ? 0 : STAGES * P_BYTES);
   const uint32_t q_full = bar;
   const uint32_t k_full = bar + 8;       // [2]
   const uint32_t k_empty = bar + 24;     // [2]
@@ -148,7 +178,9 @@ __global__ void __launch_bounds__(THREADS, 1) attn_fwd_kernel(const __grid_const
       mbar_init(v_full + 8 * i, 1);
       mbar_init(v_empty + 8 * i, 1);
       mbar_init(s_full + 8 * i, 1);
-      mbar_init(s_empty + 8 * i, 4);
+      // S buffer free: the softmax warps read it (P in shared memory) or PV
+      // read the P written over it (P_TMEM, one commit)
+      mbar_init(s_empty + 8 * i, P_TMEM ? 1 : 4);
       mbar_init(p_full + 8 * i, 4);
       mbar_init(pv_full + 8 * i, 1);
       mbar_init(pv_empty + 8 * i, 4);
@@ -249,19 +281,32 @@ __global__ void __launch_bounds__(THREADS, 1) attn_fwd_kernel(const __grid_const
           const int pb = j & 1;
           if (!mbar_wait(p_full + 8 * pb, (j >> 1) & 1, abort_flag) ||
               !mbar_wait(v_full + 8 * pb, (j >> 1) & 1, abort_flag) ||
-              (j >= 2 && !mbar_wait(pv_empty + 8 * pb, ((j >> 1) - 1) & 1, abort_flag))) {
+              (!P_TMEM && j >= 2 &&
+               !mbar_wait(pv_empty + 8 * pb, ((j >> 1) - 1) & 1, abort_flag))) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t d = tmem + PV_COL + static_cast<uint32_t>(pb * D);
-          const uint32_t pt = sp + pb * P_BYTES;
+          if constexpr (P_TMEM) {
+            // P_j sits in score buffer j & 1 (K step x: its columns 8x .. 8x+7);
+            // O accumulates in place over all blocks
+            const uint32_t pa = tmem + static_cast<uint32_t>(pb * BN);
 #pragma unroll
-          for (int x = 0; x < BN / 8; ++x) {
-            // K step x covers keys 8x .. 8x+7: P atom x / 4 (32 keys), +32 B
-            // per step inside it; V rows 8x.., 8 rows of 128 B = 1024 B per step
-            mma_tf32(d, desc_kmajor(pt + (x >> 2) * Q_ATOM + (x & 3) * 32),
-                     desc_v(sv + pb * V_BYTES + x * 1024), idesc_pv, x > 0 ? 1u : 0u);
+            for (int x = 0; x < BN / 8; ++x) {
+              mma_tf32_tmem_a(tmem + PV_COL, pa + 8u * x, desc_v(sv + pb * V_BYTES + x * 1024),
+                              idesc_pv, (j > 0 || x > 0) ? 1u : 0u);
+            }
+            mma_commit(s_empty + 8 * pb);  // P_j read: the buffer may take S_{j+2}
+          } else {
+            const uint32_t d = tmem + PV_COL + static_cast<uint32_t>(pb * D);
+            const uint32_t pt = sp + pb * P_BYTES;
+#pragma unroll
+            for (int x = 0; x < BN / 8; ++x) {
+              // K step x covers keys 8x .. 8x+7: P atom x / 4 (32 keys), +32 B
+              // per step inside it; V rows 8x.., 8 rows of 128 B = 1024 B per step
+              mma_tf32(d, desc_kmajor(pt + (x >> 2) * Q_ATOM + (x & 3) * 32),
+                       desc_v(sv + pb * V_BYTES + x * 1024), idesc_pv, x > 0 ? 1u : 0u);
+            }
           }
           mma_commit(v_empty + 8 * pb);
           mma_commit(pv_full + 8 * pb);
@@ -276,6 +321,110 @@ __global__ void __launch_bounds__(THREADS, 1) attn_fwd_kernel(const __grid_const
     }
     __syncwarp();
     if (lane == 0 && !mbar_wait(drain, 0, nullptr)) record_status(p.status, TVR_DEV_TIMEOUT_DRAIN);
+    __syncwarp();
+  } else if constexpr (P_TMEM) {
+    // ------------------- softmax rows, P and O in tensor memory -------------------
+    // O accumulates in TMEM (PV_j adds P_j V_j to it).  O and l are kept
+    // relative to a running maximum m that is raised only when a block's
+    // maximum exceeds it by more than 2^kLazyLog2, or at the first visible
+    // scores; then the warp rescales its rows of O (a TMEM round trip after
+    // PV_{j-1} has landed).  Between raises P = 2^(x - m) <= 2^kLazyLog2,
+    // far from the fp32 range, and O / l is unchanged by the choice of m.
+    const int q = warp & 3;
+    const int t = 32 * q + lane;  // TMEM lane = query row within the tile
+    const int qidx = q0 + t;
+    const uint32_t lane_off = static_cast<uint32_t>(32 * q) << 16;
+    const uint32_t orow = tmem + lane_off + PV_COL;
+    float m = -INFINITY, l = 0.f;
+    bool ok = true;
+    // PV_j done: completion j >> 1 of pv_full[j & 1]
+    auto wait_pv = [&](int j) -> bool {
+      const bool got = mbar_wait(pv_full + 8 * (j & 1), (j >> 1) & 1, abort_flag);
+      return __all_sync(0xffffffffu, got);
+    };
+    for (int j = 0; j < nkb; ++j) {
+      const int sb = j & 1;
+      const bool got = mbar_wait(s_full + 8 * sb, (j >> 1) & 1, abort_flag);
+      if (!__all_sync(0xffffffffu, got)) {
+        ok = false;
+        break;
+      }
+      // S_j was issued after PV_{j-2} finished, so this returns at once; it
+      // keeps the thread's view of each pv_full barrier within one phase
+      // of its state, which the parity waits below rely on
+      if (j >= 2 && !wait_pv(j - 2)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t srow = tmem + lane_off + static_cast<uint32_t>(sb * BN);
+      const int key0 = j * BN;
+      int key_end = min(seq_k, key0 + BN);
+      if (p.causal) key_end = min(key_end, qidx + 1);
+      const int nvis = key_end - key0;  // may be <= 0 for padding rows
+      float sc[BN];
+#pragma unroll
+      for (int c = 0; c < BN / 32; ++c) tmem_load_32_async(srow + 32 * c, sc + 32 * c);
+      tmem_wait_loads();
+      float mx = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < BN; ++i) {
+        if (i < nvis) mx = fmaxf(mx, sc[i] * p.scale_log2);
+      }
+      const float m_new = fmaxf(m, mx);
+      if (__any_sync(0xffffffffu, m_new > m + kLazyLog2)) {
+        const float alpha = ex2(m - (m_new == -INFINITY ? 0.f : m_new));  // 0 while m = -inf
+        if (j >= 1) {
+          if (!wait_pv(j - 1)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+#pragma unroll
+          for (int c = 0; c < D / 32; ++c) {
+            float ov[32];
+            tmem_load_32_async(orow + 32 * c, ov);
+            tmem_wait_loads();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) ov[i] *= alpha;
+            tmem_store_32(orow + 32 * c, ov);
+          }
+        }
+        l *= alpha;
+        m = m_new;
+      }
+      const float m_use = m == -INFINITY ? 0.f : m;
+      float sum = 0.f;
+#pragma unroll
+      for (int i = 0; i < BN; ++i) {
+        const float e = i < nvis ? ex2(fmaf(sc[i], p.scale_log2, -m_use)) : 0.f;
+        sc[i] = e;
+        sum += e;
+      }
+      // P_j over S_j in this row's lane; PV_j reads it from there.  The wait
+      // also covers the O rescale above.
+#pragma unroll
+      for (int c = 0; c < BN / 32; ++c) tmem_store_32(srow + 32 * c, sc + 32 * c);
+      tmem_wait_stores();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(p_full + 8 * sb);
+      l += sum;
+    }
+    if (ok && !wait_pv(nkb - 1)) ok = false;  // nkb >= 1: key 0 is always visible
+    if (!ok) {
+      if (lane == 0) {
+        record_status(p.status, TVR_DEV_TIMEOUT_EPILOGUE);
+        *const_cast<volatile int*>(abort_flag) = 1;
+      }
+    } else {
+      tc_fence_after();
+      float o[D];
+#pragma unroll
+      for (int c = 0; c < D / 32; ++c) tmem_load_32_async(orow + 32 * c, o + 32 * c);
+      tmem_wait_loads();
+      if (qidx < p.seq_q) store_row(p, b, h, qidx, o, m, l);
+    }
     __syncwarp();
   } else {
     // ------------------------------ softmax rows ------------------------------
@@ -377,22 +526,7 @@ __global__ void __launch_bounds__(THREADS, 1) attn_fwd_kernel(const __grid_const
         *const_cast<volatile int*>(abort_flag) = 1;
       }
     } else if (qidx < p.seq_q) {
-      const float inv = l > 0.f ? 1.f / l : 0.f;
-      float* dst = p.out + b * p.o_sb + h * p.o_sh + static_cast<int64_t>(qidx) * p.o_ss;
-      if ((reinterpret_cast<uintptr_t>(dst) & 15u) == 0) {
-#pragma unroll
-        for (int i = 0; i < D / 4; ++i) {
-          reinterpret_cast<float4*>(dst)[i] =
-              make_float4(o[4 * i] * inv, o[4 * i + 1] * inv, o[4 * i + 2] * inv, o[4 * i + 3] * inv);
-        }
-      } else {
-#pragma unroll
-        for (int i = 0; i < D; ++i) dst[i] = o[i] * inv;
-      }
-      if (p.lse != nullptr) {
-        p.lse[(static_cast<int64_t>(b) * p.heads + h) * p.seq_q + qidx] =
-            m * 0.69314718055994531f + logf(l);
-      }
+      store_row(p, b, h, qidx, o, m, l);
     }
     __syncwarp();
   }
@@ -475,16 +609,30 @@ int attention_impl(const float* q, const float* k, const float* v, float* out, f
   p.status = device_status_ptr(dev);
   p.key_len = key_len;
   p.key_len_add = key_len_add;
+  // P in tensor memory (two CTAs per SM) is chosen with
+  // TVARANT_ATTENTION_P_TMEM=1 until it has been measured against the
+  // shared-memory form on the device; both compute the same values.
+  static const bool p_tmem = [] {
+    const char* env = std::getenv("TVARANT_ATTENTION_P_TMEM");
+    return env != nullptr && env[0] == '1';
+  }();
   static std::once_flag once[64];
   static cudaError_t attr_err[64];
   std::call_once(once[dev & 63], [&]() {
-    attr_err[dev & 63] = cudaFuncSetAttribute(attn_fwd_kernel,
-                                              cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                              SMEM_BYTES);
+    attr_err[dev & 63] = cudaFuncSetAttribute(
+        attn_fwd_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes(false));
+    if (attr_err[dev & 63] == cudaSuccess) {
+      attr_err[dev & 63] = cudaFuncSetAttribute(
+          attn_fwd_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes(true));
+    }
   });
   TVR_CUDA_TRY(attr_err[dev & 63]);
   const dim3 grid(static_cast<unsigned>(ceil_div(seq_q, BM)), static_cast<unsigned>(batch * heads));
-  attn_fwd_kernel<<<grid, THREADS, SMEM_BYTES, as_stream(stream)>>>(p);
+  if (p_tmem) {
+    attn_fwd_kernel<true><<<grid, THREADS, smem_bytes(true), as_stream(stream)>>>(p);
+  } else {
+    attn_fwd_kernel<false><<<grid, THREADS, smem_bytes(false), as_stream(stream)>>>(p);
+  }
   TVR_LAUNCH_CHECK();
   return TVR_OK;
 }
