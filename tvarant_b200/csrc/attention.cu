@@ -199,6 +199,9 @@ __global__ void __launch_bounds__(THREADS, P_TMEM ? 2 : 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(&s_tmem);
+  // a few-row GEMM launched as a programmatic dependent (the projection after
+  // a decode step's attention) may start streaming its weights now
+  if (threadIdx.x == 0) grid_launch_dependents();
 
   if (warp == 0) {
     // ------------------------------ TMA producers ------------------------------

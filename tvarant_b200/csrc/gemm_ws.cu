@@ -94,6 +94,7 @@ struct Params {
   int m, n;
   int num_kb;
   int kb_per_split;
+  int pdl;  // launched as a programmatic dependent of the previous kernel
   int* status;
 };
 
@@ -205,6 +206,9 @@ __global__ void __launch_bounds__(Cfg<MB, SPLIT3>::THREADS, Cfg<MB, SPLIT3>::CTA
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *reinterpret_cast<volatile uint32_t*>(holder_ptr);
+  // a programmatic dependent (the next few-row GEMM) may start its own
+  // weight stream now; it still waits for this grid before reading its output
+  if (p.pdl && threadIdx.x == 0) grid_launch_dependents();
 
   if (warp == 0) {
     // ------------------------------ TMA producer ------------------------------
@@ -214,7 +218,29 @@ __global__ void __launch_bounds__(Cfg<MB, SPLIT3>::THREADS, Cfg<MB, SPLIT3>::CTA
       uint32_t issued_mask = 0;
       uint32_t issued_parity = 0;
       bool ok = true;
-      for (int kb = kb0; kb < kb1; ++kb) {
+      int kb_first = kb0;
+      if (p.pdl) {
+        // The weights do not depend on earlier kernels: the first pass of the
+        // ring starts streaming them while the previous kernel on the stream
+        // may still run.  X, written by that kernel, is loaded only after it
+        // has completed.  (The first pass needs no wait for a free slot.)
+        const int n_pre = min(STAGES, kb1 - kb0);
+        for (int i = 0; i < n_pre; ++i) {
+          const uint32_t fb = full_bar + 8 * i;
+          mbar_expect_tx(fb, Cf::LOAD_BYTES);
+          tma_load_3d(ring + i * Cf::STAGE_BYTES, &p.tma_w, fb, (kb0 + i) * BK, tile * BM, 0);
+        }
+        grid_dependency_wait();
+        for (int i = 0; i < n_pre; ++i) {
+          tma_load_3d(ring + i * Cf::STAGE_BYTES + Cf::W_BYTES, &p.tma_x, full_bar + 8 * i,
+                      (kb0 + i) * BK, 0, 0);
+        }
+        issued_mask = (1u << n_pre) - 1u;  // all in phase 0
+        kb_first = kb0 + n_pre;
+        stage = n_pre % STAGES;
+        phase = n_pre == STAGES ? 1u : 0u;
+      }
+      for (int kb = kb_first; kb < kb1; ++kb) {
         if (!mbar_wait(empty_bar + 8 * stage, phase ^ 1u, abort_flag)) {
           ok = false;
           break;
@@ -437,13 +463,16 @@ int launch(Params& p, int tiles, int sms, cudaStream_t stream, int dev) {
   cfg.blockDim = dim3(Cf::THREADS, 1, 1);
   cfg.dynamicSmemBytes = Cf::SMEM_BYTES;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
+  memset(attr, 0, sizeof(attr));
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = static_cast<unsigned>(splits);
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = p.pdl ? 2 : 1;
   TVR_CUDA_TRY(cudaLaunchKernelEx(&cfg, gemm_ws_kernel<MB, SPLIT3>, p));
   return TVR_OK;
 }
@@ -487,6 +516,7 @@ int gemm_ws(const float* x, const float* w, const float* bias, float* c, int64_t
   p.m = static_cast<int>(m);
   p.n = static_cast<int>(n);
   p.num_kb = num_kb;
+  p.pdl = pdl_enabled() ? 1 : 0;
   p.status = device_status_ptr(dev);
   switch (mb) {
     case 16: return launch_mb<16>(p, split3, tiles, sms, stream, dev);

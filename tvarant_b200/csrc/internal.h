@@ -58,6 +58,25 @@ struct Scratch {
 
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
 
+// Whether the few-row GEMM is launched as a programmatic dependent of the
+// kernel before it on the stream (TVARANT_PDL=1; read once).
+bool pdl_enabled();
+
+#ifdef __CUDACC__
+// Programmatic dependent launch.  A kernel launched with programmatic stream
+// serialization may start while the kernel before it on the stream is still
+// running; grid_dependency_wait() blocks the calling thread until that kernel
+// has completed and its memory operations are visible to this grid.  A kernel
+// calls grid_launch_dependents() to let such a successor start before it
+// ends.  Without a programmatic dependency both do nothing.
+__device__ __forceinline__ void grid_dependency_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+__device__ __forceinline__ void grid_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+#endif
+
 inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
 // Grid size for grid-stride elementwise kernels: enough blocks to cover the

@@ -239,6 +239,9 @@ __global__ void __launch_bounds__(1024) layer_norm_kernel(
     float* __restrict__ y, float* __restrict__ mean_out, float* __restrict__ rstd_out, int n,
     float eps) {
   __shared__ float red[32];
+  // a few-row GEMM launched as a programmatic dependent (decode steps) may
+  // start streaming its weights now
+  if (threadIdx.x == 0) grid_launch_dependents();
   const int64_t row = blockIdx.x;
   const int n4 = n >> 2;
   const float4* xr = reinterpret_cast<const float4*>(x + row * n);
@@ -307,6 +310,7 @@ __global__ void __launch_bounds__(256) layer_norm_generic_kernel(
     float* __restrict__ y, float* __restrict__ mean_out, float* __restrict__ rstd_out, int64_t n,
     float eps) {
   __shared__ float red[32];
+  if (threadIdx.x == 0) grid_launch_dependents();
   const float* xr = x + static_cast<int64_t>(blockIdx.x) * n;
   float* yr = y + static_cast<int64_t>(blockIdx.x) * n;
   float s = 0.f;

@@ -19,6 +19,7 @@ those workloads.  All work runs through the torch_tvarant device API.
 
 from __future__ import annotations
 
+import os
 import statistics
 import time
 
@@ -466,6 +467,8 @@ def _gpt2_decode(args, rank, world, local_rank):
                    "eager_tokens_per_s": world * batch / (eager_ms / 1e3),
                    "prefill_ms": prefill_ms, "parallelism": f"replicas x{world}",
                    "weights_mb": weight_bytes / 1e6,
+                   "programmatic_launch": os.environ.get("TVARANT_PDL") == "1",
+                   "attention_p_in_tmem": os.environ.get("TVARANT_ATTENTION_P_TMEM") == "1",
                    "l2": "the 0.5 GB of weights exceed L2; every step streams them"},
         "roofline": {"bound": "hbm", "achieved": weight_bytes / (ms / 1e3) / 1e9,
                      "peak": bench._peaks().get("hbm_gbs", 6650.0), "unit": "GB/s",
@@ -557,6 +560,7 @@ def _gpt2(args, rank, world, local_rank):
                                   else "fused scaled_dot_product_attention (TF32 kernel)")
                                + ", tied LM head",
                    "attention": att,
+                   "attention_p_in_tmem": os.environ.get("TVARANT_ATTENTION_P_TMEM") == "1",
                    "cuda_graph": not args.no_graph,
                    "eager_tokens_per_s": batch * seq / (eager_ms / 1e3),
                    "parallelism": f"batch split over {world} rank(s) (attention split over batch x heads)",
