@@ -699,6 +699,9 @@ def _main() -> int:
     ap.add_argument("--comm", choices=["nccl", "nvls"], default="nccl",
                     help="mlp workload at N>1: NCCL all-reduce, or this library's NVLink SHARP "
                          "all-reduce over symmetric memory")
+    ap.add_argument("--gemm-sms", type=int, default=0,
+                    help="mlp workload at N>1: SMs the GEMMs may use while the all-reduce runs "
+                         "(0: all but the collective's CTAs)")
     ap.add_argument("--nvls-blocks", type=int, default=32,
                     help="mlp workload, --comm nvls: CTAs of the all-reduce kernel")
     ap.add_argument("--nccl-ctas", type=int, default=32,

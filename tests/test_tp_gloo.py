@@ -97,3 +97,11 @@ def test_shards_reject_uneven_splits():
 def test_llama_dff_splits_over_1_2_4_8():
     for world in (1, 2, 4, 8):
         assert 11008 % world == 0
+
+
+def test_stack_rejects_a_negative_sm_limit():
+    from tvarant_b200.tp import TPMLPStack
+
+    with pytest.raises(ValueError):
+        TPMLPStack([], None, gemm_sms=-1)
+    assert TPMLPStack([], None, gemm_sms=118).gemm_sms == 118

@@ -123,11 +123,19 @@ class TPMLPStack:
     """A stack of gated-SiLU MLP layers split over the ranks of ``comm``
     (NCCL) or of ``nvls`` (one ``NvlsAllReduce`` per token chunk)."""
 
-    def __init__(self, layers, comm: Communicator | None, chunks: int = 2, nvls=None):
+    def __init__(self, layers, comm: Communicator | None, chunks: int = 2, nvls=None,
+                 gemm_sms: int = 0):
         self.layers = layers  # list of (gate, up, down) shards on this device
         self.comm = comm
         self.nvls = list(nvls) if nvls else None
         self.chunks = len(self.nvls) if self.nvls else max(1, chunks)
+        # SMs the GEMMs may use while the stack runs (0: all but the
+        # collective's CTAs).  The GEMMs run whole waves of tiles over these
+        # SMs, so a limit that divides a chunk's tile count evenly can be
+        # worth more than a few more SMs.
+        if gemm_sms < 0:
+            raise ValueError(f"gemm_sms {gemm_sms} < 0")
+        self.gemm_sms = gemm_sms
         self._streams = None
 
     def _comm_streams(self, device: int):
@@ -148,7 +156,9 @@ class TPMLPStack:
 
         prev_limit = _C.gemm_sm_limit(device)
         ctas = self.nvls[0].blocks if self.nvls else self.comm.max_ctas
-        if ctas > 0 and self.chunks > 1:
+        if self.gemm_sms > 0:
+            _C.set_gemm_sm_limit(device, self.gemm_sms)
+        elif ctas > 0 and self.chunks > 1:
             _C.set_gemm_sm_limit(device, max(1, _C.sm_count(device) - ctas))
         try:
             if self.nvls:

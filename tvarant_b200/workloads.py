@@ -263,7 +263,8 @@ def _mlp(args, rank, world, local_rank):
                 for _ in range(chunks)]
     elif world > 1:
         comm = Communicator.from_process_group(local_rank, args.nccl_ctas)
-    stack = TPMLPStack(layers, comm, chunks=args.chunks if world > 1 else 1, nvls=nvls)
+    stack = TPMLPStack(layers, comm, chunks=args.chunks if world > 1 else 1, nvls=nvls,
+                       gemm_sms=args.gemm_sms if world > 1 else 0)
     g = torch.Generator().manual_seed(7)
     x_host = torch.randn(TOKENS, D_MODEL, generator=g)
     if torch.cuda.is_available():
@@ -338,6 +339,7 @@ def _mlp(args, rank, world, local_rank):
                                 f"{args.nvls_blocks} CTAs)" if use_nvls
                                 else ("NCCL all-reduce" if world > 1 else None)),
                    "nccl_max_ctas": args.nccl_ctas if comm is not None else None,
+                   "gemm_sms": args.gemm_sms if world > 1 else None,
                    "cuda_graph": not args.no_graph,
                    "eager_tokens_per_s": TOKENS / (eager_ms / 1e3),
                    "layer_ms_one_rank_gemms": layer_ms,
