@@ -80,6 +80,7 @@ struct Params {
   int* status;
   const int64_t* key_len;    // non-null: attend to clamp(*key_len + key_len_add, 1, seq_k) keys
   int key_len_add;
+  int pdl_trigger;           // let a programmatic dependent launch once this CTA is set up
 };
 
 // N-major V operand: 32-wide atoms of the head dimension, each [64 keys x
@@ -201,7 +202,7 @@ __global__ void __launch_bounds__(THREADS, P_TMEM ? 2 : 1)
   const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(&s_tmem);
   // a few-row GEMM launched as a programmatic dependent (the projection after
   // a decode step's attention) may start streaming its weights now
-  if (threadIdx.x == 0) grid_launch_dependents();
+  if (p.pdl_trigger && threadIdx.x == 0) grid_launch_dependents();
 
   if (warp == 0) {
     // ------------------------------ TMA producers ------------------------------
@@ -612,6 +613,7 @@ int attention_impl(const float* q, const float* k, const float* v, float* out, f
   p.status = device_status_ptr(dev);
   p.key_len = key_len;
   p.key_len_add = key_len_add;
+  p.pdl_trigger = pdl_enabled() ? 1 : 0;
   // P in tensor memory (two CTAs per SM) is chosen with
   // TVARANT_ATTENTION_P_TMEM=1 until it has been measured against the
   // shared-memory form on the device; both compute the same values.
