@@ -371,6 +371,13 @@ class GemmChain:
         return y
 
 
+def _kernel_options() -> dict:
+    """Kernel-form switches set in the environment (tvarant_b200.workloads)."""
+    from tvarant_b200.workloads import kernel_options
+
+    return kernel_options()
+
+
 def _dist_init(world: int):
     import torch.distributed as dist
 
@@ -558,6 +565,7 @@ def run_gemm(args, rank, world, local_rank) -> dict | None:
                    else f"steps rotate over {wl.copies} weight copies ({wl.copies * 67} MB > L2), "
                         "so each step reads its weight from HBM"),
             "fusions": wl.fusions,
+            "kernel_options": _kernel_options(),
         },
         "e2e": {"value": world * wl.flops / (pt["e2e_ms"] / 1e3) / 1e12, "unit": "TFLOP/s",
                 "h2d_bytes_per_step": wl.h2d_bytes, "d2h_bytes_per_step": wl.d2h_bytes,

@@ -35,6 +35,7 @@
 #include "internal.h"
 
 #include <atomic>
+#include <cstdlib>
 #include <mutex>
 
 #include "epilogue_prog.cuh"
@@ -875,6 +876,30 @@ int gemm_tcgen05(const float* a, const float* b, const float* bias, float* c, in
     bn = cand;
     tiles = t;
     if (t >= (sms * 4) / 5) break;
+  }
+  // TVARANT_GEMM_WAVE_FIT=1: among the tile widths that fill a wave, take
+  // the one whose whole waves over the SMs the persistent grid may use cost
+  // least (rounds x width, 128-wide tiles charged 5 % more for their lower
+  // operand reuse).  N = 768 at M = 8192 is 192 tiles of 256 (2 rounds on
+  // 148 SMs: 65 % of the time does work) or 384 of 128 (3 rounds: 86 %).
+  static const bool wave_fit = [] {
+    const char* env = std::getenv("TVARANT_GEMM_WAVE_FIT");
+    return env != nullptr && env[0] == '1';
+  }();
+  if (wave_fit && tiles >= (sms * 4) / 5) {
+    const int64_t g = grid_sms(dev, sms);
+    double best = 0.0;
+    for (int cand : {256, 128}) {
+      if (cand > bn_cap) continue;
+      const int64_t t = batch * ceil_div(m, BM) * ceil_div(n, cand);
+      if (t < (sms * 4) / 5) continue;
+      const double cost = static_cast<double>(ceil_div(t, g)) * cand * (cand == 128 ? 1.05 : 1.0);
+      if (best == 0.0 || cost < best) {
+        best = cost;
+        bn = cand;
+        tiles = t;
+      }
+    }
   }
   const bool c_vec = al16(c) && ldc % 4 == 0 && (batch == 1 || sc % 4 == 0);
   int splits = 1;

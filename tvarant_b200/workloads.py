@@ -27,6 +27,17 @@ import torch
 
 D_MODEL, D_FF, LAYERS, TOKENS = 4096, 11008, 32, 8192
 
+# Kernel forms chosen by environment variables, read by the library at its
+# first use: the attention kernel with P and O in tensor memory, programmatic
+# dependent launch of the few-row GEMM, and the tile width chosen by whole
+# waves for the large GEMMs.
+KERNEL_OPTIONS = ("TVARANT_ATTENTION_P_TMEM", "TVARANT_PDL", "TVARANT_GEMM_WAVE_FIT")
+
+
+def kernel_options() -> dict:
+    """The kernel-form switches set for this process (for the JSON line)."""
+    return {name: os.environ.get(name) == "1" for name in KERNEL_OPTIONS}
+
 
 def _events():
     return (torch.Event(device="tvarant", enable_timing=True),
@@ -340,6 +351,7 @@ def _mlp(args, rank, world, local_rank):
                                 else ("NCCL all-reduce" if world > 1 else None)),
                    "nccl_max_ctas": args.nccl_ctas if comm is not None else None,
                    "gemm_sms": args.gemm_sms if world > 1 else None,
+                   "kernel_options": kernel_options(),
                    "cuda_graph": not args.no_graph,
                    "eager_tokens_per_s": TOKENS / (eager_ms / 1e3),
                    "layer_ms_one_rank_gemms": layer_ms,
@@ -469,8 +481,7 @@ def _gpt2_decode(args, rank, world, local_rank):
                    "eager_tokens_per_s": world * batch / (eager_ms / 1e3),
                    "prefill_ms": prefill_ms, "parallelism": f"replicas x{world}",
                    "weights_mb": weight_bytes / 1e6,
-                   "programmatic_launch": os.environ.get("TVARANT_PDL") == "1",
-                   "attention_p_in_tmem": os.environ.get("TVARANT_ATTENTION_P_TMEM") == "1",
+                   "kernel_options": kernel_options(),
                    "l2": "the 0.5 GB of weights exceed L2; every step streams them"},
         "roofline": {"bound": "hbm", "achieved": weight_bytes / (ms / 1e3) / 1e9,
                      "peak": bench._peaks().get("hbm_gbs", 6650.0), "unit": "GB/s",
@@ -562,7 +573,7 @@ def _gpt2(args, rank, world, local_rank):
                                   else "fused scaled_dot_product_attention (TF32 kernel)")
                                + ", tied LM head",
                    "attention": att,
-                   "attention_p_in_tmem": os.environ.get("TVARANT_ATTENTION_P_TMEM") == "1",
+                   "kernel_options": kernel_options(),
                    "cuda_graph": not args.no_graph,
                    "eager_tokens_per_s": batch * seq / (eager_ms / 1e3),
                    "parallelism": f"batch split over {world} rank(s) (attention split over batch x heads)",
