@@ -207,7 +207,7 @@ __global__ void __launch_bounds__(Cfg<MB, SPLIT3>::THREADS, Cfg<MB, SPLIT3>::CTA
   tc_fence_after();
   const uint32_t tmem_base = *reinterpret_cast<volatile uint32_t*>(holder_ptr);
   // a programmatic dependent (the next few-row GEMM) may start its own
-  // weight stream now; it still waits for this grid before reading its output
+  // weight prefetch now; it still waits for this grid before reading anything
   if (p.pdl && threadIdx.x == 0) grid_launch_dependents();
 
   if (warp == 0) {
@@ -218,29 +218,17 @@ __global__ void __launch_bounds__(Cfg<MB, SPLIT3>::THREADS, Cfg<MB, SPLIT3>::CTA
       uint32_t issued_mask = 0;
       uint32_t issued_parity = 0;
       bool ok = true;
-      int kb_first = kb0;
       if (p.pdl) {
-        // The weights do not depend on earlier kernels: the first pass of the
-        // ring starts streaming them while the previous kernel on the stream
-        // may still run.  X, written by that kernel, is loaded only after it
-        // has completed.  (The first pass needs no wait for a free slot.)
-        const int n_pre = min(STAGES, kb1 - kb0);
-        for (int i = 0; i < n_pre; ++i) {
-          const uint32_t fb = full_bar + 8 * i;
-          mbar_expect_tx(fb, Cf::LOAD_BYTES);
-          tma_load_3d(ring + i * Cf::STAGE_BYTES, &p.tma_w, fb, (kb0 + i) * BK, tile * BM, 0);
-        }
+        // Launched as a programmatic dependent: the kernel before this one
+        // on the stream may still run.  The weight panel's first k-blocks
+        // start moving from HBM into L2 now; nothing is read into shared
+        // memory until that kernel has completed, so a weight it writes is
+        // still read as written.
+        const int n_pre = min(2 * STAGES, kb1 - kb0);
+        for (int i = 0; i < n_pre; ++i) tma_prefetch_l2_3d(&p.tma_w, (kb0 + i) * BK, tile * BM, 0);
         grid_dependency_wait();
-        for (int i = 0; i < n_pre; ++i) {
-          tma_load_3d(ring + i * Cf::STAGE_BYTES + Cf::W_BYTES, &p.tma_x, full_bar + 8 * i,
-                      (kb0 + i) * BK, 0, 0);
-        }
-        issued_mask = (1u << n_pre) - 1u;  // all in phase 0
-        kb_first = kb0 + n_pre;
-        stage = n_pre % STAGES;
-        phase = n_pre == STAGES ? 1u : 0u;
       }
-      for (int kb = kb_first; kb < kb1; ++kb) {
+      for (int kb = kb0; kb < kb1; ++kb) {
         if (!mbar_wait(empty_bar + 8 * stage, phase ^ 1u, abort_flag)) {
           ok = false;
           break;

@@ -75,6 +75,16 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map
       : "memory");
 }
 
+// A hint: bring one tile of the tensor into L2 (no shared memory, no
+// barrier).  L2 is where the GPU's writes become visible, so a prefetch that
+// runs before the tile's writer has finished brings in nothing stale: later
+// loads read the written values.
+__device__ __forceinline__ void tma_prefetch_l2_3d(const CUtensorMap* map, int c0, int c1, int c2) {
+  asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%0, {%1, %2, %3}];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(c0), "r"(c1), "r"(c2)
+               : "memory");
+}
 
 // Tile store shared -> global through the tensor map (bulk-group completion).
 // Elements outside the tensor's extent are not written.  The x coordinate
