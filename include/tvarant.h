@@ -40,7 +40,7 @@ extern "C" {
 #define TVR_OK 0
 #define TVR_ERR_INVALID 1     /* bad argument (shape, null pointer, op id)      */
 #define TVR_ERR_CUDA 2        /* a CUDA runtime/driver call failed              */
-#define TVR_ERR_UNSUPPORTED 3 /* valid request this build does not implement   */
+#define TVR_ERR_UNSUPPORTED 3 /* valid request the library does not implement */
 #define TVR_ERR_OOM 4         /* device or pinned allocation failed             */
 #define TVR_ERR_TIMEOUT 5     /* a bounded wait expired (host or device side)   */
 #define TVR_ERR_NCCL 6        /* NCCL missing or an NCCL call failed            */
@@ -400,7 +400,7 @@ int tvr_rope(const float* x, float* y, const float* cos_table, const float* sin_
 
 /* One SSA node.  Opcodes 0-8 keep the reference numbering
  * (csrc/jit/Jit.h:11-21): Load, Const, Add (a + alpha*b), Mul, Relu, Silu,
- * Neg, Scale (alpha*a), Sigmoid; this build appends Sub (a - alpha*b) = 9,
+ * Neg, Scale (alpha*a), Sigmoid; this library appends Sub (a - alpha*b) = 9,
  * Exp = 10, Abs = 11. */
 typedef struct tvr_pw_node {
   int32_t op;
