@@ -42,7 +42,7 @@ void init_once() {
     const char* env = std::getenv("TVARANT_BACKEND");
     if (env != nullptr && env[0] != '\0' && std::string(env) != "cuda") {
       g_init_error = std::string("TVARANT_BACKEND=") + env +
-                     " is not available in this build (expected 'cuda'; the CPU simulator "
+                     " is not available in this package (expected 'cuda'; the CPU simulator "
                      "and OpenCL runtimes are replaced by the B200 CUDA runtime)";
       return;
     }
