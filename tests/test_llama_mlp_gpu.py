@@ -20,9 +20,10 @@ from conftest import rel_frobenius
 
 pytestmark = pytest.mark.gpu
 
-# d_ff = 11008 / 16: five full 128-row weight tiles and a 48-row tail, like
-# the 1376 rows (10 tiles + 96) one rank holds at 8 GPUs
-TOKENS, D_MODEL, D_FF = 64, 256, 688
+# More than 128 tokens, so TF32 runs the fused SwiGLU tensor-core GEMM;
+# d_ff = 11008 / 16 gives it five full 128-column output tiles and a 48-column
+# tail, like the 1376 columns (10 tiles + 96) one rank holds at 8 GPUs
+TOKENS, D_MODEL, D_FF = 256, 256, 688
 
 
 def _oracle_layer(x, wg, wu, wd):
