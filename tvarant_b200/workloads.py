@@ -29,9 +29,10 @@ D_MODEL, D_FF, LAYERS, TOKENS = 4096, 11008, 32, 8192
 
 # Kernel forms chosen by environment variables, read by the library at its
 # first use: the attention kernel with P and O in tensor memory, programmatic
-# dependent launch of the few-row GEMM, and the tile width chosen by whole
-# waves for the large GEMMs.
-KERNEL_OPTIONS = ("TVARANT_ATTENTION_P_TMEM", "TVARANT_PDL", "TVARANT_GEMM_WAVE_FIT")
+# dependent launch of the few-row GEMM, the tile width chosen by whole waves
+# for the large GEMMs, and pointwise programs in the few-row GEMM's epilogue.
+KERNEL_OPTIONS = ("TVARANT_ATTENTION_P_TMEM", "TVARANT_PDL", "TVARANT_GEMM_WAVE_FIT",
+                  "TVARANT_WS_PROGRAM")
 
 
 def kernel_options() -> dict:
