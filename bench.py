@@ -704,9 +704,10 @@ def _main() -> int:
                     help="gpt2 workload: bmm + mask + softmax + bmm (the config), or the fused "
                          "F.scaled_dot_product_attention kernel")
     ap.add_argument("--chunks", type=int, default=2, help="mlp workload: token chunks overlapped with the all-reduce")
-    ap.add_argument("--comm", choices=["nccl", "nvls"], default="nccl",
-                    help="mlp workload at N>1: NCCL all-reduce, or this library's NVLink SHARP "
-                         "all-reduce over symmetric memory")
+    ap.add_argument("--comm", choices=["nccl", "nvls", "nvls-fused"], default="nccl",
+                    help="mlp workload at N>1: NCCL all-reduce, this library's NVLink SHARP "
+                         "all-reduce over symmetric memory, or (TF32) the down projection and "
+                         "that all-reduce in one kernel")
     ap.add_argument("--gemm-sms", type=int, default=0,
                     help="mlp workload at N>1: SMs the GEMMs may use while the all-reduce runs "
                          "(0: all but the collective's CTAs)")

@@ -483,8 +483,11 @@ int tvr_nccl_comm_abort(void* comm);
 
 #define TVR_NVLS_MAX_RANKS 8
 #define TVR_NVLS_MAX_BLOCKS 64
-/* uint32 words of one rank's flag array */
-#define TVR_NVLS_FLAG_WORDS (2 * TVR_NVLS_MAX_BLOCKS * TVR_NVLS_MAX_RANKS)
+/* output tiles of one tvr_gemm_nvls_all_reduce_f32 call (128 x 256 each) */
+#define TVR_NVLS_MAX_TILES 4096
+/* uint32 words of one rank's flag array: barrier words for three phases,
+ * then one arrival counter per output tile */
+#define TVR_NVLS_FLAG_WORDS (3 * TVR_NVLS_MAX_BLOCKS * TVR_NVLS_MAX_RANKS + TVR_NVLS_MAX_TILES)
 
 /* In-place sum of `count` fp32 values over `world` ranks (one process per
  * GPU) of a buffer bound to an NVLink multicast object: `multicast` is the
@@ -504,6 +507,28 @@ int tvr_nccl_comm_abort(void* comm);
  * returns: check tvr_get_status after synchronizing. */
 int tvr_nvls_all_reduce_f32(void* multicast, int64_t count, void* const* peer_flags, int rank,
                             int world, uint32_t* epoch_counter, int blocks, void* stream);
+
+/* C = A . B^T (TF32; A [m, k] with row stride lda, B [n, k] with row stride
+ * ldb: an nn.Linear weight) followed by the in-place sum of C over `world`
+ * ranks, in one kernel: the row-parallel projection of a tensor-parallel
+ * layer and its all-reduce.  c is this rank's copy of a buffer bound to an
+ * NVLink multicast object and c_multicast its multicast address; peer_flags,
+ * epoch_counter, rank and world as for tvr_nvls_all_reduce_f32 (the same
+ * flag arrays may serve both calls).  GEMM CTAs store each 128 x 256 output
+ * tile to c and count it in the flag array of the rank that owns the tile
+ * (tile index mod world); reduce_ctas further CTAs of the same launch (a
+ * cooperative one, so every CTA is resident) wait for their rank's tiles to
+ * arrive from every rank, sum each through the switch (multimem.ld_reduce)
+ * and store the sum to every rank (multimem.st), so the exchange runs while
+ * the GEMM is still computing other tiles.  A closing barrier keeps every
+ * rank in the call until all tiles are summed.  Requires n % 4 == 0, 16-byte
+ * aligned rows, m, n >= 32 and at most TVR_NVLS_MAX_TILES tiles;
+ * 1 <= reduce_ctas <= TVR_NVLS_MAX_BLOCKS.  Expired waits (2 s) set
+ * TVR_DEV_TIMEOUT_PEER. */
+int tvr_gemm_nvls_all_reduce_f32(const float* a, const float* b, float* c, void* c_multicast,
+                                 int64_t m, int64_t n, int64_t k, int64_t lda, int64_t ldb,
+                                 int64_t ldc, void* const* peer_flags, int rank, int world,
+                                 uint32_t* epoch_counter, int reduce_ctas, void* stream);
 
 #if defined(__GNUC__)
 #pragma GCC visibility pop

@@ -146,6 +146,35 @@ def test_nvls_all_reduce_validates_before_touching_a_device():
     assert call(count=0) == capi.OK  # nothing to do: no launch, no device needed
 
 
+def test_gemm_nvls_all_reduce_validates_before_touching_a_device():
+    import ctypes
+
+    capi.load()
+    flags = (ctypes.c_void_p * 2)(16, 32)
+    vp = ctypes.c_void_p
+
+    def call(m=256, n=256, k=64, world=2, rank=0, ctas=8, counter=vp(64), mc=vp(4096),
+             a=vp(1024), lda=64, ldc=256, flag_array=ctypes.addressof(flags)):
+        return capi.try_call("tvr_gemm_nvls_all_reduce_f32", a, vp(2048), vp(8192), mc, m, n, k,
+                             lda, 64, ldc, flag_array, rank, world, counter, ctas, None)
+
+    assert call(world=1) == capi.ERR_INVALID
+    assert call(world=9) == capi.ERR_INVALID
+    assert call(rank=-1) == capi.ERR_INVALID
+    assert call(m=-1) == capi.ERR_INVALID
+    assert call(a=None) == capi.ERR_INVALID
+    assert call(mc=None) == capi.ERR_INVALID
+    assert call(counter=None) == capi.ERR_INVALID
+    assert call(counter=vp(66)) == capi.ERR_INVALID  # unaligned epoch counter
+    assert call(flag_array=None) == capi.ERR_INVALID
+    # shape checks come before the epoch advances and anything launches
+    assert call(mc=vp(4100)) == capi.ERR_INVALID  # unaligned multicast address
+    assert call(n=254, ldc=254) == capi.ERR_INVALID  # n % 4 != 0
+    assert call(m=16) == capi.ERR_INVALID  # fewer than one 32-row box
+    assert call(lda=63) == capi.ERR_INVALID
+    assert "gemm_nvls_all_reduce" in capi.last_error()
+
+
 def test_rms_norm_and_rope_validate_arguments():
     import ctypes
 

@@ -51,3 +51,22 @@ def test_nvls_all_reduce_and_tp_stack(tmp_path):
     assert float(r["worst"]) <= 6e-8, float(r["worst"])
     assert rel_frobenius(r["tp"], r["full"]) <= 3e-5, rel_frobenius(r["tp"], r["full"])
     assert rel_frobenius(r["graph2"], r["full2"]) <= 3e-5
+
+
+@pytest.mark.skipif(_gpus() < 2, reason="needs two GPUs")
+def test_gemm_with_nvls_all_reduce_in_one_kernel(tmp_path):
+    """tvr_gemm_nvls_all_reduce_f32 (TF32): the buffer holds the sum of both
+    ranks' products within the TF32 GEMM tolerance, over calls whose tile
+    counts differ; the TP stack on it equals the unsharded stack in TF32,
+    eagerly and replayed from a graph."""
+    out = tmp_path / "fused.npz"
+    cmd = ["timeout", "-k", "30", "240", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+           "--nproc-per-node", "2", "--master-addr", "127.0.0.1", "--master-port", str(_port()),
+           str(HERE / "nvls_worker.py"), str(out), "fused"]
+    proc = subprocess.run(cmd, capture_output=True, text=True)
+    assert proc.returncode == 0, proc.stdout[-3000:] + proc.stderr[-3000:]
+    r = np.load(out)
+    assert int(r["status_gemm"]) == 0 and int(r["status_tp"]) == 0
+    assert float(np.max(r["gemm_err"])) <= 5e-3, r["gemm_err"]
+    assert rel_frobenius(r["tp"], r["full"]) <= 5e-3, rel_frobenius(r["tp"], r["full"])
+    assert rel_frobenius(r["graph2"], r["full2"]) <= 5e-3

@@ -130,6 +130,8 @@ SIGNATURES: dict[str, list] = {
     "tvr_gemm_pointwise": [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _f32, _f32,
                            _i32, _i32, _i32, _vp, _i32, _i32, _i32, _vp, _pi64, _vp],
     "tvr_nvls_all_reduce_f32": [_vp, _i64, _vp, _i32, _i32, _vp, _i32, _vp],
+    "tvr_gemm_nvls_all_reduce_f32": [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _vp,
+                                     _i32, _i32, _vp, _i32, _vp],
     "tvr_nccl_available": [_pi],
     "tvr_nccl_get_unique_id": [_vp],
     "tvr_nccl_comm_init": [_pvp, _i32, _vp, _i32, _i32],

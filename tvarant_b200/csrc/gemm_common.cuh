@@ -75,6 +75,15 @@ int gemm_tcgen05_swiglu(const float* x, const float* wg, const float* wu, float*
                         int64_t n, int64_t k, int64_t ldx, int64_t ldwg, int64_t ldwu,
                         int64_t ldo, cudaStream_t stream);
 
+// C = A . B^T (TF32, K-major B) summed over `world` ranks through NVLink
+// SHARP in the same kernel; tvr_gemm_nvls_all_reduce_f32 validates the
+// cross-rank arguments.  Checks the shapes, then advances the epoch counter
+// on the stream and launches (nothing is launched when a check fails).
+int gemm_tcgen05_nvls(const float* a, const float* b, float* c, void* c_multicast, int64_t m,
+                      int64_t n, int64_t k, int64_t lda, int64_t ldb, int64_t ldc,
+                      void* const* peer_flags, int rank, int world, uint32_t* epoch,
+                      int reduce_ctas, cudaStream_t stream);
+
 // Returns TVR_ERR_UNSUPPORTED (without recording an error) when the
 // operands cannot be described by TMA tensor maps; the caller then uses
 // gemm_simt.  With a pointwise program (prog non-null with nodes), the

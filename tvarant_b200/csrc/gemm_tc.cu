@@ -40,6 +40,7 @@
 
 #include "epilogue_prog.cuh"
 #include "gemm_common.cuh"
+#include "nvls_common.cuh"
 #include "tc_ptx.cuh"
 
 // TMA_C instances leave the chunk loop early (`continue`), so the register-
@@ -97,6 +98,12 @@ struct Params {
   int total_units;
   int* status;
   EpiProg prog;  // PROG kernels: pointwise program applied to each output element
+  // NVLS kernels (tvr_gemm_nvls_all_reduce_f32): the output summed over ranks
+  float* nv_mc;               // multicast address of c
+  nvls::PeerFlags nv_flags;   // every rank's flag array
+  const uint32_t* nv_epoch;   // this call's epoch (advanced before the launch)
+  int nv_rank, nv_world;
+  int nv_gemm_ctas;           // CTAs [0, nv_gemm_ctas) compute tiles, the rest reduce them
 };
 
 // N-major tile: 32-wide N atoms of [BK rows x 128 B] placed BK*128 B apart
@@ -130,6 +137,64 @@ __device__ __forceinline__ void decode_unit(const Params& p, int u, int& b, int&
   tn = rr / gm;
 }
 
+// NVLS kernels: the CTAs past the GEMM's sum this rank's output tiles (unit
+// u with u % world == rank) over all ranks.  Each epilogue warp of every
+// rank counts its part of tile u, once stored, in the owner's counter u; a
+// reducer waits for all EPI_WARPS x world arrivals, resets the counter for
+// the next call, reads the tile's sum through the switch and stores it to
+// every rank.  The closing barrier keeps every rank in the kernel until all
+// ranks' reducers are done, so each rank's c holds the whole sum when the
+// kernel ends.
+template <int OUT_BN>
+__device__ __forceinline__ void nvls_reduce_tiles(const Params& p) {
+  using namespace nvls;
+  __shared__ int expired;
+  constexpr int kUnroll = 4;
+  const int rc = static_cast<int>(blockIdx.x) - p.nv_gemm_ctas;
+  const int nred = static_cast<int>(gridDim.x) - p.nv_gemm_ctas;
+  const int rank = p.nv_rank, world = p.nv_world;
+  const uint32_t epoch = *p.nv_epoch;
+  const uint32_t arrivals = static_cast<uint32_t>(EPI_WARPS * world);
+  uint32_t* mine = p.nv_flags.flags[rank] + kTileCounters;
+  if (threadIdx.x == 0) expired = 0;
+  __syncthreads();
+  for (int i = rc;; i += nred) {
+    const int u = rank + world * i;
+    if (u >= p.total_units) break;
+    if (threadIdx.x == 0) {
+      if (wait_at_least(mine + u, arrivals, p.status)) {
+        mine[u] = 0;  // every arrival of this call is in; the next call counts afresh
+      } else {
+        expired = 1;
+      }
+    }
+    __syncthreads();
+    if (expired) break;
+    int b, s, tm, tn;
+    decode_unit(p, u, b, s, tm, tn);
+    const int row0 = tm * BM, col0 = tn * OUT_BN;
+    const int c4 = min(OUT_BN, p.n - col0) / 4;  // n % 4 == 0
+    const int total = min(BM, p.m - row0) * c4;
+    const int nt = static_cast<int>(blockDim.x);
+    for (int e = static_cast<int>(threadIdx.x); e < total; e += kUnroll * nt) {
+      float4 v[kUnroll];
+      float* at[kUnroll];
+#pragma unroll
+      for (int q = 0; q < kUnroll; ++q) {
+        const int idx = e + q * nt;
+        const int r = idx / c4;
+        at[q] = p.nv_mc + static_cast<int64_t>(row0 + r) * p.ldc + col0 + 4 * (idx - r * c4);
+        if (idx < total) v[q] = multimem_ld_reduce_add(at[q]);
+      }
+#pragma unroll
+      for (int q = 0; q < kUnroll; ++q) {
+        if (e + q * nt < total) multimem_st(at[q], v[q]);
+      }
+    }
+  }
+  rank_barrier(p.nv_flags, rank, world, 2, rc, epoch, p.status, &expired);
+}
+
 // GATED (TF32, K-major weights, BN = 256): the B tile stacks 128 rows of the
 // gate weight (tma_b) over the same 128 rows of the up weight (tma_b_lo), the
 // MMA fills accumulator columns 0..127 with x.Wg^T and 128..255 with x.Wu^T,
@@ -146,16 +211,25 @@ __device__ __forceinline__ void decode_unit(const Params& p, int u, int& b, int&
 // is what small-K GEMMs (batched attention scores, K = 64..128), whose time
 // is the output stream, need.
 template <int BN, bool SPLIT3, bool B_NMAJOR, bool GATED = false, bool PROG = false,
-          bool TMA_C = false>
+          bool TMA_C = false, bool NVLS = false>
 __global__ void __launch_bounds__(NUM_THREADS, 1) gemm_tc_kernel(const __grid_constant__ Params p) {
   using Cf = Cfg<BN, SPLIT3>;
   static_assert(!GATED || (BN == 256 && !SPLIT3 && !B_NMAJOR), "gated GEMM shape");
   static_assert(!PROG || (!GATED && !B_NMAJOR), "pointwise-epilogue GEMM shape");
   static_assert(!TMA_C || (!GATED && !PROG), "TMA-store epilogue");
+  static_assert(!NVLS || (TMA_C && !SPLIT3 && !B_NMAJOR), "GEMM + NVLS all-reduce shape");
   constexpr int OUT_BN = GATED ? BN / 2 : BN;  // output columns per tile
   constexpr int STAGES = Cf::STAGES;
   extern __shared__ uint8_t smem_raw[];
   __shared__ int s_abort;
+  if constexpr (NVLS) {
+    if (static_cast<int>(blockIdx.x) >= p.nv_gemm_ctas) {
+      nvls_reduce_tiles<OUT_BN>(p);
+      return;
+    }
+  }
+  // the CTAs that compute tiles (all of them, except in NVLS kernels)
+  const int grid_stride = NVLS ? p.nv_gemm_ctas : static_cast<int>(gridDim.x);
 
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
@@ -206,7 +280,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) gemm_tc_kernel(const __grid_co
       uint32_t issued_mask = 0;  // stages with a load issued
       uint32_t issued_parity = 0;
       bool ok = true;
-      for (int u = blockIdx.x; ok && u < p.total_units; u += gridDim.x) {
+      for (int u = blockIdx.x; ok && u < p.total_units; u += grid_stride) {
         int b, s, tm, tn;
         decode_unit(p, u, b, s, tm, tn);
         const int kb0 = s * p.kb_per_split;
@@ -277,7 +351,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) gemm_tc_kernel(const __grid_co
       uint32_t acc_phase = 0;
       bool ok = true;
       bool issued = false;
-      for (int u = blockIdx.x; ok && u < p.total_units; u += gridDim.x) {
+      for (int u = blockIdx.x; ok && u < p.total_units; u += grid_stride) {
         int b, s, tm, tn;
         decode_unit(p, u, b, s, tm, tn);
         const int kb0 = s * p.kb_per_split;
@@ -356,7 +430,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) gemm_tc_kernel(const __grid_co
     int acc = 0;
     uint32_t acc_phase = 0;
     bool ok = true;
-    for (int u = blockIdx.x; u < p.total_units; u += gridDim.x) {
+    for (int u = blockIdx.x; u < p.total_units; u += grid_stride) {
       int b, s, tm, tn;
       decode_unit(p, u, b, s, tm, tn);
       const bool got = mbar_wait(tfull_bar + 8 * acc, acc_phase, abort_flag);
@@ -686,6 +760,18 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) gemm_tc_kernel(const __grid_co
         }
         __syncwarp();  // the staging buffer is rewritten by the next chunk
       }
+      if constexpr (NVLS) {
+        // this warp's 32 x HC part of tile u is in c: count it at the tile's
+        // owner once the stores are complete and ordered before the count
+        if (lane == 0) {
+          bulk_wait_all();
+          asm volatile("fence.proxy.async.global;" ::: "memory");
+          nvls::fence_sys();
+          nvls::red_release_sys_add(
+              p.nv_flags.flags[u % p.nv_world] + nvls::kTileCounters + u, 1u);
+        }
+        __syncwarp();
+      }
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1u;
     }
@@ -792,6 +878,36 @@ int launch_kernel(const Params& p, int grid, cudaStream_t stream, int dev) {
   gemm_tc_kernel<BN, SPLIT3, B_NMAJOR, GATED, PROG, TMA_C>
       <<<grid, NUM_THREADS, Cf::SMEM_BYTES, stream>>>(p);
   TVR_LAUNCH_CHECK();
+  return TVR_OK;
+}
+
+__global__ void nvls_epoch_advance_kernel(uint32_t* counter) { *counter += 1; }
+
+// NVLS kernels: one cooperative launch, so that every GEMM and reducer CTA
+// is resident at once (the reducers wait for tiles the GEMM CTAs produce).
+int launch_nvls(const Params& p, int grid, cudaStream_t stream, int dev) {
+  using Cf = Cfg<256, false>;
+  auto kernel = gemm_tc_kernel<256, false, false, false, false, true, true>;
+  static std::once_flag once[64];
+  static cudaError_t attr_err[64];
+  std::call_once(once[dev & 63], [&]() {
+    attr_err[dev & 63] =
+        cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Cf::SMEM_BYTES);
+  });
+  TVR_CUDA_TRY(attr_err[dev & 63]);
+  cudaLaunchConfig_t cfg;
+  memset(&cfg, 0, sizeof(cfg));
+  cfg.gridDim = dim3(static_cast<unsigned>(grid), 1, 1);
+  cfg.blockDim = dim3(NUM_THREADS, 1, 1);
+  cfg.dynamicSmemBytes = Cf::SMEM_BYTES;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  memset(attr, 0, sizeof(attr));
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  TVR_CUDA_TRY(cudaLaunchKernelEx(&cfg, kernel, p));
   return TVR_OK;
 }
 
@@ -1095,6 +1211,67 @@ int gemm_tcgen05_swiglu(const float* x, const float* wg, const float* wu, float*
   p.status = device_status_ptr(dev);
   const int grid = static_cast<int>(std::min<int64_t>(units, tc::grid_sms(dev, sms)));
   return launch_kernel<256, false, false, true>(p, grid, stream, dev);
+}
+
+// C = A . B^T (TF32, K-major B) with C then summed over the ranks through
+// NVLink SHARP inside the same kernel (tvr_gemm_nvls_all_reduce_f32).
+int gemm_tcgen05_nvls(const float* a, const float* b, float* c, void* c_multicast, int64_t m,
+                      int64_t n, int64_t k, int64_t lda, int64_t ldb, int64_t ldc,
+                      void* const* peer_flags, int rank, int world, uint32_t* epoch,
+                      int reduce_ctas, cudaStream_t stream) {
+  using namespace tc;
+  TVR_CHECK(al16(a) && al16(b) && al16(c) && al16(c_multicast) && lda % 4 == 0 && ldb % 4 == 0 &&
+                ldc % 4 == 0 && n % 4 == 0,
+            "gemm_nvls_all_reduce: operands need 16-byte aligned bases, row strides and n %% 4 == 0");
+  TVR_CHECK(m >= 32 && n >= 32 && k >= 1 && m <= 0x7fffff00 && n <= 0x7fffff00 &&
+                k <= 0x7fffff00 && lda >= k && ldb >= k && ldc >= n && ldc <= (int64_t(1) << 34),
+            "gemm_nvls_all_reduce: shape (%lld, %lld, %lld) out of range", (long long)m,
+            (long long)n, (long long)k);
+  const int dev = current_device();
+  const int sms = sm_count(dev);
+  TVR_CHECK(reduce_ctas >= 1 && reduce_ctas <= TVR_NVLS_MAX_BLOCKS && reduce_ctas < sms,
+            "gemm_nvls_all_reduce: %d reducing CTAs (1..%d, fewer than the %d SMs)", reduce_ctas,
+            TVR_NVLS_MAX_BLOCKS, sms);
+  constexpr int kBn = 256;
+  Params p;
+  memset(&p, 0, sizeof(p));
+  int rc;
+  if ((rc = encode_3d(&p.tma_a, a, k, m, 1, lda * 4, m * lda * 4, BK, BM)) != TVR_OK) return rc;
+  if ((rc = encode_3d(&p.tma_b, b, k, n, 1, ldb * 4, n * ldb * 4, BK, kBn)) != TVR_OK) return rc;
+  if ((rc = encode_3d(&p.tma_c, c, n, m, 1, ldc * 4, m * ldc * 4, 32, 32)) != TVR_OK) return rc;
+  p.c = c;
+  p.ldc = ldc;
+  p.stride_c = m * ldc;
+  p.alpha = 1.f;
+  p.beta = 0.f;
+  p.act = TVR_ACT_NONE;
+  p.c_vec = 1;
+  p.m = static_cast<int>(m);
+  p.n = static_cast<int>(n);
+  p.k = static_cast<int>(k);
+  p.batch = 1;
+  p.tiles_m = static_cast<int>(ceil_div(m, BM));
+  p.tiles_n = static_cast<int>(ceil_div(n, kBn));
+  p.splits = 1;
+  p.num_kb = static_cast<int>(ceil_div(k, BK));
+  p.kb_per_split = p.num_kb;
+  const int64_t units = static_cast<int64_t>(p.tiles_m) * p.tiles_n;
+  TVR_CHECK(units <= TVR_NVLS_MAX_TILES, "gemm_nvls_all_reduce: %lld output tiles (at most %d)",
+            (long long)units, TVR_NVLS_MAX_TILES);
+  p.total_units = static_cast<int>(units);
+  p.status = device_status_ptr(dev);
+  TVR_CHECK(p.status != nullptr, "gemm_nvls_all_reduce: device status word unavailable");
+  p.nv_mc = static_cast<float*>(c_multicast);
+  for (int r = 0; r < world; ++r) p.nv_flags.flags[r] = static_cast<uint32_t*>(peer_flags[r]);
+  p.nv_epoch = epoch;
+  p.nv_rank = rank;
+  p.nv_world = world;
+  p.nv_gemm_ctas = static_cast<int>(std::min<int64_t>(units, sms - reduce_ctas));
+  // a fresh epoch for the closing barrier on every call (and every replay of
+  // a captured graph)
+  nvls_epoch_advance_kernel<<<1, 1, 0, stream>>>(epoch);
+  TVR_LAUNCH_CHECK();
+  return launch_nvls(p, p.nv_gemm_ctas + reduce_ctas, stream, dev);
 }
 
 }  // namespace tvr

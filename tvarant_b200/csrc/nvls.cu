@@ -21,83 +21,17 @@
 // The reference has one device and no collectives; this serves the
 // tensor-parallel MLP stack (tvarant_b200/tp.py).  No load here uses TMA or
 // cluster multicast; multimem accesses go through the NVSwitch.
-#include "internal.h"
+#include "nvls_common.cuh"
+
+#include "gemm_common.cuh"
 
 namespace tvr {
 namespace {
 
+using namespace nvls;
+
 constexpr int kThreads = 512;
 constexpr int kUnroll = 4;
-constexpr unsigned long long kPeerTimeoutNs = 2000000000ull;  // 2 s per barrier
-
-struct PeerFlags {
-  uint32_t* flags[TVR_NVLS_MAX_RANKS];  // each rank's flag array, by its address here
-};
-
-__device__ __forceinline__ unsigned long long now_ns() {
-  unsigned long long t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
-
-__device__ __forceinline__ void store_release_sys(uint32_t* p, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-
-__device__ __forceinline__ uint32_t load_acquire_sys(const uint32_t* p) {
-  uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-
-__device__ __forceinline__ float4 multimem_ld_reduce_add(const float* mc) {
-  float4 v;
-  asm volatile("multimem.ld_reduce.relaxed.sys.global.add.v4.f32 {%0, %1, %2, %3}, [%4];"
-               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
-               : "l"(mc)
-               : "memory");
-  return v;
-}
-
-__device__ __forceinline__ void multimem_st(float* mc, float4 v) {
-  asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(mc),
-               "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w)
-               : "memory");
-}
-
-// Flag word of (phase, block, source rank) in a rank's flag array.
-__device__ __forceinline__ size_t flag_index(int phase, int block, int src) {
-  return (static_cast<size_t>(phase) * TVR_NVLS_MAX_BLOCKS + block) * TVR_NVLS_MAX_RANKS + src;
-}
-
-// Block b meets block b of every rank: thread t < world publishes `epoch`
-// into rank t's slot (phase, b, rank) and waits for this rank's slot
-// (phase, b, t).  Returns false for the whole block when a wait expired.
-__device__ bool rank_barrier(const PeerFlags& pf, int rank, int world, int phase, uint32_t epoch,
-                             int* status, int* expired) {
-  __syncthreads();
-  const int t = threadIdx.x;
-  if (t < world) {
-    // everything this block (and, by the kernel boundary, this stream) wrote
-    // before is visible to every rank before the flag is
-    asm volatile("fence.acq_rel.sys;" ::: "memory");
-    store_release_sys(pf.flags[t] + flag_index(phase, blockIdx.x, rank), epoch);
-    const uint32_t* mine = pf.flags[rank] + flag_index(phase, blockIdx.x, t);
-    if (load_acquire_sys(mine) < epoch) {
-      const unsigned long long t0 = now_ns();
-      unsigned polls = 0;
-      while (load_acquire_sys(mine) < epoch) {
-        if ((++polls & 63u) == 0 && now_ns() - t0 > kPeerTimeoutNs) {
-          atomicCAS(status, TVR_DEV_OK, TVR_DEV_TIMEOUT_PEER);
-          *expired = 1;
-          break;
-        }
-      }
-    }
-  }
-  __syncthreads();
-  return *expired == 0;
-}
 
 // Advances the call counter: one launch before each all-reduce, so that
 // every replay of a captured graph uses a fresh epoch.
@@ -109,7 +43,7 @@ __global__ void __launch_bounds__(kThreads)
   __shared__ int expired;
   if (threadIdx.x == 0) expired = 0;
   const uint32_t epoch = *counter;
-  if (!rank_barrier(pf, rank, world, 0, epoch, status, &expired)) return;
+  if (!rank_barrier(pf, rank, world, 0, blockIdx.x, epoch, status, &expired)) return;
   float* slice = mc + static_cast<int64_t>(rank) * per_rank;
   const int64_t n4 = per_rank / 4;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
@@ -122,7 +56,7 @@ __global__ void __launch_bounds__(kThreads)
     for (int u = 0; u < kUnroll; ++u) multimem_st(slice + 4 * (i + u * stride), v[u]);
   }
   for (; i < n4; i += stride) multimem_st(slice + 4 * i, multimem_ld_reduce_add(slice + 4 * i));
-  rank_barrier(pf, rank, world, 1, epoch, status, &expired);
+  rank_barrier(pf, rank, world, 1, blockIdx.x, epoch, status, &expired);
 }
 
 }  // namespace
@@ -165,4 +99,28 @@ extern "C" int tvr_nvls_all_reduce_f32(void* multicast, int64_t count, void* con
                                                       epoch_counter, status);
   TVR_LAUNCH_CHECK();
   return TVR_OK;
+}
+
+extern "C" int tvr_gemm_nvls_all_reduce_f32(const float* a, const float* b, float* c,
+                                            void* c_multicast, int64_t m, int64_t n, int64_t k,
+                                            int64_t lda, int64_t ldb, int64_t ldc,
+                                            void* const* peer_flags, int rank, int world,
+                                            uint32_t* epoch_counter, int reduce_ctas,
+                                            void* stream) {
+  TVR_CHECK(world >= 2 && world <= TVR_NVLS_MAX_RANKS, "gemm_nvls_all_reduce: world %d (2..%d)",
+            world, TVR_NVLS_MAX_RANKS);
+  TVR_CHECK(rank >= 0 && rank < world, "gemm_nvls_all_reduce: rank %d of %d", rank, world);
+  TVR_CHECK(m >= 0 && n >= 0 && k >= 0, "gemm_nvls_all_reduce: negative size");
+  TVR_CHECK(a != nullptr && b != nullptr && c != nullptr && c_multicast != nullptr,
+            "gemm_nvls_all_reduce: null operand");
+  TVR_CHECK(epoch_counter != nullptr && reinterpret_cast<uintptr_t>(epoch_counter) % 4 == 0,
+            "gemm_nvls_all_reduce: null or unaligned epoch counter");
+  TVR_CHECK(peer_flags != nullptr, "gemm_nvls_all_reduce: null flag array");
+  for (int r = 0; r < world; ++r) {
+    TVR_CHECK(peer_flags[r] != nullptr && reinterpret_cast<uintptr_t>(peer_flags[r]) % 4 == 0,
+              "gemm_nvls_all_reduce: flag array of rank %d is null or unaligned", r);
+  }
+  // (the shape checks, the epoch advance and the launch: gemm_tc.cu)
+  return gemm_tcgen05_nvls(a, b, c, c_multicast, m, n, k, lda, ldb, ldc, peer_flags, rank, world,
+                           epoch_counter, reduce_ctas, as_stream(stream));
 }

@@ -23,7 +23,7 @@ import torch
 
 from . import capi
 
-FLAG_WORDS = 2 * 64 * 8  # TVR_NVLS_FLAG_WORDS
+FLAG_WORDS = 3 * 64 * 8 + 4096  # TVR_NVLS_FLAG_WORDS
 
 
 class NvlsAllReduce:
@@ -71,6 +71,23 @@ class NvlsAllReduce:
         capi.call("tvr_nvls_all_reduce_f32", ctypes.c_void_p(self.multicast), count,
                   ctypes.addressof(self.flags), self.rank, self.world,
                   ctypes.c_void_p(self.epoch.data_ptr()), self.blocks, ctypes.c_void_p(stream))
+
+    def gemm_all_reduce(self, a_ptr: int, w: torch.Tensor, rows: int, k: int, lda: int,
+                        stream: int, reduce_ctas: int | None = None) -> None:
+        """``C = A W^T`` (TF32; A ``rows`` x ``k`` at device address ``a_ptr``
+        with row stride ``lda``, W an [n, k] weight) into the first
+        ``rows * n`` values of the buffer, summed over the ranks in the same
+        kernel (``tvr_gemm_nvls_all_reduce_f32``): the row-parallel projection
+        of a tensor-parallel layer and its exchange.  ``reduce_ctas`` CTAs
+        (default: ``blocks``) sum tiles while the rest compute them."""
+        n = w.shape[0]
+        if rows * n > self.numel:
+            raise ValueError(f"{rows} x {n} values exceed the buffer's {self.numel}")
+        vp = ctypes.c_void_p
+        capi.call("tvr_gemm_nvls_all_reduce_f32", vp(a_ptr), vp(w.data_ptr()), vp(self.data_ptr),
+                  vp(self.multicast), rows, n, k, lda, w.stride(0), n, ctypes.addressof(self.flags),
+                  self.rank, self.world, vp(self.epoch.data_ptr()),
+                  reduce_ctas if reduce_ctas else self.blocks, vp(stream))
 
     def close(self) -> None:
         """Drops the buffer (after the device is idle)."""

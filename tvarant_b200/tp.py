@@ -124,11 +124,16 @@ class TPMLPStack:
     (NCCL) or of ``nvls`` (one ``NvlsAllReduce`` per token chunk)."""
 
     def __init__(self, layers, comm: Communicator | None, chunks: int = 2, nvls=None,
-                 gemm_sms: int = 0):
+                 gemm_sms: int = 0, fused: bool = False):
         self.layers = layers  # list of (gate, up, down) shards on this device
         self.comm = comm
         self.nvls = list(nvls) if nvls else None
         self.chunks = len(self.nvls) if self.nvls else max(1, chunks)
+        # with NVLS in TF32: the down projection and its exchange as one kernel
+        # (tvr_gemm_nvls_all_reduce_f32) on the compute stream
+        if fused and not self.nvls:
+            raise ValueError("the fused exchange needs NVLS buffers")
+        self.fused = fused
         # SMs the GEMMs may use while the stack runs (0: all but the
         # collective's CTAs).  The GEMMs run whole waves of tiles over these
         # SMs, so a limit that divides a chunk's tile count evenly can be
@@ -152,13 +157,13 @@ class TPMLPStack:
         # The persistent GEMM otherwise holds every SM and the all-reduce of
         # chunk i would wait for the GEMMs of chunk i+1 instead of overlapping
         # them: leave the collective's CTAs their SMs while the stack runs.
-        from tvarant_b200 import _C
+        from tvarant_b200 import _C, capi
 
         prev_limit = _C.gemm_sm_limit(device)
         ctas = self.nvls[0].blocks if self.nvls else self.comm.max_ctas
         if self.gemm_sms > 0:
             _C.set_gemm_sm_limit(device, self.gemm_sms)
-        elif ctas > 0 and self.chunks > 1:
+        elif ctas > 0 and self.chunks > 1 and not (self.fused and _gemm_mode() == capi.GEMM_TF32):
             _C.set_gemm_sm_limit(device, max(1, _C.sm_count(device) - ctas))
         try:
             if self.nvls:
@@ -204,6 +209,11 @@ class TPMLPStack:
                 capi.call("tvr_gemm_swiglu", vp(src), vp(wg.data_ptr()), vp(wu.data_ptr()),
                           vp(h.data_ptr()), rc, f, d, d, wg.stride(0), wu.stride(0), f, mode,
                           vp(c_h))
+                if self.fused and mode == capi.GEMM_TF32:
+                    # the down projection's tiles are summed over the ranks
+                    # as they are stored, in the same kernel, on this stream
+                    self.nvls[c].gemm_all_reduce(h.data_ptr(), wd, rc, f, f, c_h)
+                    continue
                 capi.call("tvr_gemm_bias_act", vp(h.data_ptr()), vp(wd.data_ptr()), None,
                           vp(self.nvls[c].data_ptr), rc, d, f, f, wd.stride(0), d, 1.0, 0.0, 0,
                           1, mode, vp(c_h))

@@ -265,7 +265,8 @@ def _mlp(args, rank, world, local_rank):
     dev = f"tvarant:{local_rank}"
     layers = build_stack(rank, world, dev, layers=args.layers)
     comm, nvls = None, None
-    use_nvls = world > 1 and args.comm == "nvls"
+    use_nvls = world > 1 and args.comm in ("nvls", "nvls-fused")
+    fused = use_nvls and args.comm == "nvls-fused" and args.mode == "tf32"
     if use_nvls:
         from tvarant_b200.nvls import NvlsAllReduce
 
@@ -276,7 +277,7 @@ def _mlp(args, rank, world, local_rank):
     elif world > 1:
         comm = Communicator.from_process_group(local_rank, args.nccl_ctas)
     stack = TPMLPStack(layers, comm, chunks=args.chunks if world > 1 else 1, nvls=nvls,
-                       gemm_sms=args.gemm_sms if world > 1 else 0)
+                       gemm_sms=args.gemm_sms if world > 1 else 0, fused=fused)
     g = torch.Generator().manual_seed(7)
     x_host = torch.randn(TOKENS, D_MODEL, generator=g)
     if torch.cuda.is_available():
@@ -347,8 +348,10 @@ def _mlp(args, rank, world, local_rank):
         "config": {"workload": f"Llama-7B-shaped gated-SiLU MLP stack, {args.layers} layers, "
                                f"d_model {D_MODEL}, d_ff {D_FF}, {TOKENS} tokens, TP x{world}",
                    "parallelism": f"tp{world}", "chunks": stack.chunks,
-                   "exchange": ("NVLS all-reduce (multimem, this library's kernel, "
-                                f"{args.nvls_blocks} CTAs)" if use_nvls
+                   "exchange": (("down projection and NVLS all-reduce in one kernel "
+                                 f"({args.nvls_blocks} reducing CTAs)") if fused
+                                else ("NVLS all-reduce (multimem, this library's kernel, "
+                                      f"{args.nvls_blocks} CTAs)") if use_nvls
                                 else ("NCCL all-reduce" if world > 1 else None)),
                    "nccl_max_ctas": args.nccl_ctas if comm is not None else None,
                    "gemm_sms": args.gemm_sms if world > 1 else None,
@@ -367,7 +370,7 @@ def _mlp(args, rank, world, local_rank):
                      "peak_source": "cuBLAS TF32 8192^3 measured in this run; NVLink 770 GB/s"},
         # per layer and chunk: the SwiGLU GEMM and the down GEMM, plus the
         # epoch step and the all-reduce kernel with NVLS (NCCL's are not ours)
-        "gpu_launches": args.steps * args.layers * stack.chunks * (4 if use_nvls else 2),
+        "gpu_launches": args.steps * args.layers * stack.chunks * (3 if fused else 4 if use_nvls else 2),
         "clocks": clocks.summary(),
         "device_status": status,
     }
