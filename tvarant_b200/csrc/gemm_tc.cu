@@ -223,13 +223,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) gemm_tc_kernel(const __grid_co
   extern __shared__ uint8_t smem_raw[];
   __shared__ int s_abort;
   if constexpr (NVLS) {
+    // CTAs past the first nv_gemm_ctas reduce; the tile loops below stride
+    // over the GEMM CTAs only
     if (static_cast<int>(blockIdx.x) >= p.nv_gemm_ctas) {
       nvls_reduce_tiles<OUT_BN>(p);
       return;
     }
   }
-  // the CTAs that compute tiles (all of them, except in NVLS kernels)
-  const int grid_stride = NVLS ? p.nv_gemm_ctas : static_cast<int>(gridDim.x);
 
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
@@ -280,7 +280,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) gemm_tc_kernel(const __grid_co
       uint32_t issued_mask = 0;  // stages with a load issued
       uint32_t issued_parity = 0;
       bool ok = true;
-      for (int u = blockIdx.x; ok && u < p.total_units; u += grid_stride) {
+      for (int u = blockIdx.x; ok && u < p.total_units; u += NVLS ? static_cast<unsigned>(p.nv_gemm_ctas) : gridDim.x) {
         int b, s, tm, tn;
         decode_unit(p, u, b, s, tm, tn);
         const int kb0 = s * p.kb_per_split;
@@ -351,7 +351,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) gemm_tc_kernel(const __grid_co
       uint32_t acc_phase = 0;
       bool ok = true;
       bool issued = false;
-      for (int u = blockIdx.x; ok && u < p.total_units; u += grid_stride) {
+      for (int u = blockIdx.x; ok && u < p.total_units; u += NVLS ? static_cast<unsigned>(p.nv_gemm_ctas) : gridDim.x) {
         int b, s, tm, tn;
         decode_unit(p, u, b, s, tm, tn);
         const int kb0 = s * p.kb_per_split;
@@ -430,7 +430,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) gemm_tc_kernel(const __grid_co
     int acc = 0;
     uint32_t acc_phase = 0;
     bool ok = true;
-    for (int u = blockIdx.x; u < p.total_units; u += grid_stride) {
+    for (int u = blockIdx.x; u < p.total_units; u += NVLS ? static_cast<unsigned>(p.nv_gemm_ctas) : gridDim.x) {
       int b, s, tm, tn;
       decode_unit(p, u, b, s, tm, tn);
       const bool got = mbar_wait(tfull_bar + 8 * acc, acc_phase, abort_flag);
