@@ -219,3 +219,16 @@ def test_extension_loads_without_gpu():
     if not torch.cuda.is_available():
         assert torch.tvarant.is_available() is False
         assert torch.tvarant.device_count() == 0
+
+
+@pytest.mark.skipif(shutil.which("gcc") is None, reason="gcc not available")
+def test_header_is_plain_c(tmp_path):
+    """include/tvarant.h is the boundary for non-C++ hosts (cgo, JNI, ctypes):
+    it compiles as strict C99 with every warning on."""
+    src = tmp_path / "use.c"
+    src.write_text('#include "tvarant.h"\nint main(void) { return tvr_init == 0; }\n')
+    include = Path(__file__).resolve().parents[1] / "include"
+    proc = subprocess.run(["gcc", "-std=c99", "-Wall", "-Wextra", "-pedantic", "-Werror", "-I",
+                           str(include), "-c", str(src), "-o", str(tmp_path / "use.o")],
+                          capture_output=True, text=True)
+    assert proc.returncode == 0, proc.stderr
