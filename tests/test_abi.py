@@ -226,7 +226,8 @@ def test_header_is_plain_c(tmp_path):
     """include/tvarant.h is the boundary for non-C++ hosts (cgo, JNI, ctypes):
     it compiles as strict C99 with every warning on."""
     src = tmp_path / "use.c"
-    src.write_text('#include "tvarant.h"\nint main(void) { return tvr_init == 0; }\n')
+    src.write_text('#include "tvarant.h"\n'
+                   'int main(void) { int (*init)(void) = tvr_init; return init != tvr_init; }\n')
     include = Path(__file__).resolve().parents[1] / "include"
     proc = subprocess.run(["gcc", "-std=c99", "-Wall", "-Wextra", "-pedantic", "-Werror", "-I",
                            str(include), "-c", str(src), "-o", str(tmp_path / "use.o")],
