@@ -206,7 +206,11 @@ int tvr_gemm_bias_act(const float* a, const float* b, const float* bias, float* 
  * call before any stream capture.  All calls share the array: two calls that
  * may run at the same time on the GPU (different streams, different host
  * threads) race on it and must be ordered by the caller.  Nothing in the
- * array needs to start at zero: each call writes every element it reads. */
+ * array needs to start at zero: each call writes every element it reads.
+ * The SM limit of tvr_set_gemm_sm_limit applies.  An expired bounded wait
+ * inside the kernel is reported through tvr_get_status only on a device that
+ * tvr_init (or any other call of this library) has set up; setting a device up
+ * allocates its status word, which this entry point never does itself. */
 int tvr_gemm_bias_act_noalloc(const float* a, const float* b, const float* bias, float* c,
                               int64_t m, int64_t n, int64_t k,
                               int64_t lda, int64_t ldb, int64_t ldc,

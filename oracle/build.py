@@ -9,7 +9,9 @@
   in ``oracle/shim``.  Only built where the reference checkout exists; the
   built file travels with the repository snapshot.
 
-Usage: ``python oracle/build.py [--reference DIR]``.
+Usage: ``python oracle/build.py [--reference DIR]``.  Without ``--reference``
+the checkout is ``$TVARANT_REFERENCE_DIR``, else ``../reference`` relative to
+the repository root.
 """
 
 from __future__ import annotations
@@ -23,7 +25,10 @@ HERE = Path(__file__).resolve().parent
 REF_OUT = HERE / "_ref"
 LIB = HERE / "liboracle.so"
 REF_LIB = REF_OUT / "libtvr_ref.so"
-DEFAULT_REFERENCE = Path(os.environ.get("TVARANT_REFERENCE_DIR", "/root/reference"))
+# The reference checkout: $TVARANT_REFERENCE_DIR, else a directory named
+# "reference" beside this repository's root.
+DEFAULT_REFERENCE = Path(os.environ.get("TVARANT_REFERENCE_DIR",
+                                        str(HERE.parent.parent / "reference")))
 
 
 def _run(cmd):

@@ -310,6 +310,43 @@ def test_softmax(lib, rng, shape, dim):
     assert max_rel(y, ref, 1e-30) <= TOL_POINTWISE
 
 
+@pytest.mark.parametrize("shape,dim", [
+    ((5, 7), -1), ((3, 1001), -1), ((4, 6, 3), 1), ((6, 33, 4), 0), ((2, 4096), -1),
+    ((3, 8), -1), ((2, 5000), -1),
+])
+def test_softmax_leading_minus_inf(lib, rng, shape, dim):
+    """Softmax along a dimension whose first positions are -inf (a left-padding
+    mask): the reference takes the maximum first and gives finite
+    probabilities, so every kernel form must too (the column-wise kernel serves
+    dims that are not a multiple of 4 and softmax over a non-last dimension).
+    One column of only -inf gives NaN in the reference and here."""
+    x = (rng.standard_normal(shape) * np.sqrt(2)).astype(np.float32)
+    d = dim % len(shape)
+    lead = [slice(None)] * len(shape)
+    lead[d] = slice(0, 3)
+    x[tuple(lead)] = -np.inf
+    outer = int(np.prod(shape[:d]))
+    inner = int(np.prod(shape[d + 1:]))
+    dx = _dev(x)
+    dy = _dev(np.zeros_like(x))
+    lib.call("tvr_softmax", _p(dx), _p(dy), outer, shape[d], inner, _stream())
+    y = _host(dy)
+    ref = oracle.softmax(x, dim)
+    assert np.isfinite(ref).all()
+    assert np.isfinite(y).all()
+    assert max_rel(y, ref, 1e-30) <= TOL_POINTWISE
+    # a column of only -inf: NaN, as the reference
+    x2 = x.copy()
+    x2[tuple(slice(0, 1) if i != d else slice(None) for i in range(len(shape)))] = -np.inf
+    dx2 = _dev(x2)
+    lib.call("tvr_softmax", _p(dx2), _p(dy), outer, shape[d], inner, _stream())
+    y2 = _host(dy)
+    ref2 = oracle.softmax(x2, dim)
+    assert np.array_equal(np.isnan(y2), np.isnan(ref2))
+    ok = ~np.isnan(ref2)
+    assert max_rel(y2[ok], ref2[ok], 1e-30) <= TOL_POINTWISE
+
+
 @pytest.mark.parametrize("batch,L,S", [(6, 128, 1024), (2, 64, 64), (3, 5, 2048), (1, 7, 4)])
 def test_softmax_add_causal_mask(lib, rng, batch, L, S):
     """softmax(scores + mask) with an [L, S] mask shared by every batch row:

@@ -61,14 +61,22 @@ def _host(t):
     return t.cpu().numpy()
 
 
+def _pool_stats(lib):
+    reserved, in_use = ctypes.c_size_t(), ctypes.c_size_t()
+    lib.call("tvr_memory_stats", 0, ctypes.byref(reserved), ctypes.byref(in_use))
+    return reserved.value, in_use.value
+
+
 @pytest.mark.parametrize("m,n,k,act,trans_b,with_bias", [
-    (64, 1024, 2048, 0, True, False),     # skinny: split-K partials in the fixed scratch
-    (300, 256, 512, 2, True, True),       # bias + SiLU epilogue after the split-K reduction
-    (1000, 1000, 1000, 1, False, True),   # B given as [K, N]; partials fill 4,000,000 floats
+    (64, 1024, 2048, 0, True, False),     # skinny: 9 split-K partials in the fixed scratch
+    (300, 256, 512, 2, True, True),       # bias + SiLU epilogue after 4 split-K partials
+    (1000, 1000, 1000, 1, False, True),   # B given as [K, N]; 128 tiles fill the SMs, no split
     (2048, 2048, 256, 0, True, False),    # output exactly at the limit, no split needed
     (37, 29, 53, 2, True, True),          # unaligned rows: CUDA-core kernel, no scratch
 ])
 def test_noalloc_matches_gemm_bias_act_twice(lib, m, n, k, act, trans_b, with_bias):
+    import torch
+
     rng = np.random.default_rng(m * 7 + n)
     a = rng.standard_normal((m, k), dtype=np.float32)
     b = rng.uniform(-1 / np.sqrt(k), 1 / np.sqrt(k), (n, k) if trans_b else (k, n)).astype(np.float32)
@@ -81,11 +89,19 @@ def test_noalloc_matches_gemm_bias_act_twice(lib, m, n, k, act, trans_b, with_bi
     lib.call("tvr_gemm_bias_act", _p(da), _p(db), _p(dbias), _p(ref), m, n, k, k, ldb, n, 1.0,
              beta, act, int(trans_b), lib.GEMM_TF32, _stream())
     expected = _host(ref)
+    dev_outs = [_dev(np.full((m, n), np.nan, np.float32)) for _ in range(2)]
     outs = []
-    for _ in range(2):
-        out = _dev(np.full((m, n), np.nan, np.float32))
+    for i, out in enumerate(dev_outs):
+        torch.cuda.synchronize()
+        before = (torch.cuda.mem_get_info()[0], _pool_stats(lib))
         lib.call("tvr_gemm_bias_act_noalloc", _p(da), _p(db), _p(dbias), _p(out), m, n, k, k,
                  ldb, n, 1.0, beta, act, int(trans_b), _stream())
+        torch.cuda.synchronize()
+        after = (torch.cuda.mem_get_info()[0], _pool_stats(lib))
+        if i == 1:
+            # the second call (the first looked the scratch up) takes no device
+            # memory from the driver or from this library's pool
+            assert after == before
         outs.append(_host(out))
     for got in outs:
         assert np.isfinite(got).all()

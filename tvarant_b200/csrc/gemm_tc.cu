@@ -1406,7 +1406,8 @@ int gemm_tcgen05_noalloc(const float* a, const float* b, const float* bias, floa
   if (units > 0x7fffffff) return TVR_ERR_UNSUPPORTED;
   p.total_units = static_cast<int>(units);
   p.status = device_status_ptr_if_ready(dev);  // never sets the device up (no allocation)
-  const int grid = static_cast<int>(std::min<int64_t>(units, sms));
+  // the SM limit of tvr_set_gemm_sm_limit applies here too
+  const int grid = static_cast<int>(std::min<int64_t>(units, grid_sms(dev, sms)));
   switch (bn) {
     case 256: rc = launch_bn<256>(p, false, !trans_b, grid, stream, dev); break;
     case 128: rc = launch_bn<128>(p, false, !trans_b, grid, stream, dev); break;

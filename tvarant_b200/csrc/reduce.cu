@@ -171,7 +171,11 @@ __global__ void __launch_bounds__(1024) softmax_block_kernel(const float* __rest
 // Any (outer, dim, inner) layout: one thread per (outer, inner) column,
 // adjacent threads on adjacent inner indices (coalesced), online max/sum in
 // one pass, then a second pass that writes.  Also the path for rows that do
-// not fit the register kernels.
+// not fit the register kernels.  A -inf element adds nothing to the sum, so it
+// is skipped: while the running maximum is still -inf (a column that starts
+// with masked positions), exp(-inf - -inf) would be NaN.  A column of only
+// -inf still ends with s = 0 and NaN outputs, as the reference's max-first
+// softmax (HostKernels.cpp:174-198) gives.
 __global__ void __launch_bounds__(256) softmax_generic_kernel(const float* __restrict__ x,
                                                               float* __restrict__ y,
                                                               int64_t outer, int64_t dim,
@@ -189,7 +193,7 @@ __global__ void __launch_bounds__(256) softmax_generic_kernel(const float* __res
       if (v > m) {
         s = s * expf(m - v) + 1.f;
         m = v;
-      } else {
+      } else if (v != -INFINITY) {
         s += expf(v - m);
       }
     }
