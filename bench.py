@@ -1,29 +1,32 @@
 #!/usr/bin/env python
 """Benchmark of the tvarant B200 backend (one JSON line on rank 0).
 
-Default workload — the fused-GEMM sweep's largest point: ``nn.Linear(4096,
-4096)`` + SiLU on X [16384, 4096] (TF32 tensor cores), then the chain
-``abs(neg(exp(Y - Z)))`` on the output, compiled by
-``torch_tvarant.compiler.compile`` into one ``tvarant.linear_pointwise``
-(the chain runs in the GEMM's epilogue).  A step is one pass of that graph
-over one batch.
+Default workload, at every number of GPUs — the Llama-7B-shaped gated-SiLU
+MLP stack (32 layers, d_model 4096, d_ff 11008, 8192 tokens, TF32),
+tensor-parallel over the ranks (gate/up column shards, down row shards, one
+all-reduce of the layer output per layer).  A step is one pass of the stack
+over the 8192 tokens.
 
-* ``value``: TFLOP/s of the GEMM (2*M*N*K per step) over the whole step with
-  inputs resident in HBM, summed over ranks (weak scaling: every rank runs
-  its own replica; this path has no exchange step).
-* ``e2e``: the same metric through the same API with host buffers: X and Z
-  copied from pinned host memory and the result copied back every step
-  (consecutive steps' copies overlap on two copy streams).
-* ``roofline``: the step's kernel, timed with events on the stream it runs
-  on, against the TF32 dense peak measured with cuBLAS in this run.
-* ``cpu_baseline``: the reference's own simulator kernels
-  (HostKernels.cpp, built into oracle/_ref) on a row sample, all host cores.
+* ``value``: tokens/s of the whole job (strong scaling: the same 8192 tokens
+  at every N), the step replayed from a CUDA graph, inputs resident.
+* ``e2e``: the same through the same API with the activations copied in from
+  pinned host memory and the result copied back every step.
+* ``roofline``: the stack's dominant kernel, the SwiGLU GEMM at the stack's
+  shard and chunk shape, timed back to back with events on its stream,
+  against the TF32 dense peak measured with cuBLAS in this run (and against
+  half the measured bf16 peak, a fixed figure).
+* ``cpu_baseline``: the reference's own simulator kernels (HostKernels.cpp,
+  built into oracle/_ref) running one MLP layer on a token sample, all host
+  cores, with the single-thread figure beside it.
 
-``--workload sweep`` runs the whole sweep (M in {1, 16, 128, 1024, 4096,
-16384}, TF32 and 3xTF32).  Other workloads (``--workload llm-ops | mlp | bmm |
-gpt2``) report the
-memory-bound LLM ops, the tensor-parallel Llama MLP stack, the LLM op set's
-bmm alone, and the GPT-2-small-shaped forward split over the ranks by batch.
+On one GPU the line also carries, under ``config``, the fused-GEMM sweep's
+largest point (linear+bias+SiLU M=16384 K=N=4096 with the sub/exp/neg/abs
+chain in the GEMM epilogue, TF32 and 3xTF32) and the memory-bound LLM op set
+(softmax, layer norm, embedding, bmm) with each op's fraction of HBM.
+
+``--workload gemm`` gives the fused-GEMM line alone, ``--workload sweep``
+the whole sweep (M in {1, 16, 128, 1024, 4096, 16384}, TF32 and 3xTF32);
+``llm-ops | bmm | gpt2 | gpt2-decode | llama-ops`` the other workloads.
 
 ``--impl reference`` times the reference's CPU implementation of the same
 workload (rank 0 only) and prints the line with ``"impl": "reference"``.
@@ -44,6 +47,7 @@ from pathlib import Path
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
+METRIC = "fused-GEMM TFLOP/s (% peak); LLM-op GB/s (% HBM); tokens/s at 1/2/4/8 GPU"
 M_DEFAULT, K_DEFAULT, N_DEFAULT = 16384, 4096, 4096
 L2_FLUSH_BYTES = 256 << 20  # twice the B200's 126 MB L2
 
@@ -216,9 +220,95 @@ def cpu_baseline_gemm(budget_s: float = 12.0) -> dict:
     if rows2 > rows:
         dt, fl = reference_gemm_chain_rows(rows2, threads)
         rows = rows2
+    dt1, fl1 = reference_gemm_chain_rows(4, 1)
     return {"value": fl / dt / 1e12, "unit": "TFLOP/s", "cores": threads, "kind": "reference",
             "sample": f"{rows} of {M_DEFAULT} rows of the GEMM+SiLU and the sub/exp/neg/abs chain, "
-                      f"reference HostKernels.cpp compiled in oracle/_ref, {threads} threads"}
+                      f"reference HostKernels.cpp compiled in oracle/_ref, {threads} threads",
+            "single_thread": {"value": fl1 / dt1 / 1e12, "unit": "TFLOP/s", "cores": 1,
+                              "sample": "4 rows, 1 thread (the simulator has no parallel loops)"}}
+
+
+D_MODEL, D_FF, MLP_LAYERS, MLP_TOKENS = 4096, 11008, 32, 8192
+_MLP_REF_WEIGHTS = None
+
+
+def _mlp_ref_weights():
+    """One layer's gate, up and down weights ~N(0, 0.02), drawn once."""
+    global _MLP_REF_WEIGHTS
+    if _MLP_REF_WEIGHTS is None:
+        import numpy as np
+
+        rng = np.random.default_rng(0)
+        _MLP_REF_WEIGHTS = tuple(0.02 * rng.standard_normal(shape, dtype=np.float32)
+                                 for shape in ((D_FF, D_MODEL), (D_FF, D_MODEL),
+                                               (D_MODEL, D_FF)))
+    return _MLP_REF_WEIGHTS
+
+
+def reference_mlp_rows(rows: int, threads: int, seed: int = 7) -> float:
+    """Seconds for one gated-SiLU MLP layer of the reference path on ``rows``
+    tokens split over ``threads`` host threads: HostKernels gemm_bias_act with
+    SiLU (gate), gemm_bias_act (up), the eager elementwise product, and
+    gemm_bias_act (down), as the reference runs
+    ``linear(linear_act(x, Wg, None, "silu") * linear(x, Wu), Wd)``."""
+    import ctypes
+    from concurrent.futures import ThreadPoolExecutor
+
+    import numpy as np
+
+    import oracle
+
+    impl = "ref" if oracle.available("ref") else "port"
+    lib = oracle._lib(impl)
+    pre = "ref_" if impl == "ref" else "tvo_"
+    gemm = getattr(lib, pre + "gemm_bias_act")
+    binary = getattr(lib, pre + "binary")
+    wg, wu, wd = _mlp_ref_weights()
+    rng = np.random.default_rng(seed)
+    x = rng.standard_normal((rows, D_MODEL), dtype=np.float32)
+    g = np.empty((rows, D_FF), np.float32)
+    u = np.empty_like(g)
+    h = np.empty_like(g)
+    y = np.empty((rows, D_MODEL), np.float32)
+    chunks = np.array_split(np.arange(rows), max(1, min(threads, rows)))
+    vp = ctypes.c_void_p
+
+    def work(idx):
+        r0, r1 = int(idx[0]), int(idx[-1]) + 1
+        n = r1 - r0
+        p = lambda arr: vp(arr[r0:r1].ctypes.data)  # noqa: E731
+        gemm(p(x), vp(wg.ctypes.data), None, p(g), n, D_FF, D_MODEL, 1.0, 0.0, 2, 1)
+        gemm(p(x), vp(wu.ctypes.data), None, p(u), n, D_FF, D_MODEL, 1.0, 0.0, 0, 1)
+        binary(1, p(g), p(u), p(h), n * D_FF, 1.0)
+        gemm(p(h), vp(wd.ctypes.data), None, p(y), n, D_MODEL, D_FF, 1.0, 0.0, 0, 1)
+
+    t0 = time.perf_counter()
+    with ThreadPoolExecutor(max_workers=len(chunks)) as ex:
+        list(ex.map(work, chunks))
+    return time.perf_counter() - t0
+
+
+def cpu_baseline_mlp(budget_s: float = 12.0) -> dict:
+    """The reference's MLP layer on a token sample sized toward ``budget_s``,
+    all host threads, as tokens/s of the whole 32-layer stack; plus the same
+    on one thread (the simulator's own setting: it has no parallel loops)."""
+    threads = _cpu_cores()
+    rows = max(2 * threads, 16)
+    dt = reference_mlp_rows(rows, threads)
+    rows2 = int(min(MLP_TOKENS, max(rows, rows * budget_s / max(dt, 1e-3) * 0.5)))
+    if rows2 > rows:
+        dt = reference_mlp_rows(rows2, threads)
+        rows = rows2
+    single_rows = 4
+    dt1 = reference_mlp_rows(single_rows, 1)
+    return {"value": rows / (dt * MLP_LAYERS), "unit": "tokens/s", "cores": threads,
+            "kind": "reference",
+            "sample": f"one gated-SiLU MLP layer (4096 -> 11008 -> 4096) on {rows} of "
+                      f"{MLP_TOKENS} tokens, reference HostKernels.cpp compiled in oracle/_ref, "
+                      f"{threads} threads; tokens/s of the {MLP_LAYERS}-layer stack = tokens / "
+                      f"({MLP_LAYERS} x layer time)",
+            "single_thread": {"value": single_rows / (dt1 * MLP_LAYERS), "unit": "tokens/s",
+                              "cores": 1, "sample": f"{single_rows} tokens, one layer, 1 thread"}}
 
 
 # ------------------------------------------------------------------ GPU side
@@ -541,7 +631,7 @@ def run_gemm(args, rank, world, local_rank) -> dict | None:
     peaks = _peaks()
     tf32_peak = tf32_peak_tflops(torch)
     line = {
-        "metric": "fused-GEMM TFLOP/s (% peak); LLM-op GB/s (% HBM); tokens/s at 1/2/4/8 GPU",
+        "metric": METRIC,
         "value": world * wl.flops / (pt["step_ms"] / 1e3) / 1e12,
         "unit": "TFLOP/s",
         "n_gpus": world,
@@ -583,6 +673,51 @@ def run_gemm(args, rank, world, local_rank) -> dict | None:
     return line
 
 
+def fixed_tf32_peak(peaks: dict) -> float:
+    """Half the measured dense bf16 burst peak: the TF32 tensor rate of the
+    same tensor cores, a figure that does not move with the cuBLAS TF32 run of
+    the day."""
+    return peaks.get("bf16_tflops", 1590.0) / 2
+
+
+def single_gpu_extras(torch, args, tf32_peak) -> dict:
+    """The fused-GEMM sweep's largest point in both precision modes and the
+    LLM op set, for the one-GPU default line."""
+    from tvarant_b200 import workloads
+
+    peaks = _peaks()
+    steps = max(5, min(args.steps, 10))
+    out = {}
+    for mode in ("tf32", "3xtf32"):
+        pt = measure_gemm_point(torch, M_DEFAULT, mode, steps, 3, 1)
+        pt.pop("wl")
+        torch.tvarant.empty_cache()
+        rl = _roofline(pt, tf32_peak, peaks)
+        fixed = fixed_tf32_peak(peaks) / (3 if mode == "3xtf32" else 1)
+        out[f"gemm_m{M_DEFAULT}_{mode}"] = {
+            "workload": f"linear+bias+SiLU M={M_DEFAULT} K={K_DEFAULT} N={N_DEFAULT} + "
+                        "abs(neg(exp(Y - Z))) compiled into one launch",
+            "step_ms": pt["step_ms"], "step_tflops": pt["step_tflops"],
+            "plain_gemm_ms": pt["plain_gemm_ms"],
+            "e2e_tflops": pt["flops"] / (pt["e2e_ms"] / 1e3) / 1e12,
+            "kernel": pt["kernel"], "frac": rl["frac"], "peak": rl["peak"],
+            "peak_source": rl["peak_source"],
+            "frac_fixed": pt["kernel_tflops"] / fixed,
+            "peak_fixed": fixed,
+            "peak_fixed_source": "MEASURED_PEAKS.json bf16_tflops / 2 (of measured)"
+                                 + (" / 3" if mode == "3xtf32" else "")}
+    res = workloads.measure_llm_ops(steps, 3)
+    torch.tvarant.empty_cache()
+    out["llm_ops"] = {"per_op": res["per_op"], "GB/s": res["GB/s"], "frac_hbm": res["frac_hbm"],
+                      "peak_gbs": res["peak_gbs"], "inputs": res["inputs"]}
+    res = workloads.measure_mem_kernels(steps, 3)
+    torch.tvarant.empty_cache()
+    out["memory_bound_kernels"] = {k: {"GB/s": v["GB/s"], "frac_hbm": v["frac_hbm"], "ms": v["ms"]}
+                                   for k, v in res["per_kernel"].items()}
+    torch.set_float32_matmul_precision("high" if args.mode == "tf32" else "highest")
+    return out
+
+
 SWEEP_M = (1, 16, 128, 1024, 4096, 16384)
 
 
@@ -614,7 +749,7 @@ def run_sweep(args, rank, world, local_rank) -> dict | None:
                       "e2e_tflops": pt["flops"] / (pt["e2e_ms"] / 1e3) / 1e12})
     head = next(p for p in points if p["M"] == SWEEP_M[-1] and p["mode"] == "tf32")
     return {
-        "metric": "fused-GEMM TFLOP/s (% peak); LLM-op GB/s (% HBM); tokens/s at 1/2/4/8 GPU",
+        "metric": METRIC,
         "value": world * head["step_tflops"], "unit": "TFLOP/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": head["step_ms"],
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
@@ -635,8 +770,59 @@ def run_sweep(args, rank, world, local_rank) -> dict | None:
 
 
 def run_reference(args, rank, world) -> dict | None:
+    """The reference's CPU implementation of the selected workload, rank 0 only."""
     if rank != 0:
         return None
+    if args.workload == "mlp":
+        return run_reference_mlp(args, world)
+    if args.workload in ("gemm", "sweep"):
+        return run_reference_gemm(args, world)
+    return {"impl": "reference",
+            "unavailable": f"no CPU reference arm for --workload {args.workload}; the default "
+                           "(mlp) and gemm workloads have one"}
+
+
+def run_reference_mlp(args, world) -> dict:
+    """The MLP stack on the reference's simulator kernels: each step one layer
+    on a token sample (all host threads), reported as tokens/s of the whole
+    stack."""
+    threads = _cpu_cores()
+    rows = args.ref_rows or 4 * threads
+    for _ in range(args.warmup):
+        reference_mlp_rows(rows, threads)
+    times = [reference_mlp_rows(rows, threads) for _ in range(args.steps)]
+    dt = sum(times) / len(times)
+    value = rows / (dt * args.layers)
+    return {
+        "metric": METRIC,
+        "value": value,
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": dt * 1e3,
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic (N(0,0.02) weights, N(0,1) activations)",
+        "config": {"workload": f"Llama-7B-shaped gated-SiLU MLP stack, {args.layers} layers, "
+                               f"d_model {D_MODEL}, d_ff {D_FF}, {MLP_TOKENS} tokens (the "
+                               "reference's eager linear_act / linear / mul / linear)",
+                   "parallelism": "host threads",
+                   "step": f"one layer on {rows} tokens (the timed sample); value = tokens / "
+                           f"({args.layers} x step time)"},
+        "impl": "reference",
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "reference",
+                         "sample": f"one layer on {rows} of {MLP_TOKENS} tokens per step, "
+                                   f"reference HostKernels.cpp (oracle/_ref), {threads} threads; "
+                                   f"stack time = {args.layers} x layer time"},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+
+
+def run_reference_gemm(args, world) -> dict:
     threads = _cpu_cores()
     rows = args.ref_rows or min(args.m, 64 * threads)
     for _ in range(args.warmup):
@@ -649,7 +835,7 @@ def run_reference(args, rank, world) -> dict | None:
     dt = sum(times) / len(times)
     value = fl / dt / 1e12
     return {
-        "metric": "fused-GEMM TFLOP/s (% peak); LLM-op GB/s (% HBM); tokens/s at 1/2/4/8 GPU",
+        "metric": METRIC,
         "value": value,
         "unit": "TFLOP/s",
         "n_gpus": world,
@@ -688,9 +874,10 @@ def _main() -> int:
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["tvarant", "reference"], default="tvarant")
-    ap.add_argument("--workload", choices=["gemm", "sweep", "llm-ops", "llama-ops", "mlp", "bmm",
-                                           "gpt2", "gpt2-decode"],
-                    default="gemm")
+    ap.add_argument("--workload", choices=["mlp", "gemm", "sweep", "llm-ops", "mem-kernels",
+                                           "llama-ops", "bmm", "gpt2", "gpt2-decode"],
+                    default="mlp",
+                    help="mlp (default, at every N): the tensor-parallel Llama MLP stack")
     ap.add_argument("--batch", type=int, default=256, help="bmm workload: batch size")
     ap.add_argument("--m", type=int, default=M_DEFAULT)
     ap.add_argument("--mode", choices=["tf32", "3xtf32"], default="tf32")
@@ -716,6 +903,8 @@ def _main() -> int:
     ap.add_argument("--nccl-ctas", type=int, default=32,
                     help="mlp workload: CTAs NCCL may use per collective (the GEMMs leave that many SMs free; 0: no limit)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="mlp workload on one GPU: skip the GEMM and LLM-op points in config")
     ap.add_argument("--no-graph", action="store_true",
                     help="mlp / gpt2 workloads: time the eager calls instead of a CUDA graph replay")
     args = ap.parse_args()

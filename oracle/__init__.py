@@ -16,6 +16,7 @@ Only ``tests/``, ``__graft_entry__.smoke()`` and the CPU-baseline leg of
 from __future__ import annotations
 
 import ctypes
+import os
 from pathlib import Path
 
 import numpy as np
@@ -102,17 +103,57 @@ def _p(x):
     return None if x is None else x.ctypes.data
 
 
+def host_threads() -> int:
+    """Host threads available to this process."""
+    try:
+        return max(1, len(os.sched_getaffinity(0)))
+    except Exception:
+        return max(1, os.cpu_count() or 1)
+
+
+def _split(n: int, threads: int):
+    """[begin, end) spans that cover range(n) in up to ``threads`` parts."""
+    parts = max(1, min(threads, n))
+    step = -(-n // parts)
+    return [(i, min(n, i + step)) for i in range(0, n, step)]
+
+
+def _parallel(fn, spans):
+    if len(spans) == 1:
+        fn(*spans[0])
+        return
+    from concurrent.futures import ThreadPoolExecutor
+
+    # ctypes releases the GIL during the foreign call, so the spans run on
+    # separate cores
+    with ThreadPoolExecutor(max_workers=len(spans)) as ex:
+        list(ex.map(lambda sp: fn(*sp), spans))
+
+
 def gemm_bias_act(a, b, bias=None, *, alpha=1.0, beta=1.0, act=0, trans_b=True, c=None,
-                  impl="port") -> np.ndarray:
-    """``act(alpha * a @ op(b) + beta * prev)``; op(b) = b.T when trans_b."""
+                  impl="port", threads: int = 1) -> np.ndarray:
+    """``act(alpha * a @ op(b) + beta * prev)``; op(b) = b.T when trans_b.
+
+    With ``threads`` > 1 the rows are split over host threads, one kernel call
+    per span of rows; every output row is computed exactly as in one call
+    (rows are independent in HostKernels.cpp:100-144)."""
     a = _c(a)
     b = _c(b)
     m, k = a.shape
     n = b.shape[0] if trans_b else b.shape[1]
     bias = None if bias is None else _c(bias)
     out = np.zeros((m, n), np.float32) if c is None else _c(c).copy()
-    _fn(impl, "gemm_bias_act")(_p(a), _p(b), _p(bias), _p(out), m, n, k, alpha, beta, act,
-                               int(bool(trans_b)))
+    fn = _fn(impl, "gemm_bias_act")
+
+    def rows(r0, r1):
+        fn(a[r0:r1].ctypes.data if r1 > r0 else None, _p(b), _p(bias),
+           out[r0:r1].ctypes.data if r1 > r0 else None, r1 - r0, n, k, alpha, beta, act,
+           int(bool(trans_b)))
+
+    if m == 0:
+        fn(_p(a), _p(b), _p(bias), _p(out), m, n, k, alpha, beta, act, int(bool(trans_b)))
+        return out
+    _parallel(rows, _split(m, threads if m >= 2 * threads else 1))
     return out
 
 
@@ -129,23 +170,46 @@ def gemm_rows(a, b, bias, row0, row1, *, alpha=1.0, beta=1.0, act=0, trans_b=Tru
     return out[row0:row1]
 
 
-def bmm(a, b, *, trans_b=False, impl="port") -> np.ndarray:
+def bmm(a, b, *, trans_b=False, impl="port", threads: int = 1) -> np.ndarray:
+    """``a[i] @ op(b[i])`` per batch entry (HostKernels.cpp:146-172); with
+    ``threads`` > 1 the batch is split over host threads."""
     a = _c(a)
     b = _c(b)
     batch, m, k = a.shape
     n = b.shape[1] if trans_b else b.shape[2]
     out = np.zeros((batch, m, n), np.float32)
-    _fn(impl, "bmm")(_p(a), _p(b), _p(out), batch, m, n, k, int(bool(trans_b)))
+    fn = _fn(impl, "bmm")
+
+    def part(b0, b1):
+        fn(a[b0:b1].ctypes.data, b[b0:b1].ctypes.data, out[b0:b1].ctypes.data, b1 - b0, m, n, k,
+           int(bool(trans_b)))
+
+    if batch == 0 or a.size == 0 or b.size == 0:
+        fn(_p(a), _p(b), _p(out), batch, m, n, k, int(bool(trans_b)))
+        return out
+    _parallel(part, _split(batch, threads))
     return out
 
 
-def softmax(x, dim=-1, *, impl="port") -> np.ndarray:
+def softmax(x, dim=-1, *, impl="port", threads: int = 1) -> np.ndarray:
+    """Softmax along ``dim`` (HostKernels.cpp:174-198); with ``threads`` > 1
+    the outer index is split over host threads."""
     x = _c(x)
     dim = dim % x.ndim
     outer = int(np.prod(x.shape[:dim], dtype=np.int64))
     inner = int(np.prod(x.shape[dim + 1:], dtype=np.int64))
     out = np.empty_like(x)
-    _fn(impl, "softmax")(_p(x), _p(out), outer, x.shape[dim], inner)
+    fn = _fn(impl, "softmax")
+    if outer < 2 * threads or x.size == 0:
+        fn(_p(x), _p(out), outer, x.shape[dim], inner)
+        return out
+    xs = x.reshape(outer, -1)
+    os_ = out.reshape(outer, -1)
+
+    def part(o0, o1):
+        fn(xs[o0:o1].ctypes.data, os_[o0:o1].ctypes.data, o1 - o0, x.shape[dim], inner)
+
+    _parallel(part, _split(outer, threads))
     return out
 
 

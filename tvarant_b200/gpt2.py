@@ -131,6 +131,47 @@ def _linear_residual(r, x, w, b):
     return r + torch.nn.functional.linear(x, w, b)
 
 
+def embed(model: GPT2, ids: torch.Tensor) -> torch.Tensor:
+    """Token embedding plus learned positions for ids [B, S]: [B, S, d]."""
+    return torch.nn.functional.embedding(ids, model.wte) + model.wpe[:ids.shape[1]]
+
+
+def block(x: torch.Tensor, L: Layer, cfg: GPT2Config, mask: torch.Tensor | None = None,
+          attention: str = "bmm") -> torch.Tensor:
+    """One pre-LayerNorm decoder layer on [B, S, d] activations: causal
+    self-attention (``attention`` as in ``forward``; ``mask`` the [S, S]
+    additive causal mask the bmm form adds) and the SiLU MLP, each added to the
+    residual stream."""
+    F = torch.nn.functional
+    B, S, d = x.shape
+    H = cfg.n_head
+    hd = d // H
+    scale = 1.0 / math.sqrt(hd)
+    h = F.layer_norm(x, (d,), L.ln1_g, L.ln1_b, 1e-5)
+    qkv = F.linear(h, L.w_qkv, L.b_qkv).view(B, S, 3, H, hd).permute(2, 0, 3, 1, 4)
+    if attention == "sdpa":
+        o = F.scaled_dot_product_attention(qkv[0], qkv[1], qkv[2], is_causal=True, scale=scale)
+        o = o.transpose(1, 2).reshape(B, S, d)
+    else:
+        if mask is None:
+            mask = causal_mask(S, x.device)
+        q = (qkv[0] * scale).reshape(B * H, S, hd)
+        k = qkv[1].reshape(B * H, S, hd)
+        v = qkv[2].reshape(B * H, S, hd)
+        att = _softmax_masked(torch.bmm(q, k.transpose(1, 2)), mask)
+        o = torch.bmm(att, v).view(B, H, S, hd).permute(0, 2, 1, 3).reshape(B, S, d)
+    x = _linear_residual(x, o, L.w_proj, L.b_proj)
+    h = F.layer_norm(x, (d,), L.ln2_g, L.ln2_b, 1e-5)
+    return _linear_residual(x, _linear_silu(h, L.w_fc, L.b_fc), L.w_out, L.b_out)
+
+
+def head(model: GPT2, x: torch.Tensor) -> torch.Tensor:
+    """Final LayerNorm and the LM head tied to the token embedding."""
+    F = torch.nn.functional
+    x = F.layer_norm(x, (model.cfg.d_model,), model.lnf_g, model.lnf_b, 1e-5)
+    return F.linear(x, model.wte)
+
+
 def forward(model: GPT2, ids: torch.Tensor, mask: torch.Tensor | None = None,
             attention: str = "bmm") -> torch.Tensor:
     """Logits [B, S, vocab] for token ids [B, S] (int64, on the model's device).
@@ -139,34 +180,14 @@ def forward(model: GPT2, ids: torch.Tensor, mask: torch.Tensor | None = None,
     mask, softmax, bmm); ``"sdpa"`` calls F.scaled_dot_product_attention with
     ``is_causal=True`` on the heads of the fused QKV projection, which on the
     tvarant device runs the fused attention kernel in TF32 mode."""
-    F = torch.nn.functional
-    cfg = model.cfg
-    B, S = ids.shape
-    d, H = cfg.d_model, cfg.n_head
-    hd = d // H
     if attention not in ("bmm", "sdpa"):
         raise ValueError(f"attention must be 'bmm' or 'sdpa', got {attention!r}")
     if mask is None and attention == "bmm":
-        mask = causal_mask(S, ids.device)
-    scale = 1.0 / math.sqrt(hd)
-    x = F.embedding(ids, model.wte) + model.wpe[:S]
+        mask = causal_mask(ids.shape[1], ids.device)
+    x = embed(model, ids)
     for L in model.layers:
-        h = F.layer_norm(x, (d,), L.ln1_g, L.ln1_b, 1e-5)
-        qkv = F.linear(h, L.w_qkv, L.b_qkv).view(B, S, 3, H, hd).permute(2, 0, 3, 1, 4)
-        if attention == "sdpa":
-            o = F.scaled_dot_product_attention(qkv[0], qkv[1], qkv[2], is_causal=True, scale=scale)
-            o = o.transpose(1, 2).reshape(B, S, d)
-        else:
-            q = (qkv[0] * scale).reshape(B * H, S, hd)
-            k = qkv[1].reshape(B * H, S, hd)
-            v = qkv[2].reshape(B * H, S, hd)
-            att = _softmax_masked(torch.bmm(q, k.transpose(1, 2)), mask)
-            o = torch.bmm(att, v).view(B, H, S, hd).permute(0, 2, 1, 3).reshape(B, S, d)
-        x = _linear_residual(x, o, L.w_proj, L.b_proj)
-        h = F.layer_norm(x, (d,), L.ln2_g, L.ln2_b, 1e-5)
-        x = _linear_residual(x, _linear_silu(h, L.w_fc, L.b_fc), L.w_out, L.b_out)
-    x = F.layer_norm(x, (d,), model.lnf_g, model.lnf_b, 1e-5)
-    return F.linear(x, model.wte)
+        x = block(x, L, model.cfg, mask, attention)
+    return head(model, x)
 
 
 @dataclass

@@ -143,6 +143,22 @@ class TPMLPStack:
         self.gemm_sms = gemm_sms
         self._streams = None
 
+    def sm_limit(self, device: int) -> int:
+        """SMs the stack's GEMMs may use on ``device`` (0: all).  The persistent
+        GEMM otherwise holds every SM and the all-reduce of chunk i would wait
+        for the GEMMs of chunk i+1 instead of overlapping them, so the
+        collective's CTAs keep their SMs while the stack runs."""
+        from tvarant_b200 import _C, capi
+
+        if self.nvls is None and (self.comm is None or self.comm.world == 1):
+            return 0
+        if self.gemm_sms > 0:
+            return self.gemm_sms
+        ctas = self.nvls[0].blocks if self.nvls else self.comm.max_ctas
+        if ctas > 0 and self.chunks > 1 and not (self.fused and _gemm_mode() == capi.GEMM_TF32):
+            return max(1, _C.sm_count(device) - ctas)
+        return 0
+
     def _comm_streams(self, device: int):
         if self._streams is None:
             self._streams = (torch.Stream(device=f"tvarant:{device}"),)
@@ -154,17 +170,12 @@ class TPMLPStack:
                 x = mlp_layer(x, wg, wu, wd)
             return x
         device = x.device.index or 0
-        # The persistent GEMM otherwise holds every SM and the all-reduce of
-        # chunk i would wait for the GEMMs of chunk i+1 instead of overlapping
-        # them: leave the collective's CTAs their SMs while the stack runs.
-        from tvarant_b200 import _C, capi
+        from tvarant_b200 import _C
 
         prev_limit = _C.gemm_sm_limit(device)
-        ctas = self.nvls[0].blocks if self.nvls else self.comm.max_ctas
-        if self.gemm_sms > 0:
-            _C.set_gemm_sm_limit(device, self.gemm_sms)
-        elif ctas > 0 and self.chunks > 1 and not (self.fused and _gemm_mode() == capi.GEMM_TF32):
-            _C.set_gemm_sm_limit(device, max(1, _C.sm_count(device) - ctas))
+        limit = self.sm_limit(device)
+        if limit > 0:
+            _C.set_gemm_sm_limit(device, limit)
         try:
             if self.nvls:
                 return self._forward_nvls(x, device)

@@ -69,6 +69,8 @@ def run(args, rank: int, world: int, local_rank: int):
         return _llama_ops(args, rank, world, local_rank)
     if args.workload == "gpt2-decode":
         return _gpt2_decode(args, rank, world, local_rank)
+    if args.workload == "mem-kernels":
+        return _mem_kernels(args, rank, world, local_rank)
     return _mlp(args, rank, world, local_rank)
 
 
@@ -118,7 +120,7 @@ def _llama_ops(args, rank, world, local_rank):
         v["frac_hbm"] = v["GB/s"] / hbm
     value = total_bytes / (total_ms / 1e3) / 1e9
     return {
-        "metric": "fused-GEMM TFLOP/s (% peak); LLM-op GB/s (% HBM); tokens/s at 1/2/4/8 GPU",
+        "metric": bench.METRIC,
         "value": value * world, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": total_ms, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32",
@@ -161,7 +163,7 @@ def _bmm(args, rank, world, local_rank):
     hbm = bench._peaks().get("hbm_gbs", 6650.0)
     gbs = nbytes / (ms / 1e3) / 1e9
     return {
-        "metric": "fused-GEMM TFLOP/s (% peak); LLM-op GB/s (% HBM); tokens/s at 1/2/4/8 GPU",
+        "metric": bench.METRIC,
         "value": gbs * world, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "tf32" if args.mode == "tf32" else "f32 (3xTF32)",
@@ -178,62 +180,206 @@ def _bmm(args, rank, world, local_rank):
 
 # ----------------------------------------------------------------------------- llm-ops
 
-def _llm_ops(args, rank, world, local_rank):
+def device_randn(shape, seed: int, std: float = 1.0, mean: float = 0.0) -> torch.Tensor:
+    """A tvarant tensor ~N(mean, std^2) drawn on the GPU by torch's CUDA
+    generator (seeded) and copied device to device: multi-GB benchmark inputs
+    without a host draw and a PCIe copy."""
+    import ctypes
+
+    from . import capi
+
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    src = torch.randn(*shape, device="cuda", generator=g)
+    if std != 1.0:
+        src.mul_(std)
+    if mean != 0.0:
+        src.add_(mean)
+    torch.cuda.synchronize()
+    out = torch.empty(*shape, device="tvarant")
+    stream = torch.tvarant.stream_handle(torch.tvarant.current_stream())
+    capi.call("tvr_memcpy_d2d", ctypes.c_void_p(out.data_ptr()), ctypes.c_void_p(src.data_ptr()),
+              src.numel() * 4, ctypes.c_void_p(stream))
+    torch.tvarant.synchronize()
+    del src
+    torch.cuda.empty_cache()
+    return out
+
+
+def measure_llm_ops(steps: int, warmup: int, mode: str = "tf32") -> dict:
+    """The LLM op set, each op timed back to back on its own stream with
+    events: softmax(dim=-1) on [8, 32, 2048, 2048] ~N(0, 2), layer_norm over
+    [16384, 4096] (gamma ~N(1, 0.1), beta ~N(0, 0.1)), embedding of int64 ids
+    [16, 2048] from a [32000, 4096] table ~N(0, 0.02), bmm [256, 2048, 128] x
+    [256, 128, 2048].  Returns per-op ms, algorithmic GB/s and fraction of the
+    measured copy rate, and the time of one pass over all four."""
     import bench
 
     g = torch.Generator().manual_seed(1)
     dev = "tvarant"
-    sm_x = (torch.randn(8, 32, 2048, 2048, generator=g) * 2 ** 0.5).to(dev)
-    ln_x = torch.randn(16384, 4096, generator=g).to(dev)
-    ln = torch.nn.LayerNorm(4096).to(dev)
-    with torch.no_grad():
-        ln.weight.copy_((1 + 0.1 * torch.randn(4096, generator=g)).to(dev))
-        ln.bias.copy_((0.1 * torch.randn(4096, generator=g)).to(dev))
-    table = (0.02 * torch.randn(32000, 4096, generator=g)).to(dev)
+    sm_x = device_randn((8, 32, 2048, 2048), seed=1, std=2 ** 0.5)
+    ln_x = device_randn((16384, 4096), seed=2)
+    ln_w = (1 + 0.1 * torch.randn(4096, generator=g)).to(dev)
+    ln_b = (0.1 * torch.randn(4096, generator=g)).to(dev)
+    table = device_randn((32000, 4096), seed=3, std=0.02)
     ids = torch.randint(0, 32000, (16, 2048), generator=g).to(dev)
-    a = torch.randn(256, 2048, 128, generator=g).to(dev)
-    b = torch.randn(256, 128, 2048, generator=g).to(dev)
-    torch.set_float32_matmul_precision("high" if args.mode == "tf32" else "highest")
+    a = device_randn((256, 2048, 128), seed=4)
+    b = device_randn((256, 128, 2048), seed=5)
+    torch.set_float32_matmul_precision("high" if mode == "tf32" else "highest")
     F = torch.nn.functional
     ops = {
         "softmax": (lambda: F.softmax(sm_x, dim=-1), 2 * sm_x.numel() * 4),
-        "layer_norm": (lambda: ln(ln_x), 2 * ln_x.numel() * 4 + 2 * 4096 * 4 + 2 * 16384 * 4),
+        "layer_norm": (lambda: F.layer_norm(ln_x, (4096,), ln_w, ln_b, 1e-5),
+                       2 * ln_x.numel() * 4 + 2 * 4096 * 4 + 2 * 16384 * 4),
         "embedding": (lambda: F.embedding(ids, table), 2 * 32768 * 4096 * 4 + 32768 * 8),
         "bmm": (lambda: torch.bmm(a, b), 4 * 256 * (2048 * 128 * 2 + 2048 * 2048)),
     }
     for fn, _ in ops.values():
-        for _ in range(args.warmup):
+        for _ in range(warmup):
             fn()
     torch.tvarant.synchronize()
+    hbm = bench._peaks().get("hbm_gbs", 6650.0)
     per = {}
     for name, (fn, nbytes) in ops.items():
-        ms = _time_steps(fn, args.steps)
-        per[name] = {"ms": ms, "GB/s": nbytes / (ms / 1e3) / 1e9}
+        ms = _time_steps(fn, steps)
+        per[name] = {"ms": ms, "GB/s": nbytes / (ms / 1e3) / 1e9,
+                     "frac_hbm": nbytes / (ms / 1e3) / 1e9 / hbm}
+    per["bmm"]["tflops"] = 2 * 256 * 2048 * 2048 * 128 / (per["bmm"]["ms"] / 1e3) / 1e12
+    total_ms = _time_steps(lambda: [fn() for fn, _ in ops.values()], steps)
+    total_bytes = sum(nb for _, nb in ops.values())
+    return {"per_op": per, "total_ms": total_ms, "total_bytes": total_bytes,
+            "GB/s": total_bytes / (total_ms / 1e3) / 1e9,
+            "frac_hbm": total_bytes / (total_ms / 1e3) / 1e9 / hbm,
+            "peak_gbs": hbm, "peak_source": "MEASURED_PEAKS.json hbm_gbs (of measured)",
+            "inputs": "seeded N(mean, std) drawn on the GPU (torch CUDA generator), ids on the host"}
+
+
+# abs(neg(exp(y - z))) as a pointwise SSA program (the fused-GEMM sweep's chain):
+# Load y, Load z, Sub, Exp, Neg, Abs
+_CHAIN_PROGRAM = ([0, 0, 9, 10, 6, 11], [-1, -1, 0, 2, 3, 4], [-1, -1, 1, -1, -1, -1],
+                  [0, 1, -1, -1, -1, -1], [1.0] * 6, [0.0] * 6)
+
+
+def measure_mem_kernels(steps: int, warmup: int) -> dict:
+    """Every memory-bound kernel family on operands of 150-540 MB (above the
+    126 MB L2), each timed back to back with events: softmax rows of 2048 (the
+    LLM op set's row length), softmax with an additive [1024, 1024] mask,
+    layer norm, embedding gather, unary exp, broadcast add, the NVRTC
+    pointwise chain sub/exp/neg/abs, RMSNorm, RoPE (rotate-half) and the
+    strided copy of a GPT-2 head split.  Returns per-kernel ms, algorithmic
+    bytes, GB/s and fraction of the measured copy rate."""
+    import bench
+
+    g = torch.Generator().manual_seed(3)
+    dev = "tvarant"
+    F = torch.nn.functional
+    big = (16384, 4096)
+    x = device_randn(big, seed=11)
+    z = device_randn(big, seed=12)
+    sm = device_randn((32768, 2048), seed=13, std=2 ** 0.5)
+    scores = device_randn((64, 1024, 1024), seed=14)
+    mask = torch.full((1024, 1024), float("-inf")).triu(1).to(dev)
+    gamma = (1 + 0.1 * torch.randn(4096, generator=g)).to(dev)
+    beta = (0.1 * torch.randn(4096, generator=g)).to(dev)
+    table = device_randn((32000, 4096), seed=15, std=0.02)
+    ids = torch.randint(0, 32000, (16, 1024), generator=g).to(dev)
+    q = device_randn((1, 32, 16384, 128), seed=16)
+    inv = 1.0 / (10000 ** (torch.arange(0, 128, 2, dtype=torch.float32) / 128))
+    ang = torch.arange(16384, dtype=torch.float32)[:, None] * inv[None, :]
+    cos = torch.cat([ang.cos(), ang.cos()], -1).to(dev)
+    sin = torch.cat([ang.sin(), ang.sin()], -1).to(dev)
+    qkv = device_randn((16, 1024, 3, 12, 64), seed=17)
+    n = x.numel() * 4
+    cases = {
+        "softmax_warp_kernel [32768, 2048]": (lambda: F.softmax(sm, dim=-1), 2 * sm.numel() * 4),
+        "softmax_warp_kernel<MASK> [64, 1024, 1024] + [1024, 1024] mask": (
+            lambda: torch.ops.tvarant.softmax_add(scores, mask), 2 * scores.numel() * 4),
+        "layer_norm_kernel [16384, 4096]": (
+            lambda: F.layer_norm(x, (4096,), gamma, beta, 1e-5), 2 * n + 2 * 4096 * 4 + 2 * 16384 * 4),
+        "embedding_kernel [16, 1024] ids from [32000, 4096]": (
+            lambda: F.embedding(ids, table), 2 * ids.numel() * 4096 * 4 + ids.numel() * 8),
+        "unary exp [16384, 4096]": (lambda: torch.exp(x), 2 * n),
+        "binary add [16384, 4096] + [4096]": (lambda: x + beta, 2 * n + 4096 * 4),
+        "tvr_pointwise_kernel abs(neg(exp(x - z))) [16384, 4096]": (
+            lambda: torch.ops.tvarant.pointwise([x, z], *_CHAIN_PROGRAM), 3 * n),
+        "rms_norm_kernel [16384, 4096]": (lambda: F.rms_norm(x, (4096,), gamma, 1e-6), 2 * n + 4096 * 4),
+        "rope_half_vec_kernel q [1, 32, 16384, 128]": (
+            lambda: torch.ops.tvarant.rope(q, cos, sin), 2 * q.numel() * 4 + 2 * 16384 * 64 * 4),
+        "strided_copy_kernel qkv [16, 1024, 3, 12, 64] -> [3, 16, 12, 1024, 64]": (
+            lambda: qkv.permute(2, 0, 3, 1, 4).contiguous(), 2 * qkv.numel() * 4),
+    }
+    for fn, _ in cases.values():
+        for _ in range(warmup):
+            fn()
+    torch.tvarant.synchronize()
+    hbm = bench._peaks().get("hbm_gbs", 6650.0)
+    per = {}
+    for name, (fn, nbytes) in cases.items():
+        ms = _time_steps(fn, steps)
+        per[name] = {"ms": ms, "bytes": nbytes, "GB/s": nbytes / (ms / 1e3) / 1e9,
+                     "frac_hbm": nbytes / (ms / 1e3) / 1e9 / hbm}
+    return {"per_kernel": per, "peak_gbs": hbm,
+            "peak_source": "MEASURED_PEAKS.json hbm_gbs (of measured)"}
+
+
+def _mem_kernels(args, rank, world, local_rank):
+    import bench
+
     with bench.ClockSampler(local_rank) as clocks:
         h0 = time.perf_counter()
-        total_ms = _time_steps(lambda: [fn() for fn, _ in ops.values()], args.steps)
+        res = measure_mem_kernels(args.steps, args.warmup)
         clocks.mark(h0, time.perf_counter())
-    total_bytes = sum(nb for _, nb in ops.values())
+    per = res["per_kernel"]
+    total_ms = bench._max_over_ranks(sum(v["ms"] for v in per.values()), world)
     if rank != 0:
         return None
-    hbm = bench._peaks().get("hbm_gbs", 6650.0)
-    for v in per.values():
-        v["frac_hbm"] = v["GB/s"] / hbm
-    bmm_tflops = 2 * 256 * 2048 * 2048 * 128 / (per["bmm"]["ms"] / 1e3) / 1e12
+    total_bytes = sum(v["bytes"] for v in per.values())
     value = total_bytes / (total_ms / 1e3) / 1e9
+    hbm = res["peak_gbs"]
+    worst = min(per, key=lambda k: per[k]["frac_hbm"])
     return {
-        "metric": "fused-GEMM TFLOP/s (% peak); LLM-op GB/s (% HBM); tokens/s at 1/2/4/8 GPU",
+        "metric": bench.METRIC,
+        "value": value * world, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": total_ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded N(0,1)-family inputs drawn on the GPU)",
+        "config": {"workload": "every memory-bound kernel family once per step, operands "
+                               "150-540 MB", "per_kernel": per,
+                   "parallelism": f"replicas x{world}",
+                   "l2": "every operand exceeds the 126 MB L2"},
+        "roofline": {"bound": "hbm", "achieved": value, "peak": hbm, "unit": "GB/s",
+                     "frac": value / hbm, "traffic": None, "peak_source": res["peak_source"],
+                     "lowest": {"kernel": worst, "frac_hbm": per[worst]["frac_hbm"]}},
+        "gpu_launches": args.steps * len(per),
+        "clocks": clocks.summary(),
+        "device_status": torch.tvarant.get_status(),
+    }
+
+
+def _llm_ops(args, rank, world, local_rank):
+    import bench
+
+    with bench.ClockSampler(local_rank) as clocks:
+        h0 = time.perf_counter()
+        res = measure_llm_ops(args.steps, args.warmup, args.mode)
+        clocks.mark(h0, time.perf_counter())
+    total_ms = bench._max_over_ranks(res["total_ms"], world)
+    if rank != 0:
+        return None
+    hbm = res["peak_gbs"]
+    value = res["total_bytes"] / (total_ms / 1e3) / 1e9
+    return {
+        "metric": bench.METRIC,
         "value": value * world, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": total_ms, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded, shapes and distributions of the LLM op set)",
         "config": {"workload": "softmax [8,32,2048,2048] + layer_norm [16384,4096] + embedding "
                                "[16,2048] from [32000,4096] + bmm [256,2048,128]x[256,128,2048]",
-                   "per_op": per, "bmm_tflops": bmm_tflops, "parallelism": f"replicas x{world}",
+                   "per_op": res["per_op"], "parallelism": f"replicas x{world}",
                    "l2": "every operand exceeds the 126 MB L2 except the LN row vectors"},
         "roofline": {"bound": "hbm", "achieved": value, "peak": hbm, "unit": "GB/s",
                      "frac": value / hbm, "traffic": None,
-                     "peak_source": "MEASURED_PEAKS.json hbm_gbs"},
+                     "peak_source": res["peak_source"]},
         "clocks": clocks.summary(),
         "device_status": torch.tvarant.get_status(),
     }
@@ -308,9 +454,24 @@ def _mlp(args, rank, world, local_rank):
     ms = bench._max_over_ranks(ms, world)
     # the per-layer GEMMs alone (one rank's share of the FLOPs)
     wg, wu, wd = layers[0]
+    from tvarant_b200 import _C
     from tvarant_b200.tp import mlp_layer
 
     layer_ms = _time_steps(lambda: mlp_layer(x, wg, wu, wd), args.steps)
+    # the dominant kernel, the SwiGLU GEMM, at the stack's chunk shape and
+    # under the stack's SM limit, timed back to back on its stream
+    rows = -(-TOKENS // stack.chunks)
+    xc = x[:rows]
+    prev_limit = _C.gemm_sm_limit(local_rank)
+    sm_limit = stack.sm_limit(local_rank)
+    _C.set_gemm_sm_limit(local_rank, sm_limit)
+    try:
+        for _ in range(3):
+            torch.ops.tvarant.linear_swiglu(xc, wg, wu)
+        swiglu_ms = _time_steps(lambda: torch.ops.tvarant.linear_swiglu(xc, wg, wu), args.steps)
+    finally:
+        _C.set_gemm_sm_limit(local_rank, prev_limit)
+    swiglu_flops = 2.0 * rows * (2 * wg.shape[0]) * D_MODEL
 
     def e2e_step():
         x.copy_(x_host, non_blocking=True)
@@ -331,16 +492,22 @@ def _mlp(args, rank, world, local_rank):
         for buf in nvls:
             buf.close()
         bench._barrier(world)
+    swiglu_ms = bench._max_over_ranks(swiglu_ms, world)
     if rank != 0:
         return None
     flops_total = 3 * 2 * TOKENS * D_MODEL * D_FF * args.layers
     per_rank_flops = flops_total / world
     peak = bench.tf32_peak_tflops(torch) or 750.0
+    peaks = bench._peaks()
+    fixed = bench.fixed_tf32_peak(peaks)
     achieved = per_rank_flops / (ms / 1e3) / 1e12
     nvlink_bytes = (2 * (world - 1) / world) * TOKENS * D_MODEL * 4 * args.layers if world > 1 else 0
     target_s = max(per_rank_flops / (peak * 1e12), nvlink_bytes / 770e9)
-    return {
-        "metric": "fused-GEMM TFLOP/s (% peak); LLM-op GB/s (% HBM); tokens/s at 1/2/4/8 GPU",
+    swiglu_tflops = swiglu_flops / (swiglu_ms / 1e3) / 1e12
+    tf32 = args.mode == "tf32"
+    kpeak = peak if tf32 else peak / 3
+    line = {
+        "metric": bench.METRIC,
         "value": TOKENS / (ms / 1e3), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "tf32" if args.mode == "tf32" else "f32 (3xTF32)",
@@ -363,17 +530,38 @@ def _mlp(args, rank, world, local_rank):
         "e2e": {"value": TOKENS / (e2e_ms / 1e3), "unit": "tokens/s",
                 "h2d_bytes_per_step": TOKENS * D_MODEL * 4,
                 "d2h_bytes_per_step": TOKENS * D_MODEL * 4, "ms_per_step": e2e_ms},
-        "roofline": {"bound": "tensor" if world == 1 else "tensor+nvlink",
-                     "achieved": achieved, "peak": peak, "unit": "TFLOP/s per GPU",
-                     "frac": (target_s * 1e3) / ms,
-                     "traffic": None,
-                     "peak_source": "cuBLAS TF32 8192^3 measured in this run; NVLink 770 GB/s"},
+        "roofline": {"bound": "tensor",
+                     "achieved": swiglu_tflops, "peak": kpeak, "unit": "TFLOP/s",
+                     "frac": swiglu_tflops / kpeak,
+                     "traffic": (bench._traffic("gemm_swiglu_m8192_n11008")
+                                 if world == 1 and rows == TOKENS and tf32 else None),
+                     "kernel": ("tvr::tc::gemm_tc_kernel<256, tf32, K-major B, GATED> (SwiGLU: "
+                                f"[{rows}, {D_MODEL}] x [2 x {wg.shape[0]}, {D_MODEL}])"
+                                if tf32 else "3xTF32 SwiGLU composition"),
+                     "kernel_ms": swiglu_ms,
+                     "algorithmic_flops": swiglu_flops,
+                     "peak_source": "cuBLAS TF32 8192^3 measured in this run"
+                                    + ("" if tf32 else " / 3"),
+                     "frac_fixed": swiglu_tflops / (fixed if tf32 else fixed / 3),
+                     "peak_fixed": fixed if tf32 else fixed / 3,
+                     "peak_fixed_source": "MEASURED_PEAKS.json bf16_tflops / 2 (of measured)",
+                     "gemm_sm_limit": sm_limit,
+                     "step": {"achieved_tflops_per_gpu": achieved,
+                              "frac": (target_s * 1e3) / ms,
+                              "target": "max(FLOPs per GPU / measured TF32 peak, all-reduce "
+                                        "bytes per GPU / 770 GB/s NVLink)"}},
         # per layer and chunk: the SwiGLU GEMM and the down GEMM, plus the
         # epoch step and the all-reduce kernel with NVLS (NCCL's are not ours)
         "gpu_launches": args.steps * args.layers * stack.chunks * (3 if fused else 4 if use_nvls else 2),
         "clocks": clocks.summary(),
         "device_status": status,
     }
+    if world == 1:
+        if not args.no_extras:
+            line["config"]["one_gpu_points"] = bench.single_gpu_extras(torch, args, peak)
+        if not args.no_cpu_baseline:
+            line["cpu_baseline"] = bench.cpu_baseline_mlp()
+    return line
 
 
 # ----------------------------------------------------------------------------- gpt2
@@ -479,7 +667,7 @@ def _gpt2_decode(args, rank, world, local_rank):
     step_bytes = weight_bytes + kv_bytes
     peak_gbs = bench._peaks().get("hbm_gbs", 6650.0)
     return {
-        "metric": "fused-GEMM TFLOP/s (% peak); LLM-op GB/s (% HBM); tokens/s at 1/2/4/8 GPU",
+        "metric": bench.METRIC,
         "value": world * batch / (ms / 1e3), "unit": "tokens/s (decode)", "n_gpus": world,
         "steps": steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None,
@@ -575,7 +763,7 @@ def _gpt2(args, rank, world, local_rank):
     peak = bench.tf32_peak_tflops(torch) or 750.0
     achieved = flops_rank / (ms / 1e3) / 1e12
     line = {
-        "metric": "fused-GEMM TFLOP/s (% peak); LLM-op GB/s (% HBM); tokens/s at 1/2/4/8 GPU",
+        "metric": bench.METRIC,
         "value": tokens / (ms / 1e3), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "tf32" if args.mode == "tf32" else "f32 (3xTF32)",
