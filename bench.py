@@ -793,6 +793,8 @@ def run_reference_mlp(args, world) -> dict:
     times = [reference_mlp_rows(rows, threads) for _ in range(args.steps)]
     dt = sum(times) / len(times)
     value = rows / (dt * args.layers)
+    # the simulator itself has no parallel loops: the same layer on one thread
+    dt1 = reference_mlp_rows(4, 1)
     return {
         "metric": METRIC,
         "value": value,
@@ -811,7 +813,8 @@ def run_reference_mlp(args, world) -> dict:
                                "reference's eager linear_act / linear / mul / linear)",
                    "parallelism": "host threads",
                    "step": f"one layer on {rows} tokens (the timed sample); value = tokens / "
-                           f"({args.layers} x step time)"},
+                           f"({args.layers} x step time)",
+                   "single_thread_tokens_per_s": 4 / (dt1 * args.layers)},
         "impl": "reference",
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "reference",
                          "sample": f"one layer on {rows} of {MLP_TOKENS} tokens per step, "

@@ -94,3 +94,58 @@ def test_nvls_units_are_reduced_once_by_their_owner(world, nred, units):
             taken.append(u)
             i += nred
     assert sorted(taken) == list(range(units))
+
+
+# ---- persistent GEMM tile raster (csrc/gemm_tc.cu decode_unit / pick_raster) ----
+
+RASTER_L2_BYTES = 48 << 20
+
+
+def pick_raster(tiles_m, tiles_n, panel_a, panel_b, budget=RASTER_L2_BYTES):
+    gm = max(1, min(tiles_m, budget // max(1, panel_a)))
+    gn = max(1, min(tiles_n, budget // max(1, panel_b)))
+    bytes_m = tiles_m * panel_a + tiles_n * panel_b * -(-tiles_m // gm)
+    bytes_n = tiles_n * panel_b + tiles_m * panel_a * -(-tiles_n // gn)
+    return (1, gn) if bytes_n < bytes_m else (0, gm)
+
+
+def decode_unit(u, tiles_m, tiles_n, splits, raster_n, group):
+    per = tiles_m * tiles_n
+    outer, r = divmod(u, per)
+    b, s = divmod(outer, splits)
+    if raster_n == 0:
+        span = group * tiles_n
+        g, rr = divmod(r, span)
+        first = g * group
+        gm = min(tiles_m - first, group)
+        return b, s, first + rr % gm, rr // gm
+    span = group * tiles_m
+    g, rr = divmod(r, span)
+    first = g * group
+    gn = min(tiles_n - first, group)
+    return b, s, rr // gn, first + rr % gn
+
+
+@pytest.mark.parametrize("tiles_m,tiles_n", [(1, 1), (1, 7), (9, 1), (128, 16), (64, 86),
+                                             (33, 17), (5, 40), (32, 11)])
+@pytest.mark.parametrize("raster_n,group", [(0, 1), (0, 8), (0, 24), (0, 200), (1, 1), (1, 5),
+                                            (1, 12), (1, 300)])
+@pytest.mark.parametrize("batch,splits", [(1, 1), (3, 1), (1, 4)])
+def test_raster_visits_every_tile_once(tiles_m, tiles_n, raster_n, group, batch, splits):
+    group = min(group, tiles_n if raster_n else tiles_m)
+    total = batch * splits * tiles_m * tiles_n
+    seen = [decode_unit(u, tiles_m, tiles_n, splits, raster_n, group) for u in range(total)]
+    assert len(set(seen)) == total
+    for b, s, tm, tn in seen:
+        assert 0 <= b < batch and 0 <= s < splits and 0 <= tm < tiles_m and 0 <= tn < tiles_n
+
+
+def test_raster_choice_for_the_benchmark_shapes():
+    """M=16384 x N=4096 (K=4096, 256-wide tiles): hold 12 B panels (48 MB) and
+    stream A twice instead of B sixteen times; the SwiGLU GEMM M=8192 x
+    2 x 11008: hold 24 A panels and stream the 361 MB of weights 3 times."""
+    k4 = 4096 * 4
+    assert pick_raster(128, 16, 128 * k4, 256 * k4) == (1, 12)
+    assert pick_raster(64, 86, 128 * k4, 256 * k4) == (0, 24)
+    # everything fits: one group, A held (M fastest), each operand read once
+    assert pick_raster(8, 16, 128 * k4, 256 * k4) == (0, 8)

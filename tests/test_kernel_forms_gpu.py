@@ -4,16 +4,10 @@ tests that exercise it.
 The library reads each switch once, at its first use, so every form runs in
 a child pytest process with its variable set:
 
-* ``TVARANT_ATTENTION_P_TMEM``: the fused attention kernel with P and O in
-  tensor memory (two CTAs per SM);
-* ``TVARANT_PDL``: the few-row GEMM launched as a programmatic dependent of
-  the kernel before it, streaming its weights before that kernel ends;
-* ``TVARANT_GEMM_WAVE_FIT``: the large GEMMs' tile width chosen by whole
-  waves over the SMs;
 * ``TVARANT_WS_PROGRAM``: a pointwise program after a few-row GEMM applied
   in that kernel's epilogue instead of as a pass over its output.
 
-None of them is the default, so this file runs only when
+It is not the default, so this file runs only when
 ``TVARANT_TEST_KERNEL_FORMS=1`` is set.
 """
 
@@ -30,10 +24,6 @@ ROOT = Path(__file__).resolve().parents[1]
 
 # each form: the device tests whose kernels it changes
 FORMS = {
-    "TVARANT_ATTENTION_P_TMEM": ["tests/test_attention_gpu.py", "tests/test_gpt2.py"],
-    "TVARANT_PDL": ["tests/test_capi_gpu.py", "tests/test_gpt2.py", "tests/test_llama_ops_gpu.py"],
-    "TVARANT_GEMM_WAVE_FIT": ["tests/test_capi_gpu.py", "tests/test_api_gpu.py",
-                              "tests/test_gemm_pointwise_gpu.py", "tests/test_gpt2.py"],
     "TVARANT_WS_PROGRAM": ["tests/test_gemm_pointwise_gpu.py", "tests/test_api_gpu.py",
                            "tests/test_gpt2.py"],
 }

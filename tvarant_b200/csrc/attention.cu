@@ -5,25 +5,27 @@
 // the fused kernel is a roadmap item — so this kernel serves
 // F.scaled_dot_product_attention on the tvarant device (TF32 mode).
 //
-// One CTA per (128-query tile, batch x head).  Head dimension 64.
+// One CTA per (128-query tile, batch x head), two CTAs per SM.  Head
+// dimension 64.
 //   warp 0     TMA producers: lane 0 loads the Q tile once and the K tile of
 //              each block of 64 keys, lane 1 the V tiles (two buffers each),
 //              straight from strided [B, H, S, 64] views (no head-split
 //              copies);
 //   warp 1     TMEM owner; lane 0 issues S_j = Q K_j^T (M=128, N=64, K=64)
 //              into one of two TMEM score buffers, ahead of the softmax;
-//              lane 1 issues PV_j = P_j V_j (M=128, N=64, K=64) into one of
-//              two TMEM buffers, V read as an N-major operand;
+//              lane 1 issues PV_j = P_j V_j (M=128, N=64, K=64) with P_j read
+//              from tensor memory and V as an N-major operand, accumulating O
+//              in tensor memory over all blocks;
 //   warps 2-5  one thread per query row: online softmax in the log2 domain
 //              over the row's 64 scores of a block (two TMEM loads in flight,
-//              one wait), P_j written to one of two shared-memory tiles in the
-//              128-byte-swizzled K-major layout the MMA reads, and the output
-//              row kept in 64 registers.  The output update trails the
-//              softmax by one block — O = O * exp2(m_{j-2} - m_{j-1}) +
-//              PV_{j-1} runs after the softmax of block j — so the tensor core
-//              computes PV_{j-1} and S_{j+1} while the softmax of block j runs.
-//              At the end O / l is stored and the log-sum-exp (natural log) is
-//              written.
+//              one wait), P_j written back over S_j in tensor memory.  The
+//              running maximum is raised lazily (only when a block's maximum
+//              exceeds it by more than 2^8), and only then are the warp's rows
+//              of O rescaled in tensor memory; O / l does not depend on which
+//              maximum was used.  At the end O / l is stored and the
+//              log-sum-exp (natural log) is written.
+// Without P tiles in shared memory a CTA needs 97 KB, so two CTAs share an SM
+// and each SM scheduler holds two softmax warps.
 // Causal masking follows PyTorch's is_causal (key index <= query index,
 // aligned at the top-left); keys at or beyond seq_k are masked.  Every
 // mbarrier wait is bounded (status word + abort flag), as in gemm_tc.  No TMA
@@ -51,21 +53,14 @@ constexpr int Q_BYTES = BM * D * 4;      // D/32 atoms
 constexpr int K_BYTES = BN * D * 4;      // D/32 atoms
 constexpr int V_ATOM = BN * 128;         // one 32-wide slice of the head dimension: [64 keys x 128 B]
 constexpr int V_BYTES = BN * D * 4;      // D/32 atoms
-constexpr int P_BYTES = BM * BN * 4;     // BN/32 atoms of [128 x 128 B]
-constexpr int STAGES = 2;                // K, V, P and both TMEM accumulators are double-buffered
+constexpr int STAGES = 2;                // K, V and the TMEM score buffers are double-buffered
 constexpr int THREADS = 192;
-constexpr uint32_t TMEM_COLS = 256;      // S buffers at 0 and 64, PV buffers at 128 and 192
+constexpr uint32_t TMEM_COLS = 256;      // S / P buffers at 0 and 64, O at 128
 constexpr uint32_t PV_COL = 2 * BN;
-constexpr float kLazyLog2 = 8.f;         // P_TMEM: raise the running maximum past 2^8 growth
+constexpr float kLazyLog2 = 8.f;         // raise the running maximum past 2^8 growth
 constexpr int BAR_BYTES = 8 * 24;
-// P_j in shared memory (the A operand of PV_j read through a descriptor), or
-// written back over S_j in tensor memory and read from there (P_TMEM): the
-// second form needs no P tiles, so two CTAs fit on one SM.
-constexpr int smem_bytes(bool p_tmem) {
-  return 1024 + Q_BYTES + STAGES * (K_BYTES + V_BYTES + (p_tmem ? 0 : P_BYTES)) + BAR_BYTES;
-}
-static_assert(smem_bytes(false) <= 232448, "shared memory budget");
-static_assert(2 * (smem_bytes(true) + 1024 + 64) <= 233472, "two CTAs per SM with P in TMEM");
+constexpr int SMEM_BYTES = 1024 + Q_BYTES + STAGES * (K_BYTES + V_BYTES) + BAR_BYTES;
+static_assert(2 * (SMEM_BYTES + 1024 + 64) <= 233472, "two CTAs per SM");
 
 struct Params {
   CUtensorMap tma_q;  // {D, seq_q, heads, batch}, box {32, 128}
@@ -80,7 +75,6 @@ struct Params {
   int* status;
   const int64_t* key_len;    // non-null: attend to clamp(*key_len + key_len_add, 1, seq_k) keys
   int key_len_add;
-  int pdl_trigger;           // let a programmatic dependent launch once this CTA is set up
 };
 
 // N-major V operand: 32-wide atoms of the head dimension, each [64 keys x
@@ -121,15 +115,7 @@ __device__ __forceinline__ void store_row(const Params& p, int b, int h, int qid
   }
 }
 
-__device__ __forceinline__ void st_shared4(uint32_t addr, float a, float b, float c, float d) {
-  asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(a), "f"(b), "f"(c),
-               "f"(d)
-               : "memory");
-}
-
-template <bool P_TMEM>
-__global__ void __launch_bounds__(THREADS, P_TMEM ? 2 : 1)
-    attn_fwd_kernel(const __grid_constant__ Params p) {
+__global__ void __launch_bounds__(THREADS, 2) attn_fwd_kernel(const __grid_constant__ Params p) {
   extern __shared__ uint8_t smem_raw[];
   __shared__ int s_abort;
   __shared__ uint64_t s_drain;
@@ -139,9 +125,8 @@ __global__ void __launch_bounds__(THREADS, P_TMEM ? 2 : 1)
   const uint32_t sq = base;
   const uint32_t sk = sq + Q_BYTES;                 // [2] K tiles
   const uint32_t sv = sk + STAGES * K_BYTES;        // [2] V tiles
-  const uint32_t sp = sv + STAGES * V_BYTES;        // [2] P tiles (unless P_TMEM)
   // mbarriers, one 8-byte slot each; [2] = one per buffer
-  const uint32_t bar = sp + (P_TMEM ? 0 : STAGES * P_BYTES);
+  const uint32_t bar = sv + STAGES * V_BYTES;
   const uint32_t q_full = bar;
   const uint32_t k_full = bar + 8;       // [2]
   const uint32_t k_empty = bar + 24;     // [2]
@@ -151,7 +136,6 @@ __global__ void __launch_bounds__(THREADS, P_TMEM ? 2 : 1)
   const uint32_t s_empty = bar + 88;     // [2]
   const uint32_t p_full = bar + 104;     // [2]
   const uint32_t pv_full = bar + 120;    // [2]
-  const uint32_t pv_empty = bar + 136;   // [2]
   const uint32_t drain = smem_u32(&s_drain);
 
   const int warp = threadIdx.x >> 5;
@@ -179,12 +163,10 @@ __global__ void __launch_bounds__(THREADS, P_TMEM ? 2 : 1)
       mbar_init(v_full + 8 * i, 1);
       mbar_init(v_empty + 8 * i, 1);
       mbar_init(s_full + 8 * i, 1);
-      // S buffer free: the softmax warps read it (P in shared memory) or PV
-      // read the P written over it (P_TMEM, one commit)
-      mbar_init(s_empty + 8 * i, P_TMEM ? 1 : 4);
+      // S buffer free: PV read the P written over it (one commit)
+      mbar_init(s_empty + 8 * i, 1);
       mbar_init(p_full + 8 * i, 4);
       mbar_init(pv_full + 8 * i, 1);
-      mbar_init(pv_empty + 8 * i, 4);
     }
     mbar_init(drain, 2);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -202,7 +184,7 @@ __global__ void __launch_bounds__(THREADS, P_TMEM ? 2 : 1)
   const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(&s_tmem);
   // a few-row GEMM launched as a programmatic dependent (the projection after
   // a decode step's attention) may start streaming its weights now
-  if (p.pdl_trigger && threadIdx.x == 0) grid_launch_dependents();
+  if (threadIdx.x == 0) grid_launch_dependents();
 
   if (warp == 0) {
     // ------------------------------ TMA producers ------------------------------
@@ -251,10 +233,10 @@ __global__ void __launch_bounds__(THREADS, P_TMEM ? 2 : 1)
     // ------------------------------ MMA issuers ------------------------------
     // Two threads issue independently, so that neither stream of MMAs waits
     // behind the other's operands: lane 0 the scores S_i = Q K_i^T into score
-    // buffer i & 1 (free once the softmax of i-2 read it), lane 1 the products
-    // PV_j = P_j V_j into PV buffer j & 1 (free once the output update of j-2
-    // read it).  Each commits its own barriers and, at the end, the drain
-    // barrier (count 2) that TMEM release waits for.
+    // buffer i & 1 (free once PV_{i-2} has read the P written over S_{i-2}),
+    // lane 1 the products PV_j = P_j V_j, accumulated into O.  Each commits
+    // its own barriers and, at the end, the drain barrier (count 2) that TMEM
+    // release waits for.
     if (lane < 2) {
       constexpr uint32_t idesc_s = idesc_tf32(BM, BN, false);
       constexpr uint32_t idesc_pv = idesc_tf32(BM, D, true);
@@ -284,34 +266,20 @@ __global__ void __launch_bounds__(THREADS, P_TMEM ? 2 : 1)
         for (int j = 0; ok && j < nkb; ++j) {
           const int pb = j & 1;
           if (!mbar_wait(p_full + 8 * pb, (j >> 1) & 1, abort_flag) ||
-              !mbar_wait(v_full + 8 * pb, (j >> 1) & 1, abort_flag) ||
-              (!P_TMEM && j >= 2 &&
-               !mbar_wait(pv_empty + 8 * pb, ((j >> 1) - 1) & 1, abort_flag))) {
+              !mbar_wait(v_full + 8 * pb, (j >> 1) & 1, abort_flag)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          if constexpr (P_TMEM) {
-            // P_j sits in score buffer j & 1 (K step x: its columns 8x .. 8x+7);
-            // O accumulates in place over all blocks
-            const uint32_t pa = tmem + static_cast<uint32_t>(pb * BN);
+          // P_j sits in score buffer j & 1 (K step x: its columns 8x .. 8x+7);
+          // O accumulates in place over all blocks
+          const uint32_t pa = tmem + static_cast<uint32_t>(pb * BN);
 #pragma unroll
-            for (int x = 0; x < BN / 8; ++x) {
-              mma_tf32_tmem_a(tmem + PV_COL, pa + 8u * x, desc_v(sv + pb * V_BYTES + x * 1024),
-                              idesc_pv, (j > 0 || x > 0) ? 1u : 0u);
-            }
-            mma_commit(s_empty + 8 * pb);  // P_j read: the buffer may take S_{j+2}
-          } else {
-            const uint32_t d = tmem + PV_COL + static_cast<uint32_t>(pb * D);
-            const uint32_t pt = sp + pb * P_BYTES;
-#pragma unroll
-            for (int x = 0; x < BN / 8; ++x) {
-              // K step x covers keys 8x .. 8x+7: P atom x / 4 (32 keys), +32 B
-              // per step inside it; V rows 8x.., 8 rows of 128 B = 1024 B per step
-              mma_tf32(d, desc_kmajor(pt + (x >> 2) * Q_ATOM + (x & 3) * 32),
-                       desc_v(sv + pb * V_BYTES + x * 1024), idesc_pv, x > 0 ? 1u : 0u);
-            }
+          for (int x = 0; x < BN / 8; ++x) {
+            mma_tf32_tmem_a(tmem + PV_COL, pa + 8u * x, desc_v(sv + pb * V_BYTES + x * 1024),
+                            idesc_pv, (j > 0 || x > 0) ? 1u : 0u);
           }
+          mma_commit(s_empty + 8 * pb);  // P_j read: the buffer may take S_{j+2}
           mma_commit(v_empty + 8 * pb);
           mma_commit(pv_full + 8 * pb);
         }
@@ -326,7 +294,7 @@ __global__ void __launch_bounds__(THREADS, P_TMEM ? 2 : 1)
     __syncwarp();
     if (lane == 0 && !mbar_wait(drain, 0, nullptr)) record_status(p.status, TVR_DEV_TIMEOUT_DRAIN);
     __syncwarp();
-  } else if constexpr (P_TMEM) {
+  } else {
     // ------------------- softmax rows, P and O in tensor memory -------------------
     // O accumulates in TMEM (PV_j adds P_j V_j to it).  O and l are kept
     // relative to a running maximum m that is raised only when a block's
@@ -430,109 +398,6 @@ __global__ void __launch_bounds__(THREADS, P_TMEM ? 2 : 1)
       if (qidx < p.seq_q) store_row(p, b, h, qidx, o, m, l);
     }
     __syncwarp();
-  } else {
-    // ------------------------------ softmax rows ------------------------------
-    const int q = warp & 3;
-    const int t = 32 * q + lane;  // TMEM lane = query row within the tile
-    const int qidx = q0 + t;
-    const uint32_t lane_off = static_cast<uint32_t>(32 * q) << 16;
-    float o[D];
-#pragma unroll
-    for (int i = 0; i < D; ++i) o[i] = 0.f;
-    float m = -INFINITY, l = 0.f;
-    float alpha_prev = 1.f;  // rescale factor that goes with PV_{j-1}
-    bool ok = true;
-    // O = O * alpha + PV_j, then PV buffer j & 1 is free again
-    auto update_o = [&](int j, float alpha) -> bool {
-      const bool got = mbar_wait(pv_full + 8 * (j & 1), (j >> 1) & 1, abort_flag);
-      if (!__all_sync(0xffffffffu, got)) return false;
-      tc_fence_after();
-      float pv[D];
-#pragma unroll
-      for (int c = 0; c < D / 32; ++c)
-        tmem_load_32_async(tmem + lane_off + PV_COL + static_cast<uint32_t>((j & 1) * D + 32 * c),
-                           pv + 32 * c);
-      tmem_wait_loads();
-#pragma unroll
-      for (int i = 0; i < D; ++i) o[i] = fmaf(o[i], alpha, pv[i]);
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(pv_empty + 8 * (j & 1));
-      return true;
-    };
-    for (int j = 0; j < nkb; ++j) {
-      const int sb = j & 1;
-      const bool got = mbar_wait(s_full + 8 * sb, (j >> 1) & 1, abort_flag);
-      if (!__all_sync(0xffffffffu, got)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      const uint32_t srow = tmem + lane_off + static_cast<uint32_t>(sb * BN);
-      const int key0 = j * BN;
-      // keys [key0, key_end) are visible to this row
-      int key_end = min(seq_k, key0 + BN);
-      if (p.causal) key_end = min(key_end, qidx + 1);
-      const int nvis = key_end - key0;  // may be <= 0 for padding rows
-      // the row's BN scores: all TMEM loads in flight, one wait
-      float sc[BN];
-#pragma unroll
-      for (int c = 0; c < BN / 32; ++c) tmem_load_32_async(srow + 32 * c, sc + 32 * c);
-      tmem_wait_loads();
-      // scores consumed: the buffer may take S_{j+2}
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(s_empty + 8 * sb);
-      float mx = -INFINITY;
-#pragma unroll
-      for (int i = 0; i < BN; ++i) {
-        if (i < nvis) mx = fmaxf(mx, sc[i] * p.scale_log2);
-      }
-      // scores are scaled inside exp2: x * scale_log2 - m in one FMA
-      const float m_new = fmaxf(m, mx);
-      const float m_use = m_new == -INFINITY ? 0.f : m_new;
-      const float alpha = ex2(m - m_use);
-      float sum = 0.f;
-#pragma unroll
-      for (int i = 0; i < BN; ++i) {
-        const float e = i < nvis ? ex2(fmaf(sc[i], p.scale_log2, -m_use)) : 0.f;
-        sc[i] = e;
-        sum += e;
-      }
-      // P tile j & 1 is free: PV_{j-2} was consumed by the output update of j-2
-      const uint32_t pt = sp + sb * P_BYTES;
-#pragma unroll
-      for (int c = 0; c < BN / 32; ++c) {
-        const uint32_t row = pt + c * Q_ATOM + t * 128;
-#pragma unroll
-        for (int cc = 0; cc < 8; ++cc) {
-          const float* q4 = sc + 32 * c + 4 * cc;
-          st_shared4(row + ((cc ^ (t & 7)) << 4), q4[0], q4[1], q4[2], q4[3]);
-        }
-      }
-      // P visible to the tensor core
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      __syncwarp();
-      if (lane == 0) mbar_arrive(p_full + 8 * sb);
-      l = l * alpha + sum;
-      m = m_new;
-      // the previous block's output contribution, while PV_j runs
-      if (j >= 1 && !update_o(j - 1, alpha_prev)) {
-        ok = false;
-        break;
-      }
-      alpha_prev = alpha;
-    }
-    if (ok && nkb > 0 && !update_o(nkb - 1, alpha_prev)) ok = false;
-    if (!ok) {
-      if (lane == 0) {
-        record_status(p.status, TVR_DEV_TIMEOUT_EPILOGUE);
-        *const_cast<volatile int*>(abort_flag) = 1;
-      }
-    } else if (qidx < p.seq_q) {
-      store_row(p, b, h, qidx, o, m, l);
-    }
-    __syncwarp();
   }
 
   tc_fence_before();
@@ -613,31 +478,15 @@ int attention_impl(const float* q, const float* k, const float* v, float* out, f
   p.status = device_status_ptr(dev);
   p.key_len = key_len;
   p.key_len_add = key_len_add;
-  p.pdl_trigger = pdl_enabled() ? 1 : 0;
-  // P in tensor memory (two CTAs per SM) is chosen with
-  // TVARANT_ATTENTION_P_TMEM=1 until it has been measured against the
-  // shared-memory form on the device; both compute the same values.
-  static const bool p_tmem = [] {
-    const char* env = std::getenv("TVARANT_ATTENTION_P_TMEM");
-    return env != nullptr && env[0] == '1';
-  }();
   static std::once_flag once[64];
   static cudaError_t attr_err[64];
   std::call_once(once[dev & 63], [&]() {
     attr_err[dev & 63] = cudaFuncSetAttribute(
-        attn_fwd_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes(false));
-    if (attr_err[dev & 63] == cudaSuccess) {
-      attr_err[dev & 63] = cudaFuncSetAttribute(
-          attn_fwd_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes(true));
-    }
+        attn_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
   });
   TVR_CUDA_TRY(attr_err[dev & 63]);
   const dim3 grid(static_cast<unsigned>(ceil_div(seq_q, BM)), static_cast<unsigned>(batch * heads));
-  if (p_tmem) {
-    attn_fwd_kernel<true><<<grid, THREADS, smem_bytes(true), as_stream(stream)>>>(p);
-  } else {
-    attn_fwd_kernel<false><<<grid, THREADS, smem_bytes(false), as_stream(stream)>>>(p);
-  }
+  attn_fwd_kernel<<<grid, THREADS, SMEM_BYTES, as_stream(stream)>>>(p);
   TVR_LAUNCH_CHECK();
   return TVR_OK;
 }

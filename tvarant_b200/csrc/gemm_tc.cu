@@ -57,7 +57,10 @@ constexpr int NUM_THREADS = 64 + 32 * EPI_WARPS;  // producer, MMA, epilogue war
 constexpr int STAGE_SMEM = 192 * 1024;
 constexpr int EPI_BUF_BYTES = 32 * 32 * 4;                 // one 32 x 32 fp32 sub-tile
 constexpr int EPI_SMEM = EPI_WARPS * EPI_BUF_BYTES;        // one staging buffer per warp
-constexpr int GROUP_M = 8;                                 // tile raster group height
+// Tile raster: units walk groups of tile rows (or columns) small enough that
+// the group's panels of one operand stay in L2 while the other operand
+// streams past them (pick_raster).
+constexpr int64_t kRasterL2Bytes = int64_t(48) << 20;
 
 template <int BN, bool SPLIT3>
 struct Cfg {
@@ -66,12 +69,25 @@ struct Cfg {
   static constexpr int OPERANDS = SPLIT3 ? 2 : 1;
   static constexpr int STAGE_BYTES = OPERANDS * (A_BYTES + B_BYTES);
   static constexpr int STAGES = STAGE_SMEM / STAGE_BYTES;
-  static constexpr int TMEM_COLS = 2 * BN;  // 128, 256 or 512: powers of two
+  // two accumulators (one being filled while the epilogue drains the
+  // other); 3xTF32 adds the running sum of a tile's K chunks (at column
+  // 2 * BN).  Allocations are powers of two.
+  static constexpr int TMEM_COLS = SPLIT3 ? (BN == 64 ? 256 : 512) : 2 * BN;
   static constexpr int BAR_BYTES = 8 * (2 * STAGES + 5) + 8;
   static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + EPI_SMEM + BAR_BYTES;
   static_assert(SMEM_BYTES <= 232448 - 64, "shared memory budget");
   static_assert(BN == 64 || BN == 128 || BN == 256, "BN");
+  static_assert(!SPLIT3 || BN <= 128, "3xTF32 tiles keep a running sum beside two accumulators");
 };
+
+// 3xTF32: k-blocks per accumulation chunk.  The tensor core adds each MMA's
+// products into its fp32 accumulator with truncation, so the accumulator's
+// error grows with the number of MMAs added into it (3 per k-step in
+// 3xTF32): over K = 4096 that is ~3e-5 relative, over K = 512 ~4e-6.  Each
+// chunk of 512 K therefore starts a fresh accumulator, and the epilogue
+// warps add the chunks in fp32 (round to nearest) into a running sum kept in
+// tensor memory.
+constexpr int SPLIT3_KCHUNK = 16;
 
 struct Params {
   CUtensorMap tma_a;     // A or A_hi: dims {K, M, batch}
@@ -92,8 +108,11 @@ struct Params {
   int batch;
   int b_broadcast;  // every batch entry uses B[0]
   int tiles_m, tiles_n;
+  int group;        // raster group: tile rows (raster_n == 0) or tile columns (1)
+  int raster_n;
   int splits;       // > 1: split-K, raw partial sums to the workspace at c
   int kb_per_split;
+  int kchunk;       // 3xTF32: k-blocks per accumulation chunk
   int num_kb;
   int total_units;
   int* status;
@@ -119,8 +138,10 @@ __host__ __device__ constexpr uint32_t make_idesc(int n, bool b_nmajor) {
 }
 
 // Work unit -> (operand batch index, k split, tile row, tile column).
-// Tiles are rastered in groups of GROUP_M tile rows so CTAs running at the
-// same time share A and B panels in L2.
+// Tiles are rastered in groups of p.group tile rows (M fastest inside a
+// group), or with raster_n of p.group tile columns (N fastest), so the CTAs
+// running at the same time share panels, and the group's panels of one
+// operand stay in L2 while the whole other operand streams past them once.
 __device__ __forceinline__ void decode_unit(const Params& p, int u, int& b, int& s, int& tm,
                                             int& tn) {
   const int per = p.tiles_m * p.tiles_n;
@@ -128,13 +149,44 @@ __device__ __forceinline__ void decode_unit(const Params& p, int u, int& b, int&
   const int r = u - outer * per;
   b = outer / p.splits;
   s = outer - b * p.splits;
-  const int span = GROUP_M * p.tiles_n;
-  const int g = r / span;
-  const int first_m = g * GROUP_M;
-  const int gm = min(p.tiles_m - first_m, GROUP_M);
-  const int rr = r - g * span;
-  tm = first_m + rr % gm;
-  tn = rr / gm;
+  const int G = p.group;
+  if (p.raster_n == 0) {
+    const int span = G * p.tiles_n;
+    const int g = r / span;
+    const int first_m = g * G;
+    const int gm = min(p.tiles_m - first_m, G);
+    const int rr = r - g * span;
+    tm = first_m + rr % gm;
+    tn = rr / gm;
+  } else {
+    const int span = G * p.tiles_m;
+    const int g = r / span;
+    const int first_n = g * G;
+    const int gn = min(p.tiles_n - first_n, G);
+    const int rr = r - g * span;
+    tn = first_n + rr % gn;
+    tm = rr / gn;
+  }
+}
+
+// Raster for a tiles_m x tiles_n grid whose A panels (one tile row over the
+// whole K) take panel_a bytes and B panels panel_b: hold a group of A panels
+// in L2 and stream B once per group, or the other way round, whichever
+// moves fewer bytes from HBM when a group may take kRasterL2Bytes.
+inline void pick_raster(Params& p, int64_t panel_a, int64_t panel_b) {
+  const int64_t budget = kRasterL2Bytes;
+  const int64_t tm = p.tiles_m, tn = p.tiles_n;
+  const int64_t gm = std::max<int64_t>(1, std::min<int64_t>(tm, budget / std::max<int64_t>(1, panel_a)));
+  const int64_t gn = std::max<int64_t>(1, std::min<int64_t>(tn, budget / std::max<int64_t>(1, panel_b)));
+  const int64_t bytes_m = tm * panel_a + tn * panel_b * ceil_div(tm, gm);
+  const int64_t bytes_n = tn * panel_b + tm * panel_a * ceil_div(tn, gn);
+  if (bytes_n < bytes_m) {
+    p.raster_n = 1;
+    p.group = static_cast<int>(gn);
+  } else {
+    p.raster_n = 0;
+    p.group = static_cast<int>(gm);
+  }
 }
 
 // NVLS kernels: the CTAs past the GEMM's sum this rank's output tiles (unit
@@ -356,49 +408,56 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) gemm_tc_kernel(const __grid_co
         decode_unit(p, u, b, s, tm, tn);
         const int kb0 = s * p.kb_per_split;
         const int kb1 = min(p.num_kb, kb0 + p.kb_per_split);
-        if (!mbar_wait(tempty_bar + 8 * acc, acc_phase ^ 1u, abort_flag)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        const uint32_t d = tmem_base + static_cast<uint32_t>(acc * BN);
-        for (int kb = kb0; kb < kb1; ++kb) {
-          if (!mbar_wait(full_bar + 8 * stage, phase, abort_flag)) {
+        // one accumulation chunk per unit, or (3xTF32) one per p.kchunk
+        // k-blocks, each into the next accumulator buffer
+        const int kc = SPLIT3 ? p.kchunk : kb1 - kb0;
+        for (int c0 = kb0; c0 < kb1; c0 += kc) {
+          const int c1 = min(kb1, c0 + kc);
+          if (!mbar_wait(tempty_bar + 8 * acc, acc_phase ^ 1u, abort_flag)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t sa = stage0 + stage * Cf::STAGE_BYTES;
-          const uint32_t sb = sa + Cf::A_BYTES;
+          const uint32_t d = tmem_base + static_cast<uint32_t>(acc * BN);
+          for (int kb = c0; kb < c1; ++kb) {
+            if (!mbar_wait(full_bar + 8 * stage, phase, abort_flag)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t sa = stage0 + stage * Cf::STAGE_BYTES;
+            const uint32_t sb = sa + Cf::A_BYTES;
 #pragma unroll
-          for (int kk = 0; kk < BK / 8; ++kk) {
-            const uint64_t da = desc_kmajor(sa + kk * 32);
-            const uint64_t db = B_NMAJOR ? desc_nmajor(sb + kk * 1024) : desc_kmajor(sb + kk * 32);
-            const uint32_t first = (kb > kb0 || kk > 0) ? 1u : 0u;
-            if (SPLIT3) {
-              const uint32_t sa_lo = sb + Cf::B_BYTES;
-              const uint32_t sb_lo = sa_lo + Cf::A_BYTES;
-              const uint64_t da_lo = desc_kmajor(sa_lo + kk * 32);
-              const uint64_t db_lo =
-                  B_NMAJOR ? desc_nmajor(sb_lo + kk * 1024) : desc_kmajor(sb_lo + kk * 32);
-              mma_tf32(d, da_lo, db, idesc, first);
-              mma_tf32(d, da, db_lo, idesc, 1u);
-              mma_tf32(d, da, db, idesc, 1u);
-            } else {
-              mma_tf32(d, da, db, idesc, first);
+            for (int kk = 0; kk < BK / 8; ++kk) {
+              const uint64_t da = desc_kmajor(sa + kk * 32);
+              const uint64_t db = B_NMAJOR ? desc_nmajor(sb + kk * 1024) : desc_kmajor(sb + kk * 32);
+              const uint32_t first = (kb > c0 || kk > 0) ? 1u : 0u;
+              if (SPLIT3) {
+                const uint32_t sa_lo = sb + Cf::B_BYTES;
+                const uint32_t sb_lo = sa_lo + Cf::A_BYTES;
+                const uint64_t da_lo = desc_kmajor(sa_lo + kk * 32);
+                const uint64_t db_lo =
+                    B_NMAJOR ? desc_nmajor(sb_lo + kk * 1024) : desc_kmajor(sb_lo + kk * 32);
+                mma_tf32(d, da_lo, db, idesc, first);
+                mma_tf32(d, da, db_lo, idesc, 1u);
+                mma_tf32(d, da, db, idesc, 1u);
+              } else {
+                mma_tf32(d, da, db, idesc, first);
+              }
+            }
+            issued = true;
+            mma_commit(empty_bar + 8 * stage);
+            if (++stage == STAGES) {
+              stage = 0;
+              phase ^= 1u;
             }
           }
-          issued = true;
-          mma_commit(empty_bar + 8 * stage);
-          if (++stage == STAGES) {
-            stage = 0;
-            phase ^= 1u;
-          }
+          if (!ok) break;
+          mma_commit(tfull_bar + 8 * acc);
+          acc ^= 1;
+          if (acc == 0) acc_phase ^= 1u;
         }
         if (!ok) break;
-        mma_commit(tfull_bar + 8 * acc);
-        acc ^= 1;
-        if (acc == 0) acc_phase ^= 1u;
       }
       if (!ok) {
         record_status(p.status, TVR_DEV_TIMEOUT_MMA);
@@ -433,14 +492,62 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) gemm_tc_kernel(const __grid_co
     for (int u = blockIdx.x; u < p.total_units; u += NVLS ? static_cast<unsigned>(p.nv_gemm_ctas) : gridDim.x) {
       int b, s, tm, tn;
       decode_unit(p, u, b, s, tm, tn);
-      const bool got = mbar_wait(tfull_bar + 8 * acc, acc_phase, abort_flag);
-      if (!__all_sync(0xffffffffu, got)) {
-        ok = false;
-        break;
+      const uint32_t lanes = static_cast<uint32_t>(32 * q) << 16;
+      uint32_t tcol = tmem_base + lanes + static_cast<uint32_t>(acc * BN + half * HC);
+      // 3xTF32 with more than one accumulation chunk: each chunk's
+      // accumulator is added into the running sum (column 2 * BN) and handed
+      // back; the tile's epilogue then reads the running sum.
+      bool folded = false;
+      if constexpr (SPLIT3) {
+        const int kb0 = s * p.kb_per_split;
+        const int kb1 = min(p.num_kb, kb0 + p.kb_per_split);
+        const int nch = (kb1 - kb0 + p.kchunk - 1) / p.kchunk;
+        if (nch > 1) {
+          const uint32_t scol = tmem_base + lanes + static_cast<uint32_t>(2 * BN + half * HC);
+          for (int ci = 0; ci < nch; ++ci) {
+            const bool got = mbar_wait(tfull_bar + 8 * acc, acc_phase, abort_flag);
+            if (!__all_sync(0xffffffffu, got)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t acol = tmem_base + lanes + static_cast<uint32_t>(acc * BN + half * HC);
+#pragma unroll
+            for (int c = 0; c < CH; ++c) {
+              float a[32];
+              tmem_load_32_async(acol + 32 * c, a);
+              if (ci > 0) {
+                float r[32];
+                tmem_load_32_async(scol + 32 * c, r);
+                tmem_wait_loads();
+#pragma unroll
+                for (int i = 0; i < 32; ++i) a[i] = __fadd_rn(r[i], a[i]);
+              } else {
+                tmem_wait_loads();
+              }
+              tmem_store_32(scol + 32 * c, a);
+            }
+            tmem_wait_stores();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(tempty_bar + 8 * acc);
+            acc ^= 1;
+            if (acc == 0) acc_phase ^= 1u;
+          }
+          if (!ok) break;
+          tc_fence_after();
+          tcol = scol;
+          folded = true;
+        }
       }
-      tc_fence_after();
-      const uint32_t tcol = tmem_base + (static_cast<uint32_t>(32 * q) << 16) +
-                            static_cast<uint32_t>(acc * BN + half * HC);
+      if (!folded) {
+        const bool got = mbar_wait(tfull_bar + 8 * acc, acc_phase, abort_flag);
+        if (!__all_sync(0xffffffffu, got)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+      }
       const int zc = p.splits > 1 ? s : b;
       float* cbase = p.c + static_cast<int64_t>(zc) * p.stride_c;
       const int64_t row0 = static_cast<int64_t>(tm) * BM + 32 * q;
@@ -462,7 +569,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) gemm_tc_kernel(const __grid_co
       constexpr int CH_UNROLL = PROG ? 1 : CH;
 #pragma unroll CH_UNROLL
       for (int c = 0; c < CH; ++c) {
-        if (c == CH - 1) {
+        if (c == CH - 1 && !folded) {
           // accumulator fully read: hand the TMEM buffer back to the MMA warp
           tc_fence_before();
           __syncwarp();
@@ -772,8 +879,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) gemm_tc_kernel(const __grid_co
         }
         __syncwarp();
       }
-      acc ^= 1;
-      if (acc == 0) acc_phase ^= 1u;
+      if (!folded) {
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1u;
+      }
     }
     // every store this warp issued is complete before the CTA exits
     if ((TMA_C || PROG) && lane == 0) bulk_wait_all();
@@ -914,21 +1023,23 @@ int launch_nvls(const Params& p, int grid, cudaStream_t stream, int dev) {
 template <int BN>
 int launch_bn(const Params& p, bool split3, bool b_nmajor, int grid, cudaStream_t s, int dev,
               bool prog = false, bool tma_c = false) {
-  if (prog) {  // K-major weights only
-    return split3 ? launch_kernel<BN, true, false, false, true>(p, grid, s, dev)
-                  : launch_kernel<BN, false, false, false, true>(p, grid, s, dev);
-  }
-  if (tma_c) {
+  if constexpr (BN <= 128) {
     if (split3) {
-      return b_nmajor ? launch_kernel<BN, true, true, false, false, true>(p, grid, s, dev)
-                      : launch_kernel<BN, true, false, false, false, true>(p, grid, s, dev);
+      if (prog) return launch_kernel<BN, true, false, false, true>(p, grid, s, dev);
+      if (tma_c) {
+        return b_nmajor ? launch_kernel<BN, true, true, false, false, true>(p, grid, s, dev)
+                        : launch_kernel<BN, true, false, false, false, true>(p, grid, s, dev);
+      }
+      return b_nmajor ? launch_kernel<BN, true, true>(p, grid, s, dev)
+                      : launch_kernel<BN, true, false>(p, grid, s, dev);
     }
+  } else {
+    if (split3) return fail(TVR_ERR_INVALID, "gemm: 3xTF32 tiles are at most 128 columns wide");
+  }
+  if (prog) return launch_kernel<BN, false, false, false, true>(p, grid, s, dev);  // K-major only
+  if (tma_c) {
     return b_nmajor ? launch_kernel<BN, false, true, false, false, true>(p, grid, s, dev)
                     : launch_kernel<BN, false, false, false, false, true>(p, grid, s, dev);
-  }
-  if (split3) {
-    return b_nmajor ? launch_kernel<BN, true, true>(p, grid, s, dev)
-                    : launch_kernel<BN, true, false>(p, grid, s, dev);
   }
   return b_nmajor ? launch_kernel<BN, false, true>(p, grid, s, dev)
                   : launch_kernel<BN, false, false>(p, grid, s, dev);
@@ -985,37 +1096,14 @@ int gemm_tcgen05(const float* a, const float* b, const float* bias, float* c, in
   // ~a full wave of tiles; otherwise split K across CTAs.
   int bn = 64;
   int64_t tiles = 0;
-  const int bn_cap = n > 128 ? 256 : (n > 64 ? 128 : 64);
+  // (3xTF32 tiles keep a chunk running sum in tensor memory: at most 128 wide)
+  const int bn_cap = n > 128 && !split3 ? 256 : (n > 64 ? 128 : 64);
   for (int cand : {256, 128, 64}) {
     if (cand > bn_cap) continue;
     const int64_t t = batch * ceil_div(m, BM) * ceil_div(n, cand);
     bn = cand;
     tiles = t;
     if (t >= (sms * 4) / 5) break;
-  }
-  // TVARANT_GEMM_WAVE_FIT=1: among the tile widths that fill a wave, take
-  // the one whose whole waves over the SMs the persistent grid may use cost
-  // least (rounds x width, 128-wide tiles charged 5 % more for their lower
-  // operand reuse).  N = 768 at M = 8192 is 192 tiles of 256 (2 rounds on
-  // 148 SMs: 65 % of the time does work) or 384 of 128 (3 rounds: 86 %).
-  static const bool wave_fit = [] {
-    const char* env = std::getenv("TVARANT_GEMM_WAVE_FIT");
-    return env != nullptr && env[0] == '1';
-  }();
-  if (wave_fit && tiles >= (sms * 4) / 5) {
-    const int64_t g = grid_sms(dev, sms);
-    double best = 0.0;
-    for (int cand : {256, 128}) {
-      if (cand > bn_cap) continue;
-      const int64_t t = batch * ceil_div(m, BM) * ceil_div(n, cand);
-      if (t < (sms * 4) / 5) continue;
-      const double cost = static_cast<double>(ceil_div(t, g)) * cand * (cand == 128 ? 1.05 : 1.0);
-      if (best == 0.0 || cost < best) {
-        best = cost;
-        bn = cand;
-        tiles = t;
-      }
-    }
   }
   const bool c_vec = al16(c) && ldc % 4 == 0 && (batch == 1 || sc % 4 == 0);
   int splits = 1;
@@ -1115,9 +1203,15 @@ int gemm_tcgen05(const float* a, const float* b, const float* bias, float* c, in
   p.b_broadcast = b_bcast ? 1 : 0;
   p.tiles_m = static_cast<int>(ceil_div(m, BM));
   p.tiles_n = static_cast<int>(ceil_div(n, bn));
+  // panels over one split's K: 3xTF32 streams hi and lo parts
+  {
+    const int64_t kk = static_cast<int64_t>(kb_per_split) * BK * 4 * (split3 ? 2 : 1);
+    pick_raster(p, BM * kk, bn * kk);
+  }
   p.splits = splits;
   p.kb_per_split = kb_per_split;
   p.num_kb = num_kb;
+  p.kchunk = SPLIT3_KCHUNK;
   const int64_t units = static_cast<int64_t>(batch) * splits * p.tiles_m * p.tiles_n;
   if (units > 0x7fffffff) return TVR_ERR_UNSUPPORTED;
   p.total_units = static_cast<int>(units);
@@ -1202,6 +1296,7 @@ int gemm_tcgen05_swiglu(const float* x, const float* wg, const float* wu, float*
   p.batch = 1;
   p.tiles_m = static_cast<int>(ceil_div(m, BM));
   p.tiles_n = static_cast<int>(ceil_div(n, kOutBn));
+  pick_raster(p, BM * k * 4, 2 * kOutBn * k * 4);  // a B tile: gate and up rows
   p.splits = 1;
   p.num_kb = static_cast<int>(ceil_div(k, BK));
   p.kb_per_split = p.num_kb;
@@ -1252,6 +1347,7 @@ int gemm_tcgen05_nvls(const float* a, const float* b, float* c, void* c_multicas
   p.batch = 1;
   p.tiles_m = static_cast<int>(ceil_div(m, BM));
   p.tiles_n = static_cast<int>(ceil_div(n, kBn));
+  pick_raster(p, BM * k * 4, kBn * k * 4);
   p.splits = 1;
   p.num_kb = static_cast<int>(ceil_div(k, BK));
   p.kb_per_split = p.num_kb;
@@ -1399,6 +1495,10 @@ int gemm_tcgen05_noalloc(const float* a, const float* b, const float* bias, floa
   p.b_broadcast = 0;
   p.tiles_m = static_cast<int>(ceil_div(m, BM));
   p.tiles_n = static_cast<int>(ceil_div(n, bn));
+  {
+    const int64_t kk = static_cast<int64_t>(kb_per_split) * BK * 4;
+    pick_raster(p, BM * kk, bn * kk);
+  }
   p.splits = splits;
   p.kb_per_split = kb_per_split;
   p.num_kb = num_kb;

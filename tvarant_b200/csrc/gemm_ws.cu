@@ -94,7 +94,6 @@ struct Params {
   int m, n;
   int num_kb;
   int kb_per_split;
-  int pdl;  // launched as a programmatic dependent of the previous kernel
   int* status;
   EpiProg prog;  // PROG instances: the pointwise program applied to the output
 };
@@ -209,7 +208,7 @@ __global__ void __launch_bounds__(Cfg<MB, SPLIT3>::THREADS, Cfg<MB, SPLIT3>::CTA
   const uint32_t tmem_base = *reinterpret_cast<volatile uint32_t*>(holder_ptr);
   // a programmatic dependent (the next few-row GEMM) may start its own
   // weight prefetch now; it still waits for this grid before reading anything
-  if (p.pdl && threadIdx.x == 0) grid_launch_dependents();
+  if (threadIdx.x == 0) grid_launch_dependents();
 
   if (warp == 0) {
     // ------------------------------ TMA producer ------------------------------
@@ -219,7 +218,7 @@ __global__ void __launch_bounds__(Cfg<MB, SPLIT3>::THREADS, Cfg<MB, SPLIT3>::CTA
       uint32_t issued_mask = 0;
       uint32_t issued_parity = 0;
       bool ok = true;
-      if (p.pdl) {
+      {
         // Launched as a programmatic dependent: the kernel before this one
         // on the stream may still run.  The weight panel's first k-blocks
         // start moving from HBM into L2 now; nothing is read into shared
@@ -502,7 +501,7 @@ int launch(Params& p, int tiles, int sms, cudaStream_t stream, int dev) {
   attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = p.pdl ? 2 : 1;
+  cfg.numAttrs = 2;
   TVR_CUDA_TRY(cudaLaunchKernelEx(&cfg, gemm_ws_kernel<MB, SPLIT3, PROG>, p));
   return TVR_OK;
 }
@@ -551,7 +550,6 @@ int gemm_ws(const float* x, const float* w, const float* bias, float* c, int64_t
   p.m = static_cast<int>(m);
   p.n = static_cast<int>(n);
   p.num_kb = num_kb;
-  p.pdl = pdl_enabled() ? 1 : 0;
   p.status = device_status_ptr(dev);
   const bool has_prog = prog != nullptr && prog->n_nodes > 0;
   if (has_prog) p.prog = *prog;

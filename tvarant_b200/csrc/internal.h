@@ -58,10 +58,6 @@ struct Scratch {
 
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
 
-// Whether the few-row GEMM is launched as a programmatic dependent of the
-// kernel before it on the stream (TVARANT_PDL=1; read once).
-bool pdl_enabled();
-
 #ifdef __CUDACC__
 // Programmatic dependent launch.  A kernel launched with programmatic stream
 // serialization may start while the kernel before it on the stream is still

@@ -241,11 +241,11 @@ template <int VPT>
 __global__ void __launch_bounds__(1024) layer_norm_kernel(
     const float* __restrict__ x, const float* __restrict__ gamma, const float* __restrict__ beta,
     float* __restrict__ y, float* __restrict__ mean_out, float* __restrict__ rstd_out, int n,
-    float eps, int trigger) {
+    float eps) {
   __shared__ float red[32];
   // a few-row GEMM launched as a programmatic dependent (decode steps) may
   // start streaming its weights now
-  if (trigger && threadIdx.x == 0) grid_launch_dependents();
+  if (threadIdx.x == 0) grid_launch_dependents();
   const int64_t row = blockIdx.x;
   const int n4 = n >> 2;
   const float4* xr = reinterpret_cast<const float4*>(x + row * n);
@@ -312,9 +312,9 @@ __global__ void __launch_bounds__(1024) layer_norm_kernel(
 __global__ void __launch_bounds__(256) layer_norm_generic_kernel(
     const float* __restrict__ x, const float* __restrict__ gamma, const float* __restrict__ beta,
     float* __restrict__ y, float* __restrict__ mean_out, float* __restrict__ rstd_out, int64_t n,
-    float eps, int trigger) {
+    float eps) {
   __shared__ float red[32];
-  if (trigger && threadIdx.x == 0) grid_launch_dependents();
+  if (threadIdx.x == 0) grid_launch_dependents();
   const float* xr = x + static_cast<int64_t>(blockIdx.x) * n;
   float* yr = y + static_cast<int64_t>(blockIdx.x) * n;
   float s = 0.f;
@@ -479,7 +479,6 @@ int tvr_layer_norm(const float* x, const float* gamma, const float* beta, float*
   TVR_CHECK(rows <= 0x7fffffff, "tvr_layer_norm: too many rows");
   cudaStream_t s = as_stream(stream);
   const unsigned blocks = static_cast<unsigned>(rows);
-  const int trig = pdl_enabled() ? 1 : 0;
   const bool vec = n % 4 == 0 && aligned16(x) && aligned16(y) && (!gamma || aligned16(gamma)) &&
                    (!beta || aligned16(beta));
   if (vec && n <= 16384) {
@@ -489,14 +488,14 @@ int tvr_layer_norm(const float* x, const float* gamma, const float* beta, float*
     int threads = static_cast<int>(ceil_div(ceil_div(n4, vpt), 32) * 32);
     const int ni = static_cast<int>(n);
     switch (vpt) {
-      case 1: layer_norm_kernel<1><<<blocks, threads, 0, s>>>(x, gamma, beta, y, mean, rstd, ni, eps, trig); break;
-      case 2: layer_norm_kernel<2><<<blocks, threads, 0, s>>>(x, gamma, beta, y, mean, rstd, ni, eps, trig); break;
-      case 4: layer_norm_kernel<4><<<blocks, threads, 0, s>>>(x, gamma, beta, y, mean, rstd, ni, eps, trig); break;
-      case 8: layer_norm_kernel<8><<<blocks, threads, 0, s>>>(x, gamma, beta, y, mean, rstd, ni, eps, trig); break;
-      default: layer_norm_kernel<16><<<blocks, threads, 0, s>>>(x, gamma, beta, y, mean, rstd, ni, eps, trig); break;
+      case 1: layer_norm_kernel<1><<<blocks, threads, 0, s>>>(x, gamma, beta, y, mean, rstd, ni, eps); break;
+      case 2: layer_norm_kernel<2><<<blocks, threads, 0, s>>>(x, gamma, beta, y, mean, rstd, ni, eps); break;
+      case 4: layer_norm_kernel<4><<<blocks, threads, 0, s>>>(x, gamma, beta, y, mean, rstd, ni, eps); break;
+      case 8: layer_norm_kernel<8><<<blocks, threads, 0, s>>>(x, gamma, beta, y, mean, rstd, ni, eps); break;
+      default: layer_norm_kernel<16><<<blocks, threads, 0, s>>>(x, gamma, beta, y, mean, rstd, ni, eps); break;
     }
   } else {
-    layer_norm_generic_kernel<<<blocks, 256, 0, s>>>(x, gamma, beta, y, mean, rstd, n, eps, trig);
+    layer_norm_generic_kernel<<<blocks, 256, 0, s>>>(x, gamma, beta, y, mean, rstd, n, eps);
   }
   TVR_LAUNCH_CHECK();
   return TVR_OK;

@@ -163,14 +163,6 @@ int current_device() {
   return d;
 }
 
-bool pdl_enabled() {
-  static const bool on = [] {
-    const char* env = std::getenv("TVARANT_PDL");
-    return env != nullptr && env[0] == '1';
-  }();
-  return on;
-}
-
 int* device_status_ptr(int device) {
   if (device < 0 || device >= kMaxDevices) return nullptr;
   if (init_device(device) != TVR_OK) return nullptr;
