@@ -461,13 +461,6 @@ class GemmChain:
         return y
 
 
-def _kernel_options() -> dict:
-    """Kernel-form switches set in the environment (tvarant_b200.workloads)."""
-    from tvarant_b200.workloads import kernel_options
-
-    return kernel_options()
-
-
 def _dist_init(world: int):
     import torch.distributed as dist
 
@@ -655,7 +648,6 @@ def run_gemm(args, rank, world, local_rank) -> dict | None:
                    else f"steps rotate over {wl.copies} weight copies ({wl.copies * 67} MB > L2), "
                         "so each step reads its weight from HBM"),
             "fusions": wl.fusions,
-            "kernel_options": _kernel_options(),
         },
         "e2e": {"value": world * wl.flops / (pt["e2e_ms"] / 1e3) / 1e12, "unit": "TFLOP/s",
                 "h2d_bytes_per_step": wl.h2d_bytes, "d2h_bytes_per_step": wl.d2h_bytes,
@@ -894,14 +886,14 @@ def _main() -> int:
                     help="gpt2 workload: bmm + mask + softmax + bmm (the config), or the fused "
                          "F.scaled_dot_product_attention kernel")
     ap.add_argument("--chunks", type=int, default=2, help="mlp workload: token chunks overlapped with the all-reduce")
-    ap.add_argument("--comm", choices=["nccl", "nvls", "nvls-fused"], default="nccl",
+    ap.add_argument("--comm", choices=["auto", "nccl", "nvls", "nvls-fused"], default="auto",
                     help="mlp workload at N>1: NCCL all-reduce, this library's NVLink SHARP "
                          "all-reduce over symmetric memory, or (TF32) the down projection and "
                          "that all-reduce in one kernel")
     ap.add_argument("--gemm-sms", type=int, default=0,
                     help="mlp workload at N>1: SMs the GEMMs may use while the all-reduce runs "
                          "(0: all but the collective's CTAs)")
-    ap.add_argument("--nvls-blocks", type=int, default=32,
+    ap.add_argument("--nvls-blocks", type=int, default=16,
                     help="mlp workload, --comm nvls: CTAs of the all-reduce kernel")
     ap.add_argument("--nccl-ctas", type=int, default=32,
                     help="mlp workload: CTAs NCCL may use per collective (the GEMMs leave that many SMs free; 0: no limit)")

@@ -7,13 +7,14 @@ grows linearly with the number of MMAs added into one accumulator — three per
 k-step in 3xTF32.  Measured on the device at K = 4096 against the oracle:
 3.3e-5 relative Frobenius error, where the bar is 1e-5.  The 3xTF32 GEMM
 (csrc/gemm_tc.cu, SPLIT3 instances) therefore starts a fresh accumulator
-every 512 of K and adds the chunks in fp32 with rounding to nearest.
+every 256 of K and adds the chunks in fp32 with rounding to nearest (512
+left a Llama MLP layer, three GEMMs deep, at 1.2e-5).
 
 This model restates that arithmetic in numpy: TF32 hi / lo splits (the top
 19 bits of an fp32 value, and the remainder's top 19 bits), exact products
 of 8-wide MMA steps, and truncation of the accumulator after each MMA.  It
-reproduces the device's single-accumulator error and shows the 512-wide
-chunks within the bar, next to the sequential fp32 sum the reference runs
+reproduces the device's single-accumulator error and shows the 256-wide
+chunks well within the bar, next to the sequential fp32 sum the reference runs
 (HostKernels.cpp:118-129).
 """
 
@@ -82,7 +83,6 @@ def test_one_accumulator_over_k4096_misses_the_bar(case):
     assert _rel(_model_3xtf32(x, w, K), ref) > 2e-5
 
 
-@pytest.mark.parametrize("chunk", [512])
-def test_chunked_accumulation_meets_the_bar(case, chunk):
+def test_chunked_accumulation_meets_the_bar(case):
     x, w, ref = case
-    assert _rel(_model_3xtf32(x, w, chunk), ref) <= 1e-5 / 1.5
+    assert _rel(_model_3xtf32(x, w, 256), ref) <= 1e-5 / 3

@@ -3,15 +3,14 @@ reducing CTAs, restated in Python and checked for exact coverage (CPU).
 
 * ``gemm_ws_kernel`` (csrc/gemm_ws.cu): after the cluster barrier, CTA
   ``split`` of ``nsplit`` sums elements [split * share, ...) of the
-  MB x 128 tile, one element per thread and step; with a pointwise program
-  (PROG instances) it takes groups of four columns of one row instead.
+  MB x 128 tile, one element per thread and step.
 * ``nvls_reduce_tiles`` (csrc/gemm_tc.cu): reducing CTA ``rc`` of ``nred``
   on rank ``rank`` of ``world`` takes units rank + world * i for i = rc,
   rc + nred, ...; inside a tile, thread t handles float4 index
   e + q * nt for q < 4, e = t, t + 4 * nt, ..., clipped to the tile's rows
   and columns.
 
-Every element (or group, unit, float4) must be taken exactly once, and no
+Every element (or unit, float4) must be taken exactly once, and no
 address may leave the output.
 """
 
@@ -35,28 +34,12 @@ def ws_elements(mb, nsplit, threads):
     return e_total, seen
 
 
-def ws_groups(mb, nsplit, threads):
-    e4_total = mb * BM // 4
-    share4 = -(-e4_total // nsplit)
-    seen = []
-    for split in range(nsplit):
-        f0, f1 = split * share4, min(e4_total, split * share4 + share4)
-        for t in range(threads):
-            for f in range(f0 + t, f1, threads):
-                e = 4 * f
-                assert e // BM == (e + 3) // BM  # the four columns share a row
-                seen.append(f)
-    return e4_total, seen
-
-
 @pytest.mark.parametrize("mb", [16, 32, 64, 128])
 @pytest.mark.parametrize("nsplit", range(1, 9))
 @pytest.mark.parametrize("threads", [192, 320])
 def test_gemm_ws_reduction_covers_each_element_once(mb, nsplit, threads):
     total, seen = ws_elements(mb, nsplit, threads)
     assert sorted(seen) == list(range(total))
-    total4, seen4 = ws_groups(mb, nsplit, threads)
-    assert sorted(seen4) == list(range(total4))
 
 
 def reducer_float4s(rows, cols, nt=320, unroll=4):

@@ -105,3 +105,41 @@ def test_stack_rejects_a_negative_sm_limit():
     with pytest.raises(ValueError):
         TPMLPStack([], None, gemm_sms=-1)
     assert TPMLPStack([], None, gemm_sms=118).gemm_sms == 118
+
+
+def _agree_worker(rank, world, port, results, supported):
+    import sys
+    from pathlib import Path
+
+    sys.path.insert(0, str(Path(__file__).resolve().parents[1]))
+    from tvarant_b200 import nvls
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        # a fake of the per-GPU probe: rank r answers supported[r]
+        nvls.multicast_supported = lambda device: supported[rank]
+        results[rank] = nvls.agreed_multicast(rank)
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("supported", [(True, True), (True, False, True, True), (False, False)])
+def test_exchange_choice_is_the_same_on_every_rank(supported):
+    """The stack's automatic exchange (NVLS where the switch supports it, else
+    NCCL) is decided by one collective, so a rank without multicast makes
+    every rank take NCCL."""
+    world = len(supported)
+    ctx = mp.get_context("spawn")
+    manager = ctx.Manager()
+    results = manager.dict()
+    port = _free_port()
+    procs = [ctx.Process(target=_agree_worker, args=(r, world, port, results, supported))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    assert [results[r] for r in range(world)] == [all(supported)] * world

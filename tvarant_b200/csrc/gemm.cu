@@ -31,16 +31,6 @@ int resolve_mode(int mode) {
 // kernel costs more than it saves.
 constexpr int64_t kSmallMacs = int64_t(1) << 21;
 
-// Whether a program after a few-row GEMM runs in that kernel's epilogue
-// (TVARANT_WS_PROGRAM=1; read once) instead of as a pass over its output.
-bool ws_program_enabled() {
-  static const bool on = [] {
-    const char* env = std::getenv("TVARANT_WS_PROGRAM");
-    return env != nullptr && env[0] == '1';
-  }();
-  return on;
-}
-
 int run(const float* a, const float* b, const float* bias, float* c, int64_t m, int64_t n,
         int64_t k, int64_t lda, int64_t ldb, int64_t ldc, int64_t batch, int64_t sa,
         int64_t sb, int64_t sc, float alpha, float beta, int act, bool trans_b, int mode,
@@ -64,11 +54,6 @@ int run(const float* a, const float* b, const float* bias, float* c, int64_t m, 
     return then_prog(gemm_skinny(a, b, bias, c, m, n, k, lda, ldb, ldc, alpha, beta, act, stream));
   }
   if (mode != TVR_GEMM_FP32 && batch == 1 && gemm_ws_applies(a, b, m, n, k, lda, ldb, trans_b)) {
-    // TVARANT_WS_PROGRAM=1: the program in the few-row kernel's epilogue
-    if (prog != nullptr && ws_program_enabled()) {
-      return gemm_ws(a, b, bias, c, m, n, k, lda, ldb, ldc, alpha, beta, act,
-                     mode == TVR_GEMM_3XTF32, stream, prog);
-    }
     return then_prog(gemm_ws(a, b, bias, c, m, n, k, lda, ldb, ldc, alpha, beta, act,
                              mode == TVR_GEMM_3XTF32, stream));
   }

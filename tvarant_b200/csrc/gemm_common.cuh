@@ -60,14 +60,12 @@ int gemm_skinny(const float* a, const float* b, const float* bias, float* c, int
 
 // Weight-streaming tcgen05 GEMM for at most 128 rows against a K-major
 // weight (split-K over a thread-block cluster, reduced in distributed shared
-// memory); applies when gemm_ws_applies() holds.  With a pointwise program
-// (prog non-null with nodes) the program is applied to the output in the
-// reduction's epilogue.
+// memory); applies when gemm_ws_applies() holds.
 bool gemm_ws_applies(const float* x, const float* w, int64_t m, int64_t n, int64_t k,
                      int64_t ldx, int64_t ldw, bool trans_b);
 int gemm_ws(const float* x, const float* w, const float* bias, float* c, int64_t m, int64_t n,
             int64_t k, int64_t ldx, int64_t ldw, int64_t ldc, float alpha, float beta, int act,
-            bool split3, cudaStream_t stream, const EpiProg* prog = nullptr);
+            bool split3, cudaStream_t stream);
 
 // silu(x . Wg^T) * (x . Wu^T) in one TF32 tcgen05 pass (K-major weights);
 // TVR_ERR_UNSUPPORTED when the operands cannot be described by TMA maps.

@@ -83,11 +83,12 @@ struct Cfg {
 // 3xTF32: k-blocks per accumulation chunk.  The tensor core adds each MMA's
 // products into its fp32 accumulator with truncation, so the accumulator's
 // error grows with the number of MMAs added into it (3 per k-step in
-// 3xTF32): over K = 4096 that is ~3e-5 relative, over K = 512 ~4e-6.  Each
-// chunk of 512 K therefore starts a fresh accumulator, and the epilogue
+// 3xTF32): over K = 4096 that is ~3e-5 relative, over K = 256 ~3e-6.  Each
+// chunk of 256 K therefore starts a fresh accumulator, and the epilogue
 // warps add the chunks in fp32 (round to nearest) into a running sum kept in
-// tensor memory.
-constexpr int SPLIT3_KCHUNK = 16;
+// tensor memory.  (512-wide chunks left a Llama MLP layer, three GEMMs
+// deep with K up to 11008, at 1.2e-5 against the 1e-5 bar.)
+constexpr int SPLIT3_KCHUNK = 8;
 
 struct Params {
   CUtensorMap tma_a;     // A or A_hi: dims {K, M, batch}

@@ -95,7 +95,6 @@ struct Params {
   int num_kb;
   int kb_per_split;
   int* status;
-  EpiProg prog;  // PROG instances: the pointwise program applied to the output
 };
 
 __device__ __forceinline__ uint32_t cluster_rank() {
@@ -156,7 +155,7 @@ __device__ __forceinline__ void st_shared4(uint32_t addr, float4 v) {
                : "memory");
 }
 
-template <int MB, bool SPLIT3, bool PROG>
+template <int MB, bool SPLIT3>
 __global__ void __launch_bounds__(Cfg<MB, SPLIT3>::THREADS, Cfg<MB, SPLIT3>::CTAS_PER_SM)
     gemm_ws_kernel(const __grid_constant__ Params p) {
   using Cf = Cfg<MB, SPLIT3>;
@@ -404,62 +403,21 @@ __global__ void __launch_bounds__(Cfg<MB, SPLIT3>::THREADS, Cfg<MB, SPLIT3>::CTA
   tc_fence_before();
   cluster_sync();  // every CTA's partial tile is in its shared memory
   constexpr int E = MB * BM;
-  if constexpr (PROG) {
-    // Four consecutive columns of one output row per thread (BM % 4 == 0):
-    // the GEMM value as below, then the pointwise program on it, as the
-    // in-place pass (epi_prog_kernel) computes it from the stored value.  The
-    // output is written once instead of written, read and written again.
-    constexpr int E4 = E / 4;
-    const int share4 = (E4 + static_cast<int>(nsplit) - 1) / static_cast<int>(nsplit);
-    const int f0 = static_cast<int>(split) * share4;
-    const int f1 = min(E4, f0 + share4);
-    for (int f = f0 + static_cast<int>(threadIdx.x); f < f1; f += Cf::THREADS) {
-      const int e = 4 * f;
-      const int row = e / BM;
-      const int col = tile * BM + (e % BM);
-      if (row >= p.m || col >= p.n) continue;
-      float* dst = p.c + static_cast<int64_t>(row) * p.ldc + col;
-      float y[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        if (col + q >= p.n) continue;
-        const uint32_t local = ring + 4u * static_cast<uint32_t>(e + q);
-        float sum = 0.f;
-        for (uint32_t s = 0; s < nsplit; ++s) sum += ld_dsmem(dsmem_addr(local, s));
-        float prev = 0.f;
-        if (p.bias != nullptr) prev = __ldg(p.bias + col + q);
-        else if (p.use_prev) prev = dst[q];
-        y[q] = epilogue_value(sum, prev, p.alpha, p.beta, p.act);
-      }
-      const float4 x0 = p.prog.n_extra > 0 ? epi_load4(p.prog, 0, row, col, p.m, p.n)
-                                           : make_float4(0.f, 0.f, 0.f, 0.f);
-      const float4 x1 = p.prog.n_extra > 1 ? epi_load4(p.prog, 1, row, col, p.m, p.n)
-                                           : make_float4(0.f, 0.f, 0.f, 0.f);
-      const float4 r =
-          epi_eval4<EPI_MAX_NODES>(p.prog, make_float4(y[0], y[1], y[2], y[3]), x0, x1);
-      const float rv[4] = {r.x, r.y, r.z, r.w};
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        if (col + q < p.n) dst[q] = rv[q];
-      }
-    }
-  } else {
-    const int share = (E + static_cast<int>(nsplit) - 1) / static_cast<int>(nsplit);
-    const int e0 = static_cast<int>(split) * share;
-    const int e1 = min(E, e0 + share);
-    for (int e = e0 + static_cast<int>(threadIdx.x); e < e1; e += Cf::THREADS) {
-      const int row = e / BM;
-      const int col = tile * BM + (e % BM);
-      if (row >= p.m || col >= p.n) continue;
-      const uint32_t local = ring + 4u * static_cast<uint32_t>(e);
-      float sum = 0.f;
-      for (uint32_t s = 0; s < nsplit; ++s) sum += ld_dsmem(dsmem_addr(local, s));
-      float* dst = p.c + static_cast<int64_t>(row) * p.ldc + col;
-      float prev = 0.f;
-      if (p.bias != nullptr) prev = __ldg(p.bias + col);
-      else if (p.use_prev) prev = *dst;
-      *dst = epilogue_value(sum, prev, p.alpha, p.beta, p.act);
-    }
+  const int share = (E + static_cast<int>(nsplit) - 1) / static_cast<int>(nsplit);
+  const int e0 = static_cast<int>(split) * share;
+  const int e1 = min(E, e0 + share);
+  for (int e = e0 + static_cast<int>(threadIdx.x); e < e1; e += Cf::THREADS) {
+    const int row = e / BM;
+    const int col = tile * BM + (e % BM);
+    if (row >= p.m || col >= p.n) continue;
+    const uint32_t local = ring + 4u * static_cast<uint32_t>(e);
+    float sum = 0.f;
+    for (uint32_t s = 0; s < nsplit; ++s) sum += ld_dsmem(dsmem_addr(local, s));
+    float* dst = p.c + static_cast<int64_t>(row) * p.ldc + col;
+    float prev = 0.f;
+    if (p.bias != nullptr) prev = __ldg(p.bias + col);
+    else if (p.use_prev) prev = *dst;
+    *dst = epilogue_value(sum, prev, p.alpha, p.beta, p.act);
   }
   cluster_sync();  // no CTA leaves while another still reads its shared memory
   tc_fence_after();
@@ -470,7 +428,7 @@ __global__ void __launch_bounds__(Cfg<MB, SPLIT3>::THREADS, Cfg<MB, SPLIT3>::CTA
   }
 }
 
-template <int MB, bool SPLIT3, bool PROG>
+template <int MB, bool SPLIT3>
 int launch(Params& p, int tiles, int sms, cudaStream_t stream, int dev) {
   using Cf = Cfg<MB, SPLIT3>;
   // Splits of K per tile: as many as keep every CTA resident in one wave.
@@ -481,7 +439,7 @@ int launch(Params& p, int tiles, int sms, cudaStream_t stream, int dev) {
   static std::once_flag once[64];
   static cudaError_t attr_err[64];
   std::call_once(once[dev & 63], [&]() {
-    attr_err[dev & 63] = cudaFuncSetAttribute(gemm_ws_kernel<MB, SPLIT3, PROG>,
+    attr_err[dev & 63] = cudaFuncSetAttribute(gemm_ws_kernel<MB, SPLIT3>,
                                               cudaFuncAttributeMaxDynamicSharedMemorySize,
                                               Cf::SMEM_BYTES);
   });
@@ -502,18 +460,13 @@ int launch(Params& p, int tiles, int sms, cudaStream_t stream, int dev) {
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 2;
-  TVR_CUDA_TRY(cudaLaunchKernelEx(&cfg, gemm_ws_kernel<MB, SPLIT3, PROG>, p));
+  TVR_CUDA_TRY(cudaLaunchKernelEx(&cfg, gemm_ws_kernel<MB, SPLIT3>, p));
   return TVR_OK;
 }
 
 template <int MB>
-int launch_mb(Params& p, bool split3, bool prog, int tiles, int sms, cudaStream_t s, int dev) {
-  if (prog) {
-    return split3 ? launch<MB, true, true>(p, tiles, sms, s, dev)
-                  : launch<MB, false, true>(p, tiles, sms, s, dev);
-  }
-  return split3 ? launch<MB, true, false>(p, tiles, sms, s, dev)
-                : launch<MB, false, false>(p, tiles, sms, s, dev);
+int launch_mb(Params& p, bool split3, int tiles, int sms, cudaStream_t s, int dev) {
+  return split3 ? launch<MB, true>(p, tiles, sms, s, dev) : launch<MB, false>(p, tiles, sms, s, dev);
 }
 
 }  // namespace ws
@@ -527,7 +480,7 @@ bool gemm_ws_applies(const float* x, const float* w, int64_t m, int64_t n, int64
 
 int gemm_ws(const float* x, const float* w, const float* bias, float* c, int64_t m, int64_t n,
             int64_t k, int64_t ldx, int64_t ldw, int64_t ldc, float alpha, float beta, int act,
-            bool split3, cudaStream_t stream, const EpiProg* prog) {
+            bool split3, cudaStream_t stream) {
   using namespace ws;
   const int dev = current_device();
   const int sms = sm_count(dev);
@@ -551,13 +504,11 @@ int gemm_ws(const float* x, const float* w, const float* bias, float* c, int64_t
   p.n = static_cast<int>(n);
   p.num_kb = num_kb;
   p.status = device_status_ptr(dev);
-  const bool has_prog = prog != nullptr && prog->n_nodes > 0;
-  if (has_prog) p.prog = *prog;
   switch (mb) {
-    case 16: return launch_mb<16>(p, split3, has_prog, tiles, sms, stream, dev);
-    case 32: return launch_mb<32>(p, split3, has_prog, tiles, sms, stream, dev);
-    case 64: return launch_mb<64>(p, split3, has_prog, tiles, sms, stream, dev);
-    default: return launch_mb<128>(p, split3, has_prog, tiles, sms, stream, dev);
+    case 16: return launch_mb<16>(p, split3, tiles, sms, stream, dev);
+    case 32: return launch_mb<32>(p, split3, tiles, sms, stream, dev);
+    case 64: return launch_mb<64>(p, split3, tiles, sms, stream, dev);
+    default: return launch_mb<128>(p, split3, tiles, sms, stream, dev);
   }
 }
 

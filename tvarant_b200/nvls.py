@@ -26,6 +26,27 @@ from . import capi
 FLAG_WORDS = 3 * 64 * 8 + 4096  # TVR_NVLS_FLAG_WORDS
 
 
+def multicast_supported(device: int) -> bool:
+    """Whether this GPU can bind symmetric memory to an NVLink multicast object."""
+    try:
+        import torch.distributed._symmetric_memory as symm_mem
+        from torch._C._distributed_c10d import _SymmetricMemory
+
+        return bool(_SymmetricMemory.has_multicast_support(symm_mem.DeviceType.CUDA, device))
+    except Exception:
+        return False
+
+
+def agreed_multicast(device: int, group=None) -> bool:
+    """multicast_supported on every rank of ``group`` (one collective, so every
+    rank takes the same exchange)."""
+    import torch.distributed as dist
+
+    flag = torch.tensor([1 if multicast_supported(device) else 0], dtype=torch.int32)
+    dist.all_reduce(flag, op=dist.ReduceOp.MIN, group=group)
+    return bool(flag.item())
+
+
 class NvlsAllReduce:
     """A symmetric fp32 buffer of ``numel`` values and its in-place all-reduce."""
 

@@ -19,7 +19,6 @@ those workloads.  All work runs through the torch_tvarant device API.
 
 from __future__ import annotations
 
-import os
 import statistics
 import time
 
@@ -27,14 +26,6 @@ import torch
 
 D_MODEL, D_FF, LAYERS, TOKENS = 4096, 11008, 32, 8192
 
-# Kernel forms chosen by environment variables, read by the library at its
-# first use: pointwise programs in the few-row GEMM's epilogue.
-KERNEL_OPTIONS = ("TVARANT_WS_PROGRAM",)
-
-
-def kernel_options() -> dict:
-    """The kernel-form switches set for this process (for the JSON line)."""
-    return {name: os.environ.get(name) == "1" for name in KERNEL_OPTIONS}
 
 
 def _events():
@@ -410,8 +401,15 @@ def _mlp(args, rank, world, local_rank):
     dev = f"tvarant:{local_rank}"
     layers = build_stack(rank, world, dev, layers=args.layers)
     comm, nvls = None, None
-    use_nvls = world > 1 and args.comm in ("nvls", "nvls-fused")
-    fused = use_nvls and args.comm == "nvls-fused" and args.mode == "tf32"
+    kind = args.comm
+    if world > 1 and kind == "auto":
+        # this library's NVLS all-reduce where the switch supports it (every
+        # rank must agree), else NCCL's
+        from tvarant_b200.nvls import agreed_multicast
+
+        kind = "nvls" if agreed_multicast(local_rank) else "nccl"
+    use_nvls = world > 1 and kind in ("nvls", "nvls-fused")
+    fused = use_nvls and kind == "nvls-fused" and args.mode == "tf32"
     if use_nvls:
         from tvarant_b200.nvls import NvlsAllReduce
 
@@ -521,7 +519,6 @@ def _mlp(args, rank, world, local_rank):
                                 else ("NCCL all-reduce" if world > 1 else None)),
                    "nccl_max_ctas": args.nccl_ctas if comm is not None else None,
                    "gemm_sms": args.gemm_sms if world > 1 else None,
-                   "kernel_options": kernel_options(),
                    "cuda_graph": not args.no_graph,
                    "eager_tokens_per_s": TOKENS / (eager_ms / 1e3),
                    "layer_ms_one_rank_gemms": layer_ms,
@@ -681,7 +678,6 @@ def _gpt2_decode(args, rank, world, local_rank):
                    "prefill_ms": prefill_ms, "parallelism": f"replicas x{world}",
                    "weights_mb": weight_bytes / 1e6,
                    "kv_cache_read_mb_per_step": kv_bytes / 1e6,
-                   "kernel_options": kernel_options(),
                    "l2": "the 0.5 GB of weights exceed L2; every step streams them"},
         "roofline": {"bound": "hbm", "achieved": step_bytes / (ms / 1e3) / 1e9,
                      "peak": peak_gbs, "unit": "GB/s",
@@ -774,7 +770,6 @@ def _gpt2(args, rank, world, local_rank):
                                   else "fused scaled_dot_product_attention (TF32 kernel)")
                                + ", tied LM head",
                    "attention": att,
-                   "kernel_options": kernel_options(),
                    "cuda_graph": not args.no_graph,
                    "eager_tokens_per_s": batch * seq / (eager_ms / 1e3),
                    "parallelism": f"batch split over {world} rank(s) (attention split over batch x heads)",
