@@ -393,6 +393,82 @@ def build_stack(rank: int, world: int, device: str, layers: int = LAYERS, seed: 
     return out
 
 
+class _StackIO:
+    """End-to-end steps of the tensor-parallel stack with host buffers.
+
+    Rank r owns tokens [r * T/N, (r + 1) * T/N) of the job's input and output
+    (T tokens, N ranks).  Per step: its input slice is copied in from pinned
+    host memory on one copy stream, one step ahead of the compute (two device
+    slice buffers); on the compute stream the slices of all ranks are gathered
+    (NCCL all-gather) into the stack's input — on one GPU the slice is the
+    whole input and is copied device to device — the stack runs, and the
+    rank's slice of the output is copied aside and sent back to pinned host
+    memory on another copy stream (two buffers)."""
+
+    def __init__(self, x, x_host, out_host, run, rank, world, comm, device):
+        from tvarant_b200 import _C
+
+        self._C = _C
+        self.x, self.run, self.world, self.comm = x, run, world, comm
+        self.rows = x.shape[0] // world
+        self.r0 = rank * self.rows
+        dev = f"tvarant:{device}"
+        self.s_in = torch.Stream(device=dev)
+        self.s_out = torch.Stream(device=dev)
+        self.dev = dev
+        self.slices = [torch.empty(self.rows, x.shape[1], device=dev) for _ in range(2)]
+        self.outs = [torch.empty(self.rows, x.shape[1], device=dev) for _ in range(2)]
+        self.host_in = x_host[self.r0:self.r0 + self.rows]
+        spare = torch.empty(self.rows, x.shape[1])
+        if torch.cuda.is_available():
+            spare = spare.pin_memory()
+        self.host_out = [out_host[self.r0:self.r0 + self.rows], spare]
+        self.consumed = [None, None]
+        self.drained = [None, None]
+        self.j = 0
+
+    def _event(self, stream):
+        ev = torch.Event(device=self.dev)
+        ev.record(stream)
+        return ev
+
+    def begin(self):
+        """Orders both copy streams after the work queued so far."""
+        start = self._event(torch.tvarant.current_stream())
+        self.s_in.wait_event(start)
+        self.s_out.wait_event(start)
+
+    def end(self):
+        """Orders the compute stream after both copy streams."""
+        compute = torch.tvarant.current_stream()
+        compute.wait_event(self._event(self.s_in))
+        compute.wait_event(self._event(self.s_out))
+
+    def step(self):
+        k = self.j & 1
+        self.j += 1
+        compute = torch.tvarant.current_stream()
+        if self.consumed[k] is not None:
+            self.s_in.wait_event(self.consumed[k])  # slice k gathered two steps ago
+        with torch.tvarant.stream(self.s_in):
+            self.slices[k].copy_(self.host_in, non_blocking=True)
+            landed = self._event(self.s_in)
+        compute.wait_event(landed)
+        if self.world > 1:
+            self._C.all_gather(self.slices[k], self.x, self.comm.handle)
+        else:
+            self.x.copy_(self.slices[k])
+        self.consumed[k] = self._event(compute)
+        y = self.run(self.x)
+        if self.drained[k] is not None:
+            compute.wait_event(self.drained[k])  # out buffer k sent two steps ago
+        self.outs[k].copy_(y[self.r0:self.r0 + self.rows])
+        self.s_out.wait_event(self._event(compute))
+        with torch.tvarant.stream(self.s_out):
+            self.host_out[k].copy_(self.outs[k], non_blocking=True)
+            self.drained[k] = self._event(self.s_out)
+
+
 def _mlp(args, rank, world, local_rank):
     import bench
     from tvarant_b200.tp import Communicator, TPMLPStack
@@ -470,17 +546,35 @@ def _mlp(args, rank, world, local_rank):
         _C.set_gemm_sm_limit(local_rank, prev_limit)
     swiglu_flops = 2.0 * rows * (2 * wg.shape[0]) * D_MODEL
 
-    def e2e_step():
-        x.copy_(x_host, non_blocking=True)
-        out_host.copy_(run(x), non_blocking=True)
-
-    e2e_step()
+    # End to end: each rank brings its slice of the tokens in from pinned host
+    # memory and sends its slice of the output back; the slices are gathered
+    # over NVLink into the stack's input.  An NCCL communicator serves that
+    # gather when the stack's own exchange is NVLS.
+    gather = comm
+    if world > 1 and gather is None:
+        gather = Communicator.from_process_group(local_rank, args.nccl_ctas)
+    io = _StackIO(x, x_host, out_host, run, rank, world, gather, local_rank)
+    for _ in range(2):
+        io.begin()
+        io.step()
+        io.end()
     torch.tvarant.synchronize()
     bench._barrier(world)
-    e2e_ms = bench._max_over_ranks(_time_steps(e2e_step, args.steps), world)
+    e0, e1 = _events()
+    e0.record()
+    io.begin()
+    for _ in range(args.steps):
+        io.step()
+    io.end()
+    e1.record()
+    e1.synchronize()
+    e2e_ms = bench._max_over_ranks(e0.elapsed_time(e1) / args.steps, world)
     status = torch.tvarant.get_status()
     if not args.no_graph:
         graph.close()
+    if gather is not None and gather is not comm:
+        bench._barrier(world)
+        gather.destroy()
     if comm is not None:
         bench._barrier(world)
         comm.destroy()
@@ -525,7 +619,12 @@ def _mlp(args, rank, world, local_rank):
                    "l2": "weights per rank exceed L2 at tp<=4; activations 134 MB"},
         "e2e": {"value": TOKENS / (e2e_ms / 1e3), "unit": "tokens/s",
                 "h2d_bytes_per_step": TOKENS * D_MODEL * 4,
-                "d2h_bytes_per_step": TOKENS * D_MODEL * 4, "ms_per_step": e2e_ms},
+                "d2h_bytes_per_step": TOKENS * D_MODEL * 4, "ms_per_step": e2e_ms,
+                "per_rank_bytes_each_way": io.rows * D_MODEL * 4,
+                "pipeline": "each rank copies its 1/N of the tokens in from pinned host memory "
+                            "on a copy stream (one step ahead), the slices are gathered into "
+                            "the stack's input" + (" by an NCCL all-gather" if world > 1 else "")
+                            + ", and its 1/N of the output goes back on another copy stream"},
         "roofline": {"bound": "tensor",
                      "achieved": swiglu_tflops, "peak": kpeak, "unit": "TFLOP/s",
                      "frac": swiglu_tflops / kpeak,
