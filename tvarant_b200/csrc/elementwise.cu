@@ -378,18 +378,36 @@ __global__ void __launch_bounds__(kThreads) strided_copy_fast_kernel(T* __restri
                                                                      const T* __restrict__ src,
                                                                      CopyIndexFast ix, int ndim,
                                                                      uint32_t n) {
+  // Four elements per thread and step, all four loads issued before the
+  // stores, so each thread keeps four reads in flight.
+  constexpr int U = 4;
   const uint32_t stride = gridDim.x * blockDim.x;
-  for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
-    uint32_t rem = i;
-    uint32_t od = 0, os = 0;
-    for (int d = ndim - 1; d >= 0; --d) {
-      const uint32_t q = fast_div(rem, ix.div[d]);
-      const uint32_t c = rem - q * ix.div[d].d;
-      rem = q;
-      od += c * ix.sd[d];
-      os += c * ix.ss[d];
+  for (uint32_t i0 = blockIdx.x * blockDim.x + threadIdx.x; i0 < n; i0 += U * stride) {
+    uint32_t od[U], os[U];
+    T v[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const uint32_t i = i0 + u * stride;
+      uint32_t rem = i < n ? i : 0;
+      uint32_t a = 0, b = 0;
+      for (int d = ndim - 1; d >= 0; --d) {
+        const uint32_t q = fast_div(rem, ix.div[d]);
+        const uint32_t c = rem - q * ix.div[d].d;
+        rem = q;
+        a += c * ix.sd[d];
+        b += c * ix.ss[d];
+      }
+      od[u] = a;
+      os[u] = b;
     }
-    dst[od] = src[os];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      if (i0 + u * stride < n) v[u] = src[os[u]];
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      if (i0 + u * stride < n) dst[od[u]] = v[u];
+    }
   }
 }
 
