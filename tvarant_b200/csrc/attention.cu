@@ -5,25 +5,31 @@
 // the fused kernel is a roadmap item — so this kernel serves
 // F.scaled_dot_product_attention on the tvarant device (TF32 mode).
 //
-// One CTA per (128-query tile, batch x head), two CTAs per SM.  Head
-// dimension 64.
-//   warp 0     TMA producers: lane 0 loads the Q tile once and the K tile of
-//              each block of 64 keys, lane 1 the V tiles (two buffers each),
-//              straight from strided [B, H, S, 64] views (no head-split
-//              copies);
-//   warp 1     TMEM owner; lane 0 issues S_j = Q K_j^T (M=128, N=64, K=64)
-//              into one of two TMEM score buffers, ahead of the softmax;
-//              lane 1 issues PV_j = P_j V_j (M=128, N=64, K=64) with P_j read
-//              from tensor memory and V as an N-major operand, accumulating O
-//              in tensor memory over all blocks;
+// Persistent: two CTAs per SM, each working through its share of the units
+// (a unit is one 128-query tile of one (batch, head)), heaviest first in a
+// snake order over the CTAs.  Tensor memory, barriers and their phases carry
+// over from one unit to the next.  (With one CTA per unit the block
+// scheduler refilled an SM only once both of its CTAs had exited, so under
+// the causal mask, where tiles differ in length up to 16x, an SM ran one CTA
+// for much of the time.)  Head dimension 64.
+//   warp 0     TMA producer: lane 0 loads each unit's Q tile and the K and V
+//              tiles of each block of 64 keys (two buffers each), straight
+//              from strided [B, H, S, 64] views (no head-split copies), with
+//              an L2 prefetch two blocks ahead;
+//   warp 1     TMEM owner; lane 0 issues every MMA in a fixed order:
+//              PV_j = P_j V_j (M=128, N=64, K=64) as soon as P_j is written,
+//              then S_{j+3} = Q K_{j+3}^T (M=128, N=64, K=64) into the TMEM
+//              score buffer PV_j has just read, so the scores run three
+//              blocks ahead of the softmax; P_j is read from tensor memory,
+//              V as an N-major operand, and O accumulates in tensor memory;
 //   warps 2-5  one thread per query row: online softmax in the log2 domain
 //              over the row's 64 scores of a block (two TMEM loads in flight,
 //              one wait), P_j written back over S_j in tensor memory.  The
 //              running maximum is raised lazily (only when a block's maximum
 //              exceeds it by more than 2^8), and only then are the warp's rows
 //              of O rescaled in tensor memory; O / l does not depend on which
-//              maximum was used.  At the end O / l is stored and the
-//              log-sum-exp (natural log) is written.
+//              maximum was used.  At the end of a unit O / l is stored
+//              and the log-sum-exp (natural log) is written.
 // Without P tiles in shared memory a CTA needs 97 KB, so two CTAs share an SM
 // and each SM scheduler holds two softmax warps.
 // Causal masking follows PyTorch's is_causal (key index <= query index,
@@ -36,6 +42,7 @@
 #include <cmath>
 #include <cstring>
 #include <mutex>
+#include <type_traits>
 
 #include "tc_ptx.cuh"
 
@@ -53,10 +60,11 @@ constexpr int Q_BYTES = BM * D * 4;      // D/32 atoms
 constexpr int K_BYTES = BN * D * 4;      // D/32 atoms
 constexpr int V_ATOM = BN * 128;         // one 32-wide slice of the head dimension: [64 keys x 128 B]
 constexpr int V_BYTES = BN * D * 4;      // D/32 atoms
-constexpr int STAGES = 2;                // K, V and the TMEM score buffers are double-buffered
+constexpr int STAGES = 2;                // K and V tiles are double-buffered
+constexpr int SBUF = 3;                  // TMEM score / P buffers: S runs this many blocks ahead of PV
 constexpr int THREADS = 192;
-constexpr uint32_t TMEM_COLS = 256;      // S / P buffers at 0 and 64, O at 128
-constexpr uint32_t PV_COL = 2 * BN;
+constexpr uint32_t TMEM_COLS = 256;      // S / P buffers at 0, 64 and 128, O at 192
+constexpr uint32_t PV_COL = SBUF * BN;
 constexpr float kLazyLog2 = 8.f;         // raise the running maximum past 2^8 growth
 constexpr int BAR_BYTES = 8 * 24;
 constexpr int SMEM_BYTES = 1024 + Q_BYTES + STAGES * (K_BYTES + V_BYTES) + BAR_BYTES;
@@ -75,6 +83,58 @@ struct Params {
   int* status;
   const int64_t* key_len;    // non-null: attend to clamp(*key_len + key_len_add, 1, seq_k) keys
   int key_len_add;
+  int batch_heads;           // batch * heads
+  int nqt;                   // query tiles per (batch, head)
+  int units;                 // nqt * batch_heads
+};
+
+// One unit of work: a 128-query tile of one (batch, head).
+struct Tile {
+  int b, h, q0, nkb;
+};
+
+// The n-th unit of this CTA, or -1.  Units are numbered heaviest first (under
+// the causal mask the last query tiles see the most keys); CTA c takes unit c
+// of the first round of gridDim.x units, unit gridDim.x - 1 - c of the
+// second, and so on (a snake order), which evens out the CTAs' total work.
+__device__ __forceinline__ int cta_unit(int n, int units) {
+  const long long ctas = gridDim.x;
+  const long long c = blockIdx.x;
+  const long long idx = n * ctas + ((n & 1) ? ctas - 1 - c : c);
+  return idx < units ? static_cast<int>(idx) : -1;
+}
+
+__device__ __forceinline__ Tile tile_of(const Params& p, int idx, int kblocks) {
+  const int rank = idx / p.batch_heads;
+  const int bh = idx - rank * p.batch_heads;
+  Tile t;
+  t.b = bh / p.heads;
+  t.h = bh - t.b * p.heads;
+  t.q0 = (p.nqt - 1 - rank) * BM;
+  t.nkb = p.causal ? min(kblocks, (min(t.q0 + BM, p.seq_q) - 1) / BN + 1) : kblocks;
+  return t;
+}
+
+// Walks this CTA's key blocks in order: block j of its unit n.  Every role
+// keeps one, so the barrier phases run on across units.
+struct BlockCursor {
+  int n, idx, j;
+  Tile t;
+  __device__ __forceinline__ void start(const Params& p, int kblocks) {
+    n = 0;
+    j = 0;
+    idx = cta_unit(0, p.units);
+    if (idx >= 0) t = tile_of(p, idx, kblocks);
+  }
+  __device__ __forceinline__ bool valid() const { return idx >= 0; }
+  __device__ __forceinline__ bool last_of_unit() const { return j == t.nkb - 1; }
+  __device__ __forceinline__ void advance(const Params& p, int kblocks) {
+    if (++j == t.nkb) {
+      j = 0;
+      idx = cta_unit(++n, p.units);
+      if (idx >= 0) t = tile_of(p, idx, kblocks);
+    }
+  }
 };
 
 // N-major V operand: 32-wide atoms of the head dimension, each [64 keys x
@@ -99,7 +159,19 @@ __device__ __forceinline__ void store_row(const Params& p, int b, int h, int qid
                                           float m, float l) {
   const float inv = l > 0.f ? 1.f / l : 0.f;
   float* dst = p.out + b * p.o_sb + h * p.o_sh + static_cast<int64_t>(qidx) * p.o_ss;
-  if ((reinterpret_cast<uintptr_t>(dst) & 15u) == 0) {
+  if ((reinterpret_cast<uintptr_t>(dst) & 31u) == 0) {
+    // 32-byte stores: every lane of a warp writes a different row, so each
+    // store instruction touches 32 rows; whole sectors halve the instructions
+    // and leave no partly written sector
+#pragma unroll
+    for (int i = 0; i < D / 8; ++i) {
+      const float* v = o + 8 * i;
+      asm volatile("st.global.v8.f32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(dst + 8 * i),
+                   "f"(v[0] * inv), "f"(v[1] * inv), "f"(v[2] * inv), "f"(v[3] * inv),
+                   "f"(v[4] * inv), "f"(v[5] * inv), "f"(v[6] * inv), "f"(v[7] * inv)
+                   : "memory");
+    }
+  } else if ((reinterpret_cast<uintptr_t>(dst) & 15u) == 0) {
 #pragma unroll
     for (int i = 0; i < D / 4; ++i) {
       reinterpret_cast<float4*>(dst)[i] =
@@ -127,48 +199,42 @@ __global__ void __launch_bounds__(THREADS, 2) attn_fwd_kernel(const __grid_const
   const uint32_t sv = sk + STAGES * K_BYTES;        // [2] V tiles
   // mbarriers, one 8-byte slot each; [2] = one per buffer
   const uint32_t bar = sv + STAGES * V_BYTES;
+  // One commit per MMA block: s_done (the scores of block g are in buffer
+  // g % 3 and K buffer g & 1 is free) and pv_done (the P of block g has been
+  // read, so its score buffer and V buffer g & 1 are free, and O holds it).
   const uint32_t q_full = bar;
   const uint32_t k_full = bar + 8;       // [2]
-  const uint32_t k_empty = bar + 24;     // [2]
-  const uint32_t v_full = bar + 40;      // [2]
-  const uint32_t v_empty = bar + 56;     // [2]
-  const uint32_t s_full = bar + 72;      // [2]
-  const uint32_t s_empty = bar + 88;     // [2]
-  const uint32_t p_full = bar + 104;     // [2]
-  const uint32_t pv_full = bar + 120;    // [2]
+  const uint32_t v_full = bar + 24;      // [2]
+  const uint32_t s_done = bar + 40;      // [3] one per score buffer
+  const uint32_t p_full = bar + 64;      // [3]
+  const uint32_t pv_done = bar + 88;     // [3]
+  const uint32_t q_empty = bar + 112;    // every S of a unit read its Q tile
   const uint32_t drain = smem_u32(&s_drain);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const volatile int* abort_flag = &s_abort;
-  const int bh = blockIdx.y;
-  const int b = bh / p.heads;
-  const int h = bh - b * p.heads;
-  const int qt = static_cast<int>(gridDim.x) - 1 - static_cast<int>(blockIdx.x);  // heavy tiles first
-  const int q0 = qt * BM;
   // the key count: the buffers' extent, or a length held in device memory
   // (written by earlier work on the stream, e.g. a KV cache's fill level)
   const int seq_k = p.key_len != nullptr
                         ? max(1, min(p.seq_k, static_cast<int>(*p.key_len) + p.key_len_add))
                         : p.seq_k;
   const int kblocks = (seq_k + BN - 1) / BN;
-  const int nkb = p.causal ? min(kblocks, (min(q0 + BM, p.seq_q) - 1) / BN + 1) : kblocks;
 
   if (threadIdx.x == 0) {
     s_abort = 0;
     mbar_init(q_full, 1);
-    for (int i = 0; i < 2; ++i) {
+    mbar_init(q_empty, 1);
+    for (int i = 0; i < STAGES; ++i) {
       mbar_init(k_full + 8 * i, 1);
-      mbar_init(k_empty + 8 * i, 1);
       mbar_init(v_full + 8 * i, 1);
-      mbar_init(v_empty + 8 * i, 1);
-      mbar_init(s_full + 8 * i, 1);
-      // S buffer free: PV read the P written over it (one commit)
-      mbar_init(s_empty + 8 * i, 1);
-      mbar_init(p_full + 8 * i, 4);
-      mbar_init(pv_full + 8 * i, 1);
     }
-    mbar_init(drain, 2);
+    for (int i = 0; i < SBUF; ++i) {
+      mbar_init(s_done + 8 * i, 1);
+      mbar_init(p_full + 8 * i, 4);
+      mbar_init(pv_done + 8 * i, 1);
+    }
+    mbar_init(drain, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 1) {
@@ -187,102 +253,173 @@ __global__ void __launch_bounds__(THREADS, 2) attn_fwd_kernel(const __grid_const
   if (threadIdx.x == 0) grid_launch_dependents();
 
   if (warp == 0) {
-    // ------------------------------ TMA producers ------------------------------
-    // lane 0: Q, then K_j into K buffer j & 1 once S_{j-2} has consumed it;
-    // lane 1: V_j into V buffer j & 1 once PV_{j-2} has consumed it.
-    if (lane < 2) {
-      const bool is_k = lane == 0;
-      const uint32_t full = is_k ? k_full : v_full;
-      const uint32_t empty = is_k ? k_empty : v_empty;
+    // ------------------------------ TMA producer ------------------------------
+    // One thread.  It replays the MMA thread's order (S of this CTA's blocks
+    // 0, 1 and 2, then per block g: PV_g, S_{g+3}) and after each MMA loads what
+    // that MMA frees: after S_g the K tile of block g + 2 (preceded by the
+    // next unit's Q tile when block g ends a unit), after PV_g the V tile of
+    // block g + 2.  The loads go out in the order in which their buffers
+    // free up; two producer lanes of one warp took turns in their barrier
+    // waits.  Every K and V tile is also prefetched into L2 two blocks before
+    // its load: the query tiles of a head read each tile at about the same
+    // time, so its first reads come from HBM.
+    if (lane == 0) {
       bool ok = true;
-      int issued = 0;
-      if (is_k) {
+      int gk = 0, gv = 0, nq = 0;  // K, V and Q tiles loaded
+      BlockCursor sc, pc, kc, vc;  // S and PV replay, next K and V tile
+      sc.start(p, kblocks);
+      pc = sc;
+      kc = sc;
+      vc = sc;
+      // Q of unit nq once every S of unit nq - 1 has read the buffer
+      auto load_q = [&](const Tile& t) -> bool {
+        if (nq >= 1 && !mbar_wait(q_empty, (nq - 1) & 1, abort_flag)) return false;
         mbar_expect_tx(q_full, Q_BYTES);
-        for (int a = 0; a < D / 32; ++a) tma_load_4d(sq + a * Q_ATOM, &p.tma_q, q_full, 32 * a, q0, h, b);
-      }
-      for (int j = 0; j < nkb; ++j) {
-        const int st = j & 1;
-        if (j >= 2 && !mbar_wait(empty + 8 * st, ((j >> 1) - 1) & 1, abort_flag)) {
-          ok = false;
-          break;
+        for (int a = 0; a < D / 32; ++a) tma_load_4d(sq + a * Q_ATOM, &p.tma_q, q_full, 32 * a, t.q0, t.h, t.b);
+        ++nq;
+        return true;
+      };
+      // kc's K tile into K buffer gk & 1 once S of block gk - 2 has read it
+      auto load_k = [&]() -> bool {
+        const int st = gk & 1;
+        if (gk >= STAGES && !mbar_wait(s_done + 8 * ((gk - 2) % SBUF), ((gk - 2) / SBUF) & 1, abort_flag)) {
+          return false;
         }
-        const uint32_t fb = full + 8 * st;
-        if (is_k) {
-          mbar_expect_tx(fb, K_BYTES);
-          for (int a = 0; a < D / 32; ++a)
-            tma_load_4d(sk + st * K_BYTES + a * K_ATOM, &p.tma_k, fb, 32 * a, j * BN, h, b);
-        } else {
-          mbar_expect_tx(fb, V_BYTES);
-          for (int a = 0; a < D / 32; ++a)
-            tma_load_4d(sv + st * V_BYTES + a * V_ATOM, &p.tma_v, fb, 32 * a, j * BN, h, b);
+        const uint32_t fb = k_full + 8 * st;
+        mbar_expect_tx(fb, K_BYTES);
+        for (int a = 0; a < D / 32; ++a)
+          tma_load_4d(sk + st * K_BYTES + a * K_ATOM, &p.tma_k, fb, 32 * a, kc.j * BN, kc.t.h, kc.t.b);
+        ++gk;
+        BlockCursor ahead = kc;
+        ahead.advance(p, kblocks);
+        ahead.advance(p, kblocks);
+        if (ahead.valid()) {
+          for (int a = 0; a < D / 32; ++a) {
+            tma_prefetch_l2_4d(&p.tma_k, 32 * a, ahead.j * BN, ahead.t.h, ahead.t.b);
+            tma_prefetch_l2_4d(&p.tma_v, 32 * a, ahead.j * BN, ahead.t.h, ahead.t.b);
+          }
         }
-        issued = j + 1;
+        kc.advance(p, kblocks);
+        return true;
+      };
+      // vc's V tile into V buffer gv & 1 once PV of block gv - 2 has read it
+      auto load_v = [&]() -> bool {
+        const int st = gv & 1;
+        if (gv >= STAGES && !mbar_wait(pv_done + 8 * ((gv - 2) % SBUF), ((gv - 2) / SBUF) & 1, abort_flag)) {
+          return false;
+        }
+        const uint32_t fb = v_full + 8 * st;
+        mbar_expect_tx(fb, V_BYTES);
+        for (int a = 0; a < D / 32; ++a)
+          tma_load_4d(sv + st * V_BYTES + a * V_ATOM, &p.tma_v, fb, 32 * a, vc.j * BN, vc.t.h, vc.t.b);
+        ++gv;
+        vc.advance(p, kblocks);
+        return true;
+      };
+      // S of sc's block issued: the next unit's Q after a unit's last block,
+      // then the K tile two blocks on
+      auto after_s = [&]() -> bool {
+        if (sc.last_of_unit()) {
+          BlockCursor next = sc;
+          next.advance(p, kblocks);
+          if (next.valid() && !load_q(next.t)) return false;
+        }
+        if (kc.valid() && !load_k()) return false;
+        sc.advance(p, kblocks);
+        return true;
+      };
+      if (sc.valid()) {
+        ok = load_q(sc.t);
+        for (int i = 0; ok && i < STAGES && kc.valid(); ++i) ok = load_k();
+        for (int i = 0; ok && i < STAGES && vc.valid(); ++i) ok = load_v();
+        for (int i = 0; ok && i < SBUF && sc.valid(); ++i) ok = after_s();
+        while (ok && pc.valid()) {
+          if (vc.valid()) ok = load_v();
+          pc.advance(p, kblocks);
+          if (ok && sc.valid()) ok = after_s();
+        }
       }
       if (!ok) {
         record_status(p.status, TVR_DEV_TIMEOUT_PRODUCER);
         *const_cast<volatile int*>(abort_flag) = 1;
       }
       // every issued load lands before the CTA may exit
-      if (is_k && !mbar_wait(q_full, 0, nullptr)) record_status(p.status, TVR_DEV_TIMEOUT_DRAIN);
-      for (int j = max(0, issued - 2); j < issued; ++j) {
-        if (!mbar_wait(full + 8 * (j & 1), (j >> 1) & 1, nullptr)) record_status(p.status, TVR_DEV_TIMEOUT_DRAIN);
+      if (nq > 0 && !mbar_wait(q_full, (nq - 1) & 1, nullptr)) record_status(p.status, TVR_DEV_TIMEOUT_DRAIN);
+      for (int g = max(0, gk - STAGES); g < gk; ++g) {
+        if (!mbar_wait(k_full + 8 * (g & 1), (g >> 1) & 1, nullptr)) record_status(p.status, TVR_DEV_TIMEOUT_DRAIN);
+      }
+      for (int g = max(0, gv - STAGES); g < gv; ++g) {
+        if (!mbar_wait(v_full + 8 * (g & 1), (g >> 1) & 1, nullptr)) record_status(p.status, TVR_DEV_TIMEOUT_DRAIN);
       }
     }
     __syncwarp();
   } else if (warp == 1) {
-    // ------------------------------ MMA issuers ------------------------------
-    // Two threads issue independently, so that neither stream of MMAs waits
-    // behind the other's operands: lane 0 the scores S_i = Q K_i^T into score
-    // buffer i & 1 (free once PV_{i-2} has read the P written over S_{i-2}),
-    // lane 1 the products PV_j = P_j V_j, accumulated into O.  Each commits
-    // its own barriers and, at the end, the drain barrier (count 2) that TMEM
-    // release waits for.
-    if (lane < 2) {
+    // ------------------------------ MMA issuer ------------------------------
+    // One thread, one fixed order over this CTA's key blocks (all its units
+    // in turn): S of blocks 0, 1 and 2, then for each block g the product
+    // PV_g (once P_g and V_g are in place) followed by S_{g+3} into score
+    // buffer g % 3 as soon as PV_g has read the P there.  The scores run
+    // three blocks ahead of the softmax, across units too, so a softmax warp
+    // finds the next block's scores done when it finishes one: the thread is
+    // held to the tensor core's pace while it issues (the MMA queue is
+    // shallow), and scores issued only two blocks ahead, behind PV_g, came
+    // ~0.6 us late per block.  (Two issuing lanes of one warp took turns in
+    // their barrier waits and delayed each PV by ~0.7 us.)  The drain commit
+    // at the end arrives once every MMA retired.
+    if (lane == 0) {
       constexpr uint32_t idesc_s = idesc_tf32(BM, BN, false);
       constexpr uint32_t idesc_pv = idesc_tf32(BM, D, true);
+      BlockCursor sc, pc;
+      sc.start(p, kblocks);
+      pc = sc;
+      int gs = 0, gp = 0;  // S and PV issued
+      auto issue_s = [&]() -> bool {
+        const int sb = gs % SBUF;
+        const int kb = gs & 1;
+        if ((sc.j == 0 && !mbar_wait(q_full, sc.n & 1, abort_flag)) ||
+            !mbar_wait(k_full + 8 * kb, (gs >> 1) & 1, abort_flag) ||
+            (gs >= SBUF && !mbar_wait(pv_done + 8 * sb, (gs / SBUF - 1) & 1, abort_flag))) {
+          return false;
+        }
+        tc_fence_after();
+        const uint32_t d = tmem + static_cast<uint32_t>(sb * BN);
+#pragma unroll
+        for (int x = 0; x < D / 8; ++x) {
+          const uint32_t k32 = (x & 3) * 32;
+          mma_tf32(d, desc_kmajor(sq + (x >> 2) * Q_ATOM + k32),
+                   desc_kmajor(sk + kb * K_BYTES + (x >> 2) * K_ATOM + k32), idesc_s,
+                   x > 0 ? 1u : 0u);
+        }
+        mma_commit(s_done + 8 * sb);
+        if (sc.last_of_unit()) mma_commit(q_empty);  // the unit's scores have read Q
+        ++gs;
+        sc.advance(p, kblocks);
+        return true;
+      };
       bool ok = true;
-      if (lane == 0) {
-        ok = mbar_wait(q_full, 0, abort_flag);
-        for (int i = 0; ok && i < nkb; ++i) {
-          const int sb = i & 1;
-          if (!mbar_wait(k_full + 8 * sb, (i >> 1) & 1, abort_flag) ||
-              (i >= 2 && !mbar_wait(s_empty + 8 * sb, ((i >> 1) - 1) & 1, abort_flag))) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint32_t d = tmem + static_cast<uint32_t>(sb * BN);
-#pragma unroll
-          for (int x = 0; x < D / 8; ++x) {
-            const uint32_t k32 = (x & 3) * 32;
-            mma_tf32(d, desc_kmajor(sq + (x >> 2) * Q_ATOM + k32),
-                     desc_kmajor(sk + sb * K_BYTES + (x >> 2) * K_ATOM + k32), idesc_s,
-                     x > 0 ? 1u : 0u);
-          }
-          mma_commit(k_empty + 8 * sb);
-          mma_commit(s_full + 8 * sb);
+      for (int i = 0; ok && i < SBUF && sc.valid(); ++i) ok = issue_s();
+      while (ok && pc.valid()) {
+        const int pb = gp % SBUF;
+        const int vb = gp & 1;
+        if (!mbar_wait(p_full + 8 * pb, (gp / SBUF) & 1, abort_flag) ||
+            !mbar_wait(v_full + 8 * vb, (gp >> 1) & 1, abort_flag)) {
+          ok = false;
+          break;
         }
-      } else {
-        for (int j = 0; ok && j < nkb; ++j) {
-          const int pb = j & 1;
-          if (!mbar_wait(p_full + 8 * pb, (j >> 1) & 1, abort_flag) ||
-              !mbar_wait(v_full + 8 * pb, (j >> 1) & 1, abort_flag)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          // P_j sits in score buffer j & 1 (K step x: its columns 8x .. 8x+7);
-          // O accumulates in place over all blocks
-          const uint32_t pa = tmem + static_cast<uint32_t>(pb * BN);
+        tc_fence_after();
+        // P sits in score buffer gp % 3 (K step x: its columns 8x .. 8x+7);
+        // O accumulates in place over the unit's blocks (its first block
+        // overwrites it)
+        const uint32_t pa = tmem + static_cast<uint32_t>(pb * BN);
 #pragma unroll
-          for (int x = 0; x < BN / 8; ++x) {
-            mma_tf32_tmem_a(tmem + PV_COL, pa + 8u * x, desc_v(sv + pb * V_BYTES + x * 1024),
-                            idesc_pv, (j > 0 || x > 0) ? 1u : 0u);
-          }
-          mma_commit(s_empty + 8 * pb);  // P_j read: the buffer may take S_{j+2}
-          mma_commit(v_empty + 8 * pb);
-          mma_commit(pv_full + 8 * pb);
+        for (int x = 0; x < BN / 8; ++x) {
+          mma_tf32_tmem_a(tmem + PV_COL, pa + 8u * x, desc_v(sv + vb * V_BYTES + x * 1024),
+                          idesc_pv, (pc.j > 0 || x > 0) ? 1u : 0u);
         }
+        mma_commit(pv_done + 8 * pb);  // P read: the buffer may take the scores of block gp + 3
+        ++gp;
+        pc.advance(p, kblocks);
+        if (sc.valid()) ok = issue_s();
       }
       if (!ok) {
         record_status(p.status, TVR_DEV_TIMEOUT_MMA);
@@ -296,61 +433,58 @@ __global__ void __launch_bounds__(THREADS, 2) attn_fwd_kernel(const __grid_const
     __syncwarp();
   } else {
     // ------------------- softmax rows, P and O in tensor memory -------------------
-    // O accumulates in TMEM (PV_j adds P_j V_j to it).  O and l are kept
-    // relative to a running maximum m that is raised only when a block's
-    // maximum exceeds it by more than 2^kLazyLog2, or at the first visible
-    // scores; then the warp rescales its rows of O (a TMEM round trip after
-    // PV_{j-1} has landed).  Between raises P = 2^(x - m) <= 2^kLazyLog2,
-    // far from the fp32 range, and O / l is unchanged by the choice of m.
+    // O accumulates in TMEM (PV adds P V to it).  O and l are kept relative
+    // to a running maximum m that is raised only when a block's maximum
+    // exceeds it by more than 2^kLazyLog2, or at the first visible scores;
+    // then the warp rescales its rows of O (a TMEM round trip after the
+    // previous block's PV has landed).  Between raises P = 2^(x - m) <=
+    // 2^kLazyLog2, far from the fp32 range, and O / l is unchanged by the
+    // choice of m.  At the end of a unit O / l is stored; the unit's first PV
+    // is issued only after these threads have written the next unit's first
+    // P, so it cannot overwrite O before it is read.
     const int q = warp & 3;
-    const int t = 32 * q + lane;  // TMEM lane = query row within the tile
-    const int qidx = q0 + t;
+    const int tr = 32 * q + lane;  // TMEM lane = query row within the tile
     const uint32_t lane_off = static_cast<uint32_t>(32 * q) << 16;
     const uint32_t orow = tmem + lane_off + PV_COL;
     float m = -INFINITY, l = 0.f;
     bool ok = true;
-    // PV_j done: completion j >> 1 of pv_full[j & 1]
-    auto wait_pv = [&](int j) -> bool {
-      const bool got = mbar_wait(pv_full + 8 * (j & 1), (j >> 1) & 1, abort_flag);
+    // PV of block g done: completion g / 3 of pv_done[g % 3]
+    auto wait_pv = [&](int g) -> bool {
+      const bool got = mbar_wait(pv_done + 8 * (g % SBUF), (g / SBUF) & 1, abort_flag);
       return __all_sync(0xffffffffu, got);
     };
-    for (int j = 0; j < nkb; ++j) {
-      const int sb = j & 1;
-      const bool got = mbar_wait(s_full + 8 * sb, (j >> 1) & 1, abort_flag);
-      if (!__all_sync(0xffffffffu, got)) {
-        ok = false;
-        break;
-      }
-      // S_j was issued after PV_{j-2} finished, so this returns at once; it
-      // keeps the thread's view of each pv_full barrier within one phase
-      // of its state, which the parity waits below rely on
-      if (j >= 2 && !wait_pv(j - 2)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      const uint32_t srow = tmem + lane_off + static_cast<uint32_t>(sb * BN);
-      const int key0 = j * BN;
-      int key_end = min(seq_k, key0 + BN);
-      if (p.causal) key_end = min(key_end, qidx + 1);
-      const int nvis = key_end - key0;  // may be <= 0 for padding rows
-      float sc[BN];
+    // One block of this row: raise m if needed (rescaling O), write P over S
+    // and add its sum to l.  FULL: every row of the warp sees all BN keys of
+    // the block, so no column needs a visibility test.
+    auto row_block = [&](auto full_tag, float* sc, int nvis, bool first, int g,
+                         uint32_t srow) -> bool {
+      constexpr bool FULL = decltype(full_tag)::value;
+      // the block maximum of the scaled scores from the raw ones (scaling by
+      // s >= 0 keeps their order, and rounding is monotone; s < 0 reverses
+      // it), in eight independent partial maxima (and sums below): a single
+      // chain of 64 dependent operations would be the row's critical path
+      float mp[8];
 #pragma unroll
-      for (int c = 0; c < BN / 32; ++c) tmem_load_32_async(srow + 32 * c, sc + 32 * c);
-      tmem_wait_loads();
-      float mx = -INFINITY;
+      for (int r = 0; r < 8; ++r) mp[r] = -INFINITY;
+      if (p.scale_log2 >= 0.f) {
 #pragma unroll
-      for (int i = 0; i < BN; ++i) {
-        if (i < nvis) mx = fmaxf(mx, sc[i] * p.scale_log2);
+        for (int i = 0; i < BN; ++i) {
+          if (FULL || i < nvis) mp[i & 7] = fmaxf(mp[i & 7], sc[i]);
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < BN; ++i) {
+          if (FULL || i < nvis) mp[i & 7] = fmaxf(mp[i & 7], -sc[i]);
+        }
       }
+      const float mx = fmaxf(fmaxf(fmaxf(mp[0], mp[1]), fmaxf(mp[2], mp[3])),
+                             fmaxf(fmaxf(mp[4], mp[5]), fmaxf(mp[6], mp[7]))) *
+                       fabsf(p.scale_log2);
       const float m_new = fmaxf(m, mx);
       if (__any_sync(0xffffffffu, m_new > m + kLazyLog2)) {
         const float alpha = ex2(m - (m_new == -INFINITY ? 0.f : m_new));  // 0 while m = -inf
-        if (j >= 1) {
-          if (!wait_pv(j - 1)) {
-            ok = false;
-            break;
-          }
+        if (!first) {
+          if (!wait_pv(g - 1)) return false;
           tc_fence_after();
 #pragma unroll
           for (int c = 0; c < D / 32; ++c) {
@@ -366,36 +500,85 @@ __global__ void __launch_bounds__(THREADS, 2) attn_fwd_kernel(const __grid_const
         m = m_new;
       }
       const float m_use = m == -INFINITY ? 0.f : m;
-      float sum = 0.f;
+      // P over S in this row's lane, each 32-column half stored as soon as it
+      // is computed; PV reads it from there.  The wait also covers the O
+      // rescale above.
+      float sp[8];
 #pragma unroll
-      for (int i = 0; i < BN; ++i) {
-        const float e = i < nvis ? ex2(fmaf(sc[i], p.scale_log2, -m_use)) : 0.f;
-        sc[i] = e;
-        sum += e;
+      for (int r = 0; r < 8; ++r) sp[r] = 0.f;
+#pragma unroll
+      for (int c = 0; c < BN / 32; ++c) {
+#pragma unroll
+        for (int i = 32 * c; i < 32 * c + 32; ++i) {
+          const float e = (FULL || i < nvis) ? ex2(fmaf(sc[i], p.scale_log2, -m_use)) : 0.f;
+          sc[i] = e;
+          sp[i & 7] += e;
+        }
+        tmem_store_32(srow + 32 * c, sc + 32 * c);
       }
-      // P_j over S_j in this row's lane; PV_j reads it from there.  The wait
-      // also covers the O rescale above.
-#pragma unroll
-      for (int c = 0; c < BN / 32; ++c) tmem_store_32(srow + 32 * c, sc + 32 * c);
+      l += ((sp[0] + sp[1]) + (sp[2] + sp[3])) + ((sp[4] + sp[5]) + (sp[6] + sp[7]));
       tmem_wait_stores();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(p_full + 8 * sb);
-      l += sum;
-    }
-    if (ok && !wait_pv(nkb - 1)) ok = false;  // nkb >= 1: key 0 is always visible
-    if (!ok) {
-      if (lane == 0) {
-        record_status(p.status, TVR_DEV_TIMEOUT_EPILOGUE);
-        *const_cast<volatile int*>(abort_flag) = 1;
+      return true;
+    };
+    int g = 0;  // this CTA's key blocks so far, over all its units
+    for (int n = 0; ok; ++n) {
+      const int idx = cta_unit(n, p.units);
+      if (idx < 0) break;
+      const Tile t = tile_of(p, idx, kblocks);
+      const int qidx = t.q0 + tr;
+      m = -INFINITY;
+      l = 0.f;
+      for (int j = 0; j < t.nkb; ++j, ++g) {
+        const int sb = g % SBUF;
+        const bool got = mbar_wait(s_done + 8 * sb, (g / SBUF) & 1, abort_flag);
+        if (!__all_sync(0xffffffffu, got)) {
+          ok = false;
+          break;
+        }
+        // S_g was issued after PV_{g-3} had read buffer g % 3, so this
+        // returns at once; it keeps the thread's view of each pv_done barrier
+        // within one phase of its state, which the parity waits for PV_{g-1}
+        // and at the end of a unit rely on
+        if (g >= SBUF && !wait_pv(g - SBUF)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t srow = tmem + lane_off + static_cast<uint32_t>(sb * BN);
+        const int key0 = j * BN;
+        int key_end = min(seq_k, key0 + BN);
+        if (p.causal) key_end = min(key_end, qidx + 1);
+        const int nvis = key_end - key0;  // may be <= 0 for padding rows
+        float sc[BN];
+#pragma unroll
+        for (int c = 0; c < BN / 32; ++c) tmem_load_32_async(srow + 32 * c, sc + 32 * c);
+        tmem_wait_loads();
+        const bool done = __all_sync(0xffffffffu, nvis >= BN)
+                              ? row_block(std::true_type{}, sc, nvis, j == 0, g, srow)
+                              : row_block(std::false_type{}, sc, nvis, j == 0, g, srow);
+        if (!done) {
+          ok = false;
+          break;
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(p_full + 8 * sb);
       }
-    } else {
+      // the unit's last PV (t.nkb >= 1: key 0 is always visible)
+      if (!ok || !wait_pv(g - 1)) {
+        ok = false;
+        break;
+      }
       tc_fence_after();
       float o[D];
 #pragma unroll
       for (int c = 0; c < D / 32; ++c) tmem_load_32_async(orow + 32 * c, o + 32 * c);
       tmem_wait_loads();
-      if (qidx < p.seq_q) store_row(p, b, h, qidx, o, m, l);
+      if (qidx < p.seq_q) store_row(p, t.b, t.h, qidx, o, m, l);
+    }
+    if (!ok && lane == 0) {
+      record_status(p.status, TVR_DEV_TIMEOUT_EPILOGUE);
+      *const_cast<volatile int*>(abort_flag) = 1;
     }
     __syncwarp();
   }
@@ -438,8 +621,9 @@ int attention_impl(const float* q, const float* k, const float* v, float* out, f
   if (mode != TVR_GEMM_TF32) {
     return fail(TVR_ERR_UNSUPPORTED, "attention: the fused kernel computes in TF32 only");
   }
-  TVR_CHECK(batch * heads <= 65535 && seq_q <= 0x7fffff00 && seq_k <= 0x7fffff00,
-            "attention: too many (batch, head) pairs or positions");
+  TVR_CHECK(seq_q <= 0x7fffff00 && seq_k <= 0x7fffff00, "attention: too many positions");
+  const int64_t nqt = ceil_div(seq_q, BM);
+  TVR_CHECK(batch * heads <= 0x7fffffff / nqt, "attention: too many query tiles");
   auto strides_ok = [](const float* ptr, const int64_t* s) {
     return tc::al16(ptr) && s[0] % 4 == 0 && s[1] % 4 == 0 && s[2] % 4 == 0 && s[0] > 0 &&
            s[1] > 0 && s[2] > 0;
@@ -478,6 +662,9 @@ int attention_impl(const float* q, const float* k, const float* v, float* out, f
   p.status = device_status_ptr(dev);
   p.key_len = key_len;
   p.key_len_add = key_len_add;
+  p.batch_heads = static_cast<int>(batch * heads);
+  p.nqt = static_cast<int>(nqt);
+  p.units = static_cast<int>(nqt * batch * heads);
   static std::once_flag once[64];
   static cudaError_t attr_err[64];
   std::call_once(once[dev & 63], [&]() {
@@ -485,8 +672,9 @@ int attention_impl(const float* q, const float* k, const float* v, float* out, f
         attn_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
   });
   TVR_CUDA_TRY(attr_err[dev & 63]);
-  const dim3 grid(static_cast<unsigned>(ceil_div(seq_q, BM)), static_cast<unsigned>(batch * heads));
-  attn_fwd_kernel<<<grid, THREADS, SMEM_BYTES, as_stream(stream)>>>(p);
+  // persistent: two CTAs per SM, each working through its share of the units
+  const int ctas = static_cast<int>(std::min<int64_t>(p.units, 2 * static_cast<int64_t>(sm_count(dev))));
+  attn_fwd_kernel<<<ctas, THREADS, SMEM_BYTES, as_stream(stream)>>>(p);
   TVR_LAUNCH_CHECK();
   return TVR_OK;
 }

@@ -86,6 +86,14 @@ __device__ __forceinline__ void tma_prefetch_l2_3d(const CUtensorMap* map, int c
                : "memory");
 }
 
+__device__ __forceinline__ void tma_prefetch_l2_4d(const CUtensorMap* map, int c0, int c1, int c2,
+                                                   int c3) {
+  asm volatile("cp.async.bulk.prefetch.tensor.4d.L2.global.tile [%0, {%1, %2, %3, %4}];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+               : "memory");
+}
+
 // Tile store shared -> global through the tensor map (bulk-group completion).
 // Elements outside the tensor's extent are not written.  The x coordinate
 // (c0, fp32 elements) must be a multiple of 4 and no coordinate negative.
