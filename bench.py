@@ -673,8 +673,9 @@ def fixed_tf32_peak(peaks: dict) -> float:
 
 
 def single_gpu_extras(torch, args, tf32_peak) -> dict:
-    """The fused-GEMM sweep's largest point in both precision modes and the
-    LLM op set, for the one-GPU default line."""
+    """The fused-GEMM sweep's largest point in both precision modes, the LLM
+    op set, the memory-bound kernels and the fused attention kernel at GPT-2's
+    shapes, for the one-GPU default line."""
     from tvarant_b200 import workloads
 
     peaks = _peaks()
@@ -706,6 +707,8 @@ def single_gpu_extras(torch, args, tf32_peak) -> dict:
     torch.tvarant.empty_cache()
     out["memory_bound_kernels"] = {k: {"GB/s": v["GB/s"], "frac_hbm": v["frac_hbm"], "ms": v["ms"]}
                                    for k, v in res["per_kernel"].items()}
+    out["attention"] = workloads.measure_attention(max(10, steps), 3)
+    torch.tvarant.empty_cache()
     torch.set_float32_matmul_precision("high" if args.mode == "tf32" else "highest")
     return out
 

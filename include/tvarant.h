@@ -241,9 +241,9 @@ int tvr_gemm_swiglu(const float* x, const float* w_gate, const float* w_up, floa
  * contiguous last dimension; out has its own strides; lse (optional, may be
  * NULL) receives the natural-log log-sum-exp per (batch, head, query) as
  * [batch, heads, seq_q].  causal != 0 hides key j from query i when j > i
- * (PyTorch's is_causal).  The kernel computes in TF32 with head_dim 64;
- * other head dimensions and modes return TVR_ERR_UNSUPPORTED (the caller
- * then composes bmm / softmax / bmm).  No reference counterpart: the
+ * (PyTorch's is_causal).  The kernel computes in TF32 with head_dim 64 and
+ * scale > 0; other head dimensions, modes and scales return
+ * TVR_ERR_UNSUPPORTED (the caller then composes bmm / softmax / bmm).  No reference counterpart: the
  * reference materialises the scores (csrc/aten/LlmOps.cpp:68-148). */
 int tvr_attention_fwd(const float* q, const float* k, const float* v, float* out, float* lse,
                       int64_t batch, int64_t heads, int64_t seq_q, int64_t seq_k,

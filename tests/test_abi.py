@@ -208,6 +208,21 @@ def test_decode_entry_points_validate_arguments():
     assert "key length" in capi.last_error()
 
 
+def test_fused_attention_leaves_non_positive_scales_to_the_caller():
+    """The fused kernel takes scale > 0 (its partly masked blocks hold -inf
+    scores); other scales return TVR_ERR_UNSUPPORTED before any device work,
+    and the SDPA hook then composes matmul / softmax / matmul."""
+    import ctypes
+
+    capi.load()
+    st = capi.int64_array([4096, 4096, 64])
+    ptr = ctypes.c_void_p(256)
+    for scale in (0.0, -0.125, float("inf"), float("nan")):
+        assert capi.try_call("tvr_attention_fwd", ptr, ptr, ptr, ptr, None, 1, 1, 64, 64, 64, st,
+                             st, st, st, scale, 1, capi.GEMM_TF32, None) == capi.ERR_UNSUPPORTED
+        assert "positive finite scale" in capi.last_error()
+
+
 def test_extension_loads_without_gpu():
     import torch
 

@@ -10,6 +10,11 @@ reducing CTAs, restated in Python and checked for exact coverage (CPU).
   e + q * nt for q < 4, e = t, t + 4 * nt, ..., clipped to the tile's rows
   and columns.
 
+* ``attn_fwd_kernel`` (csrc/attention.cu): CTA c of ``ctas`` (two per SM)
+  takes unit n * ctas + c in even rounds n and n * ctas + (ctas - 1 - c) in
+  odd ones, while below the unit count; a CTA stops at its first empty
+  round.
+
 Every element (or unit, float4) must be taken exactly once, and no
 address may leave the output.
 """
@@ -132,3 +137,46 @@ def test_raster_choice_for_the_benchmark_shapes():
     assert pick_raster(64, 86, 128 * k4, 256 * k4) == (0, 24)
     # everything fits: one group, A held (M fastest), each operand read once
     assert pick_raster(8, 16, 128 * k4, 256 * k4) == (0, 8)
+
+
+def attention_slot_units(units, ctas, slots_per_cta=1):
+    """Every CTA's (slot's) units in the order it takes them."""
+    slots = slots_per_cta * ctas
+    out = {}
+    for s in range(slots_per_cta):
+        for c in range(ctas):
+            v = s * ctas + c
+            taken, n = [], 0
+            while True:
+                idx = n * slots + ((slots - 1 - v) if n & 1 else v)
+                if idx >= units:
+                    break
+                taken.append(idx)
+                n += 1
+            # nothing valid after the first empty round
+            for later in range(n + 1, n + 4):
+                assert later * slots + ((slots - 1 - v) if later & 1 else v) >= units
+            out[(c, s)] = taken
+    return out
+
+
+@pytest.mark.parametrize("units", [1, 5, 147, 148, 149, 200, 296, 297, 768, 1000, 6144])
+@pytest.mark.parametrize("ctas", [1, 7, 296])
+def test_attention_ctas_take_every_unit_once(units, ctas):
+    ctas = min(ctas, units)  # the host launches min(units, 2 x SMs) CTAs
+    got = attention_slot_units(units, ctas)
+    flat = [u for taken in got.values() for u in taken]
+    assert sorted(flat) == list(range(units))
+
+
+def test_attention_schedule_balances_gpt2_causal_tiles():
+    """GPT-2 [8, 12, 1024]: 768 units of 8 query tiles per head, unit u of
+    cost (tile index + 1) with the heaviest numbered first; on 296 CTAs the
+    busiest carries 13 tiles' worth of 128 keys against a mean of 11.7 (units
+    come in whole tiles), the lightest 10."""
+    bh, nqt, ctas = 96, 8, 296
+    cost = lambda u: nqt - u // bh  # rank 0 = last query tile = nqt blocks of 128 keys
+    got = attention_slot_units(bh * nqt, ctas)
+    per_cta = [sum(cost(u) for u in got[(c, 0)]) for c in range(ctas)]
+    mean = sum(per_cta) / ctas
+    assert max(per_cta) <= 1.12 * mean and min(per_cta) >= 0.85 * mean, (per_cta, mean)

@@ -4,6 +4,7 @@ It exists for callers that must not allocate device memory during a call
 (hosts with a fixed device-memory budget they hand out themselves, runtimes
 that forbid the allocator while serving); its
 split-K scratch is a fixed array inside the library.  Its results must match
+the oracle (the reference's GEMM, HostKernels.cpp:100-144) and
 tvr_gemm_bias_act in TF32 mode within the TF32 GEMM tolerance, on two calls
 in a row (the second call reuses the scratch the first left behind), and it
 must refuse outputs larger than its scratch limit.
@@ -19,6 +20,7 @@ import ctypes
 import numpy as np
 import pytest
 
+import oracle
 from conftest import rel_frobenius
 
 pytestmark = pytest.mark.gpu
@@ -103,9 +105,12 @@ def test_noalloc_matches_gemm_bias_act_twice(lib, m, n, k, act, trans_b, with_bi
             # memory from the driver or from this library's pool
             assert after == before
         outs.append(_host(out))
+    want = oracle.gemm_bias_act(a, b, bias, beta=beta, act=act, trans_b=trans_b,
+                                threads=oracle.host_threads())
     for got in outs:
         assert np.isfinite(got).all()
         assert rel_frobenius(got, expected) <= TOL_TF32
+        assert rel_frobenius(got, want) <= TOL_TF32
     assert np.array_equal(outs[0], outs[1])
     assert lib.get_status(0) == 0
 

@@ -42,7 +42,6 @@
 #include <cmath>
 #include <cstring>
 #include <mutex>
-#include <type_traits>
 
 #include "tc_ptx.cuh"
 
@@ -454,32 +453,23 @@ __global__ void __launch_bounds__(THREADS, 2) attn_fwd_kernel(const __grid_const
       return __all_sync(0xffffffffu, got);
     };
     // One block of this row: raise m if needed (rescaling O), write P over S
-    // and add its sum to l.  FULL: every row of the warp sees all BN keys of
-    // the block, so no column needs a visibility test.
-    auto row_block = [&](auto full_tag, float* sc, int nvis, bool first, int g,
-                         uint32_t srow) -> bool {
-      constexpr bool FULL = decltype(full_tag)::value;
+    // and add its sum to l.  Columns the row does not see hold -inf (set by
+    // the caller), so one body serves every block: exp2 maps them to 0 and the
+    // maximum passes over them.  (Two unrolled copies, for whole and partly
+    // masked blocks, left the softmax warps waiting on instruction fetch.)
+    auto row_block = [&](float* sc, bool first, int g, uint32_t srow) -> bool {
       // the block maximum of the scaled scores from the raw ones (scaling by
-      // s >= 0 keeps their order, and rounding is monotone; s < 0 reverses
-      // it), in eight independent partial maxima (and sums below): a single
-      // chain of 64 dependent operations would be the row's critical path
+      // s > 0 keeps their order, and rounding is monotone), in eight
+      // independent partial maxima (and sums below): a single chain of 64
+      // dependent operations would be the row's critical path
       float mp[8];
 #pragma unroll
       for (int r = 0; r < 8; ++r) mp[r] = -INFINITY;
-      if (p.scale_log2 >= 0.f) {
 #pragma unroll
-        for (int i = 0; i < BN; ++i) {
-          if (FULL || i < nvis) mp[i & 7] = fmaxf(mp[i & 7], sc[i]);
-        }
-      } else {
-#pragma unroll
-        for (int i = 0; i < BN; ++i) {
-          if (FULL || i < nvis) mp[i & 7] = fmaxf(mp[i & 7], -sc[i]);
-        }
-      }
+      for (int i = 0; i < BN; ++i) mp[i & 7] = fmaxf(mp[i & 7], sc[i]);
       const float mx = fmaxf(fmaxf(fmaxf(mp[0], mp[1]), fmaxf(mp[2], mp[3])),
                              fmaxf(fmaxf(mp[4], mp[5]), fmaxf(mp[6], mp[7]))) *
-                       fabsf(p.scale_log2);
+                       p.scale_log2;
       const float m_new = fmaxf(m, mx);
       if (__any_sync(0xffffffffu, m_new > m + kLazyLog2)) {
         const float alpha = ex2(m - (m_new == -INFINITY ? 0.f : m_new));  // 0 while m = -inf
@@ -510,7 +500,7 @@ __global__ void __launch_bounds__(THREADS, 2) attn_fwd_kernel(const __grid_const
       for (int c = 0; c < BN / 32; ++c) {
 #pragma unroll
         for (int i = 32 * c; i < 32 * c + 32; ++i) {
-          const float e = (FULL || i < nvis) ? ex2(fmaf(sc[i], p.scale_log2, -m_use)) : 0.f;
+          const float e = ex2(fmaf(sc[i], p.scale_log2, -m_use));
           sc[i] = e;
           sp[i & 7] += e;
         }
@@ -553,9 +543,11 @@ __global__ void __launch_bounds__(THREADS, 2) attn_fwd_kernel(const __grid_const
 #pragma unroll
         for (int c = 0; c < BN / 32; ++c) tmem_load_32_async(srow + 32 * c, sc + 32 * c);
         tmem_wait_loads();
-        const bool done = __all_sync(0xffffffffu, nvis >= BN)
-                              ? row_block(std::true_type{}, sc, nvis, j == 0, g, srow)
-                              : row_block(std::false_type{}, sc, nvis, j == 0, g, srow);
+        if (!__all_sync(0xffffffffu, nvis >= BN)) {
+#pragma unroll
+          for (int i = 0; i < BN; ++i) sc[i] = i < nvis ? sc[i] : -INFINITY;
+        }
+        const bool done = row_block(sc, j == 0, g, srow);
         if (!done) {
           ok = false;
           break;
@@ -620,6 +612,9 @@ int attention_impl(const float* q, const float* k, const float* v, float* out, f
   }
   if (mode != TVR_GEMM_TF32) {
     return fail(TVR_ERR_UNSUPPORTED, "attention: the fused kernel computes in TF32 only");
+  }
+  if (!(scale > 0.f) || !std::isfinite(scale)) {
+    return fail(TVR_ERR_UNSUPPORTED, "attention: the fused kernel takes a positive finite scale");
   }
   TVR_CHECK(seq_q <= 0x7fffff00 && seq_k <= 0x7fffff00, "attention: too many positions");
   const int64_t nqt = ceil_div(seq_q, BM);

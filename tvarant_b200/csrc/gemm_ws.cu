@@ -33,6 +33,8 @@
 // bounded as in gemm_tc: an expired wait records a TVR_DEV_* code in the
 // device status word, raises the CTA abort flag, and every role still
 // reaches both cluster barriers, so no CTA of the cluster is left waiting.
+// The waits poll in suspensions of at most 32 ns (a call is a chain of a few
+// latency-bound hops, and a plain try_wait woke ~0.37 us after a commit).
 // No TMA load uses cluster multicast.
 #include "internal.h"
 
@@ -228,7 +230,7 @@ __global__ void __launch_bounds__(Cfg<MB, SPLIT3>::THREADS, Cfg<MB, SPLIT3>::CTA
         grid_dependency_wait();
       }
       for (int kb = kb0; kb < kb1; ++kb) {
-        if (!mbar_wait(empty_bar + 8 * stage, phase ^ 1u, abort_flag)) {
+        if (!mbar_wait_poll(empty_bar + 8 * stage, phase ^ 1u, abort_flag)) {
           ok = false;
           break;
         }
@@ -250,7 +252,7 @@ __global__ void __launch_bounds__(Cfg<MB, SPLIT3>::THREADS, Cfg<MB, SPLIT3>::CTA
       }
       for (int st = 0; st < STAGES; ++st) {
         if ((issued_mask & (1u << st)) &&
-            !mbar_wait(full_bar + 8 * st, (issued_parity >> st) & 1u, nullptr)) {
+            !mbar_wait_poll(full_bar + 8 * st, (issued_parity >> st) & 1u, nullptr)) {
           record_status(p.status, TVR_DEV_TIMEOUT_DRAIN);
         }
       }
@@ -266,7 +268,7 @@ __global__ void __launch_bounds__(Cfg<MB, SPLIT3>::THREADS, Cfg<MB, SPLIT3>::CTA
       bool issued = false;
       for (int kb = kb0; kb < kb1; ++kb) {
         const uint32_t ready = (SPLIT3 ? conv_bar : full_bar) + 8 * stage;
-        if (!mbar_wait(ready, phase, abort_flag)) {
+        if (!mbar_wait_poll(ready, phase, abort_flag)) {
           ok = false;
           break;
         }
@@ -301,7 +303,7 @@ __global__ void __launch_bounds__(Cfg<MB, SPLIT3>::THREADS, Cfg<MB, SPLIT3>::CTA
       }
       if (issued) {
         mma_commit(drain_bar);
-        if (!mbar_wait(drain_bar, 0, nullptr)) record_status(p.status, TVR_DEV_TIMEOUT_DRAIN);
+        if (!mbar_wait_poll(drain_bar, 0, nullptr)) record_status(p.status, TVR_DEV_TIMEOUT_DRAIN);
       }
     }
     __syncwarp();
@@ -321,7 +323,7 @@ __global__ void __launch_bounds__(Cfg<MB, SPLIT3>::THREADS, Cfg<MB, SPLIT3>::CTA
       uint32_t phase = 0;
       bool ok = true;
       for (int kb = kb0; kb < kb1; ++kb) {
-        const bool got = mbar_wait(full_bar + 8 * stage, phase, abort_flag);
+        const bool got = mbar_wait_poll(full_bar + 8 * stage, phase, abort_flag);
         if (!__all_sync(0xffffffffu, got)) {
           ok = false;
           break;
@@ -361,7 +363,7 @@ __global__ void __launch_bounds__(Cfg<MB, SPLIT3>::THREADS, Cfg<MB, SPLIT3>::CTA
     // every landed stage has been consumed by the MMAs).  In 3xTF32 mode
     // value j is the sum of accumulator columns j and MB + j.
     const int q = warp & 3;
-    const bool got = mbar_wait(tfull_bar, 0, abort_flag);
+    const bool got = mbar_wait_poll(tfull_bar, 0, abort_flag);
     if (__all_sync(0xffffffffu, got)) {
       tc_fence_after();
       const int t = 32 * q + lane;

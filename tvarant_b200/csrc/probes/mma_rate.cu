@@ -4,7 +4,8 @@
 // from shared or tensor memory and B K-major or N-major, on 148 CTAs (one per
 // SM) and on 296 (two per SM, sharing the tensor core); it prints the time per
 // instruction and how long the issuing thread itself took (the MMA queue is
-// shallow, so issue keeps pace with execution).  Operands are zeroed shared
+// shallow, so issue keeps pace with execution).  The last rows put a
+// tcgen05.commit after every 8 MMAs, with and without a wait for it.  Operands are zeroed shared
 // and tensor memory; every address stays inside the CTA's own buffers and the
 // one completion wait is bounded.
 //
@@ -18,10 +19,16 @@ using namespace tvr::tc;
 
 constexpr int SMEM = 1024 + 16384 + 32768 + 64;
 
-template <int N, bool A_TMEM, bool B_NMAJOR>
+// COMMIT: 0 = no commits, 1 = a tcgen05.commit after every 8 MMAs (to an
+// mbarrier nobody waits on), 2 = the same commit and a wait for it
+// (mbarrier.try_wait, which may suspend the thread), 3 = the commit and a
+// spin on mbarrier.test_wait (bounded by a poll count), 4 = the commit and
+// a wait in try_wait polls that suspend for at most 32 ns each.
+template <int N, bool A_TMEM, bool B_NMAJOR, int COMMIT = 0>
 __global__ void __launch_bounds__(128) mma_probe(unsigned long long* out, int iters) {
   extern __shared__ uint8_t smem_raw[];
   __shared__ uint64_t s_bar;
+  __shared__ uint64_t s_step;
   __shared__ uint32_t s_tmem;
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
@@ -31,8 +38,10 @@ __global__ void __launch_bounds__(128) mma_probe(unsigned long long* out, int it
   for (int i = threadIdx.x; i < (16384 + 32768) / 4; i += blockDim.x) fz[i] = 0.f;
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
   const uint32_t bar = smem_u32(&s_bar);
+  const uint32_t step = smem_u32(&s_step);
   if (threadIdx.x == 0) {
     mbar_init(bar, 1);
+    mbar_init(step, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 0) {
@@ -63,6 +72,17 @@ __global__ void __launch_bounds__(128) mma_probe(unsigned long long* out, int it
       } else {
         mma_tf32(tmem, desc_kmajor(sa + k32), db, idesc, it > 0 ? 1u : 0u);
       }
+      if (COMMIT != 0 && (it & 7) == 7) {
+        mma_commit(step);
+        if (COMMIT == 2 && !mbar_wait(step, (it >> 3) & 1, nullptr)) break;
+        if (COMMIT == 4 && !mbar_wait_poll(step, (it >> 3) & 1, nullptr)) break;
+        if (COMMIT == 3) {
+          unsigned polls = 0;
+          while (!mbar_test(step, (it >> 3) & 1) && ++polls < (1u << 26)) {
+          }
+          if (polls >= (1u << 26)) break;
+        }
+      }
     }
     const unsigned long long t1 = global_ns();
     mma_commit(bar);
@@ -80,9 +100,9 @@ __global__ void __launch_bounds__(128) mma_probe(unsigned long long* out, int it
   if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(256u) : "memory");
 }
 
-template <int N, bool AT, bool BN_>
+template <int N, bool AT, bool BN_, int COMMIT = 0>
 void run(const char* name, int ctas, int iters, unsigned long long* d) {
-  auto k = mma_probe<N, AT, BN_>;
+  auto k = mma_probe<N, AT, BN_, COMMIT>;
   cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
   k<<<ctas, 128, SMEM>>>(d, iters);  // warm
   cudaDeviceSynchronize();
@@ -112,6 +132,14 @@ int main() {
     run<64, true, false>("N=64  A tmem  B K-major", ctas, iters, d);
     run<64, true, true>("N=64  A tmem  B N-major", ctas, iters, d);
     run<128, true, false>("N=128 A tmem  B K-major", ctas, iters, d);
+    run<64, false, false, 1>("N=64 A smem, commit per 8", ctas, iters, d);
+    run<64, false, false, 2>("N=64 A smem, commit+wait/8", ctas, iters, d);
+    run<64, true, true, 1>("N=64 A tmem B N, commit/8", ctas, iters, d);
+    run<64, true, true, 2>("N=64 A tmem B N, c+wait/8", ctas, iters, d);
+    run<64, false, false, 3>("N=64 A smem, commit+spin/8", ctas, iters, d);
+    run<64, true, true, 3>("N=64 A tmem B N, c+spin/8", ctas, iters, d);
+    run<64, false, false, 4>("N=64 A smem, commit+poll/8", ctas, iters, d);
+    run<64, true, true, 4>("N=64 A tmem B N, c+poll/8", ctas, iters, d);
   }
   cudaFree(d);
   return 0;

@@ -49,6 +49,54 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
+// Non-blocking: whether the phase of `bar` with parity `parity` has completed
+// (for event loops that poll several barriers).
+__device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// try_wait that suspends the thread for at most `ns` nanoseconds before
+// returning false.  Without the hint a thread suspended in try_wait on a
+// barrier that tcgen05.commit completes woke ~0.37 us after the arrival (8
+// MMAs, commit and wait: 1.14 us against 0.77 us for a test_wait spin).
+__device__ __forceinline__ bool mbar_try_wait_ns(uint32_t bar, uint32_t parity, uint32_t ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "r"(ns)
+      : "memory");
+  return ok != 0;
+}
+
+constexpr uint32_t WAIT_POLL_NS = 32;
+
+// mbar_wait with short suspensions (WAIT_POLL_NS), for waits on the critical
+// path of a pipeline whose barriers tcgen05.commit completes.
+__device__ __forceinline__ bool mbar_wait_poll(uint32_t bar, uint32_t parity,
+                                               const volatile int* abort) {
+  if (mbar_try_wait_ns(bar, parity, WAIT_POLL_NS)) return true;
+  const unsigned long long t0 = global_ns();
+  for (unsigned polls = 1; polls < WAIT_MAX_POLLS; ++polls) {
+    if (mbar_try_wait_ns(bar, parity, WAIT_POLL_NS)) return true;
+    if ((polls & 31u) == 0) {
+      if (abort != nullptr && *abort) return false;
+      if (global_ns() - t0 > WAIT_TIMEOUT_NS) return false;
+    }
+  }
+  return false;
+}
+
 // Waits for the phase of `bar` with parity `parity` to complete.  Gives up
 // (returns false) when the CTA abort flag is raised (if `abort` is given) or
 // after WAIT_TIMEOUT_NS / WAIT_MAX_POLLS.

@@ -243,6 +243,46 @@ def measure_llm_ops(steps: int, warmup: int, mode: str = "tf32") -> dict:
             "inputs": "seeded N(mean, std) drawn on the GPU (torch CUDA generator), ids on the host"}
 
 
+def measure_attention(steps: int, warmup: int, batch: int = 8) -> dict:
+    """The fused causal attention kernel at GPT-2's shapes (q, k, v
+    [batch, 12, 1024, 64] ~N(0, 1), scale 1/8, TF32) called through the C ABI
+    with preallocated buffers, timed back to back with events.  FLOPs are
+    the unmasked work, 4 * B * H * 64 * (1024 * 1025 / 2) (QK^T and PV over
+    the keys each query sees); the TF32 fraction is against half the measured
+    bf16 peak (a fixed denominator)."""
+    import ctypes
+
+    import bench
+
+    from . import capi
+
+    h, s, d = 12, 1024, 64
+    q = device_randn((batch, h, s, d), seed=21)
+    k = device_randn((batch, h, s, d), seed=22)
+    v = device_randn((batch, h, s, d), seed=23)
+    out = torch.empty(batch, h, s, d, device="tvarant")
+    st = capi.int64_array([h * s * d, s * d, d])
+    p = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+
+    def launch():
+        stream = ctypes.c_void_p(torch.tvarant.stream_handle(torch.tvarant.current_stream()))
+        capi.call("tvr_attention_fwd", p(q), p(k), p(v), p(out), None, batch, h, s, s, d,
+                  st, st, st, st, 0.125, 1, capi.GEMM_TF32, stream)
+
+    for _ in range(warmup):
+        launch()
+    torch.tvarant.synchronize()
+    ms = min(_time_steps(launch, steps) for _ in range(3))
+    flop = 4.0 * batch * h * d * (s * (s + 1) / 2)
+    peak = bench.fixed_tf32_peak(bench._peaks())
+    tflops = flop / (ms / 1e3) / 1e12
+    return {"workload": f"causal attention q, k, v [{batch}, {h}, {s}, {d}], TF32",
+            "kernel": "tvr::attn::attn_fwd_kernel", "us": ms * 1e3, "tflops": tflops,
+            "frac": tflops / peak, "peak": peak,
+            "peak_source": "MEASURED_PEAKS.json bf16_tflops / 2 (of measured)",
+            "flop": flop, "flop_note": "unmasked work: QK^T and PV over the keys each query sees"}
+
+
 # abs(neg(exp(y - z))) as a pointwise SSA program (the fused-GEMM sweep's chain):
 # Load y, Load z, Sub, Exp, Neg, Abs
 _CHAIN_PROGRAM = ([0, 0, 9, 10, 6, 11], [-1, -1, 0, 2, 3, 4], [-1, -1, 1, -1, -1, -1],
@@ -850,6 +890,8 @@ def _gpt2(args, rank, world, local_rank):
     if graph is not None:
         del logits
         graph.close()
+    attention_point = (measure_attention(max(5, min(args.steps, 20)), 3, batch=b1 - b0)
+                       if att == "sdpa" and seq == 1024 else None)
     if rank != 0:
         return None
     tokens = batch * seq
@@ -874,6 +916,7 @@ def _gpt2(args, rank, world, local_rank):
                    "parallelism": f"batch split over {world} rank(s) (attention split over batch x heads)",
                    "tflop_per_step": cfg.flops_per_token(seq) * tokens / 1e12,
                    "last_logits_finite": finite,
+                   "attention_kernel": attention_point,
                    "l2": "attention scores 403 MB per layer, weights 497 MB, logits 1.6 GB"},
         "e2e": {"value": tokens / (e2e_ms / 1e3), "unit": "tokens/s",
                 "h2d_bytes_per_step": batch * seq * 8, "d2h_bytes_per_step": batch * cfg.vocab * 4,
