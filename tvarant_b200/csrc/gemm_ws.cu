@@ -413,8 +413,18 @@ __global__ void __launch_bounds__(Cfg<MB, SPLIT3>::THREADS, Cfg<MB, SPLIT3>::CTA
     const int col = tile * BM + (e % BM);
     if (row >= p.m || col >= p.n) continue;
     const uint32_t local = ring + 4u * static_cast<uint32_t>(e);
+    // every partial in flight at once, then summed in the fixed order
+    // s = 0..S-1: one remote round trip per element instead of S dependent ones
+    float part[MAX_SPLITS];
+#pragma unroll
+    for (int s = 0; s < MAX_SPLITS; ++s) {
+      part[s] = s < static_cast<int>(nsplit) ? ld_dsmem(dsmem_addr(local, static_cast<uint32_t>(s))) : 0.f;
+    }
     float sum = 0.f;
-    for (uint32_t s = 0; s < nsplit; ++s) sum += ld_dsmem(dsmem_addr(local, s));
+#pragma unroll
+    for (int s = 0; s < MAX_SPLITS; ++s) {
+      if (s < static_cast<int>(nsplit)) sum += part[s];
+    }
     float* dst = p.c + static_cast<int64_t>(row) * p.ldc + col;
     float prev = 0.f;
     if (p.bias != nullptr) prev = __ldg(p.bias + col);
