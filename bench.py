@@ -674,8 +674,8 @@ def fixed_tf32_peak(peaks: dict) -> float:
 
 def single_gpu_extras(torch, args, tf32_peak) -> dict:
     """The fused-GEMM sweep's largest point in both precision modes, the LLM
-    op set, the memory-bound kernels and the fused attention kernel at GPT-2's
-    shapes, for the one-GPU default line."""
+    op set, the memory-bound kernels, and the GPT-2-small forward with the
+    fused attention kernel alone at its shapes, for the one-GPU default line."""
     from tvarant_b200 import workloads
 
     peaks = _peaks()
@@ -707,8 +707,23 @@ def single_gpu_extras(torch, args, tf32_peak) -> dict:
     torch.tvarant.empty_cache()
     out["memory_bound_kernels"] = {k: {"GB/s": v["GB/s"], "frac_hbm": v["frac_hbm"], "ms": v["ms"]}
                                    for k, v in res["per_kernel"].items()}
-    out["attention"] = workloads.measure_attention(max(10, steps), 3)
+    # GPT-2-small forward (fused attention, one CUDA graph per step), the gpt2
+    # workload's own code path; its line carries the attention kernel alone
+    import argparse
+
+    g_args = argparse.Namespace(**vars(args))
+    g_args.workload, g_args.attention, g_args.mode = "gpt2", "sdpa", "tf32"
+    g_args.seq, g_args.gpt2_batch, g_args.steps, g_args.warmup = 1024, 8, steps, 3
+    g_args.no_graph = False
+    g_line = workloads._gpt2(g_args, 0, 1, torch.tvarant.current_device())
     torch.tvarant.empty_cache()
+    out["gpt2_forward"] = {
+        "workload": g_line["config"]["workload"], "tokens_per_s": g_line["value"],
+        "ms_per_step": g_line["ms_per_step"], "e2e_tokens_per_s": g_line["e2e"]["value"],
+        "eager_tokens_per_s": g_line["config"]["eager_tokens_per_s"],
+        "tflop_per_step": g_line["config"]["tflop_per_step"],
+        "last_logits_finite": g_line["config"]["last_logits_finite"]}
+    out["attention"] = g_line["config"]["attention_kernel"]
     torch.set_float32_matmul_precision("high" if args.mode == "tf32" else "highest")
     return out
 
