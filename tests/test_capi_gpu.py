@@ -75,6 +75,8 @@ GEMM_SHAPES = [
     (128, 1024, 512),   # few tiles -> split-K
     (1000, 1000, 1000),
     (513, 264, 260),
+    (259, 1001, 192),   # N odd: output rows not 16-byte aligned (lane-per-column stores)
+    (129, 50257, 64),   # vocabulary-sized N, unaligned rows
 ]
 
 
@@ -136,9 +138,11 @@ def test_gemm_mm_layout(lib, rng, shape, mode, tol):
 
 
 @pytest.mark.parametrize("mode", [1, 2, 3])
-def test_gemm_alpha_beta_prev(lib, rng, mode):
-    """bias == NULL and beta != 0 reads the previous output (HostKernels.cpp:132-138)."""
-    m, n, k = 300, 256, 192
+@pytest.mark.parametrize("n", [256, 1001])
+def test_gemm_alpha_beta_prev(lib, rng, mode, n):
+    """bias == NULL and beta != 0 reads the previous output (HostKernels.cpp:132-138);
+    n = 1001 leaves the output rows unaligned."""
+    m, k = 300, 192
     a = rng.standard_normal((m, k), dtype=np.float32)
     w = rng.standard_normal((n, k), dtype=np.float32)
     c0 = rng.standard_normal((m, n), dtype=np.float32)

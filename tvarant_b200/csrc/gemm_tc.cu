@@ -794,6 +794,50 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) gemm_tc_kernel(const __grid_co
             tma_store_3d(&p.tma_c, sbuf, col0, static_cast<int>(row0), zc);
             bulk_commit();
           }
+        } else if (!p.c_vec) {
+          // Rows not 16-byte aligned (an LM head's N = 50257): lane = column,
+          // one row of 32 consecutive floats per store instruction, which
+          // writes a few whole sectors of that row.  (Lane = row with four
+          // scalar stores per lane made every store instruction 32 separate
+          // sector writes.)  Loads first, then stores, as below.
+          const int colj = tn * OUT_BN + half * HC + 32 * c + lane;
+          float xr[32];
+#pragma unroll
+          for (int r = 0; r < 32; ++r) {
+            const uint32_t addr =
+                sbuf + r * 128 + ((((lane >> 2) ^ (r & 7)) << 4) | ((lane & 3) << 2));
+            asm volatile("ld.shared.f32 %0, [%1];" : "=f"(xr[r]) : "r"(addr));
+          }
+          if (finish && !plain) {
+            const bool read_prev = p.bias == nullptr && p.use_prev;
+            const float bj = p.bias != nullptr && colj < p.n ? __ldg(p.bias + colj) : 0.f;
+            float prev[32];
+#pragma unroll
+            for (int r = 0; r < 32; ++r) {
+              const int64_t row = row0 + r;
+              prev[r] = read_prev && row < p.m && colj < p.n ? cbase[row * p.ldc + colj] : bj;
+            }
+            // epilogue4's arithmetic, element by element
+            if (p.act == TVR_ACT_SILU) {
+#pragma unroll
+              for (int r = 0; r < 32; ++r)
+                xr[r] = act_fixed<TVR_ACT_SILU>(__fadd_rn(__fmul_rn(p.alpha, xr[r]), __fmul_rn(p.beta, prev[r])));
+            } else if (p.act == TVR_ACT_RELU) {
+#pragma unroll
+              for (int r = 0; r < 32; ++r)
+                xr[r] = act_fixed<TVR_ACT_RELU>(__fadd_rn(__fmul_rn(p.alpha, xr[r]), __fmul_rn(p.beta, prev[r])));
+            } else {
+#pragma unroll
+              for (int r = 0; r < 32; ++r)
+                xr[r] = __fadd_rn(__fmul_rn(p.alpha, xr[r]), __fmul_rn(p.beta, prev[r]));
+            }
+          }
+          asm volatile("" ::: "memory");
+#pragma unroll
+          for (int r = 0; r < 32; ++r) {
+            const int64_t row = row0 + r;
+            if (row < p.m && colj < p.n) cbase[row * p.ldc + colj] = xr[r];
+          }
         } else {
           // All shared-memory reads (and reads of the previous output, when
           // beta applies to it) are issued before any global store: a warp's
