@@ -151,6 +151,33 @@ def test_chain_after_linear_silu(lib, rng, m, n, k, mode):
     assert lib.get_status(0) == 0
 
 
+# y + r (the residual add of a transformer's output projections): run natively
+# in the TMA-store epilogue rather than as stack code
+RESIDUAL = [(0, -1, -1, 0, 1, 0), (0, -1, -1, 1, 1, 0), (2, 0, 1, -1, 1, 0)]
+
+
+@pytest.mark.parametrize("m,n,k", [
+    (512, 768, 256),    # GPT-2-like projection shape, BN = 256 tiles
+    (300, 1000, 512),   # ragged tiles
+    (259, 1004, 128),   # N a multiple of 4 but not of 32: clipped last box
+])
+@pytest.mark.parametrize("mode", [TF32, X3])
+@pytest.mark.parametrize("gemm_input", [0, 1])
+def test_residual_add_in_the_epilogue(lib, rng, m, n, k, mode, gemm_input):
+    """Exactly the device's GEMM followed by the add (one IEEE addition per
+    element, the same tiles), and the oracle's within the GEMM tolerance."""
+    a, w, b = _operands(rng, m, n, k)
+    r = rng.standard_normal((m, n), dtype=np.float32)
+    got = _gemm_pw(lib, a, w, b, 0, mode, RESIDUAL, gemm_input, [(r, n)])
+    y = oracle.gemm_bias_act(a, w, b)
+    ref = oracle.pointwise(RESIDUAL, [y, r] if gemm_input == 0 else [r, y])
+    assert rel_frobenius(got, ref) <= _tol(mode), rel_frobenius(got, ref)
+    full = [None, r] if gemm_input == 0 else [r, None]
+    two_step = _unfused(lib, a, w, b, 0, mode, RESIDUAL, gemm_input, full)
+    assert np.array_equal(got, two_step)
+    assert lib.get_status(0) == 0
+
+
 def test_padded_output_and_strided_input(lib, rng):
     m, n, k = 260, 300, 128
     a, w, b = _operands(rng, m, n, k)

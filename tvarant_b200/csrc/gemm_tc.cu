@@ -96,6 +96,8 @@ struct Params {
   CUtensorMap tma_a_lo;  // 3xTF32 low parts, same geometry
   CUtensorMap tma_b_lo;  // or, for a gated GEMM, the up-projection weight {K, N, 1}
   CUtensorMap tma_c;     // TMA_C kernels: the output {N, M, batch}, 32 x 32 boxes, 128B swizzle
+  const float* resid;    // TMA_C kernels, non-null: add resid[row * resid_ld + col] last
+  int64_t resid_ld;
   const float* bias;
   float* c;
   int64_t ldc;
@@ -578,6 +580,31 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) gemm_tc_kernel(const __grid_co
         }
         if constexpr (TMA_C) {
           const int col0 = tn * OUT_BN + half * HC + 32 * c;
+          // A residual add (the epilogue program Load y, Load r, Add, run
+          // natively): the chunk's 32 x 32 residual block, loaded first in
+          // the coalesced layout (rows 4i + lane / 8, columns 4 (lane % 8)),
+          // added to the staged chunk after the bias step as the program
+          // adds it (one IEEE addition)
+          float4 rv[8];
+          const bool resid = p.resid != nullptr;
+          if (resid) {
+            const int cj = col0 + 4 * (lane & 7);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const int64_t row = row0 + 4 * i + (lane >> 3);
+              const float* rs = p.resid + row * p.resid_ld + cj;
+              rv[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+              if (row < p.m) {
+                if (cj + 3 < p.n) {
+                  rv[i] = __ldg(reinterpret_cast<const float4*>(rs));
+                } else {
+                  if (cj < p.n) rv[i].x = __ldg(rs);
+                  if (cj + 1 < p.n) rv[i].y = __ldg(rs + 1);
+                  if (cj + 2 < p.n) rv[i].z = __ldg(rs + 2);
+                }
+              }
+            }
+          }
           if (!plain) {
             // act(alpha * acc + beta * bias): epilogue4's arithmetic, per
             // element; one straight-line loop per activation (with the choice
@@ -610,6 +637,26 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) gemm_tc_kernel(const __grid_co
             asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(v[4 * j]),
                          "f"(v[4 * j + 1]), "f"(v[4 * j + 2]), "f"(v[4 * j + 3])
                          : "memory");
+          }
+          if (resid) {
+            __syncwarp();
+            const int jj = lane & 7;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const int rr = 4 * i + (lane >> 3);
+              const uint32_t addr = sbuf + rr * 128 + ((jj ^ (rr & 7)) << 4);
+              float4 x;
+              asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+                           : "=f"(x.x), "=f"(x.y), "=f"(x.z), "=f"(x.w)
+                           : "r"(addr));
+              x.x = __fadd_rn(x.x, rv[i].x);
+              x.y = __fadd_rn(x.y, rv[i].y);
+              x.z = __fadd_rn(x.z, rv[i].z);
+              x.w = __fadd_rn(x.w, rv[i].w);
+              asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(x.x),
+                           "f"(x.y), "f"(x.z), "f"(x.w)
+                           : "memory");
+            }
           }
           fence_proxy_async_smem();
           __syncwarp();
@@ -1272,9 +1319,24 @@ int gemm_tcgen05(const float* a, const float* b, const float* bias, float* c, in
   // least one 32 x 32 box wide.  A program runs in the epilogue only then.
   const bool tma_ok = splits == 1 && p.use_prev == 0 && c_vec && n >= 32 && m >= 32 &&
                       ldc <= (int64_t(1) << 36) / 4;
-  const bool prog_in_kernel = has_prog && tma_ok && batch == 1 && trans_b && prog->n_ops > 0;
+  // The commonest program, a residual add (Load y, Load r, Add with alpha 1,
+  // r a full row-major matrix with 16-byte aligned rows), runs natively in
+  // the TMA-store epilogue instead of as stack code.
+  const bool resid_native =
+      has_prog && tma_ok && batch == 1 && prog->n_nodes == 3 && prog->n_extra == 1 &&
+      prog->op[0] == kEpiLoad && prog->op[1] == kEpiLoad && prog->op[2] == kEpiAdd &&
+      prog->alpha[2] == 1.f &&
+      ((prog->src[0] == -1 && prog->src[1] == 0) || (prog->src[0] == 0 && prog->src[1] == -1)) &&
+      ((prog->a[2] == 0 && prog->b[2] == 1) || (prog->a[2] == 1 && prog->b[2] == 0)) &&
+      prog->in[0] != nullptr && prog->ld[0] != 0 && prog->vec[0] != 0;
+  if (resid_native) {
+    p.resid = prog->in[0];
+    p.resid_ld = prog->ld[0];
+  }
+  const bool prog_in_kernel =
+      has_prog && !resid_native && tma_ok && batch == 1 && trans_b && prog->n_ops > 0;
   if (prog_in_kernel) p.prog = *prog;
-  const bool tma_c = tma_ok && !has_prog;
+  const bool tma_c = tma_ok && (!has_prog || resid_native);
   if (tma_c || prog_in_kernel) {
     const uint64_t c_bs = static_cast<uint64_t>(batch > 1 ? sc : m * ldc) * 4;
     if ((rc = encode_3d(&p.tma_c, c, n, m, batch, ldc * 4, c_bs ? c_bs : 16, 32, 32)) != TVR_OK)
@@ -1295,7 +1357,9 @@ int gemm_tcgen05(const float* a, const float* b, const float* bias, float* c, in
         out, splits, bias, c, m, n, ldc, alpha, beta, act, p.use_prev);
     TVR_LAUNCH_CHECK();
   }
-  if (has_prog && !prog_in_kernel) return epi_prog_inplace(*prog, c, ldc, m, n, stream);
+  if (has_prog && !prog_in_kernel && !resid_native) {
+    return epi_prog_inplace(*prog, c, ldc, m, n, stream);
+  }
   return TVR_OK;
 }
 
