@@ -386,7 +386,8 @@ def test_softmax_add_declines_rows_it_does_not_take(lib):
         lib.ERR_INVALID  # 4 rows are not a whole number of 3 mask rows
 
 
-@pytest.mark.parametrize("rows,n", [(2, 8), (16, 768), (33, 4096), (5, 1000), (4, 1001), (3, 20000)])
+@pytest.mark.parametrize("rows,n", [(2, 8), (16, 768), (33, 4096), (5, 1000), (4, 1001), (3, 20000),
+                                    (20000, 64)])  # more rows than one pass of the warp kernel
 @pytest.mark.parametrize("affine", [True, False])
 def test_layer_norm(lib, rng, rows, n, affine):
     x = rng.standard_normal((rows, n), dtype=np.float32)

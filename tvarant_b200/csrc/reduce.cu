@@ -235,6 +235,85 @@ void launch_softmax_warp(const float* x, float* y, int64_t rows, int dim, cudaSt
   }
 }
 
+// ---- layer norm, rows up to 1024 wide: one warp per row -----------------------
+// A block per row spends most of a short row's time in its two block-wide
+// reductions (shared memory and __syncthreads); here a warp holds the row in
+// registers (VPL float4 per lane), reduces with shuffles, and a block of 8
+// warps walks rows in a grid-stride loop.  Same arithmetic per element as the
+// block kernel below.
+template <int VPL>
+__global__ void __launch_bounds__(256) layer_norm_warp_kernel(
+    const float* __restrict__ x, const float* __restrict__ gamma, const float* __restrict__ beta,
+    float* __restrict__ y, float* __restrict__ mean_out, float* __restrict__ rstd_out,
+    int64_t rows, int n, float eps) {
+  // a few-row GEMM launched as a programmatic dependent (decode steps) may
+  // start streaming its weights now
+  if (threadIdx.x == 0) grid_launch_dependents();
+  const int lane = threadIdx.x & 31;
+  const int n4 = n >> 2;
+  const float4* g4 = reinterpret_cast<const float4*>(gamma);
+  const float4* b4 = reinterpret_cast<const float4*>(beta);
+  const int64_t step = static_cast<int64_t>(gridDim.x) * 8;
+  for (int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5); row < rows;
+       row += step) {
+    const float4* xr = reinterpret_cast<const float4*>(x + row * n);
+    float4 v[VPL];
+    float s = 0.f;
+#pragma unroll
+    for (int j = 0; j < VPL; ++j) {
+      const int c = lane + 32 * j;
+      if (c < n4) {
+        v[j] = __ldcs(xr + c);
+        s += (v[j].x + v[j].y) + (v[j].z + v[j].w);
+      } else {
+        v[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    }
+    const float mu = warp_sum(s) / static_cast<float>(n);
+    float q = 0.f;
+#pragma unroll
+    for (int j = 0; j < VPL; ++j) {
+      if (lane + 32 * j < n4) {
+        const float a = v[j].x - mu, b = v[j].y - mu, cc = v[j].z - mu, d = v[j].w - mu;
+        q += (__fmul_rn(a, a) + __fmul_rn(b, b)) + (__fmul_rn(cc, cc) + __fmul_rn(d, d));
+      }
+    }
+    const float var = warp_sum(q) / static_cast<float>(n);
+    const float rs = 1.f / sqrtf(var + eps);
+    if (lane == 0) {
+      if (mean_out) mean_out[row] = mu;
+      if (rstd_out) rstd_out[row] = rs;
+    }
+    float4* yr = reinterpret_cast<float4*>(y + row * n);
+#pragma unroll
+    for (int j = 0; j < VPL; ++j) {
+      const int c = lane + 32 * j;
+      if (c < n4) {
+        float4 o;
+        o.x = __fmul_rn(v[j].x - mu, rs);
+        o.y = __fmul_rn(v[j].y - mu, rs);
+        o.z = __fmul_rn(v[j].z - mu, rs);
+        o.w = __fmul_rn(v[j].w - mu, rs);
+        if (gamma) {
+          const float4 g = __ldg(g4 + c);
+          o.x = __fmul_rn(o.x, g.x);
+          o.y = __fmul_rn(o.y, g.y);
+          o.z = __fmul_rn(o.z, g.z);
+          o.w = __fmul_rn(o.w, g.w);
+        }
+        if (beta) {
+          const float4 bb = __ldg(b4 + c);
+          o.x = __fadd_rn(o.x, bb.x);
+          o.y = __fadd_rn(o.y, bb.y);
+          o.z = __fadd_rn(o.z, bb.z);
+          o.w = __fadd_rn(o.w, bb.w);
+        }
+        __stcs(yr + c, o);
+      }
+    }
+  }
+}
+
 // ---- layer norm: one block per row, the row held in registers ---------------
 
 template <int VPT>
@@ -481,7 +560,25 @@ int tvr_layer_norm(const float* x, const float* gamma, const float* beta, float*
   const unsigned blocks = static_cast<unsigned>(rows);
   const bool vec = n % 4 == 0 && aligned16(x) && aligned16(y) && (!gamma || aligned16(gamma)) &&
                    (!beta || aligned16(beta));
-  if (vec && n <= 16384) {
+  if (vec && n <= 1024) {
+    // a warp per row for short rows (GPT-2's 768)
+    const int n4 = static_cast<int>(n / 4);
+    const int vpl = (n4 + 31) / 32;
+    const int64_t cap = static_cast<int64_t>(sm_count(current_device())) * 8;
+    const unsigned wblocks = static_cast<unsigned>(std::min<int64_t>(ceil_div(rows, 8), cap));
+    const int ni = static_cast<int>(n);
+    if (vpl <= 1) {
+      layer_norm_warp_kernel<1><<<wblocks, 256, 0, s>>>(x, gamma, beta, y, mean, rstd, rows, ni, eps);
+    } else if (vpl <= 2) {
+      layer_norm_warp_kernel<2><<<wblocks, 256, 0, s>>>(x, gamma, beta, y, mean, rstd, rows, ni, eps);
+    } else if (vpl <= 4) {
+      layer_norm_warp_kernel<4><<<wblocks, 256, 0, s>>>(x, gamma, beta, y, mean, rstd, rows, ni, eps);
+    } else if (vpl <= 6) {
+      layer_norm_warp_kernel<6><<<wblocks, 256, 0, s>>>(x, gamma, beta, y, mean, rstd, rows, ni, eps);
+    } else {
+      layer_norm_warp_kernel<8><<<wblocks, 256, 0, s>>>(x, gamma, beta, y, mean, rstd, rows, ni, eps);
+    }
+  } else if (vec && n <= 16384) {
     const int n4 = static_cast<int>(n / 4);
     int vpt = 1;
     while (vpt < 16 && ceil_div(n4, vpt) > 256) vpt *= 2;
