@@ -300,6 +300,7 @@ def test_bmm_broadcast_b(lib, rng):
 @pytest.mark.parametrize("shape,dim", [
     ((4, 8), -1), ((2, 4, 8), -1), ((3, 7), -1), ((64, 128), -1), ((17, 1000), -1),
     ((8, 2048), -1), ((4, 5000), -1), ((2, 20000), -1), ((3, 5, 7), 1), ((6, 33, 4), 0),
+    ((80001, 64), -1),  # two rows per warp iteration, more rows than one pass of the grid
 ])
 def test_softmax(lib, rng, shape, dim):
     x = (rng.standard_normal(shape) * np.sqrt(2)).astype(np.float32)
