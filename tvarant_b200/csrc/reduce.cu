@@ -560,8 +560,10 @@ int tvr_layer_norm(const float* x, const float* gamma, const float* beta, float*
   const unsigned blocks = static_cast<unsigned>(rows);
   const bool vec = n % 4 == 0 && aligned16(x) && aligned16(y) && (!gamma || aligned16(gamma)) &&
                    (!beta || aligned16(beta));
-  if (vec && n <= 1024) {
-    // a warp per row for short rows (GPT-2's 768)
+  if (vec && n <= 1024 && rows >= 1024) {
+    // a warp per row for many short rows (GPT-2's forward: 8192 x 768); a
+    // few rows (a decode step's 8) keep a block per row, spread over as many
+    // SMs (one block of 8 row-warps made a decode step 75 us slower)
     const int n4 = static_cast<int>(n / 4);
     const int vpl = (n4 + 31) / 32;
     const int64_t cap = static_cast<int64_t>(sm_count(current_device())) * 8;
