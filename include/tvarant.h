@@ -274,6 +274,29 @@ int tvr_kv_append(float* cache, const float* src, int64_t batch, int64_t heads, 
                   int64_t dim, int64_t max_len, const int64_t* cache_strides,
                   const int64_t* src_strides, const int64_t* pos, void* stream);
 
+/* One decode step's attention with its KV-cache append, in one launch: for
+ * p = *pos (an int64 in device memory), k_new / v_new [batch, heads, 1, dim]
+ * are written into cache position p of k_cache / v_cache [batch, heads,
+ * max_len, dim], and q [batch, heads, 1, dim] attends (no mask) to cache
+ * positions 0..p, out [batch, heads, 1, dim] = softmax(scale q k^T) v.  The
+ * result, the caches and the status word are exactly those of tvr_kv_append
+ * (k), tvr_kv_append (v), then tvr_attention_fwd_keylen with key_len = pos,
+ * key_len_add = 1; a position outside [0, max_len) appends nothing, sets
+ * TVR_DEV_CACHE_FULL and attends to clamp(p + 1, 1, max_len) cached keys.
+ * Strides are for (batch, head, position), dim contiguous; q, k_new, v_new
+ * and the caches need 16-byte aligned bases and strides that are multiples
+ * of 4 elements.  dim 64, scale > 0, TF32 or 3xTF32 mode (the kernel computes
+ * in fp32); anything else returns TVR_ERR_UNSUPPORTED and the caller runs
+ * the three calls.  *pos does not advance (tvr_counter_add).  No reference
+ * counterpart. */
+int tvr_attention_decode_append(const float* q, const float* k_new, const float* v_new,
+                                float* k_cache, float* v_cache, float* out, int64_t batch,
+                                int64_t heads, int64_t max_len, int64_t head_dim,
+                                const int64_t* q_strides, const int64_t* kn_strides,
+                                const int64_t* vn_strides, const int64_t* kc_strides,
+                                const int64_t* vc_strides, const int64_t* o_strides, float scale,
+                                const int64_t* pos, int mode, void* stream);
+
 /* *counter += delta on the stream (an int64 in device memory). */
 int tvr_counter_add(int64_t* counter, int64_t delta, void* stream);
 

@@ -208,6 +208,37 @@ def test_decode_entry_points_validate_arguments():
     assert "key length" in capi.last_error()
 
 
+def test_decode_append_validates_before_device_work():
+    """tvr_attention_decode_append: invalid arguments are errors, forms the
+    kernel does not take are TVR_ERR_UNSUPPORTED (the caller composes the
+    append and the attention), all before any device call."""
+    import ctypes
+
+    capi.load()
+    st = capi.int64_array([4096, 64, 64])
+    p = ctypes.c_void_p(256)
+    pos = ctypes.c_void_p(512)
+
+    def call(*, batch=1, heads=1, max_len=64, dim=64, q=p, pos=pos, scale=0.125,
+             mode=capi.GEMM_TF32):
+        return capi.try_call("tvr_attention_decode_append", q, p, p, p, p, p, batch, heads,
+                             max_len, dim, st, st, st, st, st, st, scale, pos, mode, None)
+
+    assert call(batch=0) == capi.OK
+    assert call(heads=-1) == capi.ERR_INVALID
+    assert call(max_len=0) == capi.ERR_INVALID
+    assert call(q=None) == capi.ERR_INVALID
+    assert call(pos=ctypes.c_void_p(516)) == capi.ERR_INVALID
+    assert "position" in capi.last_error()
+    assert call(mode=17) == capi.ERR_INVALID
+    assert call(dim=128) == capi.ERR_UNSUPPORTED
+    assert call(mode=capi.GEMM_FP32) == capi.ERR_UNSUPPORTED
+    for scale in (0.0, -1.0, float("inf"), float("nan")):
+        assert call(scale=scale) == capi.ERR_UNSUPPORTED
+    assert call(q=ctypes.c_void_p(260)) == capi.ERR_UNSUPPORTED  # not 16-byte aligned
+    assert "aligned" in capi.last_error()
+
+
 def test_fused_attention_leaves_non_positive_scales_to_the_caller():
     """The fused kernel takes scale > 0 (its partly masked blocks hold -inf
     scores); other scales return TVR_ERR_UNSUPPORTED before any device work,

@@ -557,3 +557,27 @@ def test_argmax_matches_torch(tvarant, shape, dim, keepdim):
            else x.to("tvarant").argmax(dim=dim, keepdim=keepdim)).cpu()
     assert got.dtype == torch.int64 and got.shape == want.shape
     assert torch.equal(got, want)
+
+
+def test_argmax_rows_split_over_a_cluster(tvarant):
+    """Few long rows: each row is split over the CTAs of a cluster.  The
+    winner sits in a different part of each row: ties across a part boundary
+    (the first index wins), a NaN late in a row of numbers, the maximum in the
+    last element, a row of -inf."""
+    rows, n = 6, 70001
+    g = torch.Generator().manual_seed(3)
+    x = torch.rand(rows, n, generator=g)
+    chunk = -(-n // 8)
+    x[0, 5 * chunk - 1] = 2.0  # last element of part 4 ...
+    x[0, 5 * chunk] = 2.0      # ... ties the first of part 5
+    x[1, 3] = 5.0
+    x[1, n - 10] = float("nan")
+    x[2, n - 1] = 3.0
+    x[3] = float("-inf")
+    x[4, 7 * chunk + 1] = 4.0
+    x[4, 2 * chunk + 1] = 4.0
+    x[5, :] = 1.0              # all equal: index 0
+    want = x.argmax(dim=-1)
+    got = x.to("tvarant").argmax(dim=-1).cpu()
+    assert torch.equal(got, want), (got, want)
+    assert got.tolist() == [5 * chunk - 1, n - 10, n - 1, 0, 2 * chunk + 1, 0]

@@ -152,7 +152,8 @@ def test_chain_after_linear_silu(lib, rng, m, n, k, mode):
 
 
 # y + r (the residual add of a transformer's output projections): run natively
-# in the TMA-store epilogue rather than as stack code
+# in the TMA-store epilogue and in the few-row GEMM's reduction rather than as
+# stack code or a separate pass
 RESIDUAL = [(0, -1, -1, 0, 1, 0), (0, -1, -1, 1, 1, 0), (2, 0, 1, -1, 1, 0)]
 
 
@@ -160,6 +161,9 @@ RESIDUAL = [(0, -1, -1, 0, 1, 0), (0, -1, -1, 1, 1, 0), (2, 0, 1, -1, 1, 0)]
     (512, 768, 256),    # GPT-2-like projection shape, BN = 256 tiles
     (300, 1000, 512),   # ragged tiles
     (259, 1004, 128),   # N a multiple of 4 but not of 32: clipped last box
+    (8, 768, 3072),     # a decode step's down projection: the few-row GEMM
+    (100, 1001, 512),   # few rows, a ragged weight tile and unaligned rows
+    (2, 768, 768),      # two rows (3xTF32: the fp32 GEMV, then the pass)
 ])
 @pytest.mark.parametrize("mode", [TF32, X3])
 @pytest.mark.parametrize("gemm_input", [0, 1])

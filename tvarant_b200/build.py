@@ -51,6 +51,7 @@ CUDA_SOURCES = [
     "gemm_tc.cu",
     "gemm_ws.cu",
     "attention.cu",
+    "attention_decode.cu",
     "pointwise_jit.cu",
     "nccl.cu",
     "nvls.cu",

@@ -106,6 +106,8 @@ SIGNATURES: dict[str, list] = {
     "tvr_attention_fwd_keylen": [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _pi64, _pi64,
                                  _pi64, _pi64, _f32, _vp, _i32, _i32, _vp],
     "tvr_kv_append": [_vp, _vp, _i64, _i64, _i64, _i64, _i64, _pi64, _pi64, _vp, _vp],
+    "tvr_attention_decode_append": [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _pi64,
+                                    _pi64, _pi64, _pi64, _pi64, _pi64, _f32, _vp, _i32, _vp],
     "tvr_counter_add": [_vp, _i64, _vp],
     "tvr_attention_fwd": [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _pi64, _pi64,
                           _pi64, _pi64, _f32, _i32, _i32, _vp],

@@ -628,6 +628,13 @@ int attention_impl(const float* q, const float* k, const float* v, float* out, f
                 "attention: operands need 16-byte aligned bases and strides that are multiples "
                 "of 4 elements (TMA)");
   }
+  // a few query rows (a decode step): the keys and values are streamed on
+  // the CUDA cores instead of through mostly empty 128-row MMA tiles
+  if (attention_decode_applies(seq_q, head_dim)) {
+    return attention_decode(q, k, v, out, lse, batch, heads, seq_q, seq_k, q_strides, k_strides,
+                            v_strides, o_strides, scale, causal, key_len, key_len_add,
+                            as_stream(stream));
+  }
   const int dev = current_device();
   Params p;
   memset(&p, 0, sizeof(p));

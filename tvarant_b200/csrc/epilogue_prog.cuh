@@ -94,6 +94,19 @@ enum EpiOp {
   kEpiAbs = 11,
 };
 
+// True when the program is the residual add y + r (Load y, Load r, Add with
+// alpha 1, in either operand order), r being extra input 0 as a full
+// row-major matrix (row stride in[0] / ld[0], not a broadcast row).  The GEMM
+// kernels add r in their own epilogues then; in IEEE arithmetic y + 1 * r is
+// y + r in either order, so the result is bit-identical to the program.
+inline bool epi_is_residual_add(const EpiProg& g) {
+  return g.n_nodes == 3 && g.n_extra == 1 && g.op[0] == kEpiLoad && g.op[1] == kEpiLoad &&
+         g.op[2] == kEpiAdd && g.alpha[2] == 1.f &&
+         ((g.src[0] == -1 && g.src[1] == 0) || (g.src[0] == 0 && g.src[1] == -1)) &&
+         ((g.a[2] == 0 && g.b[2] == 1) || (g.a[2] == 1 && g.b[2] == 0)) && g.in[0] != nullptr &&
+         g.ld[0] != 0;
+}
+
 // Extra input e at (row, col..col+3); zeros outside [m) x [n).
 __device__ __forceinline__ float4 epi_load4(const EpiProg& g, int e, int64_t row, int col, int m,
                                             int n) {

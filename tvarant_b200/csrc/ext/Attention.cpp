@@ -173,6 +173,53 @@ at::Tensor attention_keylen(const at::Tensor& q, const at::Tensor& k, const at::
   return out;
 }
 
+// One decode step's attention with its cache append: k_new / v_new
+// [B, H, 1, D] go into cache position *pos, and q [B, H, 1, D] attends to
+// positions 0..*pos, in one launch (tvr_attention_decode_append).  Exactly
+// kv_append_(k_cache, k_new, pos); kv_append_(v_cache, v_new, pos);
+// attention_keylen(q, k_cache, v_cache, pos, 1, scale), which it runs when the
+// fused kernel does not take the operands.
+at::Tensor attention_decode_append(const at::Tensor& q, const at::Tensor& k_new,
+                                   const at::Tensor& v_new, at::Tensor& k_cache,
+                                   at::Tensor& v_cache, const at::Tensor& pos, double scale) {
+  for (const at::Tensor* t : std::initializer_list<const at::Tensor*>{
+           &q, &k_new, &v_new, &k_cache, &v_cache}) {
+    check_fp32(*t, "attention_decode_append");
+  }
+  TORCH_CHECK(q.dim() == 4 && q.size(2) == 1 && k_new.sizes() == q.sizes() &&
+                  v_new.sizes() == q.sizes() && k_cache.dim() == 4 &&
+                  v_cache.sizes() == k_cache.sizes() && k_cache.size(0) == q.size(0) &&
+                  k_cache.size(1) == q.size(1) && k_cache.size(3) == q.size(3),
+              "attention_decode_append: expected q, k_new, v_new [B, H, 1, D] and caches "
+              "[B, H, T, D]");
+  check_pos(pos, q, "attention_decode_append");
+  c10::DeviceGuard guard(q.device());
+  const bool inner = q.stride(3) == 1 && k_new.stride(3) == 1 && v_new.stride(3) == 1 &&
+                     k_cache.stride(3) == 1 && v_cache.stride(3) == 1;
+  if (inner) {
+    const int64_t B = q.size(0), H = q.size(1), E = q.size(3);
+    at::Tensor out_buf = empty_device({B, 1, H, E}, q.options());
+    at::Tensor out = out_buf.permute({0, 2, 1, 3});
+    auto st = [](const at::Tensor& t) {
+      return std::array<int64_t, 3>{t.stride(0), t.stride(1), t.stride(2)};
+    };
+    const auto qs = st(q), kns = st(k_new), vns = st(v_new), kcs = st(k_cache),
+               vcs = st(v_cache), os = st(out);
+    const int rc = tvr_attention_decode_append(
+        static_cast<const float*>(q.data_ptr()), static_cast<const float*>(k_new.data_ptr()),
+        static_cast<const float*>(v_new.data_ptr()), static_cast<float*>(k_cache.data_ptr()),
+        static_cast<float*>(v_cache.data_ptr()), static_cast<float*>(out.data_ptr()), B, H,
+        k_cache.size(2), E, qs.data(), kns.data(), vns.data(), kcs.data(), vcs.data(), os.data(),
+        static_cast<float>(scale), static_cast<const int64_t*>(pos.data_ptr()), gemm_mode(),
+        current_stream_handle());
+    if (rc == TVR_OK) return out;
+    TORCH_CHECK(rc == TVR_ERR_UNSUPPORTED, "tvarant: ", tvr_last_error());
+  }
+  kv_append_(k_cache, k_new, pos);
+  kv_append_(v_cache, v_new, pos);
+  return attention_keylen(q, k_cache, v_cache, pos, 1, scale);
+}
+
 at::Tensor& counter_add_(at::Tensor& counter, int64_t delta) {
   TORCH_CHECK(is_device(counter) && counter.scalar_type() == at::kLong && counter.numel() == 1,
               "counter_add_: expected a one-element int64 tvarant tensor");
@@ -190,12 +237,15 @@ TORCH_LIBRARY_FRAGMENT(tvarant, m) {
   m.def("attention_keylen(Tensor q, Tensor k, Tensor v, Tensor key_len, int key_len_add, "
         "float scale) -> Tensor");
   m.def("counter_add_(Tensor(a!) counter, int delta) -> Tensor(a!)");
+  m.def("attention_decode_append(Tensor q, Tensor k_new, Tensor v_new, Tensor(a!) k_cache, "
+        "Tensor(b!) v_cache, Tensor pos, float scale) -> Tensor");
 }
 
 TORCH_LIBRARY_IMPL(tvarant, PrivateUse1, m) {
   m.impl("kv_append_", TORCH_FN(tvarant::ops::kv_append_));
   m.impl("attention_keylen", TORCH_FN(tvarant::ops::attention_keylen));
   m.impl("counter_add_", TORCH_FN(tvarant::ops::counter_add_));
+  m.impl("attention_decode_append", TORCH_FN(tvarant::ops::attention_decode_append));
 }
 
 TORCH_LIBRARY_IMPL(aten, PrivateUse1, m) {

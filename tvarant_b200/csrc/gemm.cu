@@ -54,6 +54,12 @@ int run(const float* a, const float* b, const float* bias, float* c, int64_t m, 
     return then_prog(gemm_skinny(a, b, bias, c, m, n, k, lda, ldb, ldc, alpha, beta, act, stream));
   }
   if (mode != TVR_GEMM_FP32 && batch == 1 && gemm_ws_applies(a, b, m, n, k, lda, ldb, trans_b)) {
+    // a residual add runs in the kernel's reduction epilogue (one launch less
+    // in a decode step's attention projection and down projection)
+    if (prog != nullptr && epi_is_residual_add(*prog)) {
+      return gemm_ws(a, b, bias, c, m, n, k, lda, ldb, ldc, alpha, beta, act,
+                     mode == TVR_GEMM_3XTF32, stream, prog->in[0], prog->ld[0]);
+    }
     return then_prog(gemm_ws(a, b, bias, c, m, n, k, lda, ldb, ldc, alpha, beta, act,
                              mode == TVR_GEMM_3XTF32, stream));
   }

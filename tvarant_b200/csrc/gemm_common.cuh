@@ -60,12 +60,14 @@ int gemm_skinny(const float* a, const float* b, const float* bias, float* c, int
 
 // Weight-streaming tcgen05 GEMM for at most 128 rows against a K-major
 // weight (split-K over a thread-block cluster, reduced in distributed shared
-// memory); applies when gemm_ws_applies() holds.
+// memory); applies when gemm_ws_applies() holds.  A non-null `resid` [m, n]
+// (row stride resid_ld) is added to the result in the epilogue.
 bool gemm_ws_applies(const float* x, const float* w, int64_t m, int64_t n, int64_t k,
                      int64_t ldx, int64_t ldw, bool trans_b);
 int gemm_ws(const float* x, const float* w, const float* bias, float* c, int64_t m, int64_t n,
             int64_t k, int64_t ldx, int64_t ldw, int64_t ldc, float alpha, float beta, int act,
-            bool split3, cudaStream_t stream);
+            bool split3, cudaStream_t stream, const float* resid = nullptr,
+            int64_t resid_ld = 0);
 
 // silu(x . Wg^T) * (x . Wu^T) in one TF32 tcgen05 pass (K-major weights);
 // TVR_ERR_UNSUPPORTED when the operands cannot be described by TMA maps.

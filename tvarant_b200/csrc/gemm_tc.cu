@@ -1323,12 +1323,7 @@ int gemm_tcgen05(const float* a, const float* b, const float* bias, float* c, in
   // r a full row-major matrix with 16-byte aligned rows), runs natively in
   // the TMA-store epilogue instead of as stack code.
   const bool resid_native =
-      has_prog && tma_ok && batch == 1 && prog->n_nodes == 3 && prog->n_extra == 1 &&
-      prog->op[0] == kEpiLoad && prog->op[1] == kEpiLoad && prog->op[2] == kEpiAdd &&
-      prog->alpha[2] == 1.f &&
-      ((prog->src[0] == -1 && prog->src[1] == 0) || (prog->src[0] == 0 && prog->src[1] == -1)) &&
-      ((prog->a[2] == 0 && prog->b[2] == 1) || (prog->a[2] == 1 && prog->b[2] == 0)) &&
-      prog->in[0] != nullptr && prog->ld[0] != 0 && prog->vec[0] != 0;
+      has_prog && tma_ok && batch == 1 && epi_is_residual_add(*prog) && prog->vec[0] != 0;
   if (resid_native) {
     p.resid = prog->in[0];
     p.resid_ld = prog->ld[0];

@@ -8,8 +8,11 @@
 //     tcgen05.mma kind::tf32 takes 128 weight rows and the narrow side
 //     (MMA N = MB in {16, 32, 64, 128}) takes the activation rows, so no
 //     tensor work or shared memory is spent on padding rows of X;
-//   * K is split over the S CTAs (S <= 8) of a thread-block cluster, grid
-//     (S, N / 128), sized to fill the SMs; each CTA streams its 128 x K/S
+//   * K is split over the S CTAs of a thread-block cluster, grid
+//     (S, N / 128), sized to fill the SMs: S <= 8 (the portable cluster
+//     size), or up to 16 when the weight has so few 128-row tiles that 8
+//     splits would leave most SMs idle (N = 768: 48 CTAs) and the device
+//     can hold all the clusters at once; each CTA streams its 128 x K/S
 //     weight panel through a TMA ring and accumulates 128 x MB in TMEM;
 //   * the S partial tiles are combined through distributed shared memory:
 //     every CTA copies its accumulator into its own shared memory, and after
@@ -42,6 +45,7 @@
 #include <cstring>
 #include <mutex>
 
+#include "cluster.cuh"
 #include "gemm_common.cuh"
 #include "tc_ptx.cuh"
 
@@ -52,7 +56,8 @@ using namespace tc;
 
 constexpr int BM = 128;  // weight rows per tile: the MMA's M
 constexpr int BK = 32;   // fp32 per k-block: one 128-byte swizzle row
-constexpr int MAX_SPLITS = 8;
+constexpr int MAX_SPLITS = 16;
+constexpr int PORTABLE_SPLITS = 8;
 
 template <int MB, bool SPLIT3>
 struct Cfg {
@@ -89,6 +94,8 @@ struct Params {
   const float* bias;
   float* c;
   int64_t ldc;
+  const float* resid;  // non-null: added to the result (a residual stream)
+  int64_t resid_ld;
   float alpha;
   float beta;
   int act;
@@ -98,35 +105,6 @@ struct Params {
   int kb_per_split;
   int* status;
 };
-
-__device__ __forceinline__ uint32_t cluster_rank() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-  return r;
-}
-
-__device__ __forceinline__ uint32_t cluster_size() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(r));
-  return r;
-}
-
-__device__ __forceinline__ void cluster_sync() {
-  asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
-}
-
-// Address of the same shared-memory location in CTA `rank` of the cluster.
-__device__ __forceinline__ uint32_t dsmem_addr(uint32_t local, uint32_t rank) {
-  uint32_t r;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local), "r"(rank));
-  return r;
-}
-
-__device__ __forceinline__ float ld_dsmem(uint32_t addr) {
-  float v;
-  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr));
-  return v;
-}
 
 __device__ __forceinline__ void st_shared(uint32_t addr, float v) {
   asm volatile("st.shared.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
@@ -429,7 +407,9 @@ __global__ void __launch_bounds__(Cfg<MB, SPLIT3>::THREADS, Cfg<MB, SPLIT3>::CTA
     float prev = 0.f;
     if (p.bias != nullptr) prev = __ldg(p.bias + col);
     else if (p.use_prev) prev = *dst;
-    *dst = epilogue_value(sum, prev, p.alpha, p.beta, p.act);
+    float v = epilogue_value(sum, prev, p.alpha, p.beta, p.act);
+    if (p.resid != nullptr) v = __fadd_rn(v, p.resid[static_cast<int64_t>(row) * p.resid_ld + col]);
+    *dst = v;
   }
   cluster_sync();  // no CTA leaves while another still reads its shared memory
   tc_fence_after();
@@ -440,14 +420,52 @@ __global__ void __launch_bounds__(Cfg<MB, SPLIT3>::THREADS, Cfg<MB, SPLIT3>::CTA
   }
 }
 
+// How many clusters of `splits` CTAs of this kernel the device holds at once
+// (cudaOccupancyMaxActiveClusters; 0 when it cannot launch them), cached per
+// device and cluster size.  Sizes above 8 are non-portable: they depend on
+// how many SMs a GPC has free.
+template <int MB, bool SPLIT3>
+int resident_clusters(int splits, int dev) {
+  using Cf = Cfg<MB, SPLIT3>;
+  static std::mutex mu;
+  static int cache[64][MAX_SPLITS + 1];
+  static bool known[64][MAX_SPLITS + 1];
+  std::lock_guard<std::mutex> lock(mu);
+  if (known[dev & 63][splits]) return cache[dev & 63][splits];
+  int n = 0;
+  cudaError_t e = cudaSuccess;
+  if (splits > PORTABLE_SPLITS) {
+    e = cudaFuncSetAttribute(gemm_ws_kernel<MB, SPLIT3>,
+                             cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  }
+  if (e == cudaSuccess) {
+    cudaLaunchConfig_t cfg;
+    memset(&cfg, 0, sizeof(cfg));
+    cfg.gridDim = dim3(static_cast<unsigned>(splits), 1, 1);
+    cfg.blockDim = dim3(Cf::THREADS, 1, 1);
+    cfg.dynamicSmemBytes = Cf::SMEM_BYTES;
+    cudaLaunchAttribute attr[1];
+    memset(attr, 0, sizeof(attr));
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = static_cast<unsigned>(splits);
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    e = cudaOccupancyMaxActiveClusters(&n, gemm_ws_kernel<MB, SPLIT3>, &cfg);
+  }
+  if (e != cudaSuccess) {
+    (void)cudaGetLastError();  // a refused size is an answer, not a sticky error
+    n = 0;
+  }
+  cache[dev & 63][splits] = n;
+  known[dev & 63][splits] = true;
+  return n;
+}
+
 template <int MB, bool SPLIT3>
 int launch(Params& p, int tiles, int sms, cudaStream_t stream, int dev) {
   using Cf = Cfg<MB, SPLIT3>;
-  // Splits of K per tile: as many as keep every CTA resident in one wave.
-  const int slots = sms * Cf::CTAS_PER_SM;
-  int splits = std::max(1, std::min({slots / tiles, MAX_SPLITS, p.num_kb}));
-  p.kb_per_split = static_cast<int>(ceil_div(p.num_kb, splits));
-  splits = static_cast<int>(ceil_div(p.num_kb, p.kb_per_split));  // no empty split
   static std::once_flag once[64];
   static cudaError_t attr_err[64];
   std::call_once(once[dev & 63], [&]() {
@@ -456,6 +474,17 @@ int launch(Params& p, int tiles, int sms, cudaStream_t stream, int dev) {
                                               Cf::SMEM_BYTES);
   });
   TVR_CUDA_TRY(attr_err[dev & 63]);
+  // Splits of K per tile: as many as keep every CTA resident in one wave.
+  const int slots = sms * Cf::CTAS_PER_SM;
+  auto split_k = [&](int cap) {
+    const int s = std::max(1, std::min({slots / tiles, cap, p.num_kb}));
+    p.kb_per_split = static_cast<int>(ceil_div(p.num_kb, s));
+    return static_cast<int>(ceil_div(p.num_kb, p.kb_per_split));  // no empty split
+  };
+  int splits = split_k(MAX_SPLITS);
+  if (splits > PORTABLE_SPLITS && resident_clusters<MB, SPLIT3>(splits, dev) < tiles) {
+    splits = split_k(PORTABLE_SPLITS);
+  }
   cudaLaunchConfig_t cfg;
   memset(&cfg, 0, sizeof(cfg));
   cfg.gridDim = dim3(static_cast<unsigned>(splits), static_cast<unsigned>(tiles), 1);
@@ -492,7 +521,7 @@ bool gemm_ws_applies(const float* x, const float* w, int64_t m, int64_t n, int64
 
 int gemm_ws(const float* x, const float* w, const float* bias, float* c, int64_t m, int64_t n,
             int64_t k, int64_t ldx, int64_t ldw, int64_t ldc, float alpha, float beta, int act,
-            bool split3, cudaStream_t stream) {
+            bool split3, cudaStream_t stream, const float* resid, int64_t resid_ld) {
   using namespace ws;
   const int dev = current_device();
   const int sms = sm_count(dev);
@@ -508,6 +537,8 @@ int gemm_ws(const float* x, const float* w, const float* bias, float* c, int64_t
   p.bias = bias;
   p.c = c;
   p.ldc = ldc;
+  p.resid = resid;
+  p.resid_ld = resid_ld;
   p.alpha = alpha;
   p.beta = beta;
   p.act = act;

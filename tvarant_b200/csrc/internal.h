@@ -75,6 +75,17 @@ __device__ __forceinline__ void grid_launch_dependents() {
 
 inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
+// Attention of at most four query rows per (sequence, head) on the CUDA
+// cores (attention_decode.cu): the decode-step form of tvr_attention_fwd.
+// The caller has checked sizes, pointers, a positive finite scale and 16-byte
+// aligned operands with strides that are multiples of 4 elements.
+bool attention_decode_applies(int64_t seq_q, int64_t head_dim);
+int attention_decode(const float* q, const float* k, const float* v, float* out, float* lse,
+                     int64_t batch, int64_t heads, int64_t seq_q, int64_t seq_k,
+                     const int64_t* q_strides, const int64_t* k_strides,
+                     const int64_t* v_strides, const int64_t* o_strides, float scale, int causal,
+                     const int64_t* key_len, int key_len_add, cudaStream_t stream);
+
 // Grid size for grid-stride elementwise kernels: enough blocks to cover the
 // work, capped at `waves` resident waves of the device.
 inline unsigned elementwise_grid(int64_t work_items, int threads, int device, int waves = 8) {

@@ -9,11 +9,13 @@
 // path otherwise.
 #include "internal.h"
 
+#include "cluster.cuh"
 #include "fastdiv.cuh"
 
 #include <cfloat>
 #include <climits>
 #include <cmath>
+#include <cstring>
 
 namespace tvr {
 namespace {
@@ -163,8 +165,13 @@ __global__ void __launch_bounds__(kThreads) tri_kernel(const T* __restrict__ x, 
 
 // Row argmax: index of the largest value of each row of n contiguous values,
 // the first one on ties, NaN counting as larger than any number (PyTorch's
-// rule).  One block per row; each thread scans a strided slice, then a
-// (value, index) reduction across the block.
+// rule).  A row is split over the CL CTAs of a cluster (CL > 1 when there are
+// too few rows to fill the GPU, e.g. a decode step's [batch, vocab] logits):
+// each thread scans a strided slice of its CTA's part with sixteen loads in
+// flight, then a (value, index) reduction across the block and, through
+// distributed shared memory, across the cluster.  The comparison orders
+// candidates totally (value, then index), so the result does not depend on
+// how the row is split.
 __device__ __forceinline__ bool argmax_better(float v, int64_t i, float bv, int64_t bi) {
   const bool vn = v != v, bn = bv != bv;
   if (vn != bn) return vn;                    // a NaN beats a number
@@ -172,18 +179,38 @@ __device__ __forceinline__ bool argmax_better(float v, int64_t i, float bv, int6
   return i < bi;                              // equal (or both NaN): first index
 }
 
-__global__ void __launch_bounds__(256) argmax_rows_kernel(const float* __restrict__ x,
-                                                          int64_t* __restrict__ out, int64_t n) {
-  __shared__ float sv[8];
-  __shared__ int64_t si[8];
-  const float* xr = x + static_cast<int64_t>(blockIdx.x) * n;
+constexpr int kArgmaxThreads = 256;
+constexpr int kArgmaxCluster = 8;
+
+template <int CL>
+__global__ void __launch_bounds__(kArgmaxThreads) argmax_rows_kernel(const float* __restrict__ x,
+                                                                     int64_t* __restrict__ out,
+                                                                     int64_t n) {
+  __shared__ float sv[kArgmaxThreads / 32];
+  __shared__ int64_t si[kArgmaxThreads / 32];
+  const int64_t row = CL == 1 ? blockIdx.x : blockIdx.y;
+  const int64_t part = CL == 1 ? 0 : static_cast<int64_t>(cluster_rank());
+  const int64_t chunk = (n + CL - 1) / CL;
+  const int64_t begin = part * chunk;
+  const int64_t end = min(n, begin + chunk);
+  const float* xr = x + row * n;
   float bv = -INFINITY;
   int64_t bi = INT64_MAX;
-  for (int64_t i = threadIdx.x; i < n; i += blockDim.x) {
-    const float v = xr[i];
-    if (argmax_better(v, i, bv, bi)) {
-      bv = v;
-      bi = i;
+  constexpr int U = 16;
+  for (int64_t i = begin + threadIdx.x; i < end; i += U * kArgmaxThreads) {
+    float v[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int64_t j = i + u * kArgmaxThreads;
+      v[u] = j < end ? __ldg(xr + j) : 0.f;
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int64_t j = i + u * kArgmaxThreads;
+      if (j < end && argmax_better(v[u], j, bv, bi)) {
+        bv = v[u];
+        bi = j;
+      }
     }
   }
 #pragma unroll
@@ -202,14 +229,33 @@ __global__ void __launch_bounds__(256) argmax_rows_kernel(const float* __restric
   }
   __syncthreads();
   if (threadIdx.x == 0) {
-    for (int w = 1; w < static_cast<int>(blockDim.x >> 5); ++w) {
+    for (int w = 1; w < kArgmaxThreads / 32; ++w) {
       if (argmax_better(sv[w], si[w], bv, bi)) {
         bv = sv[w];
         bi = si[w];
       }
     }
-    out[blockIdx.x] = bi;
+    sv[0] = bv;
+    si[0] = bi;
   }
+  if (CL == 1) {
+    if (threadIdx.x == 0) out[row] = bi;
+    return;
+  }
+  cluster_sync();  // every CTA's candidate is in its shared memory
+  if (part == 0 && threadIdx.x == 0) {
+    const uint32_t av = smem_addr_u32(&sv[0]), ai = smem_addr_u32(&si[0]);
+    for (int r = 1; r < CL; ++r) {
+      const float ov = ld_dsmem(dsmem_addr(av, static_cast<uint32_t>(r)));
+      const int64_t oi = ld_dsmem_s64(dsmem_addr(ai, static_cast<uint32_t>(r)));
+      if (argmax_better(ov, oi, bv, bi)) {
+        bv = ov;
+        bi = oi;
+      }
+    }
+    out[row] = bi;
+  }
+  cluster_sync();  // no CTA leaves while CTA 0 still reads its shared memory
 }
 
 }  // namespace
@@ -257,7 +303,28 @@ int tvr_argmax_rows(const float* x, int64_t* out, int64_t rows, int64_t n, void*
   TVR_CHECK(rows <= 0x7fffffff, "tvr_argmax_rows: too many rows");
   if (rows == 0) return TVR_OK;
   TVR_CHECK(x && out, "tvr_argmax_rows: null pointer");
-  argmax_rows_kernel<<<static_cast<unsigned>(rows), 256, 0, as_stream(stream)>>>(x, out, n);
+  const int dev = current_device();
+  cudaStream_t s = as_stream(stream);
+  // Fewer rows than two per SM and long rows: each row over a cluster of
+  // CTAs (a single CTA streaming a 50257-float row took ~80 us).
+  if (rows < 2 * static_cast<int64_t>(sm_count(dev)) && n >= kArgmaxCluster * 2048) {
+    cudaLaunchConfig_t cfg;
+    memset(&cfg, 0, sizeof(cfg));
+    cfg.gridDim = dim3(kArgmaxCluster, static_cast<unsigned>(rows), 1);
+    cfg.blockDim = dim3(kArgmaxThreads, 1, 1);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    memset(attr, 0, sizeof(attr));
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = kArgmaxCluster;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    TVR_CUDA_TRY(cudaLaunchKernelEx(&cfg, argmax_rows_kernel<kArgmaxCluster>, x, out, n));
+    return TVR_OK;
+  }
+  argmax_rows_kernel<1><<<static_cast<unsigned>(rows), kArgmaxThreads, 0, s>>>(x, out, n);
   TVR_LAUNCH_CHECK();
   return TVR_OK;
 }

@@ -278,9 +278,9 @@ def decode_step(model: GPT2, ids: torch.Tensor, cache: KVCache, pos: torch.Tenso
     for li, L in enumerate(model.layers):
         h = F.layer_norm(x, (d,), L.ln1_g, L.ln1_b, 1e-5)
         qkv = F.linear(h, L.w_qkv, L.b_qkv).view(B, 1, 3, H, hd).permute(2, 0, 3, 1, 4)
-        torch.ops.tvarant.kv_append_(cache.k[li], qkv[1], pos)
-        torch.ops.tvarant.kv_append_(cache.v[li], qkv[2], pos)
-        o = torch.ops.tvarant.attention_keylen(qkv[0], cache.k[li], cache.v[li], pos, 1, scale)
+        # the cache append and the attention over positions 0..pos, one launch
+        o = torch.ops.tvarant.attention_decode_append(qkv[0], qkv[1], qkv[2], cache.k[li],
+                                                      cache.v[li], pos, scale)
         o = o.transpose(1, 2).reshape(B, 1, d)
         x = _linear_residual(x, o, L.w_proj, L.b_proj)
         h = F.layer_norm(x, (d,), L.ln2_g, L.ln2_b, 1e-5)
