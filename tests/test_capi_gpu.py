@@ -77,6 +77,8 @@ GEMM_SHAPES = [
     (513, 264, 260),
     (259, 1001, 192),   # N odd: output rows not 16-byte aligned (lane-per-column stores)
     (129, 50257, 64),   # vocabulary-sized N, unaligned rows
+    (8192, 768, 128),   # N = 768 at many rows: 192-wide tiles (TF32), TMA-store epilogue
+    (8192, 766, 128),   # same tiles, output rows not 16-byte aligned: register epilogue
 ]
 
 

@@ -137,6 +137,7 @@ def _tol(mode):
     (128, 1024, 512),   # few tiles: split-K, then the pass
     (16, 512, 4096),    # weight-streaming GEMM, then the pass
     (37, 29, 53),       # unaligned: CUDA-core GEMM, then the pass
+    (8192, 768, 128),   # TF32: 192-wide tiles with the program in the epilogue
 ])
 @pytest.mark.parametrize("mode", [TF32, X3])
 def test_chain_after_linear_silu(lib, rng, m, n, k, mode):
@@ -164,6 +165,7 @@ RESIDUAL = [(0, -1, -1, 0, 1, 0), (0, -1, -1, 1, 1, 0), (2, 0, 1, -1, 1, 0)]
     (8, 768, 3072),     # a decode step's down projection: the few-row GEMM
     (100, 1001, 512),   # few rows, a ragged weight tile and unaligned rows
     (2, 768, 768),      # two rows (3xTF32: the fp32 GEMV, then the pass)
+    (8192, 768, 256),   # TF32: 192-wide tiles (a GPT-2 projection at batch 8 x 1024)
 ])
 @pytest.mark.parametrize("mode", [TF32, X3])
 @pytest.mark.parametrize("gemm_input", [0, 1])

@@ -29,8 +29,9 @@
 //     cache, so the cache append costs no launch of its own; the arithmetic is
 //     the same as appending first and then attending.
 // Loads are plain coalesced 16-byte loads into registers (a cp.async ring in
-// shared memory measured slower: 35 KB per CTA left too little room to place
-// a decode step's 96 eight-CTA clusters in one wave); no TMA, no multicast.
+// shared memory measured slower, 11.8 against 10.5 us for a decode layer,
+// likely because 35 KB per CTA leaves too little room to place 96 eight-CTA
+// clusters in one wave); no TMA, no multicast.
 #include "internal.h"
 
 #include <cmath>

@@ -72,11 +72,12 @@ struct Cfg {
   // two accumulators (one being filled while the epilogue drains the
   // other); 3xTF32 adds the running sum of a tile's K chunks (at column
   // 2 * BN).  Allocations are powers of two.
-  static constexpr int TMEM_COLS = SPLIT3 ? (BN == 64 ? 256 : 512) : 2 * BN;
+  static constexpr int TMEM_COLS = SPLIT3 ? (BN == 64 ? 256 : 512) : (BN == 192 ? 512 : 2 * BN);
   static constexpr int BAR_BYTES = 8 * (2 * STAGES + 5) + 8;
   static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + EPI_SMEM + BAR_BYTES;
   static_assert(SMEM_BYTES <= 232448 - 64, "shared memory budget");
-  static_assert(BN == 64 || BN == 128 || BN == 256, "BN");
+  static_assert(BN == 64 || BN == 128 || BN == 192 || BN == 256, "BN");
+  static_assert(BN != 192 || !SPLIT3, "192-wide tiles are TF32 only");
   static_assert(!SPLIT3 || BN <= 128, "3xTF32 tiles keep a running sum beside two accumulators");
 };
 
@@ -1115,6 +1116,14 @@ int launch_nvls(const Params& p, int grid, cudaStream_t stream, int dev) {
 template <int BN>
 int launch_bn(const Params& p, bool split3, bool b_nmajor, int grid, cudaStream_t s, int dev,
               bool prog = false, bool tma_c = false) {
+  if constexpr (BN == 192) {
+    // TF32 with a K-major weight only (the tile width gemm_tcgen05 picks for
+    // N = 768-like outputs)
+    if (split3 || b_nmajor) return fail(TVR_ERR_INVALID, "gemm: 192-wide tiles are TF32 K-major");
+    if (prog) return launch_kernel<BN, false, false, false, true>(p, grid, s, dev);
+    if (tma_c) return launch_kernel<BN, false, false, false, false, true>(p, grid, s, dev);
+    return launch_kernel<BN, false, false>(p, grid, s, dev);
+  }
   if constexpr (BN <= 128) {
     if (split3) {
       if (prog) return launch_kernel<BN, true, false, false, true>(p, grid, s, dev);
@@ -1196,6 +1205,18 @@ int gemm_tcgen05(const float* a, const float* b, const float* bias, float* c, in
     bn = cand;
     tiles = t;
     if (t >= (sms * 4) / 5) break;
+  }
+  // A 192-wide tile where it cuts the wave-quantised time of the tiles by
+  // more than 15 % (time ~ waves x tile width).  N = 768 at M = 8192: 192
+  // tiles of 256 take two waves on 148 SMs, 256 tiles of 192 two waves of
+  // three-quarter-size tiles.
+  if (bn == 256 && !split3 && trans_b && batch == 1) {
+    const int64_t t192 = ceil_div(m, BM) * ceil_div(n, 192);
+    const int64_t w256 = ceil_div(tiles, sms), w192 = ceil_div(t192, sms);
+    if (w192 * 192 * 100 < w256 * 256 * 85) {
+      bn = 192;
+      tiles = t192;
+    }
   }
   const bool c_vec = al16(c) && ldc % 4 == 0 && (batch == 1 || sc % 4 == 0);
   int splits = 1;
@@ -1340,6 +1361,9 @@ int gemm_tcgen05(const float* a, const float* b, const float* bias, float* c, in
   switch (bn) {
     case 256:
       rc = launch_bn<256>(p, split3, b_nmajor, grid, stream, dev, prog_in_kernel, tma_c);
+      break;
+    case 192:
+      rc = launch_bn<192>(p, split3, b_nmajor, grid, stream, dev, prog_in_kernel, tma_c);
       break;
     case 128:
       rc = launch_bn<128>(p, split3, b_nmajor, grid, stream, dev, prog_in_kernel, tma_c);
