@@ -724,6 +724,17 @@ def single_gpu_extras(torch, args, tf32_peak) -> dict:
         "tflop_per_step": g_line["config"]["tflop_per_step"],
         "last_logits_finite": g_line["config"]["last_logits_finite"]}
     out["attention"] = g_line["config"]["attention_kernel"]
+    # GPT-2-small decode with a KV cache (batch 8, 512-token prompt, the step
+    # replayed as one CUDA graph), the gpt2-decode workload's own code path
+    d_args = argparse.Namespace(**vars(g_args))
+    d_args.workload, d_args.prompt, d_args.steps, d_args.warmup = "gpt2-decode", 512, 20, 3
+    d_line = workloads._gpt2_decode(d_args, 0, 1, torch.tvarant.current_device())
+    torch.tvarant.empty_cache()
+    out["gpt2_decode"] = {
+        "workload": d_line["config"]["workload"], "tokens_per_s": d_line["value"],
+        "ms_per_step": d_line["ms_per_step"],
+        "eager_tokens_per_s": d_line["config"]["eager_tokens_per_s"],
+        "hbm_frac_of_step_bytes": d_line["roofline"]["frac"]}
     torch.set_float32_matmul_precision("high" if args.mode == "tf32" else "highest")
     return out
 

@@ -11,8 +11,8 @@
 //   * K is split over the S CTAs of a thread-block cluster, grid
 //     (S, N / 128), sized to fill the SMs: S <= 8 (the portable cluster
 //     size), or up to 16 when the weight has so few 128-row tiles that 8
-//     splits would leave most SMs idle (N = 768: 48 CTAs) and the device
-//     can hold all the clusters at once; each CTA streams its 128 x K/S
+//     splits leave SMs without a CTA (N = 768: 48 CTAs) and the device can
+//     hold all the clusters at once; each CTA streams its 128 x K/S
 //     weight panel through a TMA ring and accumulates 128 x MB in TMEM;
 //   * the S partial tiles are combined through distributed shared memory:
 //     every CTA copies its accumulator into its own shared memory, and after
@@ -481,7 +481,10 @@ int launch(Params& p, int tiles, int sms, cudaStream_t stream, int dev) {
     p.kb_per_split = static_cast<int>(ceil_div(p.num_kb, s));
     return static_cast<int>(ceil_div(p.num_kb, p.kb_per_split));  // no empty split
   };
-  int splits = split_k(MAX_SPLITS);
+  // More than 8 splits only for weights so narrow that 8 splits leave SMs
+  // without a CTA (N = 768: 6 tiles, 48 CTAs), and only when the device holds
+  // every cluster at once.
+  int splits = split_k(tiles * PORTABLE_SPLITS <= sms ? MAX_SPLITS : PORTABLE_SPLITS);
   if (splits > PORTABLE_SPLITS && resident_clusters<MB, SPLIT3>(splits, dev) < tiles) {
     splits = split_k(PORTABLE_SPLITS);
   }
