@@ -1209,8 +1209,9 @@ int gemm_tcgen05(const float* a, const float* b, const float* bias, float* c, in
   // A 192-wide tile where it cuts the wave-quantised time of the tiles by
   // more than 15 % (time ~ waves x tile width).  N = 768 at M = 8192: 192
   // tiles of 256 take two waves on 148 SMs, 256 tiles of 192 two waves of
-  // three-quarter-size tiles.
-  if (bn == 256 && !split3 && trans_b && batch == 1) {
+  // three-quarter-size tiles.  Only with a full wave of 256-wide tiles:
+  // fewer tiles split K instead (below), which balances them better.
+  if (bn == 256 && !split3 && trans_b && batch == 1 && tiles >= (sms * 4) / 5) {
     const int64_t t192 = ceil_div(m, BM) * ceil_div(n, 192);
     const int64_t w256 = ceil_div(tiles, sms), w192 = ceil_div(t192, sms);
     if (w192 * 192 * 100 < w256 * 256 * 85) {
