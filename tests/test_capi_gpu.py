@@ -354,7 +354,12 @@ def test_softmax_leading_minus_inf(lib, rng, shape, dim):
     assert max_rel(y2[ok], ref2[ok], 1e-30) <= TOL_POINTWISE
 
 
-@pytest.mark.parametrize("batch,L,S", [(6, 128, 1024), (2, 64, 64), (3, 5, 2048), (1, 7, 4)])
+@pytest.mark.parametrize("batch,L,S", [
+    (6, 128, 1024), (2, 64, 64), (3, 5, 2048), (1, 7, 4),
+    # 8 or more rows per mask row: the shared-mask kernel (units of 8 rows),
+    # whole and partial units, every row width class
+    (8, 1024, 1024), (12, 96, 1024), (9, 3, 100), (16, 33, 2048), (96, 16, 512), (10, 2, 36),
+    (64, 1024, 256)])  # ~14 units per block: both shared-memory buffers reused
 def test_softmax_add_causal_mask(lib, rng, batch, L, S):
     """softmax(scores + mask) with an [L, S] mask shared by every batch row:
     the same bits as the device's add followed by its softmax, and the
