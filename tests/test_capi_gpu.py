@@ -489,6 +489,15 @@ def test_binary_broadcast(lib, rng, a_shape, b_shape, op, alpha):
     ((3, 8, 2, 4, 17, 5), (4, 0, 5, 2, 1, 3), np.float32),   # odd extents in every position
     ((2, 1024, 3, 12, 64), (2, 0, 3, 1, 4), np.float32),     # GPT-2 head split of a fused QKV
     ((997, 1031), (1, 0), np.float32),
+    # the transposed-run kernel: head merge, partial tiles, runs of 1, 2 and 64
+    # 16-byte elements, 8-byte elements, and more tiles than blocks
+    ((2, 12, 100, 64), (0, 2, 1, 3), np.float32),
+    ((3, 37, 5, 13, 32), (2, 0, 3, 1, 4), np.float32),
+    ((6, 10, 4), (1, 0, 2), np.float32),
+    ((2, 3, 17, 4, 8), (1, 3, 0, 2, 4), np.float32),
+    ((5, 3, 40, 256), (2, 1, 0, 3), np.float32),
+    ((4, 6, 8), (1, 0, 2), np.float64),
+    ((4, 1024, 3, 12, 64), (2, 0, 3, 1, 4), np.float32),
 ])
 def test_strided_copy(lib, rng, shape, perm, dtype):
     import torch

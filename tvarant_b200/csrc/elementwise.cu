@@ -411,6 +411,165 @@ __global__ void __launch_bounds__(kThreads) strided_copy_fast_kernel(T* __restri
   }
 }
 
+// ---- head splits and merges: a transpose of contiguous runs ------------------
+// A permutation that keeps a run of L 16-byte elements contiguous in both
+// tensors, where the destination's next dimension A (destination stride L)
+// is not the source's next dimension B (source stride L): [B, S, 3, H, D] ->
+// [3, B, H, S, D] to split attention heads, [B, H, S, D] -> [B, S, H, D] to
+// merge them.  Copied in destination order it reads L-element runs at a
+// stride of kilobytes (0.64 of the copy rate for GPT-2's head split).  Here
+// a block moves a TA x TB tile of runs through shared memory: it reads TB
+// runs that are contiguous in the source for each A index, then writes TA
+// runs that are contiguous in the destination for each B index.
+struct TransposeIndex {
+  FastDiv outer[TVR_MAX_DIMS];  // the other dimensions, outermost first
+  uint32_t outer_sd[TVR_MAX_DIMS];
+  uint32_t outer_ss[TVR_MAX_DIMS];
+  int n_outer;
+  uint32_t na, nb, run;  // extents of A and B; run length L
+  uint32_t a_ss, b_sd;   // A's source stride, B's destination stride
+  uint32_t ta, tb;       // tile extents
+  uint32_t tiles_a, tiles_b, tiles;
+  FastDiv div_run, div_tb_run, div_ta_run, div_tiles_a, div_tiles_b;
+};
+
+constexpr int kTransposeTileUnits = 2048;  // 32 KB of shared memory per block
+
+__global__ void __launch_bounds__(kThreads) copy_transpose_kernel(uint4* __restrict__ dst,
+                                                                  const uint4* __restrict__ src,
+                                                                  TransposeIndex ix) {
+  extern __shared__ uint4 tile[];  // [ta][tb][run]
+  const uint32_t units = ix.ta * ix.tb * ix.run;
+  const uint32_t tb_run = ix.tb * ix.run, ta_run = ix.ta * ix.run;
+  for (uint32_t t = blockIdx.x; t < ix.tiles; t += gridDim.x) {
+    const uint32_t q = fast_div(t, ix.div_tiles_b);
+    const uint32_t b0 = (t - q * ix.tiles_b) * ix.tb;
+    uint32_t rem = fast_div(q, ix.div_tiles_a);
+    const uint32_t a0 = (q - rem * ix.tiles_a) * ix.ta;
+    uint32_t so = 0, dso = 0;
+    for (int d = ix.n_outer - 1; d >= 0; --d) {
+      const uint32_t qq = fast_div(rem, ix.outer[d]);
+      const uint32_t c = rem - qq * ix.outer[d].d;
+      rem = qq;
+      so += c * ix.outer_ss[d];
+      dso += c * ix.outer_sd[d];
+    }
+    // tile index (a, b, v), v fastest: consecutive threads read consecutive
+    // source elements; a thread issues all U of its loads before it stores
+    // any of them, so a full tile (2048 elements over 256 threads) is in
+    // flight at once
+    constexpr int U = kTransposeTileUnits / kThreads;
+    for (uint32_t i0 = threadIdx.x; i0 < units; i0 += U * blockDim.x) {
+      uint4 val[U];
+      bool ok[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const uint32_t i = i0 + u * blockDim.x;
+        const uint32_t a = fast_div(i, ix.div_tb_run);
+        const uint32_t r = i - a * tb_run;
+        const uint32_t b = fast_div(r, ix.div_run);
+        const uint32_t v = r - b * ix.run;
+        ok[u] = i < units && a0 + a < ix.na && b0 + b < ix.nb;
+        if (ok[u]) val[u] = src[so + (a0 + a) * ix.a_ss + (b0 + b) * ix.run + v];
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        if (ok[u]) tile[i0 + u * blockDim.x] = val[u];
+      }
+    }
+    __syncthreads();
+    // (b, a, v), v fastest: consecutive threads write consecutive destination
+    // elements
+#pragma unroll 4
+    for (uint32_t i = threadIdx.x; i < units; i += blockDim.x) {
+      const uint32_t b = fast_div(i, ix.div_ta_run);
+      const uint32_t r = i - b * ta_run;
+      const uint32_t a = fast_div(r, ix.div_run);
+      const uint32_t v = r - a * ix.run;
+      if (a0 + a < ix.na && b0 + b < ix.nb) {
+        dst[dso + (b0 + b) * ix.b_sd + (a0 + a) * ix.run + v] = tile[(a * ix.tb + b) * ix.run + v];
+      }
+    }
+    __syncthreads();  // the next tile overwrites the shared memory
+  }
+}
+
+// Launches the transposed-run form when the collapsed copy (counted in
+// 16-byte elements) has that shape; *taken says whether it did.
+int launch_copy_transpose(void* dst, const void* src, const CopyIndex& ix, int r, int64_t n,
+                          cudaStream_t stream, int dev, bool* taken) {
+  *taken = false;
+  if (r < 3) return TVR_OK;
+  const int64_t run = ix.size[r - 1];
+  const int A = r - 2;
+  if (ix.sd[r - 1] != 1 || ix.ss[r - 1] != 1 || run < 1 || run > 64 || ix.sd[A] != run) {
+    return TVR_OK;
+  }
+  int B = -1;
+  for (int d = 0; d < A; ++d) {
+    if (ix.ss[d] == run) {
+      B = d;
+      break;
+    }
+  }
+  if (B < 0) return TVR_OK;
+  const int64_t lim = int64_t(1) << 31;
+  int64_t max_d = 0, max_s = 0;
+  for (int d = 0; d < r; ++d) {
+    if (ix.sd[d] < 0 || ix.ss[d] < 0 || ix.sd[d] >= lim || ix.ss[d] >= lim) return TVR_OK;
+    max_d += (ix.size[d] - 1) * ix.sd[d];
+    max_s += (ix.size[d] - 1) * ix.ss[d];
+  }
+  if (n >= lim || max_d >= lim || max_s >= lim) return TVR_OK;
+  TransposeIndex t{};
+  t.run = static_cast<uint32_t>(run);
+  t.na = static_cast<uint32_t>(ix.size[A]);
+  t.nb = static_cast<uint32_t>(ix.size[B]);
+  t.a_ss = static_cast<uint32_t>(ix.ss[A]);
+  t.b_sd = static_cast<uint32_t>(ix.sd[B]);
+  t.tb = std::min<uint32_t>(t.nb, 16);
+  t.ta = std::min<uint32_t>(t.na, std::max<uint32_t>(1, kTransposeTileUnits / (t.tb * t.run)));
+  t.tiles_a = static_cast<uint32_t>(ceil_div(int64_t(t.na), int64_t(t.ta)));
+  t.tiles_b = static_cast<uint32_t>(ceil_div(int64_t(t.nb), int64_t(t.tb)));
+  int64_t outer_count = 1;
+  t.n_outer = 0;
+  for (int d = 0; d < A; ++d) {
+    if (d == B) continue;
+    t.outer[t.n_outer] = make_fastdiv(static_cast<uint32_t>(ix.size[d]));
+    t.outer_sd[t.n_outer] = static_cast<uint32_t>(ix.sd[d]);
+    t.outer_ss[t.n_outer] = static_cast<uint32_t>(ix.ss[d]);
+    ++t.n_outer;
+    outer_count *= ix.size[d];
+  }
+  const int64_t tiles = outer_count * t.tiles_a * t.tiles_b;
+  if (tiles >= lim) return TVR_OK;
+  t.tiles = static_cast<uint32_t>(tiles);
+  t.div_run = make_fastdiv(t.run);
+  t.div_tb_run = make_fastdiv(t.tb * t.run);
+  t.div_ta_run = make_fastdiv(t.ta * t.run);
+  t.div_tiles_a = make_fastdiv(t.tiles_a);
+  t.div_tiles_b = make_fastdiv(t.tiles_b);
+  const size_t smem = static_cast<size_t>(t.ta) * t.tb * t.run * sizeof(uint4);
+  // persistent: only as many blocks as are resident at once (with the largest
+  // tile), so no block starts its share of the tiles after the others ended
+  static const int per_sm = [] {
+    int b = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, copy_transpose_kernel, kThreads,
+                                                      kTransposeTileUnits * sizeof(uint4)) !=
+            cudaSuccess ||
+        b < 1) {
+      b = 1;
+    }
+    return b;
+  }();
+  const int64_t grid = std::min<int64_t>(tiles, static_cast<int64_t>(sm_count(dev)) * per_sm);
+  copy_transpose_kernel<<<static_cast<unsigned>(grid), kThreads, smem, stream>>>(
+      static_cast<uint4*>(dst), static_cast<const uint4*>(src), t);
+  TVR_LAUNCH_CHECK();
+  *taken = true;
+  return TVR_OK;
+}
+
 // Sort dimensions so the destination is traversed in memory order, then
 // merge dimensions contiguous in both tensors.
 int collapse_copy(int ndim, const int64_t* sizes, const int64_t* sd, const int64_t* ss,
@@ -681,6 +840,11 @@ int tvr_strided_copy(void* dst, const void* src, int64_t elem_size, int ndim,
     }
     numel /= f;
     es *= f;
+  }
+  if (es == 16) {
+    bool taken = false;
+    const int rc = launch_copy_transpose(dst, src, ix, r, numel, s, dev, &taken);
+    if (rc != TVR_OK || taken) return rc;
   }
   switch (es) {
     case 1: return launch_copy<uint8_t>(dst, src, ix, r, numel, s, dev);

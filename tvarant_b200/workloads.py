@@ -321,7 +321,7 @@ def measure_mem_kernels(steps: int, warmup: int) -> dict:
     n = x.numel() * 4
     cases = {
         "softmax_warp_kernel [32768, 2048]": (lambda: F.softmax(sm, dim=-1), 2 * sm.numel() * 4),
-        "softmax_warp_kernel<MASK> [64, 1024, 1024] + [1024, 1024] mask": (
+        "softmax_shared_mask_kernel [64, 1024, 1024] + [1024, 1024] mask": (
             lambda: torch.ops.tvarant.softmax_add(scores, mask), 2 * scores.numel() * 4),
         "layer_norm_kernel [16384, 4096]": (
             lambda: F.layer_norm(x, (4096,), gamma, beta, 1e-5), 2 * n + 2 * 4096 * 4 + 2 * 16384 * 4),
@@ -334,7 +334,7 @@ def measure_mem_kernels(steps: int, warmup: int) -> dict:
         "rms_norm_kernel [16384, 4096]": (lambda: F.rms_norm(x, (4096,), gamma, 1e-6), 2 * n + 4096 * 4),
         "rope_half_vec_kernel q [1, 32, 16384, 128]": (
             lambda: torch.ops.tvarant.rope(q, cos, sin), 2 * q.numel() * 4 + 2 * 16384 * 64 * 4),
-        "strided_copy_kernel qkv [16, 1024, 3, 12, 64] -> [3, 16, 12, 1024, 64]": (
+        "copy_transpose_kernel qkv [16, 1024, 3, 12, 64] -> [3, 16, 12, 1024, 64]": (
             lambda: qkv.permute(2, 0, 3, 1, 4).contiguous(), 2 * qkv.numel() * 4),
     }
     for fn, _ in cases.values():
