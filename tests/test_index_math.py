@@ -15,6 +15,12 @@ reducing CTAs, restated in Python and checked for exact coverage (CPU).
   odd ones, while below the unit count; a CTA stops at its first empty
   round.
 
+* ``softmax_shared_mask_kernel`` (csrc/reduce.cu): with share = rows /
+  mask_rows rows per mask row, unit u of mask_rows * ceil(share / 8) is
+  (mask row u // groups, group u % groups); warp w of the block takes row
+  (8 * group + w) * mask_rows + mask row while 8 * group + w < share; block
+  b takes units b, b + grid, ...
+
 Every element (or unit, float4) must be taken exactly once, and no
 address may leave the output.
 """
@@ -180,3 +186,31 @@ def test_attention_schedule_balances_gpt2_causal_tiles():
     per_cta = [sum(cost(u) for u in got[(c, 0)]) for c in range(ctas)]
     mean = sum(per_cta) / ctas
     assert max(per_cta) <= 1.12 * mean and min(per_cta) >= 0.85 * mean, (per_cta, mean)
+
+
+def shared_mask_rows(rows, mask_rows, grid, warps=8):
+    share = rows // mask_rows
+    groups = -(-share // warps)
+    units = mask_rows * groups
+    seen = []
+    for blk in range(grid):
+        for u in range(blk, units, grid):
+            mrow, g = divmod(u, groups)
+            for w in range(warps):
+                k = g * warps + w
+                if k < share:
+                    row = k * mask_rows + mrow
+                    assert row % mask_rows == mrow  # the staged mask row is this row's
+                    seen.append(row)
+    return seen
+
+
+@pytest.mark.parametrize("rows,mask_rows,grid", [
+    (96 * 1024, 1024, 444),   # GPT-2 scores, batch 8 x 12 heads, on 148 SMs x 3
+    (8 * 1024, 1024, 444),    # one unit per mask row
+    (12 * 96, 96, 444),       # a partial group of 4 rows
+    (9 * 3, 3, 5),
+    (64 * 1024, 1024, 7),     # many units per block
+])
+def test_shared_mask_softmax_takes_every_row_once(rows, mask_rows, grid):
+    assert sorted(shared_mask_rows(rows, mask_rows, grid)) == list(range(rows))
