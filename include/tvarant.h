@@ -325,7 +325,8 @@ int tvr_softmax(const float* x, float* y, int64_t outer, int64_t dim, int64_t in
  * add is the same fp32 rounding as tvr_binary's, so the result equals
  * tvr_binary(ADD) followed by tvr_softmax.  Returns TVR_ERR_UNSUPPORTED
  * (nothing launched) unless dim % 4 == 0, dim <= 2048 and the three pointers
- * are 16-byte aligned.  No reference counterpart as one call: the reference
+ * are 16-byte aligned; TVR_ERR_INVALID unless rows is a whole number of
+ * mask_rows.  No reference counterpart as one call: the reference
  * runs add(scores, mask) then softmax (csrc/aten/LlmOps.cpp:68-105). */
 int tvr_softmax_add(const float* x, const float* mask, float* y, int64_t rows, int64_t dim,
                     int64_t mask_rows, void* stream);
